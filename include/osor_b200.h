@@ -1,0 +1,212 @@
+/*
+ * osor_b200 -- C ABI of the B200 (sm_100a) SDXL VAE hot path.
+ *
+ * This is the boundary a host binding calls: plain pointers, sizes and an
+ * opaque model handle; no framework types. Every device pointer refers to
+ * memory of the device the call runs on; `stream` is a cudaStream_t (NULL for
+ * the legacy default stream). Calls enqueue work on `stream` and return once
+ * it is enqueued; results are ready when the stream is synchronised.
+ *
+ * Each entry point names the reference (doublesharp/osor-rs) interface it
+ * replaces, by path:line inside that project.
+ */
+#ifndef OSOR_B200_H
+#define OSOR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. The first four errors mirror osor::Error (src/lib.rs:62-90):
+ * InvalidInput, InvalidArtifact, Unavailable, Cancelled; the last two are
+ * CUDA-level failures. A failed call leaves a message for
+ * osor_last_error_message() on the calling thread. */
+#define OSOR_OK 0
+#define OSOR_ERR_INVALID_INPUT 1
+#define OSOR_ERR_INVALID_ARTIFACT 2
+#define OSOR_ERR_UNAVAILABLE 3
+#define OSOR_ERR_CANCELLED 4
+#define OSOR_ERR_CUDA 5
+#define OSOR_ERR_TIMEOUT 6
+
+/* Element types. Weights and activations of a model (and the 16-bit tensors
+ * of an op call) are bf16 or f16; the reference's CUDA backend accepts both
+ * model dtypes (src/runtime.rs:406-417). f32 is accepted by the standalone
+ * group norm only. */
+#define OSOR_DTYPE_BF16 0
+#define OSOR_DTYPE_F16 1
+#define OSOR_DTYPE_F32 2
+
+/* Tensor layouts at the boundary. */
+#define OSOR_LAYOUT_NHWC 0 /* [B][H][W][C], the internal layout (16-bit) */
+#define OSOR_LAYOUT_NCHW 1 /* [B][C][H][W], the reference's layout */
+
+/* Operations for osor_vae_workspace_size. */
+#define OSOR_OP_DECODE 0
+#define OSOR_OP_ENCODE 1
+
+/* Model parts (bitmask) for osor_vae_config.parts. */
+#define OSOR_PART_DECODER 1
+#define OSOR_PART_ENCODER 2
+
+typedef struct osor_vae osor_vae;
+
+/* One named host float32 tensor of a diffusers-named VAE state dict, as the
+ * reference's VarBuilder reads it (src/native/vae_encoder.rs:224-260,388-412;
+ * src/native/vae_decoder.rs:62-101). */
+typedef struct osor_tensor {
+  const char* name;
+  const float* data;
+  int ndim;
+  int64_t shape[4];
+} osor_tensor;
+
+/* Architecture::sdxl() VAE fields (src/native.rs:94-95) plus the model dtype
+ * (LoadOptions::dtype, src/runtime.rs:137-160). */
+typedef struct osor_vae_config {
+  int channels[4]; /* block_out_channels, e.g. {128, 256, 512, 512} */
+  int layers;      /* resnets per encoder down block (decoder: layers + 1) */
+  int parts;       /* OSOR_PART_DECODER | OSOR_PART_ENCODER */
+  int dtype;       /* OSOR_DTYPE_BF16 or OSOR_DTYPE_F16 */
+} osor_vae_config;
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* osor_last_error_message(void);
+
+/* Library ABI version (major * 10000 + minor * 100 + patch). */
+int osor_version(void);
+
+/* OSOR_OK when `device` is an sm_100 GPU this library was built for, else
+ * OSOR_ERR_UNAVAILABLE. Replaces Backend::Cuda{ordinal} device resolution
+ * (src/runtime.rs:62-74). */
+int osor_device_check(int device);
+
+/* Synchronises `device`, returns its device-side status word (0 = no kernel
+ * reported a problem; 1 = a bounded wait timed out) and clears it when
+ * `reset` is non-zero. A negative value is -(status code) of a failed read. */
+int osor_device_status(int device, int reset);
+
+/* Builds a model from host float32 weights: repacks convolution weights to
+ * 16-bit [Cout][ky][kx][Cin], folds the attention scale C^-1/4 into the q and
+ * k projections and uploads everything to `device`. Missing or mis-shaped
+ * tensors return OSOR_ERR_INVALID_ARTIFACT. Replaces NativeModel::new ->
+ * VaeEncoder::new / VaeDecoder::new (src/native.rs:398-425,
+ * src/native/vae_encoder.rs:388-412, src/native/vae_decoder.rs:62-101). */
+int osor_vae_create(const osor_tensor* tensors, size_t count, const osor_vae_config* config,
+                    int device, osor_vae** out);
+void osor_vae_destroy(osor_vae* vae);
+
+/* Bytes of device workspace osor_vae_decode / osor_vae_encode_moments need
+ * for the given batch and spatial size (latent h, w for decode; image H, W
+ * for encode). 0 when the shape is not admissible. */
+size_t osor_vae_workspace_size(const osor_vae* vae, int op, int batch, int height, int width);
+
+/* Decodes unscaled latents [B][4][h][w] f32 (device) into raw RGB
+ * [B][3][8h][8w] f32 (device). `cancel` (nullable host flag) is polled
+ * between blocks; when it reads non-zero the call stops enqueuing and returns
+ * OSOR_ERR_CANCELLED. Replaces ModelBackend::decode / NativeModel::decode_checked
+ * -> VaeDecoder::forward (src/pipeline.rs:66-67, src/native.rs:525-533,
+ * src/native/vae_decoder.rs:104-114). */
+int osor_vae_decode(const osor_vae* vae, const float* latents, float* image, int batch,
+                    int latent_h, int latent_w, void* workspace, size_t workspace_bytes,
+                    void* stream, const volatile int* cancel);
+
+/* Encodes a normalized image [B][3][H][W] f32 in [-1, 1] (device) into raw
+ * posterior moments [B][8][H/8][W/8] f32 (device). Replaces
+ * ModelBackend::encode_moments / NativeModel::encode_moments_checked ->
+ * VaeEncoder::forward (src/pipeline.rs:57, src/native.rs:487-501,
+ * src/native/vae_encoder.rs:414-424). */
+int osor_vae_encode_moments(const osor_vae* vae, const float* image, float* moments, int batch,
+                            int height, int width, void* workspace, size_t workspace_bytes,
+                            void* stream, const volatile int* cancel);
+
+/* Host-side weight repack: w_oihw [Cout][Cin][k][k] f32 -> out (host,
+ * Cout*k*k*Cin 16-bit patterns of `dtype`) in [Cout][ky][kx][Cin] order, the
+ * layout osor_conv2d reads. Replaces the weight side of conv2d()
+ * (src/native/conv.rs:149-182). */
+int osor_pack_conv_weight(const float* w_oihw, uint16_t* out, int cout, int cin, int ksize,
+                          int dtype);
+
+/* 2-D convolution, square kernel, `pad` zero rows / columns before the first
+ * and `pad_end` after the last (symmetric: pad_end = pad; the encoder's
+ * downsampler, which pads one zero column / row on the right / bottom and then
+ * convolves with stride 2 and no padding, is pad = 0, pad_end = 1). Output
+ * size (H + pad + pad_end - k) / stride + 1. `dtype` (BF16 / F16) is the type
+ * of the packed weight, the residual and any NHWC operand; in/out layout:
+ * OSOR_LAYOUT_NHWC (16-bit) or OSOR_LAYOUT_NCHW (f32). bias f32 [Cout]
+ * (nullable); residual NHWC [B][Ho][Wo][Cout] (nullable, NHWC output only) is
+ * added after the bias. Tensor cores are used when both layouts are NHWC,
+ * Cin % 64 == 0, Cout % 128 == 0 and the output tiles into 128-pixel blocks;
+ * other shapes run a CUDA-core direct convolution. Replaces
+ * BandedConv2d::forward_checked + add_bias (src/native/conv.rs:54-145) and the
+ * residual add of Resnet::forward_checked (src/native/vae_encoder.rs:150). */
+int osor_conv2d(const void* x, void* y, const void* weight_packed, const float* bias,
+                const void* residual, int batch, int in_h, int in_w, int cin, int cout, int ksize,
+                int stride, int pad, int pad_end, int in_layout, int out_layout, int dtype,
+                void* stream);
+
+/* Device workspace for osor_group_norm_silu (0: unsupported shape). */
+size_t osor_group_norm_workspace_size(int batch, int channels, int height, int width, int layout,
+                                      int dtype);
+
+/* GroupNorm(32 groups) with optional SiLU, y = silu((x - mean) / sqrt(var +
+ * eps) * gamma + beta) with fp32 statistics. OSOR_LAYOUT_NCHW (dtype F32,
+ * BF16 or F16) runs one fused kernel that keeps each chunk of a group on chip
+ * between the statistics and the normalization; OSOR_LAYOUT_NHWC (BF16 / F16)
+ * runs the statistics / apply kernels used between convolutions. gamma/beta:
+ * device f32 [C]. stats (nullable, device f32 [B*32][2]) receives (mean,
+ * biased variance) per group. Replaces StableGroupNorm::forward /
+ * forward_silu (src/native/vae_encoder.rs:55-105). */
+int osor_group_norm_silu(const void* x, void* y, const float* gamma, const float* beta, int batch,
+                         int channels, int height, int width, int layout, int dtype, float eps,
+                         int silu, float* stats, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/* Nearest 2x upsample of 16-bit NHWC [B][H][W][C] -> [B][2H][2W][C], C % 8 == 0.
+ * Replaces upsample_2x (src/native/vae_decoder.rs:18-35). */
+int osor_upsample_2x(const void* x, void* y, int batch, int height, int width, int channels,
+                     void* stream);
+
+/* Device workspace for osor_attention. */
+size_t osor_attention_workspace_size(int batch, int tokens, int dim);
+
+/* out = softmax(q k^T) v per batch entry. q, k, v: device 16-bit (`dtype`)
+ * [B][N][D] with row stride ld (elements, >= D), already scaled as the caller
+ * wants (the VAE scales q and k by D^-1/4 each); out: [B][N][D]. Softmax
+ * statistics are fp32. Replaces attend (src/native/attention.rs:10-25) for the
+ * VAE mid-block attention (src/native/vae_encoder.rs:320-327). */
+int osor_attention(const void* q, const void* k, const void* v, void* out, int batch, int tokens,
+                   int dim, long long ld, int dtype, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/* One profiled op: kind ("conv_tc", "conv_direct", "groupnorm", ...),
+ * algorithmic FLOPs and bytes, device time between the CUDA events recorded
+ * on its stream, and the number of kernels it launched. */
+typedef struct osor_profile_entry {
+  char kind[32];
+  double flops;
+  double bytes;
+  float ms;
+  int launches;
+} osor_profile_entry;
+
+/* Starts recording CUDA events around every op this thread enqueues. Nothing
+ * synchronises while recording. Replaces the per-stage timing of
+ * Osor::infer_profiled (src/runtime.rs:514-540). */
+void osor_profile_begin(void);
+
+/* Stops recording, waits for the recorded events and writes up to
+ * max_entries records (the total goes to *count). */
+int osor_profile_end(osor_profile_entry* entries, int max_entries, int* count);
+
+/* Number of kernels this library has launched in this process. */
+long long osor_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OSOR_B200_H */

@@ -1,0 +1,330 @@
+// extern "C" entry points declared in include/osor_b200.h.
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+#include "conv_tc.h"
+#include "groupnorm.h"
+#include "ops.h"
+#include "vae.h"
+
+struct osor_vae {
+  osor::Vae* impl;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+int report(const osor::Status& s) {
+  if (s.good()) return OSOR_OK;
+  return fail(s.code, s.message);
+}
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(OSOR_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+bool is16(int dtype) { return dtype == OSOR_DTYPE_BF16 || dtype == OSOR_DTYPE_F16; }
+int internal_dtype(int dtype) { return dtype == OSOR_DTYPE_F16 ? osor::kF16 : osor::kBf16; }
+
+// Runs the call on the device that owns `ptr` (so callers need not set it).
+class DeviceOf {
+ public:
+  explicit DeviceOf(const void* ptr) {
+    cudaGetDevice(&prev_);
+    cudaPointerAttributes attr;
+    if (ptr && cudaPointerGetAttributes(&attr, ptr) == cudaSuccess &&
+        attr.type == cudaMemoryTypeDevice && attr.device != prev_) {
+      cudaSetDevice(attr.device);
+      switched_ = true;
+    }
+    cudaGetLastError();
+  }
+  ~DeviceOf() {
+    if (switched_) cudaSetDevice(prev_);
+  }
+
+ private:
+  int prev_ = 0;
+  bool switched_ = false;
+};
+
+}  // namespace
+
+extern "C" {
+
+const char* osor_last_error_message(void) { return g_last_error.c_str(); }
+
+int osor_version(void) { return 100; }
+
+int osor_device_check(int device) {
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || device < 0 || device >= count) {
+    cudaGetLastError();
+    return fail(OSOR_ERR_UNAVAILABLE, "no CUDA device " + std::to_string(device));
+  }
+  cudaDeviceProp prop;
+  if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess)
+    return cuda_fail(e, "device properties");
+  if (prop.major != 10 || prop.minor != 0)
+    return fail(OSOR_ERR_UNAVAILABLE, std::string("device ") + prop.name +
+                                          " is not sm_100; this library is built for sm_100a");
+  return OSOR_OK;
+}
+
+int osor_device_status(int device, int reset) {
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  int value = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&value, osor::g_device_status, sizeof(int));
+  if (e == cudaSuccess && reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(osor::g_device_status, &zero, sizeof(int));
+  }
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return -cuda_fail(e, "device status");
+  return value;
+}
+
+int osor_vae_create(const osor_tensor* tensors, size_t count, const osor_vae_config* config,
+                    int device, osor_vae** out) {
+  if (!out || (!tensors && count)) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  *out = nullptr;
+  int rc = osor_device_check(device);
+  if (rc != OSOR_OK) return rc;
+  osor::Vae* impl = nullptr;
+  osor::Status s = osor::vae_create(tensors, count, config, device, &impl);
+  if (!s.good()) return report(s);
+  *out = new osor_vae{impl};
+  return OSOR_OK;
+}
+
+void osor_vae_destroy(osor_vae* vae) {
+  if (!vae) return;
+  delete vae->impl;
+  delete vae;
+}
+
+static bool decode_shape_ok(int batch, int h, int w) {
+  // Admission rules of the reference pipeline (src/pipeline.rs:71-79): batch
+  // 1..=4, image axes 32..=1024 in multiples of 8 -> latent axes 4..=128.
+  return batch >= 1 && batch <= 4 && h >= 4 && w >= 4 && h <= 128 && w <= 128;
+}
+static bool encode_shape_ok(int batch, int h, int w) {
+  return batch >= 1 && batch <= 4 && h >= 32 && w >= 32 && h <= 1024 && w <= 1024 && h % 8 == 0 &&
+         w % 8 == 0;
+}
+
+size_t osor_vae_workspace_size(const osor_vae* vae, int op, int batch, int height, int width) {
+  if (!vae) return 0;
+  if (op == OSOR_OP_DECODE ? !decode_shape_ok(batch, height, width)
+                           : !encode_shape_ok(batch, height, width))
+    return 0;
+  return osor::vae_workspace_plan(*vae->impl, op, batch, height, width).total;
+}
+
+int osor_vae_decode(const osor_vae* vae, const float* latents, float* image, int batch,
+                    int latent_h, int latent_w, void* workspace, size_t workspace_bytes,
+                    void* stream, const volatile int* cancel) {
+  if (!vae || !latents || !image || !workspace)
+    return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (!decode_shape_ok(batch, latent_h, latent_w))
+    return fail(OSOR_ERR_INVALID_INPUT,
+                "decode needs batch 1..=4 and latent axes 4..=128 (image axes 32..=1024)");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(vae->impl->device);
+  osor::Status s = osor::vae_decode(*vae->impl, latents, image, batch, latent_h, latent_w,
+                                    workspace, workspace_bytes,
+                                    static_cast<cudaStream_t>(stream), cancel);
+  cudaSetDevice(prev);
+  return report(s);
+}
+
+int osor_vae_encode_moments(const osor_vae* vae, const float* image, float* moments, int batch,
+                            int height, int width, void* workspace, size_t workspace_bytes,
+                            void* stream, const volatile int* cancel) {
+  if (!vae || !image || !moments || !workspace)
+    return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (!encode_shape_ok(batch, height, width))
+    return fail(OSOR_ERR_INVALID_INPUT,
+                "encode needs batch 1..=4 and image axes 32..=1024 in multiples of 8");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(vae->impl->device);
+  osor::Status s = osor::vae_encode(*vae->impl, image, moments, batch, height, width, workspace,
+                                    workspace_bytes, static_cast<cudaStream_t>(stream), cancel);
+  cudaSetDevice(prev);
+  return report(s);
+}
+
+int osor_pack_conv_weight(const float* w, uint16_t* out, int cout, int cin, int k, int dtype) {
+  if (!w || !out || cout <= 0 || cin <= 0 || k <= 0)
+    return fail(OSOR_ERR_INVALID_INPUT, "invalid weight shape");
+  if (!is16(dtype)) return fail(OSOR_ERR_INVALID_INPUT, "weights must be BF16 or F16");
+  for (int co = 0; co < cout; ++co)
+    for (int ci = 0; ci < cin; ++ci)
+      for (int ky = 0; ky < k; ++ky)
+        for (int kx = 0; kx < k; ++kx) {
+          const float v = w[(((size_t)co * cin + ci) * k + ky) * k + kx];
+          uint16_t bits;
+          if (dtype == OSOR_DTYPE_F16) {
+            const __half h = __float2half_rn(v);
+            std::memcpy(&bits, &h, 2);
+          } else {
+            const __nv_bfloat16 h = __float2bfloat16_rn(v);
+            std::memcpy(&bits, &h, 2);
+          }
+          out[(((size_t)co * k + ky) * k + kx) * cin + ci] = bits;
+        }
+  return OSOR_OK;
+}
+
+int osor_conv2d(const void* x, void* y, const void* weight_packed, const float* bias,
+                const void* residual, int batch, int in_h, int in_w, int cin, int cout, int ksize,
+                int stride, int pad, int pad_end, int in_layout, int out_layout, int dtype,
+                void* stream) {
+  if (!x || !y || !weight_packed) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (batch <= 0 || in_h <= 0 || in_w <= 0 || cin <= 0 || cout <= 0 || ksize <= 0 || stride <= 0 ||
+      pad < 0 || pad_end < 0)
+    return fail(OSOR_ERR_INVALID_INPUT, "invalid convolution shape");
+  if (!is16(dtype)) return fail(OSOR_ERR_INVALID_INPUT, "convolution dtype must be BF16 or F16");
+  if ((in_layout != OSOR_LAYOUT_NHWC && in_layout != OSOR_LAYOUT_NCHW) ||
+      (out_layout != OSOR_LAYOUT_NHWC && out_layout != OSOR_LAYOUT_NCHW))
+    return fail(OSOR_ERR_INVALID_INPUT, "convolution layouts must be NHWC (16-bit) or NCHW (f32)");
+  if (residual && out_layout != OSOR_LAYOUT_NHWC)
+    return fail(OSOR_ERR_INVALID_INPUT, "a residual needs NHWC output");
+  if (in_h + pad + pad_end < ksize || in_w + pad + pad_end < ksize)
+    return fail(OSOR_ERR_INVALID_INPUT, "convolution input is smaller than its kernel");
+  DeviceOf dev(x);
+  osor::ConvLayer L;
+  L.cin = cin;
+  L.cout = cout;
+  L.k = ksize;
+  L.stride = stride;
+  L.pad = pad;
+  L.pad_end = pad_end;
+  L.w = static_cast<const uint16_t*>(weight_packed);
+  L.bias = bias;
+  const int in_mode = in_layout == OSOR_LAYOUT_NHWC ? osor::kLayoutNhwc16 : osor::kLayoutNchwF32;
+  const int out_mode = out_layout == OSOR_LAYOUT_NHWC ? osor::kLayoutNhwc16 : osor::kLayoutNchwF32;
+  return report(osor::run_conv(internal_dtype(dtype), L, x, in_mode, batch, in_h, in_w, cin, y,
+                               out_mode, cout, residual, cout, static_cast<cudaStream_t>(stream)));
+}
+
+size_t osor_group_norm_workspace_size(int batch, int channels, int height, int width, int layout,
+                                      int dtype) {
+  if (batch <= 0 || channels <= 0 || channels % 32 != 0 || height <= 0 || width <= 0) return 0;
+  const long long spatial = (long long)height * width;
+  if (layout == OSOR_LAYOUT_NHWC) {
+    if (!is16(dtype) || channels / 8 > 256) return 0;
+    return osor::gn_nhwc_plan(batch, channels, spatial, 32).workspace_bytes;
+  }
+  if (layout != OSOR_LAYOUT_NCHW || (!is16(dtype) && dtype != OSOR_DTYPE_F32)) return 0;
+  const int eb = dtype == OSOR_DTYPE_F32 ? 4 : 2;
+  const osor::GnFusedPlan p = osor::gn_fused_plan(batch, channels, spatial, 32, eb);
+  return p.feasible ? p.workspace_bytes : 0;
+}
+
+int osor_group_norm_silu(const void* x, void* y, const float* gamma, const float* beta, int batch,
+                         int channels, int height, int width, int layout, int dtype, float eps,
+                         int silu, float* stats, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  if (!x || !y || !gamma || !beta) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (batch <= 0 || height <= 0 || width <= 0 || channels <= 0 || channels % 32 != 0)
+    return fail(OSOR_ERR_INVALID_INPUT, "VAE group normalization requires channels divisible by 32");
+  const size_t need = osor_group_norm_workspace_size(batch, channels, height, width, layout, dtype);
+  if (need == 0) return fail(OSOR_ERR_INVALID_INPUT, "unsupported group-norm shape, layout or dtype");
+  if (!workspace || workspace_bytes < need)
+    return fail(OSOR_ERR_INVALID_INPUT, "group-norm workspace is too small");
+  DeviceOf dev(x);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const long long spatial = (long long)height * width;
+  cudaError_t e;
+  if (layout == OSOR_LAYOUT_NHWC) {
+    if (!aligned16(x) || !aligned16(y))
+      return fail(OSOR_ERR_INVALID_INPUT, "NHWC tensors must be 16-byte aligned");
+    e = osor::gn_nhwc_launch(internal_dtype(dtype), x, y, gamma, beta, batch, channels, spatial, 32,
+                             eps, silu, workspace, stats, s);
+  } else if (dtype == OSOR_DTYPE_F32) {
+    e = osor::gn_fused_launch<float>(static_cast<const float*>(x), static_cast<float*>(y), gamma,
+                                     beta, batch, channels, spatial, 32, eps, silu, workspace, stats,
+                                     s);
+  } else if (dtype == OSOR_DTYPE_BF16) {
+    e = osor::gn_fused_launch<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x),
+                                             static_cast<__nv_bfloat16*>(y), gamma, beta, batch,
+                                             channels, spatial, 32, eps, silu, workspace, stats, s);
+  } else {
+    e = osor::gn_fused_launch<__half>(static_cast<const __half*>(x), static_cast<__half*>(y), gamma,
+                                      beta, batch, channels, spatial, 32, eps, silu, workspace,
+                                      stats, s);
+  }
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "group norm");
+}
+
+int osor_upsample_2x(const void* x, void* y, int batch, int height, int width, int channels,
+                     void* stream) {
+  if (!x || !y) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (batch <= 0 || height <= 0 || width <= 0 || channels <= 0 || channels % 8 != 0)
+    return fail(OSOR_ERR_INVALID_INPUT, "upsample needs positive sizes and channels % 8 == 0");
+  if (!aligned16(x) || !aligned16(y))
+    return fail(OSOR_ERR_INVALID_INPUT, "tensors must be 16-byte aligned");
+  DeviceOf dev(x);
+  cudaError_t e = osor::upsample2x_nhwc_launch(x, y, batch, height, width, channels,
+                                               static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "upsample");
+}
+
+size_t osor_attention_workspace_size(int batch, int tokens, int dim) {
+  (void)batch;
+  if (tokens <= 0 || dim <= 0) return 0;
+  const size_t a = ((size_t)tokens * tokens * 4 + 255) / 256 * 256;
+  const size_t b = ((size_t)tokens * tokens * 2 + 255) / 256 * 256;
+  const size_t c = ((size_t)tokens * 4 + 255) / 256 * 256;
+  const size_t d = ((size_t)tokens * dim * 2 + 255) / 256 * 256;
+  return a + b + c + d;
+}
+
+int osor_attention(const void* q, const void* k, const void* v, void* out, int batch, int tokens,
+                   int dim, long long ld, int dtype, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  if (!q || !k || !v || !out) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (batch <= 0 || tokens <= 0 || dim <= 0 || dim > 512 || ld < dim)
+    return fail(OSOR_ERR_INVALID_INPUT, "attention tensor shapes are incompatible");
+  if (!is16(dtype)) return fail(OSOR_ERR_INVALID_INPUT, "attention dtype must be BF16 or F16");
+  const size_t need = osor_attention_workspace_size(batch, tokens, dim);
+  if (!workspace || workspace_bytes < need)
+    return fail(OSOR_ERR_INVALID_INPUT, "attention workspace is too small");
+  DeviceOf dev(q);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  float* scores = reinterpret_cast<float*>(w);
+  w += ((size_t)tokens * tokens * 4 + 255) / 256 * 256;
+  void* probs = w;
+  w += ((size_t)tokens * tokens * 2 + 255) / 256 * 256;
+  float* rowsum = reinterpret_cast<float*>(w);
+  w += ((size_t)tokens * 4 + 255) / 256 * 256;
+  void* vt = w;
+  // Batch entries are [N][D] blocks of stride N*ld inside q/k/v.
+  osor::Status s;
+  const uint16_t* qb = static_cast<const uint16_t*>(q);
+  const uint16_t* kb = static_cast<const uint16_t*>(k);
+  const uint16_t* vb = static_cast<const uint16_t*>(v);
+  uint16_t* ob = static_cast<uint16_t*>(out);
+  for (int b = 0; b < batch && s.good(); ++b) {
+    const long long off = (long long)b * tokens * ld;
+    s = osor::attention_core(internal_dtype(dtype), qb + off, kb + off, vb + off, ld,
+                             ob + (long long)b * tokens * dim, dim, 1, tokens, dim, scores, probs,
+                             rowsum, vt, static_cast<cudaStream_t>(stream));
+  }
+  return report(s);
+}
+
+}  // extern "C"

@@ -1,0 +1,441 @@
+// Implicit-GEMM convolution / GEMM on the sm_100a tensor cores.
+//
+// One kernel covers every tensor-core contraction of the VAE:
+//   * 3x3 stride-1 pad-1 and 1x1 convolutions over NHWC bf16 activations,
+//   * 3x3 stride-2 convolutions with the encoder's right/bottom zero pad,
+//   * plain row-major GEMMs (attention scores Q K^T and P V^T^T), expressed as
+//     a 1x1 "convolution" over a [1, 1, M, K] activation.
+// GEMM view: M = output pixels, N = output channels, K = taps * Cin. No im2col
+// buffer exists: for K block (tap, channel block) the producer warp issues one
+// TMA load of the shifted NHWC halo box (zero fill outside the image supplies
+// the padding) and one TMA load of the matching weight tile. tcgen05.mma
+// accumulates 128 x BLOCK_N fp32 tiles in TMEM (double buffered so the
+// epilogue of one tile overlaps the MMAs of the next); four epilogue warps read
+// TMEM, add bias / residual / per-row scale and store bf16 or fp32.
+//
+// Warp roles (192 threads, one persistent CTA per SM):
+//   warp 0      TMA producer (one elected lane)
+//   warp 1      TMEM allocator + MMA issuer (one elected lane)
+//   warps 2..5  epilogue, TMEM lane quadrant = warp % 4
+//
+// Reference counterpart: the convolution of BandedConv2d::forward_checked
+// (src/native/conv.rs:54-112) with its bias add (:116-145) and the residual
+// add of Resnet::forward_checked (src/native/vae_encoder.rs:150), and the
+// score / value matmuls of attend (src/native/attention.rs:23).
+#include "common.cuh"
+#include "conv_tc.h"
+
+#include <cstdio>
+#include <mutex>
+
+namespace osor {
+
+__device__ int g_device_status = 0;
+
+namespace {
+
+constexpr int kBlockM = 128;
+constexpr int kBlockK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int kThreads = 192;
+constexpr int kABytes = kBlockM * kBlockK * 2;
+
+struct TcParams {
+  int num_m_tiles, num_n_tiles;
+  int k_blocks, c_blocks;  // k_blocks = taps * c_blocks
+  int ksize, stride, pad;
+  int tiles_x, tiles_y;    // output tile grid per image
+  int tile_w, tile_h;      // output pixels per tile along W / H (tile_w*tile_h = 128)
+  int n_out;               // valid output columns (N)
+  const float* bias;       // [N] or nullptr
+  const void* residual;    // 16-bit [M, ld_res] or nullptr
+  long long ld_res;
+  void* out;               // [M, ld_out]
+  long long ld_out;
+  const float* row_scale;  // [M] or nullptr
+  int out_f32;
+};
+
+template <int BLOCK_N>
+struct TcConfig {
+  static constexpr int kBBytes = BLOCK_N * kBlockK * 2;
+  static constexpr int kStages = BLOCK_N == 256 ? 4 : 6;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BLOCK_N;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BLOCK_N, int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                   const __grid_constant__ CUtensorMap tmap_b, const TcParams p) {
+  using Cfg = TcConfig<BLOCK_N>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + S * kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int num_tiles = p.num_m_tiles * p.num_n_tiles;
+  const int tiles_per_image = p.tiles_x * p.tiles_y;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m_tile = tile / p.num_n_tiles;
+        const int n_tile = tile - m_tile * p.num_n_tiles;
+        const int img = m_tile / tiles_per_image;
+        const int rem = m_tile - img * tiles_per_image;
+        const int ty = rem / p.tiles_x;
+        const int tx = rem - ty * p.tiles_x;
+        const int ox = tx * p.tile_w * p.stride - p.pad;
+        const int oy = ty * p.tile_h * p.stride - p.pad;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const int tap = kb / p.c_blocks;
+          const int cb = kb - tap * p.c_blocks;
+          const int ky = tap / p.ksize;
+          const int kx = tap - ky * p.ksize;
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          tma_load_4d(smem_a + stage * kABytes, &tmap_a, &full[stage], cb * kBlockK, ox + kx,
+                      oy + ky, img);
+          tma_load_2d(smem_b + stage * Cfg::kBBytes, &tmap_b, &full[stage], kb * kBlockK,
+                      n_tile * BLOCK_N);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Let every armed load land before the CTA leaves.
+        for (int s = 0; s < S; ++s) {
+          int st = stage - 1 - s;
+          uint32_t ph = phase;
+          if (st < 0) {
+            st += S;
+            ph ^= 1;
+          }
+          const uint32_t addr = smem_u32(&full[st]);
+          const uint64_t t0 = global_timer_ns();
+          while (!mbar_try_wait(addr, ph) && global_timer_ns() - t0 < kWaitLimitNs) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
+      constexpr uint32_t idesc = umma_idesc_f32acc(kBlockM, BLOCK_N, Elem<D>::kUmmaFormat);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BLOCK_N;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem_a + stage * kABytes);
+          const uint32_t b_addr = smem_u32(smem_b + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBlockK / 16; ++k) {
+            umma_bf16(d_tmem, sw128_kmajor_desc(a_addr + k * 32),
+                      sw128_kmajor_desc(b_addr + k * 32), idesc, (kb | k) != 0);
+          }
+          issued = true;
+          umma_commit(&empty[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (!ok && issued) {
+        // Drain outstanding MMAs before TMEM is released.
+        umma_commit(drain);
+        const uint32_t addr = smem_u32(drain);
+        const uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(addr, 0) && global_timer_ns() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const int m_tile = tile / p.num_n_tiles;
+      const int n_tile = tile - m_tile * p.num_n_tiles;
+      const long long m = (long long)m_tile * kBlockM + row;
+      const float scale = p.row_scale ? __ldg(p.row_scale + m) : 1.0f;
+#pragma unroll 1
+      for (int chunk = 0; chunk < BLOCK_N / 32; ++chunk) {
+        uint32_t r[32];
+        tmem_load_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BLOCK_N +
+                                 chunk * 32,
+                             r);
+        tmem_wait_ld();
+        const int n0 = n_tile * BLOCK_N + chunk * 32;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * scale;
+        if (p.bias) {
+          const float4* b4 = reinterpret_cast<const float4*>(p.bias + n0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 b = __ldg(b4 + j);
+            v[4 * j + 0] += b.x;
+            v[4 * j + 1] += b.y;
+            v[4 * j + 2] += b.z;
+            v[4 * j + 3] += b.w;
+          }
+        }
+        if (p.residual) {
+          const uint4* r4 = reinterpret_cast<const uint4*>(
+              static_cast<const uint16_t*>(p.residual) + m * p.ld_res + n0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float f[8];
+            unpack8<D>(__ldg(r4 + j), f);
+#pragma unroll
+            for (int t = 0; t < 8; ++t) v[8 * j + t] += f[t];
+          }
+        }
+        if (p.out_f32) {
+          float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) + m * p.ld_out + n0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        } else {
+          uint4* o4 =
+              reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + m * p.ld_out + n0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            o4[j] = make_uint4(Elem<D>::pack(v[8 * j + 0], v[8 * j + 1]),
+                               Elem<D>::pack(v[8 * j + 2], v[8 * j + 3]),
+                               Elem<D>::pack(v[8 * j + 4], v[8 * j + 5]),
+                               Elem<D>::pack(v[8 * j + 6], v[8 * j + 7]));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+int sm_count(int device) {
+  static int counts[64] = {0};
+  if (device < 0 || device >= 64) return 148;
+  if (counts[device] == 0) {
+    int c = 0;
+    cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, device);
+    counts[device] = c > 0 ? c : 148;
+  }
+  return counts[device];
+}
+
+template <int BLOCK_N, int D>
+cudaError_t launch_typed(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p,
+                         cudaStream_t stream) {
+  using Cfg = TcConfig<BLOCK_N>;
+  static bool configured[64] = {false};
+  int device = 0;
+  cudaGetDevice(&device);
+  if (device >= 0 && device < 64 && !configured[device]) {
+    cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<BLOCK_N, D>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    configured[device] = true;
+  }
+  const int tiles = p.num_m_tiles * p.num_n_tiles;
+  const int grid = tiles < sm_count(device) ? tiles : sm_count(device);
+  conv_tc_kernel<BLOCK_N, D><<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+const char* conv_tc_check(const ConvTcArgs& a) {
+  if (a.ksize != 1 && a.ksize != 3) return "tensor-core convolution supports 1x1 and 3x3 kernels";
+  if (a.stride != 1 && a.stride != 2) return "tensor-core convolution supports stride 1 and 2";
+  if (a.cin <= 0 || a.cin % kBlockK != 0) return "input channels must be a multiple of 64";
+  if (a.cout <= 0 || a.cout % 128 != 0) return "output channels must be a multiple of 128";
+  if (a.out_w <= 0 || a.out_h <= 0 || a.batch <= 0) return "empty convolution";
+  const int tile_w = a.out_w >= kBlockM ? kBlockM : a.out_w;
+  if (a.out_w % tile_w != 0 || kBlockM % tile_w != 0) return "output width must divide or be a multiple of 128";
+  const int tile_h = kBlockM / tile_w;
+  if (a.out_h % tile_h != 0) return "output rows do not fill whole 128-pixel tiles";
+  if (a.pixel_stride % 8 != 0 || a.ldw % 8 != 0) return "row strides must be 16-byte multiples";
+  if ((reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.w)) & 15)
+    return "operands must be 16-byte aligned";
+  if (a.residual && (a.ld_res % 8 != 0 || (reinterpret_cast<uintptr_t>(a.residual) & 15)))
+    return "residual must be 16-byte aligned";
+  if (a.ld_out % (a.out_f32 ? 4 : 8) != 0 || (reinterpret_cast<uintptr_t>(a.out) & 15))
+    return "output must be 16-byte aligned";
+  if (a.bias && (reinterpret_cast<uintptr_t>(a.bias) & 15)) return "bias must be 16-byte aligned";
+  if ((long long)a.batch * a.out_h * a.out_w > 0x7fffffffLL) return "problem too large";
+  if (a.stride == 2 && 2 * tile_w > 256) return "stride-2 tile too wide";
+  if (a.dtype != kBf16 && a.dtype != kF16) return "unknown 16-bit type";
+  return nullptr;
+}
+
+cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
+  EncodeTiledFn encode = encode_fn();
+  if (!encode) return cudaErrorNotSupported;
+  const int tile_w = a.out_w >= kBlockM ? kBlockM : a.out_w;
+  const int tile_h = kBlockM / tile_w;
+  const int block_n = (a.cout % 256 == 0) ? 256 : 128;
+  const CUtensorMapDataType tdt =
+      a.dtype == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+
+  CUtensorMap ta, tb;
+  {
+    const cuuint64_t ps = (cuuint64_t)a.pixel_stride * 2;
+    cuuint64_t dims[4] = {(cuuint64_t)a.cin, (cuuint64_t)a.in_w, (cuuint64_t)a.in_h,
+                          (cuuint64_t)a.batch};
+    cuuint64_t strides[3] = {ps, ps * a.in_w, ps * a.in_w * a.in_h};
+    cuuint32_t box[4] = {(cuuint32_t)kBlockK, (cuuint32_t)(tile_w * a.stride),
+                         (cuuint32_t)(tile_h * a.stride), 1};
+    cuuint32_t estr[4] = {1, (cuuint32_t)a.stride, (cuuint32_t)a.stride, 1};
+    CUresult r = encode(&ta, tdt, 4, const_cast<void*>(static_cast<const void*>(a.x)), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  }
+  {
+    const int k_total = a.ksize * a.ksize * a.cin;
+    cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)a.cout};
+    cuuint64_t strides[1] = {(cuuint64_t)a.ldw * 2};
+    cuuint32_t box[2] = {(cuuint32_t)kBlockK, (cuuint32_t)block_n};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode(&tb, tdt, 2, const_cast<void*>(static_cast<const void*>(a.w)), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  }
+  TcParams p;
+  p.tile_w = tile_w;
+  p.tile_h = tile_h;
+  p.tiles_x = a.out_w / tile_w;
+  p.tiles_y = a.out_h / tile_h;
+  p.num_m_tiles = a.batch * p.tiles_x * p.tiles_y;
+  p.num_n_tiles = a.cout / block_n;
+  p.c_blocks = a.cin / kBlockK;
+  p.k_blocks = a.ksize * a.ksize * p.c_blocks;
+  p.ksize = a.ksize;
+  p.stride = a.stride;
+  p.pad = a.pad;
+  p.n_out = a.cout;
+  p.bias = a.bias;
+  p.residual = a.residual;
+  p.ld_res = a.ld_res;
+  p.out = a.out;
+  p.ld_out = a.ld_out;
+  p.row_scale = a.row_scale;
+  p.out_f32 = a.out_f32;
+  if (a.dtype == kF16)
+    return block_n == 256 ? launch_typed<256, kF16>(ta, tb, p, stream)
+                          : launch_typed<128, kF16>(ta, tb, p, stream);
+  return block_n == 256 ? launch_typed<256, kBf16>(ta, tb, p, stream)
+                        : launch_typed<128, kBf16>(ta, tb, p, stream);
+}
+
+}  // namespace osor

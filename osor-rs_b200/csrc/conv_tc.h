@@ -1,0 +1,38 @@
+// Host interface of the tensor-core implicit-GEMM convolution kernel.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace osor {
+
+// NHWC bf16 convolution (or GEMM) on tcgen05 tensor cores.
+//   input   x[batch][in_h][in_w][pixel_stride] (bf16 or f16), first cin channels used
+//   weight  w[cout][ldw], K = ksize*ksize*cin ordered (ky, kx, cin)
+//   output  out[pixel][ld_out] (pixel = (b*out_h + oy)*out_w + ox), bf16 or f32
+//   out = row_scale[pixel] * acc + bias[n] + residual[pixel][n]
+// Zero padding: output (oy, ox) tap (ky, kx) reads input (oy*stride + ky - pad,
+// ox*stride + kx - pad); reads outside the image are zero. A stride-2 3x3 with
+// pad 0 therefore equals the reference's right/bottom zero pad then conv.
+struct ConvTcArgs {
+  int dtype = 0;  // Dtype of x, w, residual and a 16-bit output (kBf16 / kF16)
+  const void* x = nullptr;
+  int batch = 0, in_h = 0, in_w = 0, cin = 0;
+  long long pixel_stride = 0;
+  int ksize = 3, stride = 1, pad = 1;
+  int out_h = 0, out_w = 0, cout = 0;
+  const void* w = nullptr;
+  long long ldw = 0;
+  const float* bias = nullptr;
+  const void* residual = nullptr;
+  long long ld_res = 0;
+  void* out = nullptr;
+  long long ld_out = 0;
+  int out_f32 = 0;
+  const float* row_scale = nullptr;
+};
+
+// nullptr when the tensor-core kernel supports the shape, else a reason.
+const char* conv_tc_check(const ConvTcArgs& a);
+cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream);
+
+}  // namespace osor

@@ -1,0 +1,538 @@
+// GroupNorm(32) (+ SiLU) kernels.
+//
+// Reference semantics (src/native/vae_encoder.rs:21-85, metal_ops.rs:23-116):
+// per (batch, group): mean over C/32 channels x H x W, variance of the
+// centered values (never E[x^2] - E[x]^2 of raw values), normalized
+// (x - mean) / sqrt(var + eps), then the per-channel affine, then SiLU.
+// Statistics are fp32 throughout.
+//
+// Two code paths:
+//  * gn_nchw_fused_kernel: standalone NCHW op. A group is one contiguous run
+//    of memory. Persistent co-resident CTAs each hold one chunk of a group in
+//    shared memory, compute the chunk's exact two-pass (count, mean, M2),
+//    publish it, wait (bounded) until every chunk of the group has published,
+//    merge the partials with Chan's formula in a fixed order (so every CTA
+//    derives bit-identical statistics), then normalize from shared memory and
+//    store. HBM traffic is one read and one write per element.
+//  * gn_nhwc_{stats,finalize,apply}: the layout used between convolutions.
+//    Stats accumulate per-channel sums of (x - anchor) and (x - anchor)^2,
+//    anchor = the group's first element (the reference Metal kernel's anchor),
+//    so partials add across chunks; finalize turns them into per-(batch,
+//    channel) (mean, rstd * gamma, beta); apply streams x once with 16-byte
+//    vectors.
+#include "common.cuh"
+#include "groupnorm.h"
+
+namespace osor {
+namespace {
+
+__device__ __forceinline__ float silu_f(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
+
+// Element access for the standalone kernel: float, bf16 or f16 storage.
+template <typename T>
+struct Scalar;
+template <>
+struct Scalar<float> {
+  static constexpr int V = 4;  // elements per 16-byte vector
+  __device__ static float to_f(float v) { return v; }
+  __device__ static float from_f(float v) { return v; }
+  __device__ static void load(const float* p, float (&f)[4]) {
+    const float4 q = *reinterpret_cast<const float4*>(p);
+    f[0] = q.x;
+    f[1] = q.y;
+    f[2] = q.z;
+    f[3] = q.w;
+  }
+  __device__ static void store(float* p, const float (&f)[4]) {
+    *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
+  }
+};
+template <int D>
+struct Scalar16 {
+  using T = typename Elem<D>::T;
+  static constexpr int V = 8;
+  __device__ static float to_f(T v) { return Elem<D>::to_f(v); }
+  __device__ static T from_f(float v) { return Elem<D>::from_f(v); }
+  __device__ static void load(const T* p, float (&f)[8]) {
+    unpack8<D>(*reinterpret_cast<const uint4*>(p), f);
+  }
+  __device__ static void store(T* p, const float (&f)[8]) {
+    *reinterpret_cast<uint4*>(p) = pack8<D>(f);
+  }
+};
+template <>
+struct Scalar<__nv_bfloat16> : Scalar16<kBf16> {};
+template <>
+struct Scalar<__half> : Scalar16<kF16> {};
+
+// Block-wide sum over 256 threads; result broadcast to all threads.
+__device__ __forceinline__ float block_sum_256(float v, float* scratch) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float t = lane < 8 ? scratch[lane] : 0.0f;
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  return __shfl_sync(0xffffffffu, t, 0);
+}
+
+constexpr int kFusedThreads = 256;
+
+struct FusedParams {
+  long long count;        // elements per group
+  long long chunk;        // elements per chunk (last chunk of a group may be shorter)
+  int chunks_per_group;
+  int groups_total;       // batch * groups
+  int groups;             // groups per image
+  int channels;
+  long long spatial;      // H * W
+  float eps;
+  int silu;
+  int use_bulk;           // chunks are 16-byte aligned and sized
+  float* partials;        // [groups_total, chunks_per_group, 3]
+  int* arrive;            // [groups_total]
+  float* stats_out;       // optional [groups_total, 2] (mean, var)
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kFusedThreads)
+    gn_nchw_fused_kernel(const T* __restrict__ x, T* __restrict__ y,
+                         const float* __restrict__ gamma, const float* __restrict__ beta,
+                         const FusedParams p) {
+  using S = Scalar<T>;
+  constexpr int V = S::V;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  T* buf = reinterpret_cast<T*>(smem_raw);
+  __shared__ float red[8];
+  __shared__ float stat[2];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  uint32_t bar_phase = 0;
+  const int cpg = p.channels / p.groups;
+  const long long items = (long long)p.groups_total * p.chunks_per_group;
+  for (long long item = blockIdx.x; item < items; item += gridDim.x) {
+    const int group = (int)(item / p.chunks_per_group);
+    const int ci = (int)(item - (long long)group * p.chunks_per_group);
+    const long long begin = (long long)ci * p.chunk;
+    const int n = (int)min(p.chunk, p.count - begin);
+    const long long base = (long long)group * p.count + begin;
+    // ---- load the chunk into shared memory
+    if (p.use_bulk) {
+      if (threadIdx.x == 0) {
+        const uint32_t bytes = (uint32_t)n * (uint32_t)sizeof(T);
+        mbar_arrive_expect_tx(&bar, bytes);
+        for (uint32_t off = 0; off < bytes; off += 65536u) {
+          const uint32_t len = min(65536u, bytes - off);
+          bulk_load(reinterpret_cast<uint8_t*>(buf) + off,
+                    reinterpret_cast<const uint8_t*>(x + base) + off, len, &bar);
+        }
+      }
+      mbar_wait(&bar, bar_phase, &abort_flag);
+      bar_phase ^= 1;
+      __syncthreads();
+      if (abort_flag) break;
+    } else {
+      for (int i = threadIdx.x; i < n; i += kFusedThreads) buf[i] = x[base + i];
+      __syncthreads();
+    }
+    const bool vec = p.use_bulk;  // 16-byte aligned chunk in shared memory
+    // ---- exact two-pass statistics of the chunk
+    float s = 0.0f;
+    if (vec) {
+      for (int i = threadIdx.x * V; i < n; i += kFusedThreads * V) {
+        float f[V];
+        S::load(buf + i, f);
+#pragma unroll
+        for (int j = 0; j < V; ++j) s += f[j];
+      }
+    } else {
+      for (int i = threadIdx.x; i < n; i += kFusedThreads) s += S::to_f(buf[i]);
+    }
+    const float chunk_mean = block_sum_256(s, red) / (float)n;
+    float m2 = 0.0f;
+    if (vec) {
+      for (int i = threadIdx.x * V; i < n; i += kFusedThreads * V) {
+        float f[V];
+        S::load(buf + i, f);
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+          const float d = f[j] - chunk_mean;
+          m2 += d * d;
+        }
+      }
+    } else {
+      for (int i = threadIdx.x; i < n; i += kFusedThreads) {
+        const float d = S::to_f(buf[i]) - chunk_mean;
+        m2 += d * d;
+      }
+    }
+    m2 = block_sum_256(m2, red);
+    if (threadIdx.x == 0) {
+      float* slot = p.partials + ((long long)group * p.chunks_per_group + ci) * 3;
+      slot[0] = (float)n;
+      slot[1] = chunk_mean;
+      slot[2] = m2;
+      __threadfence();
+      atomicAdd(p.arrive + group, 1);
+      // ---- wait (bounded) until every chunk of the group has published
+      const volatile int* arrived = p.arrive + group;
+      const uint64_t t0 = global_timer_ns();
+      bool ok = true;
+      while (*arrived < p.chunks_per_group) {
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+          record_device_error(kDevWaitTimeout);
+          ok = false;
+          break;
+        }
+      }
+      __threadfence();
+      if (ok) {
+        // Chan merge of the group's partials in chunk order.
+        const volatile float* part = p.partials + (long long)group * p.chunks_per_group * 3;
+        float cnt = part[0];
+        float mean = part[1];
+        float M2 = part[2];
+        for (int c = 1; c < p.chunks_per_group; ++c) {
+          const float nb = part[3 * c + 0], mb = part[3 * c + 1], m2b = part[3 * c + 2];
+          const float tot = cnt + nb;
+          const float delta = mb - mean;
+          mean += delta * (nb / tot);
+          M2 += m2b + delta * delta * (cnt * (nb / tot));
+          cnt = tot;
+        }
+        const float var = M2 / (float)p.count;
+        stat[0] = mean;
+        stat[1] = 1.0f / sqrtf(var + p.eps);
+        if (ci == 0 && p.stats_out) {
+          p.stats_out[2 * group] = mean;
+          p.stats_out[2 * group + 1] = var;
+        }
+      } else {
+        abort_flag = 1;
+      }
+    }
+    __syncthreads();
+    if (abort_flag) break;
+    const float mean = stat[0];
+    const float rstd = stat[1];
+    // ---- normalize from shared memory, one channel run at a time
+    const int g = group % p.groups;
+    const long long first = (long long)g * cpg * p.spatial + begin;  // offset inside the image
+    int c = (int)(first / p.spatial);
+    long long seg_end = (long long)(c + 1) * p.spatial - first;  // chunk-relative
+    int pos = 0;
+    while (pos < n) {
+      const int end = (int)min((long long)n, seg_end);
+      const float a = __ldg(gamma + c) * rstd;
+      const float bsh = __ldg(beta + c);
+      if (vec && (pos % V) == 0 && (end % V) == 0) {
+        for (int i = pos + threadIdx.x * V; i < end; i += kFusedThreads * V) {
+          float f[V];
+          S::load(buf + i, f);
+#pragma unroll
+          for (int j = 0; j < V; ++j) {
+            float v = (f[j] - mean) * a + bsh;
+            if (p.silu) v = silu_f(v);
+            f[j] = v;
+          }
+          S::store(y + base + i, f);
+        }
+      } else {
+        for (int i = pos + threadIdx.x; i < end; i += kFusedThreads) {
+          float v = (S::to_f(buf[i]) - mean) * a + bsh;
+          if (p.silu) v = silu_f(v);
+          y[base + i] = S::from_f(v);
+        }
+      }
+      pos = end;
+      ++c;
+      seg_end += p.spatial;
+    }
+    __syncthreads();  // the buffer is reused by the next item
+  }
+}
+
+// --------------------------------------------------------------- NHWC path
+constexpr int kNhwcThreads = 256;
+
+// grid (chunks, batch). Each thread owns one 8-channel vector column and
+// strides over the chunk's pixels; per-channel anchored sums are reduced over
+// the threads sharing the column and written as partials[b][chunk][c][2].
+template <int D>
+__global__ void __launch_bounds__(kNhwcThreads)
+    gn_nhwc_stats_kernel(const uint16_t* __restrict__ x, float* __restrict__ partials,
+                         int channels, long long pixels, long long pix_per_chunk, int groups) {
+  using E = Elem<D>;
+  extern __shared__ float sred[];  // [rows][vc][16]
+  const int vc = channels / 8;
+  const int rows = blockDim.x / vc;
+  const int col = threadIdx.x % vc;
+  const int r0 = threadIdx.x / vc;
+  const int b = blockIdx.y;
+  const int cpg = channels / groups;
+  const long long p_begin = (long long)blockIdx.x * pix_per_chunk;
+  const long long p_end = min(pixels, p_begin + pix_per_chunk);
+  const typename E::T* img =
+      reinterpret_cast<const typename E::T*>(x) + (long long)b * pixels * channels;
+  float anchor[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int c = col * 8 + j;
+    anchor[j] = E::to_f(img[(c / cpg) * cpg]);
+  }
+  float s1[8], s2[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s1[j] = s2[j] = 0.0f;
+  if (r0 < rows) {
+    for (long long pix = p_begin + r0; pix < p_end; pix += rows) {
+      float f[8];
+      unpack8<D>(__ldg(reinterpret_cast<const uint4*>(img + pix * channels) + col), f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = f[j] - anchor[j];
+        s1[j] += d;
+        s2[j] += d * d;
+      }
+    }
+    float* mine = sred + ((long long)r0 * vc + col) * 16;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      mine[j] = s1[j];
+      mine[8 + j] = s2[j];
+    }
+  }
+  __syncthreads();
+  // Reduce over rows: one thread per (column, value).
+  for (int idx = threadIdx.x; idx < vc * 16; idx += blockDim.x) {
+    const int c = idx / 16, j = idx % 16;
+    float acc = 0.0f;
+    for (int r = 0; r < rows; ++r) acc += sred[((long long)r * vc + c) * 16 + j];
+    const int ch = c * 8 + (j & 7);
+    float* out = partials + (((long long)b * gridDim.x + blockIdx.x) * channels + ch) * 2;
+    out[j >> 3] = acc;
+  }
+}
+
+// grid (groups, batch), 256 threads: combine partials of one (b, group) and
+// write per-channel (mean, rstd * gamma, beta) for the apply kernel.
+template <int D>
+__global__ void __launch_bounds__(256)
+    gn_nhwc_finalize_kernel(const uint16_t* __restrict__ x, const float* __restrict__ partials,
+                            int chunks, int channels, long long pixels, int groups,
+                            const float* __restrict__ gamma, const float* __restrict__ beta,
+                            float eps, float* __restrict__ coef, float* __restrict__ stats_out) {
+  using E = Elem<D>;
+  __shared__ float red[8];
+  const int g = blockIdx.x, b = blockIdx.y;
+  const int cpg = channels / groups;
+  float s1 = 0.0f, s2 = 0.0f;
+  const int items = chunks * cpg;
+  for (int i = threadIdx.x; i < items; i += blockDim.x) {
+    const int ch = i / cpg, c = g * cpg + (i % cpg);
+    const float* pp = partials + (((long long)b * chunks + ch) * channels + c) * 2;
+    s1 += pp[0];
+    s2 += pp[1];
+  }
+  s1 = block_sum_256(s1, red);
+  s2 = block_sum_256(s2, red);
+  const double count = (double)cpg * (double)pixels;
+  const typename E::T* img = reinterpret_cast<const typename E::T*>(x);
+  const float anchor = E::to_f(img[(long long)b * pixels * channels + g * cpg]);
+  const float dm = (float)(s1 / count);
+  const float mean = anchor + dm;
+  float var = (float)(s2 / count) - dm * dm;
+  var = fmaxf(var, 0.0f);
+  const float rstd = 1.0f / sqrtf(var + eps);
+  for (int i = threadIdx.x; i < cpg; i += blockDim.x) {
+    const int c = g * cpg + i;
+    float* o = coef + ((long long)b * channels + c) * 4;
+    o[0] = mean;
+    o[1] = rstd * gamma[c];
+    o[2] = beta[c];
+    o[3] = 0.0f;
+  }
+  if (threadIdx.x == 0 && stats_out) {
+    stats_out[((long long)b * groups + g) * 2] = mean;
+    stats_out[((long long)b * groups + g) * 2 + 1] = var;
+  }
+}
+
+// Streams x once: y = silu?((x - mean) * (rstd * gamma) + beta), 8 channels per thread.
+template <int D>
+__global__ void __launch_bounds__(256)
+    gn_nhwc_apply_kernel(const uint4* __restrict__ x, uint4* __restrict__ y,
+                         const float* __restrict__ coef, int channels, long long pixels,
+                         long long total_vectors, int silu) {
+  const int vc = channels / 8;
+  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < total_vectors;
+       v += (long long)gridDim.x * blockDim.x) {
+    const long long pix = v / vc;
+    const int col = (int)(v - pix * vc);
+    const int b = (int)(pix / pixels);
+    float f[8];
+    unpack8<D>(__ldg(x + v), f);
+    const float4* cf =
+        reinterpret_cast<const float4*>(coef + ((long long)b * channels + col * 8) * 4);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 c = __ldg(cf + j);
+      float a = (f[j] - c.x) * c.y + c.z;
+      if (silu) a = silu_f(a);
+      f[j] = a;
+    }
+    y[v] = pack8<D>(f);
+  }
+}
+
+int num_sms() {
+  int dev = 0, c = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
+  return c > 0 ? c : 148;
+}
+
+template <int D>
+cudaError_t gn_nhwc_typed(const void* x, void* y, const float* gamma, const float* beta, int batch,
+                          int channels, long long pixels, int groups, float eps, int silu,
+                          void* workspace, float* stats_out, cudaStream_t stream) {
+  const GnNhwcPlan plan = gn_nhwc_plan(batch, channels, pixels, groups);
+  float* partials = static_cast<float*>(workspace);
+  float* coef = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                         (plan.partial_bytes + 255) / 256 * 256);
+  const int vc = channels / 8;
+  const int rows = plan.threads / vc;
+  const size_t sred = (size_t)rows * vc * 16 * sizeof(float);
+  const uint16_t* xs = static_cast<const uint16_t*>(x);
+  gn_nhwc_stats_kernel<D><<<dim3(plan.chunks, batch), plan.threads, sred, stream>>>(
+      xs, partials, channels, pixels, plan.pix_per_chunk, groups);
+  gn_nhwc_finalize_kernel<D><<<dim3(groups, batch), 256, 0, stream>>>(
+      xs, partials, plan.chunks, channels, pixels, groups, gamma, beta, eps, coef, stats_out);
+  const long long vectors = (long long)batch * pixels * vc;
+  long long blocks = (vectors + 255) / 256;
+  const long long max_blocks = (long long)num_sms() * 16;
+  if (blocks > max_blocks) blocks = max_blocks;
+  gn_nhwc_apply_kernel<D><<<(int)blocks, 256, 0, stream>>>(static_cast<const uint4*>(x),
+                                                           static_cast<uint4*>(y), coef, channels,
+                                                           pixels, vectors, silu);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// ------------------------------------------------------------ host wrappers
+
+GnFusedPlan gn_fused_plan(int batch, int channels, long long spatial, int groups, int elem_bytes) {
+  GnFusedPlan plan{};
+  plan.groups_total = batch * groups;
+  plan.count = (long long)(channels / groups) * spatial;
+  plan.grid = num_sms() * kGnFusedCtasPerSm;
+  // Chunk capacity: fits kGnFusedSmemBytes, multiple of 16 bytes.
+  const long long cap = kGnFusedSmemBytes / elem_bytes;
+  long long chunks = (plan.count + cap - 1) / cap;
+  if (chunks < 1) chunks = 1;
+  const long long align = 16 / elem_bytes;
+  long long chunk = (plan.count + chunks - 1) / chunks;
+  chunk = (chunk + align - 1) / align * align;
+  chunks = (plan.count + chunk - 1) / chunk;
+  plan.chunk = chunk;
+  plan.chunks_per_group = (int)chunks;
+  plan.feasible = plan.chunks_per_group <= plan.grid;
+  plan.workspace_bytes = (size_t)plan.groups_total * plan.chunks_per_group * 3 * sizeof(float) +
+                         ((size_t)plan.groups_total * sizeof(int) + 255) / 256 * 256;
+  return plan;
+}
+
+template <typename T>
+cudaError_t gn_fused_launch(const T* x, T* y, const float* gamma, const float* beta, int batch,
+                            int channels, long long spatial, int groups, float eps, int silu,
+                            void* workspace, float* stats_out, cudaStream_t stream) {
+  const GnFusedPlan plan = gn_fused_plan(batch, channels, spatial, groups, (int)sizeof(T));
+  if (!plan.feasible) return cudaErrorInvalidValue;
+  FusedParams p;
+  p.count = plan.count;
+  p.chunk = plan.chunk;
+  p.chunks_per_group = plan.chunks_per_group;
+  p.groups_total = plan.groups_total;
+  p.groups = groups;
+  p.channels = channels;
+  p.spatial = spatial;
+  p.eps = eps;
+  p.silu = silu;
+  p.use_bulk = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) &&
+               ((reinterpret_cast<uintptr_t>(y) & 15) == 0) &&
+               ((plan.count * (long long)sizeof(T)) % 16 == 0) &&
+               ((plan.chunk * (long long)sizeof(T)) % 16 == 0);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.arrive = reinterpret_cast<int*>(ws);
+  const size_t arrive_bytes = ((size_t)plan.groups_total * sizeof(int) + 255) / 256 * 256;
+  p.partials = reinterpret_cast<float*>(ws + arrive_bytes);
+  p.stats_out = stats_out;
+  cudaError_t e = cudaMemsetAsync(p.arrive, 0, (size_t)plan.groups_total * sizeof(int), stream);
+  if (e != cudaSuccess) return e;
+  static bool configured[64] = {false};
+  int device = 0;
+  cudaGetDevice(&device);
+  if (device >= 0 && device < 64 && !configured[device]) {
+    e = cudaFuncSetAttribute(gn_nchw_fused_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kGnFusedSmemBytes);
+    if (e != cudaSuccess) return e;
+    configured[device] = true;
+  }
+  const int smem = (int)(plan.chunk * sizeof(T));
+  const long long items = (long long)plan.groups_total * plan.chunks_per_group;
+  int grid = plan.grid;
+  if (items < grid) grid = (int)items;
+  void* args[] = {(void*)&x, (void*)&y, (void*)&gamma, (void*)&beta, (void*)&p};
+  // A cooperative launch guarantees that all CTAs are resident, which the
+  // cross-CTA group wait relies on.
+  return cudaLaunchCooperativeKernel((const void*)gn_nchw_fused_kernel<T>, dim3(grid),
+                                     dim3(kFusedThreads), args, (size_t)smem, stream);
+}
+
+template cudaError_t gn_fused_launch<float>(const float*, float*, const float*, const float*, int,
+                                            int, long long, int, float, int, void*, float*,
+                                            cudaStream_t);
+template cudaError_t gn_fused_launch<__nv_bfloat16>(const __nv_bfloat16*, __nv_bfloat16*,
+                                                    const float*, const float*, int, int, long long,
+                                                    int, float, int, void*, float*, cudaStream_t);
+template cudaError_t gn_fused_launch<__half>(const __half*, __half*, const float*, const float*,
+                                             int, int, long long, int, float, int, void*, float*,
+                                             cudaStream_t);
+
+GnNhwcPlan gn_nhwc_plan(int batch, int channels, long long pixels, int groups) {
+  GnNhwcPlan plan{};
+  const int vc = channels / 8;
+  plan.threads = (kNhwcThreads / vc) * vc;
+  const int target_ctas = num_sms() * 4;
+  long long chunks = (target_ctas + batch - 1) / batch;
+  if (chunks > pixels) chunks = pixels;
+  if (chunks < 1) chunks = 1;
+  plan.pix_per_chunk = (pixels + chunks - 1) / chunks;
+  plan.chunks = (int)((pixels + plan.pix_per_chunk - 1) / plan.pix_per_chunk);
+  plan.partial_bytes = (size_t)batch * plan.chunks * channels * 2 * sizeof(float);
+  plan.coef_bytes = (size_t)batch * channels * 4 * sizeof(float);
+  plan.workspace_bytes = (plan.partial_bytes + 255) / 256 * 256 + plan.coef_bytes;
+  plan.groups = groups;
+  return plan;
+}
+
+cudaError_t gn_nhwc_launch(int dtype, const void* x, void* y, const float* gamma, const float* beta,
+                           int batch, int channels, long long pixels, int groups, float eps,
+                           int silu, void* workspace, float* stats_out, cudaStream_t stream) {
+  if (dtype == kF16)
+    return gn_nhwc_typed<kF16>(x, y, gamma, beta, batch, channels, pixels, groups, eps, silu,
+                               workspace, stats_out, stream);
+  return gn_nhwc_typed<kBf16>(x, y, gamma, beta, batch, channels, pixels, groups, eps, silu,
+                              workspace, stats_out, stream);
+}
+
+}  // namespace osor

@@ -1,0 +1,47 @@
+// Host interface of the GroupNorm(+SiLU) kernels.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace osor {
+
+// Shared-memory chunk capacity of the fused NCHW kernel and CTAs per SM.
+constexpr int kGnFusedSmemBytes = 96 * 1024;
+constexpr int kGnFusedCtasPerSm = 2;
+
+struct GnFusedPlan {
+  int groups_total;
+  long long count;
+  long long chunk;
+  int chunks_per_group;
+  int grid;
+  bool feasible;  // every chunk of a group fits in one wave of resident CTAs
+  size_t workspace_bytes;
+};
+GnFusedPlan gn_fused_plan(int batch, int channels, long long spatial, int groups, int elem_bytes);
+
+// Standalone NCHW GroupNorm(+SiLU), T = float, __nv_bfloat16 or __half. stats_out
+// (nullable) receives [batch*groups][2] = (mean, biased variance).
+template <typename T>
+cudaError_t gn_fused_launch(const T* x, T* y, const float* gamma, const float* beta, int batch,
+                            int channels, long long spatial, int groups, float eps, int silu,
+                            void* workspace, float* stats_out, cudaStream_t stream);
+
+struct GnNhwcPlan {
+  int threads;
+  int chunks;
+  long long pix_per_chunk;
+  size_t partial_bytes, coef_bytes, workspace_bytes;
+  int groups;
+};
+GnNhwcPlan gn_nhwc_plan(int batch, int channels, long long pixels, int groups);
+
+// NHWC 16-bit (dtype kBf16 / kF16) GroupNorm(+SiLU): stats, finalize and
+// apply kernels.
+cudaError_t gn_nhwc_launch(int dtype, const void* x, void* y, const float* gamma, const float* beta,
+                           int batch, int channels, long long pixels, int groups, float eps,
+                           int silu, void* workspace, float* stats_out, cudaStream_t stream);
+
+}  // namespace osor

@@ -1,0 +1,418 @@
+// CUDA-core kernels around the tensor-core contractions: thin convolutions
+// (Cin or Cout below the tensor-core tile), nearest 2x upsampling, the
+// attention softmax and V transpose, a CUDA-core attention for shapes the
+// tensor-core tiles do not cover, layout conversions and the posterior
+// elementwise op. 16-bit tensors are bf16 or f16 (Dtype), chosen per call.
+#include "common.cuh"
+#include "ops.h"
+
+namespace osor {
+namespace {
+
+// ------------------------------------------------------------ direct conv
+// One thread per output pixel and block of COB output channels.
+// Weights: 16-bit [cout][ksize*ksize*cin] ordered (ky, kx, ci).
+template <int D, int IN_MODE, int OUT_MODE, int COB>
+__global__ void __launch_bounds__(128)
+    direct_conv_kernel(const void* __restrict__ xin, const uint16_t* __restrict__ wbits,
+                       const float* __restrict__ bias, const uint16_t* __restrict__ residual,
+                       void* __restrict__ out, DirectConvArgs a) {
+  using E = Elem<D>;
+  using T = typename E::T;
+  const T* w = reinterpret_cast<const T*>(wbits);
+  const long long pix = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long total = (long long)a.batch * a.out_h * a.out_w;
+  if (pix >= total) return;
+  const int co0 = blockIdx.y * COB;
+  const int ox = (int)(pix % a.out_w);
+  const long long t = pix / a.out_w;
+  const int oy = (int)(t % a.out_h);
+  const int b = (int)(t / a.out_h);
+  const long long kdim = (long long)a.ksize * a.ksize * a.cin;
+  float acc[COB];
+#pragma unroll
+  for (int j = 0; j < COB; ++j) acc[j] = 0.0f;
+  for (int ky = 0; ky < a.ksize; ++ky) {
+    const int iy = oy * a.stride + ky - a.pad;
+    if (iy < 0 || iy >= a.in_h) continue;
+    for (int kx = 0; kx < a.ksize; ++kx) {
+      const int ix = ox * a.stride + kx - a.pad;
+      if (ix < 0 || ix >= a.in_w) continue;
+      const long long wtap = (long long)(ky * a.ksize + kx) * a.cin;
+      if (IN_MODE == kLayoutNhwc16) {
+        const T* xp = static_cast<const T*>(xin) +
+                      (((long long)b * a.in_h + iy) * a.in_w + ix) * a.in_pixel_stride;
+        if ((a.cin & 7) == 0 && (a.in_pixel_stride & 7) == 0) {
+          for (int ci = 0; ci < a.cin; ci += 8) {
+            float xv[8];
+            unpack8<D>(__ldg(reinterpret_cast<const uint4*>(xp + ci)), xv);
+#pragma unroll
+            for (int j = 0; j < COB; ++j) {
+              if (co0 + j < a.cout) {
+                float wv[8];
+                unpack8<D>(__ldg(reinterpret_cast<const uint4*>(w + (long long)(co0 + j) * kdim +
+                                                                wtap + ci)),
+                           wv);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) acc[j] += xv[u] * wv[u];
+              }
+            }
+          }
+        } else {
+          for (int ci = 0; ci < a.cin; ++ci) {
+            const float xv = E::to_f(xp[ci]);
+#pragma unroll
+            for (int j = 0; j < COB; ++j)
+              if (co0 + j < a.cout) acc[j] += xv * E::to_f(w[(long long)(co0 + j) * kdim + wtap + ci]);
+          }
+        }
+      } else {  // NCHW f32
+        const float* xp = static_cast<const float*>(xin);
+        for (int ci = 0; ci < a.cin; ++ci) {
+          const float xv = __ldg(xp + (((long long)b * a.cin + ci) * a.in_h + iy) * a.in_w + ix);
+#pragma unroll
+          for (int j = 0; j < COB; ++j)
+            if (co0 + j < a.cout) acc[j] += xv * E::to_f(w[(long long)(co0 + j) * kdim + wtap + ci]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < COB; ++j) {
+    const int co = co0 + j;
+    if (co >= a.cout) continue;
+    float v = acc[j] + (bias ? __ldg(bias + co) : 0.0f);
+    if (OUT_MODE == kLayoutNhwc16) {
+      if (residual) v += E::to_f(reinterpret_cast<const T*>(residual)[pix * a.ld_res + co]);
+      static_cast<T*>(out)[pix * a.out_pixel_stride + co] = E::from_f(v);
+    } else {
+      const long long o = (((long long)b * a.cout + co) * a.out_h + oy) * a.out_w + ox;
+      static_cast<float*>(out)[o] = v;
+    }
+  }
+}
+
+template <int D, int IN_MODE, int OUT_MODE>
+cudaError_t direct_dispatch(const void* x, const void* w, const float* bias, const void* residual,
+                            void* out, const DirectConvArgs& a, cudaStream_t s) {
+  const long long total = (long long)a.batch * a.out_h * a.out_w;
+  const int threads = 128;
+  const unsigned gx = (unsigned)((total + threads - 1) / threads);
+  const uint16_t* wb = static_cast<const uint16_t*>(w);
+  const uint16_t* rb = static_cast<const uint16_t*>(residual);
+  if (a.cout <= 4) {
+    direct_conv_kernel<D, IN_MODE, OUT_MODE, 4>
+        <<<dim3(gx, (a.cout + 3) / 4), threads, 0, s>>>(x, wb, bias, rb, out, a);
+  } else {
+    direct_conv_kernel<D, IN_MODE, OUT_MODE, 8>
+        <<<dim3(gx, (a.cout + 7) / 8), threads, 0, s>>>(x, wb, bias, rb, out, a);
+  }
+  return cudaGetLastError();
+}
+
+template <int D>
+cudaError_t direct_typed(const void* x, int in_mode, const void* w, const float* bias,
+                         const void* residual, void* out, int out_mode, const DirectConvArgs& a,
+                         cudaStream_t s) {
+  if (in_mode == kLayoutNhwc16 && out_mode == kLayoutNhwc16)
+    return direct_dispatch<D, kLayoutNhwc16, kLayoutNhwc16>(x, w, bias, residual, out, a, s);
+  if (in_mode == kLayoutNhwc16 && out_mode == kLayoutNchwF32)
+    return direct_dispatch<D, kLayoutNhwc16, kLayoutNchwF32>(x, w, bias, residual, out, a, s);
+  if (in_mode == kLayoutNchwF32 && out_mode == kLayoutNhwc16)
+    return direct_dispatch<D, kLayoutNchwF32, kLayoutNhwc16>(x, w, bias, residual, out, a, s);
+  return direct_dispatch<D, kLayoutNchwF32, kLayoutNchwF32>(x, w, bias, residual, out, a, s);
+}
+
+// ------------------------------------------------------------ upsample
+__global__ void upsample2x_nhwc_kernel(const uint4* __restrict__ x, uint4* __restrict__ y,
+                                       int h, int w, int vc, long long total_out) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total_out;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int v = (int)(i % vc);
+    long long t = i / vc;
+    const int ox = (int)(t % (2 * w));
+    t /= (2 * w);
+    const int oy = (int)(t % (2 * h));
+    const long long b = t / (2 * h);
+    y[i] = __ldg(x + ((b * h + oy / 2) * w + ox / 2) * vc + v);
+  }
+}
+
+// ------------------------------------------------------------ softmax
+// One CTA per row: p = exp(s - max) stored as 16-bit, inv_sum = 1 / sum(p) in
+// fp32 (sum of the rounded values, which is what the P.V GEMM multiplies).
+constexpr int kSoftmaxThreads = 256;
+constexpr int kSoftmaxMaxVec = 16;  // rows up to 16 * 4 * 256 = 16384 columns
+
+template <int D>
+__global__ void __launch_bounds__(kSoftmaxThreads)
+    softmax_rows_kernel(const float* __restrict__ s, uint16_t* __restrict__ p,
+                        float* __restrict__ inv_sum, int cols, long long ld_s, long long ld_p) {
+  using E = Elem<D>;
+  __shared__ float red[8];
+  const long long row = blockIdx.x;
+  const float4* srow = reinterpret_cast<const float4*>(s + row * ld_s);
+  const int nv = cols / 4;
+  float4 v[kSoftmaxMaxVec];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kSoftmaxMaxVec; ++j) {
+    const int idx = threadIdx.x + j * kSoftmaxThreads;
+    if (idx < nv) {
+      v[j] = __ldcs(srow + idx);
+      mx = fmaxf(mx, fmaxf(fmaxf(v[j].x, v[j].y), fmaxf(v[j].z, v[j].w)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int k = 1; k < kSoftmaxThreads / 32; ++k) mx = fmaxf(mx, red[k]);
+  __syncthreads();
+  float sum = 0.0f;
+  uint2* prow = reinterpret_cast<uint2*>(p + row * ld_p);
+#pragma unroll
+  for (int j = 0; j < kSoftmaxMaxVec; ++j) {
+    const int idx = threadIdx.x + j * kSoftmaxThreads;
+    if (idx < nv) {
+      const uint32_t a = E::pack(__expf(v[j].x - mx), __expf(v[j].y - mx));
+      const uint32_t b = E::pack(__expf(v[j].z - mx), __expf(v[j].w - mx));
+      const float2 fa = E::unpack(a), fb = E::unpack(b);
+      sum += (fa.x + fa.y) + (fb.x + fb.y);
+      prow[idx] = make_uint2(a, b);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.0f;
+    for (int k = 0; k < kSoftmaxThreads / 32; ++k) t += red[k];
+    inv_sum[row] = 1.0f / t;
+  }
+}
+
+// ------------------------------------------------------------ transpose
+// out[c][n] = in[n][c] of 16-bit elements; 32x32 tiles through shared memory.
+__global__ void transpose16_kernel(const uint16_t* __restrict__ in, long long ld_in,
+                                   uint16_t* __restrict__ out, long long ld_out, int rows,
+                                   int cols) {
+  __shared__ uint16_t tile[32][33];
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int r = r0 + k, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) tile[k][threadIdx.x] = in[(long long)r * ld_in + c];
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int c = c0 + k, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) out[(long long)c * ld_out + r] = tile[threadIdx.x][k];
+  }
+}
+
+// ------------------------------------------------------------ CUDA-core attention
+// One warp per query row, online softmax over keys, fp32. q already scaled.
+// q/k/v rows have stride ld (elements); out rows stride ld_out.
+template <int D>
+__global__ void attention_rows_kernel(const uint16_t* __restrict__ qb,
+                                      const uint16_t* __restrict__ kb,
+                                      const uint16_t* __restrict__ vb, long long ld,
+                                      uint16_t* __restrict__ ob, long long ld_out, int tokens,
+                                      int dim) {
+  using E = Elem<D>;
+  using T = typename E::T;
+  const T* q = reinterpret_cast<const T*>(qb);
+  const T* k = reinterpret_cast<const T*>(kb);
+  const T* v = reinterpret_cast<const T*>(vb);
+  T* out = reinterpret_cast<T*>(ob);
+  extern __shared__ float qs[];  // [warps][dim]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (row >= tokens) return;
+  float* qrow = qs + warp * dim;
+  for (int c = lane; c < dim; c += 32) qrow[c] = E::to_f(q[row * ld + c]);
+  __syncwarp();
+  constexpr int kMaxPer = 16;  // dim <= 512
+  float acc[kMaxPer];
+#pragma unroll
+  for (int j = 0; j < kMaxPer; ++j) acc[j] = 0.0f;
+  float m = -INFINITY, l = 0.0f;
+  for (int t = 0; t < tokens; ++t) {
+    float s = 0.0f;
+    for (int c = lane; c < dim; c += 32) s += qrow[c] * E::to_f(k[(long long)t * ld + c]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mn = fmaxf(m, s);
+    const float corr = __expf(m - mn);
+    const float pexp = __expf(s - mn);
+    l = l * corr + pexp;
+#pragma unroll
+    for (int j = 0; j < kMaxPer; ++j) {
+      const int c = lane + 32 * j;
+      if (c < dim) acc[j] = acc[j] * corr + pexp * E::to_f(v[(long long)t * ld + c]);
+    }
+    m = mn;
+  }
+  const float inv = 1.0f / l;
+#pragma unroll
+  for (int j = 0; j < kMaxPer; ++j) {
+    const int c = lane + 32 * j;
+    if (c < dim) out[row * ld_out + c] = E::from_f(acc[j] * inv);
+  }
+}
+
+// ------------------------------------------------------------ layouts
+template <int D>
+__global__ void nchw_f32_to_nhwc16_kernel(const float* __restrict__ x, uint16_t* __restrict__ yb,
+                                          int c, long long hw, long long total) {
+  using E = Elem<D>;
+  typename E::T* y = reinterpret_cast<typename E::T*>(yb);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int ch = (int)(i % c);
+    const long long pix = i / c;
+    const long long b = pix / hw, p = pix % hw;
+    y[i] = E::from_f(__ldg(x + (b * c + ch) * hw + p));
+  }
+}
+
+template <int D>
+__global__ void nhwc16_to_nchw_f32_kernel(const uint16_t* __restrict__ xb, float* __restrict__ y,
+                                          int c, long long hw, long long total) {
+  using E = Elem<D>;
+  const typename E::T* x = reinterpret_cast<const typename E::T*>(xb);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long p = i % hw;
+    const long long t = i / hw;
+    const int ch = (int)(t % c);
+    const long long b = t / c;
+    y[i] = E::to_f(x[(b * hw + p) * c + ch]);
+  }
+}
+
+// moments [B,8,h,w] -> sample [B,4,h,w] = (mean + exp(0.5*clamp(logvar,-30,20)) * noise) * scale
+__global__ void posterior_sample_kernel(const float* __restrict__ moments,
+                                        const float* __restrict__ noise, float* __restrict__ out,
+                                        long long hw, long long total, float scale) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long p = i % hw;
+    const long long t = i / hw;
+    const int c = (int)(t % 4);
+    const long long b = t / 4;
+    const float mean = moments[(b * 8 + c) * hw + p];
+    const float logvar = fminf(fmaxf(moments[(b * 8 + 4 + c) * hw + p], -30.0f), 20.0f);
+    out[i] = (mean + expf(0.5f * logvar) * noise[i]) * scale;
+  }
+}
+
+__global__ void scale_f32_kernel(const float* __restrict__ x, float* __restrict__ y, float s,
+                                 long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    y[i] = x[i] * s;
+}
+
+int blocks_for(long long n, int threads) {
+  long long b = (n + threads - 1) / threads;
+  const long long cap = 148LL * 32;
+  return (int)(b < cap ? (b > 0 ? b : 1) : cap);
+}
+
+}  // namespace
+
+cudaError_t direct_conv_launch(int dtype, const void* x, int in_mode, const void* w,
+                               const float* bias, const void* residual, void* out, int out_mode,
+                               const DirectConvArgs& a, cudaStream_t s) {
+  if (dtype == kF16) return direct_typed<kF16>(x, in_mode, w, bias, residual, out, out_mode, a, s);
+  return direct_typed<kBf16>(x, in_mode, w, bias, residual, out, out_mode, a, s);
+}
+
+cudaError_t upsample2x_nhwc_launch(const void* x, void* y, int batch, int h, int w, int c,
+                                   cudaStream_t s) {
+  if (c % 8 != 0) return cudaErrorInvalidValue;
+  const long long total = (long long)batch * 4 * h * w * (c / 8);
+  upsample2x_nhwc_kernel<<<blocks_for(total, 256), 256, 0, s>>>(
+      static_cast<const uint4*>(x), static_cast<uint4*>(y), h, w, c / 8, total);
+  return cudaGetLastError();
+}
+
+cudaError_t softmax_rows_launch(int dtype, const float* scores, void* probs, float* inv_sum,
+                                int rows, int cols, long long ld_s, long long ld_p,
+                                cudaStream_t s) {
+  if (cols % 4 != 0 || cols > kSoftmaxMaxVec * 4 * kSoftmaxThreads || ld_s % 4 || ld_p % 4)
+    return cudaErrorInvalidValue;
+  uint16_t* p = static_cast<uint16_t*>(probs);
+  if (dtype == kF16)
+    softmax_rows_kernel<kF16><<<rows, kSoftmaxThreads, 0, s>>>(scores, p, inv_sum, cols, ld_s, ld_p);
+  else
+    softmax_rows_kernel<kBf16><<<rows, kSoftmaxThreads, 0, s>>>(scores, p, inv_sum, cols, ld_s, ld_p);
+  return cudaGetLastError();
+}
+
+cudaError_t transpose16_launch(const void* in, long long ld_in, void* out, long long ld_out,
+                               int rows, int cols, cudaStream_t s) {
+  dim3 grid((cols + 31) / 32, (rows + 31) / 32);
+  transpose16_kernel<<<grid, dim3(32, 8), 0, s>>>(static_cast<const uint16_t*>(in), ld_in,
+                                                   static_cast<uint16_t*>(out), ld_out, rows, cols);
+  return cudaGetLastError();
+}
+
+cudaError_t attention_rows_launch(int dtype, const void* q, const void* k, const void* v,
+                                  long long ld, void* out, long long ld_out, int tokens, int dim,
+                                  cudaStream_t s) {
+  if (dim > 512) return cudaErrorInvalidValue;
+  const int warps = 4;
+  const dim3 grid((tokens + warps - 1) / warps);
+  const size_t smem = (size_t)warps * dim * sizeof(float);
+  const uint16_t* qb = static_cast<const uint16_t*>(q);
+  const uint16_t* kb = static_cast<const uint16_t*>(k);
+  const uint16_t* vb = static_cast<const uint16_t*>(v);
+  uint16_t* ob = static_cast<uint16_t*>(out);
+  if (dtype == kF16)
+    attention_rows_kernel<kF16><<<grid, warps * 32, smem, s>>>(qb, kb, vb, ld, ob, ld_out, tokens, dim);
+  else
+    attention_rows_kernel<kBf16><<<grid, warps * 32, smem, s>>>(qb, kb, vb, ld, ob, ld_out, tokens, dim);
+  return cudaGetLastError();
+}
+
+cudaError_t nchw_f32_to_nhwc16_launch(int dtype, const float* x, void* y, int batch, int c,
+                                      long long hw, cudaStream_t s) {
+  const long long total = (long long)batch * c * hw;
+  uint16_t* yb = static_cast<uint16_t*>(y);
+  if (dtype == kF16)
+    nchw_f32_to_nhwc16_kernel<kF16><<<blocks_for(total, 256), 256, 0, s>>>(x, yb, c, hw, total);
+  else
+    nchw_f32_to_nhwc16_kernel<kBf16><<<blocks_for(total, 256), 256, 0, s>>>(x, yb, c, hw, total);
+  return cudaGetLastError();
+}
+
+cudaError_t nhwc16_to_nchw_f32_launch(int dtype, const void* x, float* y, int batch, int c,
+                                      long long hw, cudaStream_t s) {
+  const long long total = (long long)batch * c * hw;
+  const uint16_t* xb = static_cast<const uint16_t*>(x);
+  if (dtype == kF16)
+    nhwc16_to_nchw_f32_kernel<kF16><<<blocks_for(total, 256), 256, 0, s>>>(xb, y, c, hw, total);
+  else
+    nhwc16_to_nchw_f32_kernel<kBf16><<<blocks_for(total, 256), 256, 0, s>>>(xb, y, c, hw, total);
+  return cudaGetLastError();
+}
+
+cudaError_t posterior_sample_launch(const float* moments, const float* noise, float* out,
+                                    int batch, long long hw, float scale, cudaStream_t s) {
+  const long long total = (long long)batch * 4 * hw;
+  posterior_sample_kernel<<<blocks_for(total, 256), 256, 0, s>>>(moments, noise, out, hw, total,
+                                                                 scale);
+  return cudaGetLastError();
+}
+
+cudaError_t scale_f32_launch(const float* x, float* y, float scale, long long n, cudaStream_t s) {
+  scale_f32_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, y, scale, n);
+  return cudaGetLastError();
+}
+
+}  // namespace osor

@@ -1,0 +1,50 @@
+// Host interface of the CUDA-core support kernels. `dtype` is the Dtype
+// (kBf16 / kF16) of every 16-bit tensor of the call.
+#pragma once
+#include <cuda_runtime.h>
+
+namespace osor {
+
+enum : int { kLayoutNhwc16 = 0, kLayoutNchwF32 = 1 };
+
+struct DirectConvArgs {
+  int batch = 0, in_h = 0, in_w = 0, cin = 0;
+  long long in_pixel_stride = 0;  // NHWC input only
+  int ksize = 3, stride = 1, pad = 1;
+  int out_h = 0, out_w = 0, cout = 0;
+  long long out_pixel_stride = 0;  // NHWC output only
+  long long ld_res = 0;            // NHWC residual row stride
+};
+
+// Direct convolution on CUDA cores for thin layers; weights 16-bit
+// [cout][ksize*ksize*cin] in (ky, kx, ci) order, bias f32 (nullable),
+// residual (NHWC output only, nullable).
+cudaError_t direct_conv_launch(int dtype, const void* x, int in_mode, const void* w,
+                               const float* bias, const void* residual, void* out, int out_mode,
+                               const DirectConvArgs& a, cudaStream_t s);
+
+cudaError_t upsample2x_nhwc_launch(const void* x, void* y, int batch, int h, int w, int c,
+                                   cudaStream_t s);
+
+// probs[r][c] = 16-bit(exp(scores[r][c] - max_r)); inv_sum[r] = 1 / sum_c probs[r][c].
+cudaError_t softmax_rows_launch(int dtype, const float* scores, void* probs, float* inv_sum,
+                                int rows, int cols, long long ld_s, long long ld_p,
+                                cudaStream_t s);
+
+cudaError_t transpose16_launch(const void* in, long long ld_in, void* out, long long ld_out,
+                               int rows, int cols, cudaStream_t s);
+
+// softmax(q k^T) v on CUDA cores, one warp per query (dim <= 512).
+cudaError_t attention_rows_launch(int dtype, const void* q, const void* k, const void* v,
+                                  long long ld, void* out, long long ld_out, int tokens, int dim,
+                                  cudaStream_t s);
+
+cudaError_t nchw_f32_to_nhwc16_launch(int dtype, const float* x, void* y, int batch, int c,
+                                      long long hw, cudaStream_t s);
+cudaError_t nhwc16_to_nchw_f32_launch(int dtype, const void* x, float* y, int batch, int c,
+                                      long long hw, cudaStream_t s);
+cudaError_t posterior_sample_launch(const float* moments, const float* noise, float* out,
+                                    int batch, long long hw, float scale, cudaStream_t s);
+cudaError_t scale_f32_launch(const float* x, float* y, float scale, long long n, cudaStream_t s);
+
+}  // namespace osor

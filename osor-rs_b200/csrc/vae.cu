@@ -1,0 +1,705 @@
+// VAE encoder / decoder runtime on one device and one stream.
+//
+// Block topology follows the reference:
+//   Resnet      src/native/vae_encoder.rs:107-152
+//   DownBlock   src/native/vae_encoder.rs:154-215
+//   Attention   src/native/vae_encoder.rs:237-340
+//   MidBlock    src/native/vae_encoder.rs:342-376
+//   VaeEncoder  src/native/vae_encoder.rs:378-425
+//   UpBlock / VaeDecoder  src/native/vae_decoder.rs:13-114
+// Activations stay NHWC 16-bit (bf16 or f16, fixed per model) in HBM between
+// kernels; the thin first/last layers read / write the boundary's NCHW f32
+// directly. Bias and residual adds run in the convolution epilogue,
+// GroupNorm+SiLU is one stats pass plus one streaming apply, and the resnet
+// output overwrites its input in place (the epilogue reads each residual
+// element before writing the same element).
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "conv_tc.h"
+#include "groupnorm.h"
+#include "ops.h"
+#include "profile.h"
+#include "vae.h"
+
+namespace osor {
+namespace {
+
+constexpr int kGroups = 32;
+constexpr float kEps = 1e-6f;
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+Status cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return Status::ok();
+  return Status::err(OSOR_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+uint16_t to_bits(float v, int dtype) {
+  uint16_t bits;
+  if (dtype == kF16) {
+    const __half h = __float2half_rn(v);
+    std::memcpy(&bits, &h, 2);
+  } else {
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    std::memcpy(&bits, &h, 2);
+  }
+  return bits;
+}
+
+class Loader {
+ public:
+  Loader(const osor_tensor* t, size_t n, Vae* m) : model_(m) {
+    for (size_t i = 0; i < n; ++i)
+      if (t[i].name) by_name_[t[i].name] = &t[i];
+  }
+  bool has(const std::string& name) const { return by_name_.count(name) != 0; }
+  Status tensor(const std::string& name, std::vector<int64_t> shape, const osor_tensor** out) {
+    auto it = by_name_.find(name);
+    if (it == by_name_.end())
+      return Status::err(OSOR_ERR_INVALID_ARTIFACT, "missing VAE tensor " + name);
+    const osor_tensor* t = it->second;
+    bool ok = t->data != nullptr && t->ndim == (int)shape.size();
+    for (size_t d = 0; ok && d < shape.size(); ++d) ok = t->shape[d] == shape[d];
+    if (!ok)
+      return Status::err(OSOR_ERR_INVALID_ARTIFACT, "VAE tensor " + name + " has the wrong shape");
+    *out = t;
+    return Status::ok();
+  }
+  template <typename T>
+  Status upload(const std::vector<T>& host, const T** dev) {
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, host.size() * sizeof(T));
+    if (e != cudaSuccess) return cuda_status(e, "weight allocation");
+    model_->allocations.push_back(p);
+    e = cudaMemcpy(p, host.data(), host.size() * sizeof(T), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_status(e, "weight upload");
+    *dev = static_cast<const T*>(p);
+    return Status::ok();
+  }
+  Status conv(const std::string& prefix, int cin, int cout, int k, int stride, int pad,
+              ConvLayer* L) {
+    const osor_tensor *w, *b;
+    Status s = tensor(prefix + ".weight", {cout, cin, k, k}, &w);
+    if (!s.good()) return s;
+    if (!(s = tensor(prefix + ".bias", {cout}, &b)).good()) return s;
+    return conv_from(w->data, b->data, cin, cout, k, stride, pad, L);
+  }
+  Status conv_from(const float* w, const float* b, int cin, int cout, int k, int stride, int pad,
+                   ConvLayer* L) {
+    std::vector<uint16_t> packed((size_t)cout * k * k * cin);
+    for (int co = 0; co < cout; ++co)
+      for (int ci = 0; ci < cin; ++ci)
+        for (int ky = 0; ky < k; ++ky)
+          for (int kx = 0; kx < k; ++kx)
+            packed[(((size_t)co * k + ky) * k + kx) * cin + ci] =
+                to_bits(w[(((size_t)co * cin + ci) * k + ky) * k + kx], model_->dtype);
+    L->cin = cin;
+    L->cout = cout;
+    L->k = k;
+    L->stride = stride;
+    L->pad = pad;
+    L->pad_end = pad;
+    Status s = upload(packed, &L->w);
+    if (!s.good()) return s;
+    return upload(std::vector<float>(b, b + cout), &L->bias);
+  }
+  Status norm(const std::string& prefix, int c, NormLayer* L) {
+    if (c % kGroups != 0)
+      return Status::err(OSOR_ERR_INVALID_ARTIFACT,
+                         "VAE group normalization requires channels divisible by 32");
+    const osor_tensor *g, *b;
+    Status s = tensor(prefix + ".weight", {c}, &g);
+    if (!s.good()) return s;
+    if (!(s = tensor(prefix + ".bias", {c}, &b)).good()) return s;
+    L->c = c;
+    const float* gp = nullptr;
+    const float* bp = nullptr;
+    if (!(s = upload(std::vector<float>(g->data, g->data + c), &gp)).good()) return s;
+    if (!(s = upload(std::vector<float>(b->data, b->data + c), &bp)).good()) return s;
+    L->gamma = const_cast<float*>(gp);
+    L->beta = const_cast<float*>(bp);
+    return Status::ok();
+  }
+  Status resnet(const std::string& p, int cin, int cout, ResnetLayer* L) {
+    Status s = norm(p + ".norm1", cin, &L->n1);
+    if (s.good()) s = conv(p + ".conv1", cin, cout, 3, 1, 1, &L->c1);
+    if (s.good()) s = norm(p + ".norm2", cout, &L->n2);
+    if (s.good()) s = conv(p + ".conv2", cout, cout, 3, 1, 1, &L->c2);
+    L->has_shortcut = cin != cout;
+    if (s.good() && L->has_shortcut)
+      s = conv(p + ".conv_shortcut", cin, cout, 1, 1, 0, &L->shortcut);
+    return s;
+  }
+  // Linear projection stored either [c, c] or [c, c, 1, 1] (vae_encoder.rs:224-235).
+  Status linear(const std::string& p, int c, const float** w, const float** b) {
+    const osor_tensor* t;
+    Status s = tensor(p + ".weight", {c, c}, &t);
+    if (!s.good()) s = tensor(p + ".weight", {c, c, 1, 1}, &t);
+    if (!s.good()) return s;
+    *w = t->data;
+    if (!(s = tensor(p + ".bias", {c}, &t)).good()) return s;
+    *b = t->data;
+    return Status::ok();
+  }
+  Status attention(const std::string& p, int c, AttentionLayer* L) {
+    Status s = norm(p + ".group_norm", c, &L->norm);
+    if (!s.good()) return s;
+    const bool diffusers = has(p + ".to_q.weight");
+    const char* names[4] = {"to_q", "to_k", "to_v", "to_out.0"};
+    const char* legacy[4] = {"query", "key", "value", "proj_attn"};
+    const float* w[4];
+    const float* b[4];
+    for (int i = 0; i < 4; ++i) {
+      s = linear(p + "." + (diffusers ? names[i] : legacy[i]), c, &w[i], &b[i]);
+      if (!s.good()) return s;
+    }
+    // q and k each carry C^-1/4 (vae_encoder.rs:320-323); fold it into the weights.
+    const float qk_scale = (float)std::pow((double)c, -0.25);
+    std::vector<float> wq((size_t)3 * c * c), bq((size_t)3 * c);
+    for (int i = 0; i < 3; ++i) {
+      const float sc = i < 2 ? qk_scale : 1.0f;
+      for (size_t j = 0; j < (size_t)c * c; ++j) wq[(size_t)i * c * c + j] = w[i][j] * sc;
+      for (int j = 0; j < c; ++j) bq[(size_t)i * c + j] = b[i][j] * sc;
+    }
+    s = conv_from(wq.data(), bq.data(), c, 3 * c, 1, 1, 0, &L->qkv);
+    if (!s.good()) return s;
+    return conv_from(w[3], b[3], c, c, 1, 1, 0, &L->out);
+  }
+  Status mid(const std::string& p, int c, MidLayer* L) {
+    Status s = resnet(p + ".resnets.0", c, c, &L->first);
+    if (s.good()) s = attention(p + ".attentions.0", c, &L->attn);
+    if (s.good()) s = resnet(p + ".resnets.1", c, c, &L->second);
+    return s;
+  }
+
+ private:
+  Vae* model_;
+  std::unordered_map<std::string, const osor_tensor*> by_name_;
+};
+
+// ----------------------------------------------------------------- execution
+
+struct Buffers {
+  uint16_t* act[4];
+  float* f32;
+  float* scores;
+  uint16_t* probs;
+  float* rowsum;
+  void* gn;
+  size_t gn_bytes;
+};
+
+Buffers carve(const WorkspacePlan& plan, void* ws) {
+  Buffers b;
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  for (int i = 0; i < 4; ++i) {
+    b.act[i] = reinterpret_cast<uint16_t*>(p);
+    p += plan.act_bytes;
+  }
+  b.f32 = reinterpret_cast<float*>(p);
+  p += plan.f32_bytes;
+  b.scores = reinterpret_cast<float*>(p);
+  p += plan.scores_bytes;
+  b.probs = reinterpret_cast<uint16_t*>(p);
+  p += plan.probs_bytes;
+  b.rowsum = reinterpret_cast<float*>(p);
+  p += plan.rowsum_bytes;
+  b.gn = p;
+  b.gn_bytes = plan.gn_bytes;
+  return b;
+}
+
+Status check_cancel(const volatile int* cancel) {
+  if (cancel && *cancel) return Status::err(OSOR_ERR_CANCELLED, "inference was cancelled");
+  return Status::ok();
+}
+
+struct Ctx {
+  int dtype;
+  const Buffers& b;
+  cudaStream_t s;
+  const volatile int* cancel;
+};
+
+Status gn(const Ctx& c, const NormLayer& L, const void* x, void* y, int batch, long long pixels,
+          bool silu) {
+  const GnNhwcPlan plan = gn_nhwc_plan(batch, L.c, pixels, kGroups);
+  if (plan.workspace_bytes > c.b.gn_bytes)
+    return Status::err(OSOR_ERR_INVALID_INPUT, "group-norm workspace too small");
+  // Algorithmic bytes: one 16-bit read and one write per element.
+  OpScope scope("groupnorm", 0.0, 4.0 * batch * pixels * L.c, c.s, 3);
+  return cuda_status(gn_nhwc_launch(c.dtype, x, y, L.gamma, L.beta, batch, L.c, pixels, kGroups,
+                                    kEps, silu ? 1 : 0, c.b.gn, nullptr, c.s),
+                     "group norm");
+}
+
+Status conv16(const Ctx& c, const ConvLayer& L, const void* x, int batch, int h, int w, void* out,
+              const void* residual = nullptr) {
+  return run_conv(c.dtype, L, x, kLayoutNhwc16, batch, h, w, L.cin, out, kLayoutNhwc16, L.cout,
+                  residual, L.cout, c.s);
+}
+
+// x (buffer xi) -> resnet output written back into buffer xi.
+Status resnet(const Ctx& c, const ResnetLayer& L, int xi, int batch, int h, int w) {
+  Status st = check_cancel(c.cancel);
+  if (!st.good()) return st;
+  const long long pixels = (long long)h * w;
+  uint16_t* x = c.b.act[xi];
+  uint16_t* t = c.b.act[(xi + 1) % 4];
+  uint16_t* hbuf = c.b.act[(xi + 2) % 4];
+  uint16_t* sc = c.b.act[(xi + 3) % 4];
+  const uint16_t* residual = x;
+  if (L.has_shortcut) {
+    if (!(st = conv16(c, L.shortcut, x, batch, h, w, sc)).good()) return st;
+    residual = sc;
+  }
+  if (!(st = gn(c, L.n1, x, t, batch, pixels, true)).good()) return st;
+  if (!(st = conv16(c, L.c1, t, batch, h, w, hbuf)).good()) return st;
+  if (!(st = gn(c, L.n2, hbuf, t, batch, pixels, true)).good()) return st;
+  return conv16(c, L.c2, t, batch, h, w, x, residual);
+}
+
+// Mid-block attention on buffer xi (in place).
+Status attention(const Ctx& c, const AttentionLayer& L, int xi, int batch, int h, int w) {
+  Status st = check_cancel(c.cancel);
+  if (!st.good()) return st;
+  const int ch = L.norm.c;
+  const int n = h * w;
+  uint16_t* x = c.b.act[xi];
+  uint16_t* t = c.b.act[(xi + 1) % 4];
+  uint16_t* qkv = c.b.act[(xi + 2) % 4];
+  uint16_t* o = c.b.act[(xi + 3) % 4];
+  if (!(st = gn(c, L.norm, x, t, batch, n, false)).good()) return st;
+  // q|k|v for all images in one GEMM: [B*N, C] x [3C, C]^T.
+  if (!(st = conv16(c, L.qkv, t, 1, 1, batch * n, qkv)).good()) return st;
+  uint16_t* vt = t;  // the normalized input is dead after the projection
+  st = attention_core(c.dtype, qkv, qkv + ch, qkv + 2 * ch, 3 * ch, o, ch, batch, n, ch,
+                      c.b.scores, c.b.probs, c.b.rowsum, vt, c.s);
+  if (!st.good()) return st;
+  // Output projection + residual, in place.
+  return conv16(c, L.out, o, 1, 1, batch * n, x, x);
+}
+
+Status mid_block(const Ctx& c, const MidLayer& L, int xi, int batch, int h, int w) {
+  Status st = resnet(c, L.first, xi, batch, h, w);
+  if (st.good()) st = attention(c, L.attn, xi, batch, h, w);
+  if (st.good()) st = resnet(c, L.second, xi, batch, h, w);
+  return st;
+}
+
+bool attention_tc_ok(int tokens, int dim) {
+  return tokens % 128 == 0 && dim % 128 == 0 && dim <= 512 && tokens <= 16384;
+}
+
+}  // namespace
+
+Status attention_core(int dtype, const void* q, const void* k, const void* v, long long ld,
+                      void* out, long long ld_out, int batch, int tokens, int dim, float* scores,
+                      void* probs, float* rowsum, void* vt, cudaStream_t s) {
+  const uint16_t* qb = static_cast<const uint16_t*>(q);
+  const uint16_t* kb = static_cast<const uint16_t*>(k);
+  const uint16_t* vb = static_cast<const uint16_t*>(v);
+  uint16_t* ob = static_cast<uint16_t*>(out);
+  if (!attention_tc_ok(tokens, dim)) {
+    for (int bi = 0; bi < batch; ++bi) {
+      const long long off = (long long)bi * tokens;
+      OpScope scope("attn_cuda_core", 4.0 * tokens * tokens * dim, 8.0 * tokens * dim, s, 1);
+      cudaError_t e = attention_rows_launch(dtype, qb + off * ld, kb + off * ld, vb + off * ld, ld,
+                                            ob + off * ld_out, ld_out, tokens, dim, s);
+      if (e != cudaSuccess) return cuda_status(e, "attention");
+    }
+    return Status::ok();
+  }
+  for (int bi = 0; bi < batch; ++bi) {
+    const long long off = (long long)bi * tokens;
+    // scores = q k^T (fp32)
+    ConvTcArgs a;
+    a.dtype = dtype;
+    a.x = qb + off * ld;
+    a.batch = 1;
+    a.in_h = 1;
+    a.in_w = tokens;
+    a.cin = dim;
+    a.pixel_stride = ld;
+    a.ksize = 1;
+    a.stride = 1;
+    a.pad = 0;
+    a.out_h = 1;
+    a.out_w = tokens;
+    a.cout = tokens;
+    a.w = kb + off * ld;
+    a.ldw = ld;
+    a.out = scores;
+    a.ld_out = tokens;
+    a.out_f32 = 1;
+    if (const char* why = conv_tc_check(a)) return Status::err(OSOR_ERR_INVALID_INPUT, why);
+    const double nn = (double)tokens * tokens;
+    cudaError_t e;
+    {
+      OpScope scope("attn_scores", 2.0 * nn * dim, 4.0 * tokens * dim + 4.0 * nn, s, 1);
+      e = conv_tc_launch(a, s);
+    }
+    if (e != cudaSuccess) return cuda_status(e, "attention scores");
+    {
+      OpScope scope("attn_softmax", 0.0, 6.0 * nn, s, 1);
+      e = softmax_rows_launch(dtype, scores, probs, rowsum, tokens, tokens, tokens, tokens, s);
+    }
+    if (e != cudaSuccess) return cuda_status(e, "attention softmax");
+    {
+      OpScope scope("attn_transpose", 0.0, 4.0 * tokens * dim, s, 1);
+      e = transpose16_launch(vb + off * ld, ld, vt, tokens, tokens, dim, s);
+    }
+    if (e != cudaSuccess) return cuda_status(e, "attention transpose");
+    // out = (P / rowsum) V, with V^T [dim][tokens] as the K-major B operand.
+    ConvTcArgs pv;
+    pv.dtype = dtype;
+    pv.x = probs;
+    pv.batch = 1;
+    pv.in_h = 1;
+    pv.in_w = tokens;
+    pv.cin = tokens;
+    pv.pixel_stride = tokens;
+    pv.ksize = 1;
+    pv.stride = 1;
+    pv.pad = 0;
+    pv.out_h = 1;
+    pv.out_w = tokens;
+    pv.cout = dim;
+    pv.w = vt;
+    pv.ldw = tokens;
+    pv.out = ob + off * ld_out;
+    pv.ld_out = ld_out;
+    pv.row_scale = rowsum;
+    if (const char* why = conv_tc_check(pv)) return Status::err(OSOR_ERR_INVALID_INPUT, why);
+    {
+      OpScope scope("attn_values", 2.0 * nn * dim, 2.0 * nn + 4.0 * tokens * dim, s, 1);
+      e = conv_tc_launch(pv, s);
+    }
+    if (e != cudaSuccess) return cuda_status(e, "attention values");
+  }
+  return Status::ok();
+}
+
+Status run_conv(int dtype, const ConvLayer& L, const void* x, int in_mode, int batch, int in_h,
+                int in_w, long long in_pixel_stride, void* out, int out_mode,
+                long long out_pixel_stride, const void* residual, long long ld_res,
+                cudaStream_t s) {
+  const int ph = in_h + L.pad + L.pad_end, pw = in_w + L.pad + L.pad_end;
+  if (ph < L.k || pw < L.k)
+    return Status::err(OSOR_ERR_INVALID_INPUT, "convolution input is smaller than its kernel");
+  const int out_h = (ph - L.k) / L.stride + 1;
+  const int out_w = (pw - L.k) / L.stride + 1;
+  // Algorithmic work: 2 * pixels * Cout * k^2 * Cin FLOPs; bytes = input +
+  // weights + output (+ residual) at their storage widths.
+  const double out_px = (double)batch * out_h * out_w;
+  const double flops = 2.0 * out_px * L.cout * L.k * L.k * L.cin;
+  const double in_bytes = (double)batch * in_h * in_w * L.cin * (in_mode == kLayoutNchwF32 ? 4 : 2);
+  const double out_bytes = out_px * L.cout * (out_mode == kLayoutNchwF32 ? 4 : 2);
+  const double bytes = in_bytes + out_bytes + (residual ? out_px * L.cout * 2 : 0.0) +
+                       2.0 * L.cout * L.k * L.k * L.cin;
+  if (in_mode == kLayoutNhwc16 && out_mode == kLayoutNhwc16) {
+    ConvTcArgs a;
+    a.dtype = dtype;
+    a.x = x;
+    a.batch = batch;
+    a.in_h = in_h;
+    a.in_w = in_w;
+    a.cin = L.cin;
+    a.pixel_stride = in_pixel_stride;
+    a.ksize = L.k;
+    a.stride = L.stride;
+    a.pad = L.pad;
+    a.out_h = out_h;
+    a.out_w = out_w;
+    a.cout = L.cout;
+    a.w = L.w;
+    a.ldw = (long long)L.k * L.k * L.cin;
+    a.bias = L.bias;
+    a.residual = residual;
+    a.ld_res = ld_res;
+    a.out = out;
+    a.ld_out = out_pixel_stride;
+    // Reads past the input edge return the TMA zero fill, which supplies
+    // both the leading pad and the trailing (pad_end) pad.
+    if (conv_tc_check(a) == nullptr) {
+      OpScope scope(L.k == 3 ? "conv3x3_tc" : "conv1x1_tc", flops, bytes, s, 1);
+      return cuda_status(conv_tc_launch(a, s), "tensor-core conv");
+    }
+  }
+  DirectConvArgs d;
+  d.batch = batch;
+  d.in_h = in_h;
+  d.in_w = in_w;
+  d.cin = L.cin;
+  d.in_pixel_stride = in_pixel_stride;
+  d.ksize = L.k;
+  d.stride = L.stride;
+  d.pad = L.pad;
+  d.out_h = out_h;
+  d.out_w = out_w;
+  d.cout = L.cout;
+  d.out_pixel_stride = out_pixel_stride;
+  d.ld_res = ld_res;
+  OpScope scope("conv_direct", flops, bytes, s, 1);
+  return cuda_status(
+      direct_conv_launch(dtype, x, in_mode, L.w, L.bias, residual, out, out_mode, d, s),
+      "direct convolution");
+}
+
+Vae::~Vae() {
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  for (void* p : allocations) cudaFree(p);
+  cudaSetDevice(prev);
+}
+
+Status vae_create(const osor_tensor* tensors, size_t count, const osor_vae_config* cfg, int device,
+                  Vae** out) {
+  Vae* m = new Vae();
+  m->device = device;
+  int parts = OSOR_PART_DECODER | OSOR_PART_ENCODER;
+  if (cfg) {
+    for (int i = 0; i < 4; ++i) m->channels[i] = cfg->channels[i];
+    m->layers = cfg->layers;
+    parts = cfg->parts;
+    m->dtype = cfg->dtype == OSOR_DTYPE_F16 ? kF16 : kBf16;
+    if (cfg->dtype != OSOR_DTYPE_F16 && cfg->dtype != OSOR_DTYPE_BF16) {
+      delete m;
+      return Status::err(OSOR_ERR_INVALID_INPUT, "dtype must be OSOR_DTYPE_BF16 or OSOR_DTYPE_F16");
+    }
+  }
+  for (int i = 0; i < 4; ++i)
+    if (m->channels[i] <= 0 || m->channels[i] % kGroups != 0) {
+      delete m;
+      return Status::err(OSOR_ERR_INVALID_INPUT, "VAE channels must be positive multiples of 32");
+    }
+  if (m->layers < 1) {
+    delete m;
+    return Status::err(OSOR_ERR_INVALID_INPUT, "VAE layers must be positive");
+  }
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) {
+    delete m;
+    return cuda_status(e, "set device");
+  }
+  Loader ld(tensors, count, m);
+  Status s;
+  const int* ch = m->channels;
+  if (parts & OSOR_PART_DECODER) {
+    m->has_decoder = true;
+    Decoder& d = m->dec;
+    const int last = ch[3];
+    s = ld.conv("post_quant_conv", 4, 4, 1, 1, 0, &d.post_quant);
+    if (s.good()) s = ld.conv("decoder.conv_in", 4, last, 3, 1, 1, &d.conv_in);
+    if (s.good()) s = ld.mid("decoder.mid_block", last, &d.mid);
+    const int rev[4] = {ch[3], ch[2], ch[1], ch[0]};
+    for (int i = 0; s.good() && i < 4; ++i) {
+      StageLayer st;
+      const int in = i == 0 ? last : rev[i - 1];
+      for (int j = 0; s.good() && j <= m->layers; ++j) {
+        ResnetLayer r;
+        s = ld.resnet("decoder.up_blocks." + std::to_string(i) + ".resnets." + std::to_string(j),
+                      j == 0 ? in : rev[i], rev[i], &r);
+        st.resnets.push_back(r);
+      }
+      st.resample = i + 1 < 4;
+      if (s.good() && st.resample)
+        s = ld.conv("decoder.up_blocks." + std::to_string(i) + ".upsamplers.0.conv", rev[i],
+                    rev[i], 3, 1, 1, &st.resample_conv);
+      d.up.push_back(st);
+    }
+    if (s.good()) s = ld.norm("decoder.conv_norm_out", ch[0], &d.norm_out);
+    if (s.good()) s = ld.conv("decoder.conv_out", ch[0], 3, 3, 1, 1, &d.conv_out);
+  }
+  if (s.good() && (parts & OSOR_PART_ENCODER)) {
+    m->has_encoder = true;
+    Encoder& en = m->enc;
+    s = ld.conv("encoder.conv_in", 3, ch[0], 3, 1, 1, &en.conv_in);
+    for (int i = 0; s.good() && i < 4; ++i) {
+      StageLayer st;
+      const int in = i == 0 ? ch[0] : ch[i - 1];
+      for (int j = 0; s.good() && j < m->layers; ++j) {
+        ResnetLayer r;
+        s = ld.resnet("encoder.down_blocks." + std::to_string(i) + ".resnets." + std::to_string(j),
+                      j == 0 ? in : ch[i], ch[i], &r);
+        st.resnets.push_back(r);
+      }
+      st.resample = i + 1 < 4;
+      if (s.good() && st.resample) {
+        s = ld.conv("encoder.down_blocks." + std::to_string(i) + ".downsamplers.0.conv", ch[i],
+                    ch[i], 3, 2, 0, &st.resample_conv);
+        // DownBlock pads one zero column / row on the right / bottom, then
+        // convolves with stride 2 and no padding (vae_encoder.rs:206-210).
+        st.resample_conv.pad_end = 1;
+      }
+      en.down.push_back(st);
+    }
+    if (s.good()) s = ld.mid("encoder.mid_block", ch[3], &en.mid);
+    if (s.good()) s = ld.norm("encoder.conv_norm_out", ch[3], &en.norm_out);
+    if (s.good()) s = ld.conv("encoder.conv_out", ch[3], 8, 3, 1, 1, &en.conv_out);
+    if (s.good()) s = ld.conv("quant_conv", 8, 8, 1, 1, 0, &en.quant);
+  }
+  cudaSetDevice(prev);
+  if (!s.good()) {
+    delete m;
+    return s;
+  }
+  *out = m;
+  return Status::ok();
+}
+
+WorkspacePlan vae_workspace_plan(const Vae& m, int op, int batch, int height, int width) {
+  WorkspacePlan p;
+  const int* ch = m.channels;
+  // Largest activation over the graph: (pixels x channels) of every tensor a
+  // block produces, including the upsampled input of each upsampler conv and
+  // the q|k|v projection at the latent resolution.
+  long long full, latent;
+  if (op == OSOR_OP_DECODE) {
+    full = 64LL * height * width;
+    latent = (long long)height * width;
+  } else {
+    full = (long long)height * width;
+    latent = full / 64;
+  }
+  long long elems = latent * 3 * ch[3];
+  if (op == OSOR_OP_DECODE) {
+    const int rev[4] = {ch[3], ch[2], ch[1], ch[0]};
+    long long px = latent;
+    for (int i = 0; i < 4; ++i) {
+      const int in = i == 0 ? ch[3] : rev[i - 1];
+      elems = std::max(elems, px * std::max(in, rev[i]));
+      if (i + 1 < 4) {
+        px *= 4;
+        elems = std::max(elems, px * rev[i]);
+      }
+    }
+  } else {
+    long long px = full;
+    for (int i = 0; i < 4; ++i) {
+      const int in = i == 0 ? ch[0] : ch[i - 1];
+      elems = std::max(elems, px * std::max(in, ch[i]));
+      if (i + 1 < 4) px /= 4;
+    }
+  }
+  p.act_bytes = align256((size_t)batch * elems * 2);
+  p.f32_bytes = align256((size_t)batch * 8 * std::max(latent, 1LL) * 4);
+  const int tokens = (int)latent;
+  if (attention_tc_ok(tokens, ch[3])) {
+    p.scores_bytes = align256((size_t)tokens * tokens * 4);
+    p.probs_bytes = align256((size_t)tokens * tokens * 2);
+    p.rowsum_bytes = align256((size_t)tokens * 4);
+  }
+  // Group-norm scratch: the largest plan over the channel counts and
+  // resolutions used.
+  size_t g = 0;
+  for (int i = 0; i < 4; ++i)
+    for (long long px : {full, full / 4, full / 16, full / 64})
+      if (px > 0) g = std::max(g, gn_nhwc_plan(batch, ch[i], px, kGroups).workspace_bytes);
+  p.gn_bytes = align256(g);
+  p.total = 4 * p.act_bytes + p.f32_bytes + p.scores_bytes + p.probs_bytes + p.rowsum_bytes +
+            p.gn_bytes;
+  return p;
+}
+
+Status vae_decode(const Vae& m, const float* latents, float* image, int batch, int h, int w,
+                  void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                  const volatile int* cancel) {
+  if (!m.has_decoder) return Status::err(OSOR_ERR_UNAVAILABLE, "model has no decoder");
+  const WorkspacePlan plan = vae_workspace_plan(m, OSOR_OP_DECODE, batch, h, w);
+  if (workspace_bytes < plan.total)
+    return Status::err(OSOR_ERR_INVALID_INPUT, "decode workspace is too small");
+  const Buffers b = carve(plan, workspace);
+  const Ctx c{m.dtype, b, stream, cancel};
+  const Decoder& d = m.dec;
+  Status st = check_cancel(cancel);
+  if (!st.good()) return st;
+  // post_quant_conv (NCHW f32 -> NCHW f32), conv_in (NCHW f32 -> NHWC 16-bit).
+  st = run_conv(c.dtype, d.post_quant, latents, kLayoutNchwF32, batch, h, w, 0, b.f32,
+                kLayoutNchwF32, 0, nullptr, 0, stream);
+  if (!st.good()) return st;
+  int xi = 0;
+  st = run_conv(c.dtype, d.conv_in, b.f32, kLayoutNchwF32, batch, h, w, 0, b.act[xi],
+                kLayoutNhwc16, d.conv_in.cout, nullptr, 0, stream);
+  if (!st.good()) return st;
+  if (!(st = mid_block(c, d.mid, xi, batch, h, w)).good()) return st;
+  int ch_now = d.conv_in.cout;
+  for (const StageLayer& up : d.up) {
+    for (const ResnetLayer& r : up.resnets) {
+      if (!(st = resnet(c, r, xi, batch, h, w)).good()) return st;
+      ch_now = r.c2.cout;
+    }
+    if (!(st = check_cancel(cancel)).good()) return st;
+    if (up.resample) {
+      const int ui = (xi + 1) % 4;
+      cudaError_t e;
+      {
+        OpScope scope("upsample", 0.0, 10.0 * batch * h * w * ch_now, stream, 1);
+        e = upsample2x_nhwc_launch(b.act[xi], b.act[ui], batch, h, w, ch_now, stream);
+      }
+      if (e != cudaSuccess) return cuda_status(e, "upsample");
+      h *= 2;
+      w *= 2;
+      if (!(st = conv16(c, up.resample_conv, b.act[ui], batch, h, w, b.act[xi])).good()) return st;
+    }
+  }
+  const int ti = (xi + 1) % 4;
+  if (!(st = gn(c, d.norm_out, b.act[xi], b.act[ti], batch, (long long)h * w, true)).good())
+    return st;
+  return run_conv(c.dtype, d.conv_out, b.act[ti], kLayoutNhwc16, batch, h, w, ch_now, image,
+                  kLayoutNchwF32, 0, nullptr, 0, stream);
+}
+
+Status vae_encode(const Vae& m, const float* image, float* moments, int batch, int height,
+                  int width, void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                  const volatile int* cancel) {
+  if (!m.has_encoder) return Status::err(OSOR_ERR_UNAVAILABLE, "model has no encoder");
+  const WorkspacePlan plan = vae_workspace_plan(m, OSOR_OP_ENCODE, batch, height, width);
+  if (workspace_bytes < plan.total)
+    return Status::err(OSOR_ERR_INVALID_INPUT, "encode workspace is too small");
+  const Buffers b = carve(plan, workspace);
+  const Ctx c{m.dtype, b, stream, cancel};
+  const Encoder& en = m.enc;
+  Status st = check_cancel(cancel);
+  if (!st.good()) return st;
+  int xi = 0;
+  int h = height, w = width;
+  st = run_conv(c.dtype, en.conv_in, image, kLayoutNchwF32, batch, h, w, 0, b.act[xi],
+                kLayoutNhwc16, en.conv_in.cout, nullptr, 0, stream);
+  if (!st.good()) return st;
+  int ch_now = en.conv_in.cout;
+  for (const StageLayer& down : en.down) {
+    for (const ResnetLayer& r : down.resnets) {
+      if (!(st = resnet(c, r, xi, batch, h, w)).good()) return st;
+      ch_now = r.c2.cout;
+    }
+    if (!(st = check_cancel(cancel)).good()) return st;
+    if (down.resample) {
+      const int di = (xi + 1) % 4;
+      if (!(st = conv16(c, down.resample_conv, b.act[xi], batch, h, w, b.act[di])).good())
+        return st;
+      h /= 2;
+      w /= 2;
+      xi = di;
+    }
+  }
+  if (!(st = mid_block(c, en.mid, xi, batch, h, w)).good()) return st;
+  const int ti = (xi + 1) % 4;
+  if (!(st = gn(c, en.norm_out, b.act[xi], b.act[ti], batch, (long long)h * w, true)).good())
+    return st;
+  st = run_conv(c.dtype, en.conv_out, b.act[ti], kLayoutNhwc16, batch, h, w, ch_now, b.f32,
+                kLayoutNchwF32, 0, nullptr, 0, stream);
+  if (!st.good()) return st;
+  return run_conv(c.dtype, en.quant, b.f32, kLayoutNchwF32, batch, h, w, 0, moments,
+                  kLayoutNchwF32, 0, nullptr, 0, stream);
+}
+
+}  // namespace osor

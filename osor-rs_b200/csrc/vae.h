@@ -1,0 +1,127 @@
+// VAE model runtime: weights repacked once to 16-bit tensor-core layouts, and
+// the encoder / decoder graph executed as a sequence of kernel launches on one
+// stream over a caller-provided workspace.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/osor_b200.h"
+
+namespace osor {
+
+struct Status {
+  int code = OSOR_OK;
+  std::string message;
+  static Status ok() { return Status(); }
+  static Status err(int c, std::string m) {
+    Status s;
+    s.code = c;
+    s.message = std::move(m);
+    return s;
+  }
+  bool good() const { return code == OSOR_OK; }
+};
+
+struct ConvLayer {
+  int cin = 0, cout = 0, k = 1, stride = 1, pad = 0;
+  int pad_end = 0;           // zero padding after the last row / column (encoder downsample: 1)
+  const uint16_t* w = nullptr;  // 16-bit [cout][k*k*cin], (ky, kx, ci)
+  const float* bias = nullptr;  // [cout]
+};
+
+struct NormLayer {
+  int c = 0;
+  float* gamma = nullptr;
+  float* beta = nullptr;
+};
+
+struct ResnetLayer {
+  NormLayer n1, n2;
+  ConvLayer c1, c2;
+  bool has_shortcut = false;
+  ConvLayer shortcut;
+};
+
+struct AttentionLayer {
+  NormLayer norm;
+  ConvLayer qkv;  // 1x1, c -> 3c; q and k rows pre-scaled by c^-1/4
+  ConvLayer out;  // 1x1, c -> c
+};
+
+struct MidLayer {
+  ResnetLayer first, second;
+  AttentionLayer attn;
+};
+
+struct StageLayer {
+  std::vector<ResnetLayer> resnets;
+  bool resample = false;  // upsample (decoder) / downsample (encoder)
+  ConvLayer resample_conv;
+};
+
+struct Decoder {
+  ConvLayer post_quant, conv_in;
+  MidLayer mid;
+  std::vector<StageLayer> up;
+  NormLayer norm_out;
+  ConvLayer conv_out;
+};
+
+struct Encoder {
+  ConvLayer conv_in;
+  std::vector<StageLayer> down;
+  MidLayer mid;
+  NormLayer norm_out;
+  ConvLayer conv_out, quant;
+};
+
+// Per-call workspace layout (all parts 256-byte aligned).
+struct WorkspacePlan {
+  size_t act_bytes = 0;      // one activation buffer
+  size_t f32_bytes = 0;      // thin f32 NCHW scratch
+  size_t scores_bytes = 0;   // attention scores (fp32) for one image
+  size_t probs_bytes = 0;    // attention probabilities (16-bit) for one image
+  size_t rowsum_bytes = 0;
+  size_t gn_bytes = 0;
+  size_t total = 0;
+};
+
+struct Vae {
+  int device = 0;
+  int dtype = 0;  // Dtype of weights and activations
+  int channels[4] = {128, 256, 512, 512};
+  int layers = 2;
+  bool has_decoder = false, has_encoder = false;
+  Decoder dec;
+  Encoder enc;
+  std::vector<void*> allocations;
+  ~Vae();
+};
+
+Status vae_create(const osor_tensor* tensors, size_t count, const osor_vae_config* cfg, int device,
+                  Vae** out);
+WorkspacePlan vae_workspace_plan(const Vae& m, int op, int batch, int height, int width);
+Status vae_decode(const Vae& m, const float* latents, float* image, int batch, int h, int w,
+                  void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                  const volatile int* cancel);
+Status vae_encode(const Vae& m, const float* image, float* moments, int batch, int height,
+                  int width, void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                  const volatile int* cancel);
+
+// Single-op entry points shared with the C ABI. in_mode / out_mode are
+// kLayoutNhwc16 (16-bit of `dtype`) or kLayoutNchwF32.
+Status run_conv(int dtype, const ConvLayer& L, const void* x, int in_mode, int batch, int in_h,
+                int in_w, long long in_pixel_stride, void* out, int out_mode,
+                long long out_pixel_stride, const void* residual, long long ld_res,
+                cudaStream_t s);
+
+// softmax(q k^T) v for `batch` images of [tokens][dim] rows (stride ld);
+// scores/probs/rowsum/vt are per-image scratch reused across images.
+Status attention_core(int dtype, const void* q, const void* k, const void* v, long long ld,
+                      void* out, long long ld_out, int batch, int tokens, int dim, float* scores,
+                      void* probs, float* rowsum, void* vt, cudaStream_t s);
+
+}  // namespace osor

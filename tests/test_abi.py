@@ -1,0 +1,70 @@
+"""The C-ABI library loads, exports every function include/osor_b200.h
+declares, and validates arguments on the host (no device work here)."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from osor_b200 import _lib
+from osor_b200 import ops
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "osor_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(osor_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_entry_points():
+    names = declared_functions()
+    assert "osor_vae_decode" in names and "osor_conv2d" in names
+    assert set(names) == set(_lib.SIGNATURES), set(names) ^ set(_lib.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_version_and_no_error_initially():
+    lb = _lib.lib()
+    assert lb.osor_version() >= 100
+    assert _lib.last_error() == ""
+
+
+def test_pack_conv_weight_layout():
+    rng = np.random.default_rng(0)
+    w = rng.standard_normal((5, 6, 3, 3)).astype(np.float32)
+    import torch
+    for dt in (torch.bfloat16, torch.float16):
+        packed = ops.pack_conv_weight(w, dt)
+        want = torch.from_numpy(w).permute(0, 2, 3, 1).reshape(5, 54).to(dt)
+        np.testing.assert_array_equal(packed, want.view(torch.int16).numpy().view(np.uint16))
+
+
+def test_invalid_arguments_fail_before_device_work():
+    lb = _lib.lib()
+    rc = lb.osor_conv2d(None, None, None, None, None, 1, 8, 8, 4, 4, 3, 1, 1, 1, 0, 0, 0, None)
+    assert rc == _lib.OSOR_ERR_INVALID_INPUT
+    assert "null" in _lib.last_error()
+    with pytest.raises(_lib.InvalidInput):
+        _lib.check(lb.osor_pack_conv_weight(None, None, 0, 1, 3, 0))
+    f32, nchw, nhwc = _lib.DTYPE_F32, _lib.LAYOUT_NCHW, _lib.LAYOUT_NHWC
+    assert lb.osor_group_norm_workspace_size(1, 48, 4, 4, nchw, f32) == 0
+    assert lb.osor_group_norm_workspace_size(1, 64, 4, 4, nchw, f32) > 0
+    assert lb.osor_group_norm_workspace_size(1, 64, 4, 4, nhwc, f32) == 0
+    assert lb.osor_group_norm_workspace_size(1, 64, 4, 4, nhwc, _lib.DTYPE_F16) > 0
+    assert lb.osor_vae_workspace_size(None, _lib.OP_DECODE, 1, 64, 64) == 0
+
+
+def test_device_check_reports_unavailable_without_gpu():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is visible")
+    assert _lib.lib().osor_device_check(0) == _lib.OSOR_ERR_UNAVAILABLE

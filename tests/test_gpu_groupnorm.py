@@ -1,0 +1,130 @@
+"""GroupNorm(32)+SiLU parity on the GPU.
+
+Restates the reference's formula-defined GroupNorm tests
+(src/native/vae_encoder.rs:573-811) against the CUDA kernels in float32 NCHW
+(2e-5 absolute, as the reference asserts), then checks the bf16 NCHW
+standalone kernel and the NHWC pipeline kernels against the oracle: group
+mean / variance within 1e-4 relative, outputs within bf16 output rounding.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from osor_b200 import ops
+from osor_b200._lib import InvalidInput, LAYOUT_NHWC
+
+pytestmark = pytest.mark.gpu
+EPS = 1e-6
+
+
+def f64_reference(x, scale, bias, silu):
+    """Independent f64 restatement used by the reference test (vae_encoder.rs:640-671)."""
+    b, c = x.shape[:2]
+    g = x.astype(np.float64).reshape(b, 32, -1)
+    mean = g.mean(axis=2, keepdims=True)
+    var = ((g - mean) ** 2).mean(axis=2, keepdims=True)
+    y = ((g - mean) / np.sqrt(var + EPS)).reshape(x.shape)
+    y = y * scale.reshape(1, c, 1, 1) + bias.reshape(1, c, 1, 1)
+    return y / (1.0 + np.exp(-y)) if silu else y
+
+
+def gpu_gn(x, scale, bias, silu, layout=ops._lib.LAYOUT_NCHW, stats=None):
+    norm = ops.StableGroupNorm(scale, bias)
+    xt = x if torch.is_tensor(x) else torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    y = norm.forward_silu(xt, layout=layout, stats=stats) if silu else norm.forward(
+        xt, layout=layout, stats=stats)
+    torch.cuda.synchronize()
+    return y
+
+
+REF_SHAPES = [
+    (1, 32, 1, 1, False, False),
+    (2, 64, 3, 7, True, False),
+    (2, 32, 1, 257, False, False),
+    (2, 32, 1, 4097, False, False),
+    (1, 32, 128, 256, False, True),
+]
+
+
+@pytest.mark.parametrize("case", REF_SHAPES)
+@pytest.mark.parametrize("silu", [False, True])
+def test_f32_matches_f64_reference(case, silu, cuda_device):
+    batch, channels, height, width, transposed, large_offset = case
+    n = (batch + 1) * channels * height * width
+    i = np.arange(n)
+    if large_offset:
+        values = np.where(i % 2 == 0, np.float32(9.99), np.float32(10.01)).astype(np.float32)
+    else:
+        values = (((i * 37) % 101).astype(np.float32) - 50.0) * np.float32(0.03125)
+    if transposed:
+        src = values.reshape(batch + 1, channels, width, height)[1:].transpose(0, 1, 3, 2)
+    else:
+        src = values.reshape(batch + 1, channels, height, width)[1:]
+    x = np.ascontiguousarray(src)
+    scale = (0.5 + (np.arange(channels) % 5) * 0.125).astype(np.float32)
+    bias = ((np.arange(channels) % 7) * 0.0625 - 0.125).astype(np.float32)
+    got = gpu_gn(x, scale, bias, silu).cpu().numpy()
+    want = f64_reference(x, scale.astype(np.float64), bias.astype(np.float64), silu)
+    assert np.all(np.isfinite(got))
+    assert np.abs(got - want).max() <= 2e-5
+
+
+def test_wide_magnitude(cuda_device):
+    i = np.arange(2 * 32 * 4096)
+    values = np.choose(i % 4, [1e10, -1e10, 1e-10, -1e-10]).astype(np.float32)
+    x = values.reshape(2, 32, 1, 4096)
+    got = gpu_gn(x, np.ones(32, np.float32), np.zeros(32, np.float32), False).cpu().numpy()
+    denom = np.sqrt(0.5 * (1e20 + 1e-20) + EPS)
+    assert np.all(np.isfinite(got))
+    assert np.abs(got.astype(np.float64) - x.astype(np.float64) / denom).max() <= 2e-5
+
+
+def test_long_balanced_groups_closed_form(cuda_device):
+    low, high = np.float32(10.0 - 0.01), np.float32(10.0 + 0.01)
+    x = np.where(np.arange(32 * 128 * 256) % 2 == 0, low, high).astype(np.float32)
+    x = x.reshape(1, 32, 128, 256)
+    mean = (float(low) + float(high)) / 2
+    half = (float(high) - float(low)) / 2
+    denom = np.sqrt(half * half + 1e-6)
+    got = gpu_gn(x, np.ones(32, np.float32), np.zeros(32, np.float32), False).cpu().numpy()
+    want = np.where(np.arange(x.size) % 2 == 0, (float(low) - mean) / denom,
+                    (float(high) - mean) / denom).reshape(x.shape)
+    assert np.abs(got - want).max() <= 2e-5
+
+
+def test_constant_groups_return_bias(cuda_device):
+    x = np.full((1, 32, 2, 2), 7.0, np.float32)
+    got = gpu_gn(x, np.ones(32, np.float32), np.full(32, 1.25, np.float32), False).cpu().numpy()
+    assert np.all(got == 1.25)
+    norm = ops.StableGroupNorm(np.ones(32, np.float32), np.zeros(32, np.float32))
+    with pytest.raises(InvalidInput):
+        norm.forward(torch.zeros((1, 64, 2, 2), device="cuda"))
+
+
+# Standalone-op workload of the benchmark config (seed 3: x ~ N(0.5, 2),
+# gamma ~ N(1, 0.1), beta ~ N(0, 0.1)) at sizes the oracle finishes quickly.
+HALF_SHAPES = [(2, 512, 32, 32), (1, 256, 64, 64), (1, 128, 128, 128), (2, 64, 15, 17)]
+
+
+@pytest.mark.parametrize("shape", HALF_SHAPES)
+@pytest.mark.parametrize("layout", ["nchw", "nhwc"])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+def test_half_matches_oracle(shape, layout, dt, cuda_device):
+    from osor_b200 import workloads
+    x, gamma, beta = workloads.groupnorm_inputs(shape)
+    xt = torch.from_numpy(x).to(dt)
+    x = xt.float().numpy()
+    ref, mean, var = oracle.group_norm(x, gamma, beta, silu=True, return_stats=True)
+    stats = torch.zeros((shape[0] * 32, 2), dtype=torch.float32, device="cuda")
+    if layout == "nhwc":
+        xt = xt.permute(0, 2, 3, 1).contiguous()
+        y = gpu_gn(xt.cuda(), gamma, beta, True, layout=LAYOUT_NHWC, stats=stats)
+        y = y.permute(0, 3, 1, 2).float().cpu().numpy()
+    else:
+        y = gpu_gn(xt.cuda(), gamma, beta, True, stats=stats).float().cpu().numpy()
+    s = stats.cpu().numpy().reshape(shape[0], 32, 2)
+    np.testing.assert_allclose(s[..., 0], mean, rtol=1e-4, atol=1e-4 * np.abs(mean).max())
+    np.testing.assert_allclose(s[..., 1], var, rtol=1e-4)
+    err = np.abs(y - ref)
+    assert np.all(err <= 2 ** -8 * np.abs(ref) + 1e-3), err.max()
