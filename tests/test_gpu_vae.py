@@ -99,10 +99,12 @@ def test_full_size_decoder_properties(model):
     assert a.shape == (4, 3, 1024, 1024)
     assert np.all(np.isfinite(a))
     np.testing.assert_array_equal(a, b)  # deterministic
+    # A single image and the same image inside the batch differ only in the
+    # GroupNorm partial-sum order, which 16-bit rounding can amplify.
     for i in (0, 3):
         single = model.decode(x[i:i + 1].contiguous()).cpu().numpy()
-        assert workloads.psnr(single[0], a[i]) >= 50.0
-        assert np.abs(single[0] - a[i]).max() <= 2e-2
+        assert workloads.psnr(single[0], a[i]) >= (50.0 if model.dtype == "f16" else 40.0)
+        assert np.abs(single[0] - a[i]).max() <= MAX_ABS[model.dtype]
 
 
 def test_cancellation_stops_before_work(model):

@@ -1,0 +1,242 @@
+"""Pins the CPU oracle against the reference's own formula-defined tests and
+against independent float64 PyTorch CPU computations (no GPU needed).
+
+The reference's unit tests build their inputs from closed-form index formulas,
+so they can be restated exactly:
+  conv.rs:297-383      banded conv == one band bit for bit; exact vs f64 (dyadic inputs)
+  columns.rs:448-479   column conv vs direct conv, random inputs, <= 1e-5
+  conv.rs:218-271      bias add against explicit arrays
+  vae_encoder.rs:573-811  GroupNorm vs f64: views, group sizes, wide magnitude,
+                          closed form for long balanced groups, constant groups
+  vae_decoder.rs:125-152  nearest upsample against explicit arrays
+  attention.rs:114-147 query slicing changes attention by <= 2e-6; a budget below
+                       one score row is rejected (:185-195)
+  vae_decoder.rs:167-218  decoder vs an independent implementation at F64
+"""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+import oracle
+from oracle import vae as ovae
+from osor_b200.weights import random_vae_weights
+
+EPS = 1e-6
+
+
+def dyadic(n, mult, mod, shift, scale):
+    i = np.arange(n, dtype=np.int64)
+    return (((i * mult) % mod).astype(np.float32) - shift) * np.float32(scale)
+
+
+@pytest.mark.parametrize("case", [(37, 20, 3, 1, 1, 4), (37, 20, 3, 1, 1, 1), (33, 17, 3, 2, 0, 3),
+                                  (19, 11, 1, 1, 0, 5)])
+def test_banded_convolution_is_band_independent_and_exact(case):
+    h, w, k, s, p, rows = case
+    out_w = (w + 2 * p - k) // s + 1
+    limit = 2 * out_w * 6 * k * k * rows
+    wt = dyadic(5 * 6 * k * k, 7, 11, 5, 1 / 32).reshape(5, 6, k, k)
+    bias = np.array([-0.125, 0.0625, 0.0, 0.125, -0.0625], np.float32)
+    x = dyadic(2 * 6 * h * w, 13, 41, 20, 1 / 16).reshape(2, 6, h, w)
+    banded = oracle.conv2d(x, wt, bias, stride=s, padding=p, max_scratch_elements=limit)
+    one = oracle.conv2d(x, wt, bias, stride=s, padding=p, max_scratch_elements=1 << 40)
+    np.testing.assert_array_equal(banded, one)
+    direct = F.conv2d(torch.from_numpy(x).double(), torch.from_numpy(wt).double(),
+                      torch.from_numpy(bias).double(), stride=s, padding=p).numpy()
+    np.testing.assert_array_equal(banded.astype(np.float64), direct)
+
+
+@pytest.mark.parametrize("case", [(1, 6, 37, 20, 5, 3, 1, 1, 100), (2, 6, 37, 20, 5, 3, 1, 1, 4),
+                                  (1, 4, 33, 17, 3, 3, 2, 0, 3), (3, 8, 19, 11, 7, 1, 1, 0, 2)])
+def test_column_convolution_matches_direct(case):
+    b, c, h, w, out, k, s, p, rows = case
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((b, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((out, c, k, k)) * 0.2).astype(np.float32)
+    out_w = (w + 2 * p - k) // s + 1
+    got = oracle.conv2d(x, wt, None, stride=s, padding=p,
+                        max_scratch_elements=b * c * k * k * out_w * rows)
+    want = F.conv2d(torch.from_numpy(x).double(), torch.from_numpy(wt).double(), stride=s,
+                    padding=p).numpy()
+    assert np.abs(got - want).max() <= 1e-5
+
+
+def test_convolution_rejects_input_smaller_than_kernel():
+    with pytest.raises(ValueError):
+        oracle.conv2d(np.zeros((1, 1, 2, 8), np.float32), np.zeros((1, 1, 3, 3), np.float32),
+                      stride=2, padding=0)
+
+
+def test_bias_matches_explicit_arrays():
+    x = np.arange(72, dtype=np.float32).reshape(3, 3, 4, 2)[1:3].transpose(0, 1, 3, 2)
+    x = np.ascontiguousarray(x)
+    biases = np.array([1.0, -2.0, 0.5], np.float32)
+    got = oracle.conv2d(x, np.zeros((3, 3, 1, 1), np.float32), biases)
+    want = np.broadcast_to(biases.reshape(1, 3, 1, 1), got.shape)
+    np.testing.assert_array_equal(got, want)
+
+
+def _gn_f64(x, scale, bias, silu):
+    b, c = x.shape[:2]
+    g = x.astype(np.float64).reshape(b, 32, -1)
+    mean = g.mean(axis=2, keepdims=True)
+    var = ((g - mean) ** 2).mean(axis=2, keepdims=True)
+    y = ((g - mean) / np.sqrt(var + EPS)).reshape(x.shape)
+    y = y * scale.reshape(1, c, 1, 1) + bias.reshape(1, c, 1, 1)
+    return y / (1.0 + np.exp(-y)) if silu else y
+
+
+@pytest.mark.parametrize("case", [(1, 32, 1, 1, False, False), (2, 64, 3, 7, True, False),
+                                  (2, 32, 1, 257, False, False), (2, 32, 1, 4097, False, False),
+                                  (1, 32, 128, 256, False, True)])
+def test_group_norm_matches_f64_reference(case):
+    batch, channels, height, width, transposed, large_offset = case
+    n = (batch + 1) * channels * height * width
+    i = np.arange(n)
+    if large_offset:
+        values = np.where(i % 2 == 0, np.float32(9.99), np.float32(10.01)).astype(np.float32)
+    else:
+        values = (((i * 37) % 101).astype(np.float32) - 50.0) * np.float32(0.03125)
+    if transposed:
+        src = values.reshape(batch + 1, channels, width, height)[1:].transpose(0, 1, 3, 2)
+    else:
+        src = values.reshape(batch + 1, channels, height, width)[1:]
+    x = np.ascontiguousarray(src)
+    scale = (0.5 + (np.arange(channels) % 5) * 0.125).astype(np.float32)
+    bias = ((np.arange(channels) % 7) * 0.0625 - 0.125).astype(np.float32)
+    for silu in (False, True):
+        got = oracle.group_norm(x, scale, bias, silu=silu)
+        assert np.all(np.isfinite(got))
+        assert np.abs(got - _gn_f64(x, scale.astype(np.float64), bias.astype(np.float64),
+                                    silu)).max() <= 2e-5
+
+
+def test_group_norm_wide_magnitude():
+    i = np.arange(2 * 32 * 4096)
+    x = np.choose(i % 4, [1e10, -1e10, 1e-10, -1e-10]).astype(np.float32).reshape(2, 32, 1, 4096)
+    got = oracle.group_norm(x, np.ones(32, np.float32), np.zeros(32, np.float32))
+    denom = np.sqrt(0.5 * (1e20 + 1e-20) + EPS)
+    assert np.abs(got.astype(np.float64) - x.astype(np.float64) / denom).max() <= 2e-5
+
+
+def test_group_norm_long_balanced_groups_closed_form():
+    low, high = np.float32(10.0 - 0.01), np.float32(10.0 + 0.01)
+    x = np.where(np.arange(32 * 128 * 256) % 2 == 0, low, high).astype(np.float32)
+    x = x.reshape(1, 32, 128, 256)
+    mean = (float(low) + float(high)) / 2
+    half = (float(high) - float(low)) / 2
+    denom = np.sqrt(half * half + 1e-6)
+    got = oracle.group_norm(x, np.ones(32, np.float32), np.zeros(32, np.float32))
+    want = np.where(np.arange(x.size) % 2 == 0, (float(low) - mean) / denom,
+                    (float(high) - mean) / denom).reshape(x.shape)
+    assert np.abs(got - want).max() <= 2e-5
+
+
+def test_group_norm_constant_groups_and_wrong_channels():
+    got = oracle.group_norm(np.full((1, 32, 2, 2), 7.0, np.float32), np.ones(32, np.float32),
+                            np.full(32, 1.25, np.float32))
+    assert np.all(got == 1.25)
+    with pytest.raises(ValueError):
+        oracle.group_norm(np.zeros((1, 48, 2, 2), np.float32), np.ones(48, np.float32),
+                          np.zeros(48, np.float32))
+
+
+def test_upsample_matches_explicit_reference():
+    src = np.arange(48, dtype=np.float32).reshape(3, 2, 4, 2)[1:3].transpose(0, 1, 3, 2)
+    src = np.ascontiguousarray(src)
+    got = oracle.upsample_2x(src)
+    expected = []
+    for plane in src.reshape(-1, 8):
+        for row in plane.reshape(2, 4):
+            for _ in range(2):
+                for v in row:
+                    expected += [v, v]
+    assert got.shape == (2, 2, 4, 8)
+    np.testing.assert_array_equal(got.reshape(-1), np.array(expected, np.float32))
+
+
+def _attention_inputs():
+    q = (np.arange(6 * 8 * 11, dtype=np.float32) * np.float32(1 / 1024) - np.float32(0.25))
+    q = np.ascontiguousarray(q.reshape(6, 8, 11).transpose(0, 2, 1))
+    k = (np.arange(6 * 8 * 13, dtype=np.float32) * np.float32(1 / 2048) - np.float32(0.125))
+    k = k.reshape(6, 8, 13)
+    v = (np.arange(6 * 13 * 8, dtype=np.float32) * np.float32(1 / 512) - np.float32(0.5))
+    v = v.reshape(6, 13, 8)
+    return q, k, v
+
+
+def test_attention_slicing_changes_nothing():
+    q, kt, v = _attention_inputs()
+    full = torch.softmax(torch.from_numpy(q).double() @ torch.from_numpy(kt).double(), -1)
+    full = (full @ torch.from_numpy(v).double()).numpy()
+    unsliced = oracle.attend(q, kt, v)
+    for rows in (1, 3, 11, 20):
+        got = oracle.attend(q, kt, v, max_score_elements=6 * 13 * rows)
+        assert np.abs(got - unsliced).max() <= 2e-6
+        assert np.abs(got - full).max() <= 2e-6
+    with pytest.raises(ValueError):
+        oracle.attend(q, kt, v, max_score_elements=6 * 13 - 1)
+
+
+def _f64_decoder(w, latents, channels, layers):
+    """Independent float64 decoder written with torch.nn.functional."""
+    W = {k: torch.from_numpy(v).double() for k, v in w.items()}
+
+    def conv(n, x, pad=None):
+        k = W[n + ".weight"]
+        return F.conv2d(x, k, W[n + ".bias"], padding=k.shape[-1] // 2 if pad is None else pad)
+
+    def gn(n, x):
+        return F.group_norm(x, 32, W[n + ".weight"], W[n + ".bias"], eps=EPS)
+
+    def resnet(p, x):
+        sc = conv(p + ".conv_shortcut", x) if p + ".conv_shortcut.weight" in W else x
+        h = conv(p + ".conv1", F.silu(gn(p + ".norm1", x)))
+        return sc + conv(p + ".conv2", F.silu(gn(p + ".norm2", h)))
+
+    def attn(p, x):
+        b, c, hh, ww = x.shape
+        t = gn(p + ".group_norm", x).reshape(b, c, hh * ww).transpose(1, 2)
+
+        def lin(n, z):
+            return z @ W[p + "." + n + ".weight"].reshape(c, c).T + W[p + "." + n + ".bias"]
+
+        s = c ** -0.25
+        a = torch.softmax((lin("to_q", t) * s) @ (lin("to_k", t) * s).transpose(1, 2), -1)
+        o = lin("to_out.0", a @ lin("to_v", t)).transpose(1, 2).reshape(b, c, hh, ww)
+        return o + x
+
+    x = conv("decoder.conv_in", conv("post_quant_conv", torch.from_numpy(latents).double()))
+    x = resnet("decoder.mid_block.resnets.0", x)
+    x = attn("decoder.mid_block.attentions.0", x)
+    x = resnet("decoder.mid_block.resnets.1", x)
+    for i in range(4):
+        for j in range(layers + 1):
+            x = resnet(f"decoder.up_blocks.{i}.resnets.{j}", x)
+        if i < 3:
+            x = conv(f"decoder.up_blocks.{i}.upsamplers.0.conv",
+                     F.interpolate(x, scale_factor=2, mode="nearest"))
+    return conv("decoder.conv_out", F.silu(gn("decoder.conv_norm_out", x))).numpy()
+
+
+def test_decoder_matches_independent_f64_implementation():
+    channels, layers = (32, 32, 32, 32), 1
+    w = random_vae_weights(3, channels=channels, layers=layers, parts=("decoder",))
+    lat = np.random.default_rng(4).standard_normal((2, 4, 2, 2)).astype(np.float32)
+    got = ovae.decode(w, lat, channels=channels, layers=layers)
+    want = _f64_decoder(w, lat, channels, layers)
+    assert got.shape == (2, 3, 16, 16)
+    assert np.abs(got - want).max() <= 1e-4 * max(1.0, np.abs(want).max())
+
+
+def test_weights_are_deterministic_and_named_like_diffusers():
+    a = random_vae_weights(0, channels=(32, 32, 32, 32), layers=1)
+    b = random_vae_weights(0, channels=(32, 32, 32, 32), layers=1)
+    assert a.keys() == b.keys()
+    for k in a:
+        np.testing.assert_array_equal(a[k], b[k])
+    assert "decoder.up_blocks.1.upsamplers.0.conv.weight" in a
+    assert "encoder.down_blocks.0.downsamplers.0.conv.weight" in a
+    assert "decoder.mid_block.attentions.0.to_q.weight" in a
+    assert a["decoder.conv_norm_out.weight"].tolist() == [1.0] * 32
