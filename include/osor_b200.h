@@ -165,6 +165,22 @@ int osor_group_norm_silu(const void* x, void* y, const float* gamma, const float
                          int silu, float* stats, void* workspace, size_t workspace_bytes,
                          void* stream);
 
+/* The NCHW case of osor_group_norm_silu (same kernel, same results) for
+ * callers that cannot allocate device memory where they run the op, such as
+ * a host framework's enqueue callback that owns all allocations or a serving
+ * loop that must not call the allocator. It takes no workspace: the scratch
+ * lives in one fixed device array of 397312 bytes (32768 chunk partials plus
+ * 1024 group counters) that every GPU loading the library keeps until exit;
+ * shapes that need more return OSOR_ERR_INVALID_INPUT before any device work.
+ * The first call on a device looks up the array's address with that device
+ * current, so make that first call before any stream capture. All calls share
+ * the array (each call clears its counters first); calls that overlap on the
+ * GPU race and must not be issued. It calls no cudaMalloc / cudaFree. This
+ * entry point has no counterpart in the reference. */
+int osor_group_norm_silu_noalloc(const void* x, void* y, const float* gamma, const float* beta,
+                                 int batch, int channels, int height, int width, int dtype,
+                                 float eps, int silu, float* stats, void* stream);
+
 /* Nearest 2x upsample of 16-bit NHWC [B][H][W][C] -> [B][2H][2W][C], C % 8 == 0.
  * Replaces upsample_2x (src/native/vae_decoder.rs:18-35). */
 int osor_upsample_2x(const void* x, void* y, int batch, int height, int width, int channels,

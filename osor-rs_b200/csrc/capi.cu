@@ -56,6 +56,10 @@ class DeviceOf {
 
 }  // namespace
 
+namespace osor {
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+}  // namespace osor
+
 extern "C" {
 
 const char* osor_last_error_message(void) { return g_last_error.c_str(); }

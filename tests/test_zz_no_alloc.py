@@ -1,0 +1,78 @@
+"""osor_group_norm_silu_noalloc: the GroupNorm(+SiLU) entry point for callers
+that cannot allocate device memory where they run the op (a framework
+callback that owns every allocation, a serving loop that must not touch the
+allocator). Its scratch is a fixed device array inside the library, so the
+caller passes only inputs and outputs.
+
+Checked through the C ABI against the workspace-taking entry point
+(osor_group_norm_silu, NCHW) on two calls in a row, and a shape whose scratch
+would not fit is refused before any device work. This file is collected last.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from osor_b200 import _lib, workloads
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    ((2, 512, 32, 32), torch.bfloat16),
+    ((1, 128, 128, 128), torch.float16),
+    ((4, 128, 256, 256), torch.bfloat16),
+    ((2, 32, 1, 4097), torch.float32),
+]
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("shape,dt", CASES)
+def test_noalloc_matches_workspace_entry_point_twice(shape, dt, cuda_device):
+    lb = _lib.lib()
+    x, gamma, beta = workloads.groupnorm_inputs(shape, seed=3)
+    xt = torch.from_numpy(x).to(dt).cuda()
+    g = torch.from_numpy(gamma).cuda()
+    b = torch.from_numpy(beta).cuda()
+    b_, c, h, w = shape
+    code = _lib.dtype_code(dt)
+    need = lb.osor_group_norm_workspace_size(b_, c, h, w, _lib.LAYOUT_NCHW, code)
+    assert need > 0
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    ref = torch.empty_like(xt)
+    ref_stats = torch.zeros((b_ * 32, 2), dtype=torch.float32, device="cuda")
+    _lib.check(lb.osor_group_norm_silu(_p(xt), _p(ref), _p(g), _p(b), b_, c, h, w,
+                                       _lib.LAYOUT_NCHW, code, 1e-6, 1, _p(ref_stats), _p(ws),
+                                       need, _stream()))
+    for _ in range(2):
+        out = torch.full_like(xt, float("nan"))
+        stats = torch.full((b_ * 32, 2), float("nan"), dtype=torch.float32, device="cuda")
+        _lib.check(lb.osor_group_norm_silu_noalloc(_p(xt), _p(out), _p(g), _p(b), b_, c, h, w,
+                                                   code, 1e-6, 1, _p(stats), _stream()))
+        torch.cuda.synchronize()
+        # Same kernel and plan: identical values; the tolerance is the one
+        # the GroupNorm parity tests use for 16-bit outputs.
+        got, want = out.float().cpu().numpy(), ref.float().cpu().numpy()
+        assert np.all(np.isfinite(got))
+        assert np.all(np.abs(got - want) <= 2 ** -8 * np.abs(want) + 1e-3)
+        np.testing.assert_allclose(stats.cpu().numpy(), ref_stats.cpu().numpy(), rtol=1e-4,
+                                   atol=1e-6)
+    assert _lib.lib().osor_device_status(0, 1) == 0
+
+
+def test_noalloc_rejects_shapes_beyond_the_fixed_scratch(cuda_device):
+    lb = _lib.lib()
+    t = torch.zeros(64, device="cuda")
+    # 64 images x 32 groups x 86 chunks of [*, 128, 1024, 1024] 16-bit needs
+    # more scratch than the fixed array holds; refused before any device work.
+    rc = lb.osor_group_norm_silu_noalloc(_p(t), _p(t), _p(t), _p(t), 64, 128, 1024, 1024,
+                                         _lib.DTYPE_BF16, 1e-6, 1, None, _stream())
+    assert rc == _lib.OSOR_ERR_INVALID_INPUT
+    assert "fixed no-allocation scratch" in _lib.last_error()
