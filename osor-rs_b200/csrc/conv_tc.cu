@@ -53,6 +53,11 @@ struct TcParams {
   long long ld_out;
   const float* row_scale;  // [M] or nullptr
   int out_f32;
+  // GroupNorm partial statistics of the (rounded) output, written when the
+  // kernel is instantiated with CPG > 0: gn_part[m_tile][group] = (mean, M2)
+  // over the tile's 128 pixels x CPG channels of that group.
+  float* gn_part;
+  int gn_groups;  // groups per pixel row (Cout / CPG)
 };
 
 template <int BLOCK_N>
@@ -61,10 +66,38 @@ struct TcConfig {
   static constexpr int kStages = BLOCK_N == 256 ? 4 : 6;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BLOCK_N;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kStatBytes = 4 * 64 * 2 * 4;  // [warp][group in tile][mean, M2]
+  static constexpr int kSmemBytes =
+      kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ + kStatBytes;
 };
 
-template <int BLOCK_N, int D>
+// Named barrier over the 128 epilogue threads (warps 2..5); id 0 is __syncthreads.
+__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// AND of `ok` over the 128 epilogue threads (a barrier with a reduction), so
+// that the four warps always take the same branch.
+__device__ __forceinline__ bool epilogue_all(bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"((uint32_t)ok)
+      : "memory");
+  return r != 0;
+}
+
+// Merge (mean, M2) of two halves with equal counts n: Chan's formula.
+__device__ __forceinline__ void merge_equal(float& mean, float& m2, float mean_o, float m2_o,
+                                            float n) {
+  const float d = mean_o - mean;
+  m2 = m2 + m2_o + d * d * (0.5f * n);
+  mean = 0.5f * (mean + mean_o);
+}
+
+template <int BLOCK_N, int D, int CPG>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b, const TcParams p) {
@@ -82,6 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* stat_smem = reinterpret_cast<float*>(smem + S * Cfg::kStageBytes + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -224,7 +258,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
+      // The four epilogue warps leave together: the per-tile statistics
+      // below use a named barrier that all of them must reach.
+      if (!epilogue_all(mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;
       tc_fence_after();
       const int m_tile = tile / p.num_n_tiles;
       const int n_tile = tile - m_tile * p.num_n_tiles;
@@ -271,13 +307,71 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           uint4* o4 =
               reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + m * p.ld_out + n0);
+          uint32_t pk[16];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            o4[j] = make_uint4(Elem<D>::pack(v[8 * j + 0], v[8 * j + 1]),
-                               Elem<D>::pack(v[8 * j + 2], v[8 * j + 3]),
-                               Elem<D>::pack(v[8 * j + 4], v[8 * j + 5]),
-                               Elem<D>::pack(v[8 * j + 6], v[8 * j + 7]));
+          for (int j = 0; j < 16; ++j) pk[j] = Elem<D>::pack(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            o4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+          if constexpr (CPG > 0) {
+            // Statistics of the stored (rounded) values: per group of CPG
+            // channels, exact two-pass (mean, M2) of this pixel, then a
+            // butterfly of equal-count Chan merges over the warp's 32 pixels.
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float2 f = Elem<D>::unpack(pk[j]);
+              v[2 * j] = f.x;
+              v[2 * j + 1] = f.y;
+            }
+            constexpr int kGroupsPerChunk = 32 / CPG;
+#pragma unroll
+            for (int gi = 0; gi < kGroupsPerChunk; ++gi) {
+              float mean = 0.0f;
+#pragma unroll
+              for (int c = 0; c < CPG; ++c) mean += v[gi * CPG + c];
+              mean *= 1.0f / CPG;
+              float m2 = 0.0f;
+#pragma unroll
+              for (int c = 0; c < CPG; ++c) {
+                const float d = v[gi * CPG + c] - mean;
+                m2 += d * d;
+              }
+              float n = (float)CPG;
+#pragma unroll
+              for (int o = 1; o < 32; o <<= 1) {
+                const float mo = __shfl_xor_sync(0xffffffffu, mean, o);
+                const float qo = __shfl_xor_sync(0xffffffffu, m2, o);
+                merge_equal(mean, m2, mo, qo, n);
+                n *= 2.0f;
+              }
+              if (lane == 0) {
+                float* s = stat_smem + (quad * 64 + chunk * kGroupsPerChunk + gi) * 2;
+                s[0] = mean;
+                s[1] = m2;
+              }
+            }
           }
+        }
+      }
+      if constexpr (CPG > 0) {
+        if (!p.out_f32) {
+          // Merge the four warps (quadrants 0..3 in a fixed order) and publish
+          // one (mean, M2) per group of this tile.
+          epilogue_sync();
+          constexpr int kG = BLOCK_N / CPG;
+          const int t = threadIdx.x - 64;
+          if (t < kG) {
+            const float n = 32.0f * CPG;
+            float ma = stat_smem[(0 * 64 + t) * 2], qa = stat_smem[(0 * 64 + t) * 2 + 1];
+            float mb = stat_smem[(2 * 64 + t) * 2], qb = stat_smem[(2 * 64 + t) * 2 + 1];
+            merge_equal(ma, qa, stat_smem[(1 * 64 + t) * 2], stat_smem[(1 * 64 + t) * 2 + 1], n);
+            merge_equal(mb, qb, stat_smem[(3 * 64 + t) * 2], stat_smem[(3 * 64 + t) * 2 + 1], n);
+            merge_equal(ma, qa, mb, qb, 2.0f * n);
+            float* dst = p.gn_part + ((long long)m_tile * p.gn_groups + n_tile * kG + t) * 2;
+            dst[0] = ma;
+            dst[1] = qa;
+          }
+          epilogue_sync();
         }
       }
       tc_fence_before();
@@ -329,7 +423,7 @@ int sm_count(int device) {
   return counts[device];
 }
 
-template <int BLOCK_N, int D>
+template <int BLOCK_N, int D, int CPG>
 cudaError_t launch_typed(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p,
                          cudaStream_t stream) {
   using Cfg = TcConfig<BLOCK_N>;
@@ -337,7 +431,7 @@ cudaError_t launch_typed(const CUtensorMap& ta, const CUtensorMap& tb, const TcP
   int device = 0;
   cudaGetDevice(&device);
   if (device >= 0 && device < 64 && !configured[device]) {
-    cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<BLOCK_N, D>,
+    cudaError_t e = cudaFuncSetAttribute(conv_tc_kernel<BLOCK_N, D, CPG>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::kSmemBytes);
     if (e != cudaSuccess) return e;
@@ -345,8 +439,19 @@ cudaError_t launch_typed(const CUtensorMap& ta, const CUtensorMap& tb, const TcP
   }
   const int tiles = p.num_m_tiles * p.num_n_tiles;
   const int grid = tiles < sm_count(device) ? tiles : sm_count(device);
-  conv_tc_kernel<BLOCK_N, D><<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  conv_tc_kernel<BLOCK_N, D, CPG><<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
   return cudaGetLastError();
+}
+
+template <int BLOCK_N, int D>
+cudaError_t launch_cpg(int cpg, const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p,
+                       cudaStream_t stream) {
+  switch (cpg) {
+    case 4: return launch_typed<BLOCK_N, D, 4>(ta, tb, p, stream);
+    case 8: return launch_typed<BLOCK_N, D, 8>(ta, tb, p, stream);
+    case 16: return launch_typed<BLOCK_N, D, 16>(ta, tb, p, stream);
+    default: return launch_typed<BLOCK_N, D, 0>(ta, tb, p, stream);
+  }
 }
 
 }  // namespace
@@ -372,6 +477,8 @@ const char* conv_tc_check(const ConvTcArgs& a) {
   if ((long long)a.batch * a.out_h * a.out_w > 0x7fffffffLL) return "problem too large";
   if (a.stride == 2 && 2 * tile_w > 256) return "stride-2 tile too wide";
   if (a.dtype != kBf16 && a.dtype != kF16) return "unknown 16-bit type";
+  if (a.gn_part && (a.out_f32 || (a.gn_cpg != 4 && a.gn_cpg != 8 && a.gn_cpg != 16)))
+    return "fused group-norm statistics need a 16-bit output and 4, 8 or 16 channels per group";
   return nullptr;
 }
 
@@ -431,11 +538,14 @@ cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
   p.ld_out = a.ld_out;
   p.row_scale = a.row_scale;
   p.out_f32 = a.out_f32;
+  const int cpg = a.gn_part ? a.gn_cpg : 0;
+  p.gn_part = a.gn_part;
+  p.gn_groups = cpg ? a.cout / cpg : 0;
   if (a.dtype == kF16)
-    return block_n == 256 ? launch_typed<256, kF16>(ta, tb, p, stream)
-                          : launch_typed<128, kF16>(ta, tb, p, stream);
-  return block_n == 256 ? launch_typed<256, kBf16>(ta, tb, p, stream)
-                        : launch_typed<128, kBf16>(ta, tb, p, stream);
+    return block_n == 256 ? launch_cpg<256, kF16>(cpg, ta, tb, p, stream)
+                          : launch_cpg<128, kF16>(cpg, ta, tb, p, stream);
+  return block_n == 256 ? launch_cpg<256, kBf16>(cpg, ta, tb, p, stream)
+                        : launch_cpg<128, kBf16>(cpg, ta, tb, p, stream);
 }
 
 }  // namespace osor

@@ -29,6 +29,11 @@ struct ConvTcArgs {
   long long ld_out = 0;
   int out_f32 = 0;
   const float* row_scale = nullptr;
+  // Optional GroupNorm partial statistics of the 16-bit output:
+  // gn_part[m_tile][cout / gn_cpg][2] = (mean, M2) over each 128-pixel tile
+  // and group of gn_cpg channels (gn_cpg 4, 8 or 16).
+  float* gn_part = nullptr;
+  int gn_cpg = 0;
 };
 
 // nullptr when the tensor-core kernel supports the shape, else a reason.

@@ -293,9 +293,28 @@ __global__ void __launch_bounds__(kNhwcThreads)
 #pragma unroll
   for (int j = 0; j < 8; ++j) s1[j] = s2[j] = 0.0f;
   if (r0 < rows) {
-    for (long long pix = p_begin + r0; pix < p_end; pix += rows) {
+    const uint4* src = reinterpret_cast<const uint4*>(img) + col;
+    long long pix = p_begin + r0;
+    // Four independent 16-byte loads in flight per thread.
+    for (; pix + 3 * rows < p_end; pix += 4 * rows) {
+      uint4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) q[u] = __ldcs(src + (pix + u * rows) * vc);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float f[8];
+        unpack8<D>(q[u], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float d = f[j] - anchor[j];
+          s1[j] += d;
+          s2[j] += d * d;
+        }
+      }
+    }
+    for (; pix < p_end; pix += rows) {
       float f[8];
-      unpack8<D>(__ldg(reinterpret_cast<const uint4*>(img + pix * channels) + col), f);
+      unpack8<D>(__ldcs(src + pix * vc), f);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float d = f[j] - anchor[j];
@@ -366,31 +385,92 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// Streams x once: y = silu?((x - mean) * (rstd * gamma) + beta), 8 channels per thread.
+// grid (groups, batch): combine the per-tile (mean, M2) partials that the
+// producing convolution's epilogue wrote (tile_part[b*tiles + t][group][2],
+// every tile holding `tile_count` elements of the group) and write the
+// per-channel apply coefficients. With equal counts the group mean is the mean
+// of tile means and M2 = sum M2_t + tile_count * sum (mean_t - mean)^2.
+__global__ void __launch_bounds__(256)
+    gn_tiles_finalize_kernel(const float* __restrict__ tile_part, int tiles, float tile_count,
+                             int channels, int groups, const float* __restrict__ gamma,
+                             const float* __restrict__ beta, float eps, float* __restrict__ coef,
+                             float* __restrict__ stats_out) {
+  __shared__ float red[8];
+  const int g = blockIdx.x, b = blockIdx.y;
+  const int cpg = channels / groups;
+  const float* part = tile_part + (long long)b * tiles * groups * 2;
+  float s = 0.0f;
+  for (int t = threadIdx.x; t < tiles; t += blockDim.x) s += part[((long long)t * groups + g) * 2];
+  const float mean = block_sum_256(s, red) / (float)tiles;
+  float q = 0.0f;
+  for (int t = threadIdx.x; t < tiles; t += blockDim.x) {
+    const float* pp = part + ((long long)t * groups + g) * 2;
+    const float d = pp[0] - mean;
+    q += pp[1] + tile_count * d * d;
+  }
+  q = block_sum_256(q, red);
+  const float var = fmaxf(q / (tile_count * (float)tiles), 0.0f);
+  const float rstd = 1.0f / sqrtf(var + eps);
+  for (int i = threadIdx.x; i < cpg; i += blockDim.x) {
+    const int c = g * cpg + i;
+    float* o = coef + ((long long)b * channels + c) * 4;
+    o[0] = mean;
+    o[1] = rstd * gamma[c];
+    o[2] = beta[c];
+    o[3] = 0.0f;
+  }
+  if (threadIdx.x == 0 && stats_out) {
+    stats_out[((long long)b * groups + g) * 2] = mean;
+    stats_out[((long long)b * groups + g) * 2 + 1] = var;
+  }
+}
+
+// Streams x once: y = silu?((x - mean) * (rstd * gamma) + beta). grid (n, batch);
+// each thread owns one 8-channel column of one image (coefficients held in
+// registers) and keeps four 16-byte loads in flight.
 template <int D>
 __global__ void __launch_bounds__(256)
     gn_nhwc_apply_kernel(const uint4* __restrict__ x, uint4* __restrict__ y,
                          const float* __restrict__ coef, int channels, long long pixels,
-                         long long total_vectors, int silu) {
+                         int silu) {
   const int vc = channels / 8;
-  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < total_vectors;
-       v += (long long)gridDim.x * blockDim.x) {
-    const long long pix = v / vc;
-    const int col = (int)(v - pix * vc);
-    const int b = (int)(pix / pixels);
+  const int rows = blockDim.x / vc;
+  const int col = threadIdx.x % vc;
+  const int r0 = threadIdx.x / vc;
+  if (r0 >= rows) return;
+  const int b = blockIdx.y;
+  float mu[8], sc[8], sh[8];
+  const float4* cf = reinterpret_cast<const float4*>(coef + ((long long)b * channels + col * 8) * 4);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 c = __ldg(cf + j);
+    mu[j] = c.x;
+    sc[j] = c.y;
+    sh[j] = c.z;
+  }
+  const uint4* src = x + (long long)b * pixels * vc + col;
+  uint4* dst = y + (long long)b * pixels * vc + col;
+  const long long stride = (long long)gridDim.x * rows;
+  long long pix = (long long)blockIdx.x * rows + r0;
+  auto apply = [&](const uint4& q) {
     float f[8];
-    unpack8<D>(__ldg(x + v), f);
-    const float4* cf =
-        reinterpret_cast<const float4*>(coef + ((long long)b * channels + col * 8) * 4);
+    unpack8<D>(q, f);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float4 c = __ldg(cf + j);
-      float a = (f[j] - c.x) * c.y + c.z;
+      float a = (f[j] - mu[j]) * sc[j] + sh[j];
       if (silu) a = silu_f(a);
       f[j] = a;
     }
-    y[v] = pack8<D>(f);
+    return pack8<D>(f);
+  };
+  for (; pix + 3 * stride < pixels; pix += 4 * stride) {
+    uint4 q[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) q[u] = __ldcs(src + (pix + u * stride) * vc);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) dst[(pix + u * stride) * vc] = apply(q[u]);
   }
+  for (; pix < pixels; pix += stride) dst[pix * vc] = apply(__ldcs(src + pix * vc));
 }
 
 int num_sms() {
@@ -398,6 +478,21 @@ int num_sms() {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
   return c > 0 ? c : 148;
+}
+
+template <int D>
+cudaError_t apply_launch(const void* x, void* y, const float* coef, int batch, int channels,
+                         long long pixels, int silu, cudaStream_t stream) {
+  const int vc = channels / 8;
+  const int rows = 256 / vc;
+  const int threads = rows * vc;
+  long long bx = ((long long)num_sms() * 8 + batch - 1) / batch;
+  const long long need = (pixels + rows - 1) / rows;
+  if (bx > need) bx = need;
+  if (bx < 1) bx = 1;
+  gn_nhwc_apply_kernel<D><<<dim3((unsigned)bx, batch), threads, 0, stream>>>(
+      static_cast<const uint4*>(x), static_cast<uint4*>(y), coef, channels, pixels, silu);
+  return cudaGetLastError();
 }
 
 template <int D>
@@ -416,14 +511,7 @@ cudaError_t gn_nhwc_typed(const void* x, void* y, const float* gamma, const floa
       xs, partials, channels, pixels, plan.pix_per_chunk, groups);
   gn_nhwc_finalize_kernel<D><<<dim3(groups, batch), 256, 0, stream>>>(
       xs, partials, plan.chunks, channels, pixels, groups, gamma, beta, eps, coef, stats_out);
-  const long long vectors = (long long)batch * pixels * vc;
-  long long blocks = (vectors + 255) / 256;
-  const long long max_blocks = (long long)num_sms() * 16;
-  if (blocks > max_blocks) blocks = max_blocks;
-  gn_nhwc_apply_kernel<D><<<(int)blocks, 256, 0, stream>>>(static_cast<const uint4*>(x),
-                                                           static_cast<uint4*>(y), coef, channels,
-                                                           pixels, vectors, silu);
-  return cudaGetLastError();
+  return apply_launch<D>(x, y, coef, batch, channels, pixels, silu, stream);
 }
 
 }  // namespace
@@ -523,6 +611,19 @@ GnNhwcPlan gn_nhwc_plan(int batch, int channels, long long pixels, int groups) {
   plan.workspace_bytes = (plan.partial_bytes + 255) / 256 * 256 + plan.coef_bytes;
   plan.groups = groups;
   return plan;
+}
+
+cudaError_t gn_nhwc_apply_tiles_launch(int dtype, const void* x, void* y, const float* gamma,
+                                       const float* beta, int batch, int channels,
+                                       long long pixels, int groups, float eps, int silu,
+                                       const float* tile_part, float* coef, float* stats_out,
+                                       cudaStream_t stream) {
+  const int tiles = (int)(pixels / 128);
+  const float tile_count = 128.0f * (float)(channels / groups);
+  gn_tiles_finalize_kernel<<<dim3(groups, batch), 256, 0, stream>>>(
+      tile_part, tiles, tile_count, channels, groups, gamma, beta, eps, coef, stats_out);
+  if (dtype == kF16) return apply_launch<kF16>(x, y, coef, batch, channels, pixels, silu, stream);
+  return apply_launch<kBf16>(x, y, coef, batch, channels, pixels, silu, stream);
 }
 
 cudaError_t gn_nhwc_launch(int dtype, const void* x, void* y, const float* gamma, const float* beta,

@@ -44,4 +44,14 @@ cudaError_t gn_nhwc_launch(int dtype, const void* x, void* y, const float* gamma
                            int batch, int channels, long long pixels, int groups, float eps,
                            int silu, void* workspace, float* stats_out, cudaStream_t stream);
 
+// NHWC GroupNorm(+SiLU) whose statistics were produced by the preceding
+// tensor-core convolution (ConvTcArgs::gn_part): finalize from the per-tile
+// (mean, M2) partials, then the streaming apply. pixels % 128 == 0. `coef` is
+// batch * channels * 4 floats of scratch.
+cudaError_t gn_nhwc_apply_tiles_launch(int dtype, const void* x, void* y, const float* gamma,
+                                       const float* beta, int batch, int channels,
+                                       long long pixels, int groups, float eps, int silu,
+                                       const float* tile_part, float* coef, float* stats_out,
+                                       cudaStream_t stream);
+
 }  // namespace osor

@@ -186,6 +186,7 @@ class Loader {
 
 struct Buffers {
   uint16_t* act[4];
+  float* tstat[4];  // per-tile GroupNorm statistics of act[i], written by conv epilogues
   float* f32;
   float* scores;
   uint16_t* probs;
@@ -200,6 +201,10 @@ Buffers carve(const WorkspacePlan& plan, void* ws) {
   for (int i = 0; i < 4; ++i) {
     b.act[i] = reinterpret_cast<uint16_t*>(p);
     p += plan.act_bytes;
+  }
+  for (int i = 0; i < 4; ++i) {
+    b.tstat[i] = reinterpret_cast<float*>(p);
+    p += plan.tstat_bytes;
   }
   b.f32 = reinterpret_cast<float*>(p);
   p += plan.f32_bytes;
@@ -224,24 +229,46 @@ struct Ctx {
   const Buffers& b;
   cudaStream_t s;
   const volatile int* cancel;
+  // has_stats[i]: b.tstat[i] holds the per-tile statistics of act[i]'s
+  // current contents (written by the convolution that produced them).
+  bool* has_stats;
 };
 
-Status gn(const Ctx& c, const NormLayer& L, const void* x, void* y, int batch, long long pixels,
+// GroupNorm(+SiLU) of buffer xi into buffer yi.
+Status gn(const Ctx& c, const NormLayer& L, int xi, int yi, int batch, long long pixels,
           bool silu) {
+  const void* x = c.b.act[xi];
+  void* y = c.b.act[yi];
+  c.has_stats[yi] = false;
+  // Algorithmic bytes: one 16-bit read and one write per element.
+  const double bytes = 4.0 * batch * pixels * L.c;
+  if (c.has_stats[xi]) {
+    OpScope scope("groupnorm", 0.0, bytes, c.s, 2);
+    return cuda_status(gn_nhwc_apply_tiles_launch(c.dtype, x, y, L.gamma, L.beta, batch, L.c,
+                                                  pixels, kGroups, kEps, silu ? 1 : 0,
+                                                  c.b.tstat[xi], static_cast<float*>(c.b.gn),
+                                                  nullptr, c.s),
+                       "group norm");
+  }
   const GnNhwcPlan plan = gn_nhwc_plan(batch, L.c, pixels, kGroups);
   if (plan.workspace_bytes > c.b.gn_bytes)
     return Status::err(OSOR_ERR_INVALID_INPUT, "group-norm workspace too small");
-  // Algorithmic bytes: one 16-bit read and one write per element.
-  OpScope scope("groupnorm", 0.0, 4.0 * batch * pixels * L.c, c.s, 3);
+  OpScope scope("groupnorm", 0.0, bytes, c.s, 3);
   return cuda_status(gn_nhwc_launch(c.dtype, x, y, L.gamma, L.beta, batch, L.c, pixels, kGroups,
                                     kEps, silu ? 1 : 0, c.b.gn, nullptr, c.s),
                      "group norm");
 }
 
-Status conv16(const Ctx& c, const ConvLayer& L, const void* x, int batch, int h, int w, void* out,
-              const void* residual = nullptr) {
-  return run_conv(c.dtype, L, x, kLayoutNhwc16, batch, h, w, L.cin, out, kLayoutNhwc16, L.cout,
-                  residual, L.cout, c.s);
+// Convolution of buffer xi into buffer oi. With want_stats the epilogue also
+// writes the output's per-tile GroupNorm statistics when the shape allows.
+Status conv16(const Ctx& c, const ConvLayer& L, int xi, int batch, int h, int w, int oi,
+              const void* residual, bool want_stats) {
+  bool produced = false;
+  Status st = run_conv(c.dtype, L, c.b.act[xi], kLayoutNhwc16, batch, h, w, L.cin, c.b.act[oi],
+                       kLayoutNhwc16, L.cout, residual, L.cout, c.s,
+                       want_stats ? c.b.tstat[oi] : nullptr, &produced);
+  c.has_stats[oi] = produced;
+  return st;
 }
 
 // x (buffer xi) -> resnet output written back into buffer xi.
@@ -249,19 +276,16 @@ Status resnet(const Ctx& c, const ResnetLayer& L, int xi, int batch, int h, int 
   Status st = check_cancel(c.cancel);
   if (!st.good()) return st;
   const long long pixels = (long long)h * w;
-  uint16_t* x = c.b.act[xi];
-  uint16_t* t = c.b.act[(xi + 1) % 4];
-  uint16_t* hbuf = c.b.act[(xi + 2) % 4];
-  uint16_t* sc = c.b.act[(xi + 3) % 4];
-  const uint16_t* residual = x;
+  const int ti = (xi + 1) % 4, hi = (xi + 2) % 4, si = (xi + 3) % 4;
+  const uint16_t* residual = c.b.act[xi];
   if (L.has_shortcut) {
-    if (!(st = conv16(c, L.shortcut, x, batch, h, w, sc)).good()) return st;
-    residual = sc;
+    if (!(st = conv16(c, L.shortcut, xi, batch, h, w, si, nullptr, false)).good()) return st;
+    residual = c.b.act[si];
   }
-  if (!(st = gn(c, L.n1, x, t, batch, pixels, true)).good()) return st;
-  if (!(st = conv16(c, L.c1, t, batch, h, w, hbuf)).good()) return st;
-  if (!(st = gn(c, L.n2, hbuf, t, batch, pixels, true)).good()) return st;
-  return conv16(c, L.c2, t, batch, h, w, x, residual);
+  if (!(st = gn(c, L.n1, xi, ti, batch, pixels, true)).good()) return st;
+  if (!(st = conv16(c, L.c1, ti, batch, h, w, hi, nullptr, true)).good()) return st;
+  if (!(st = gn(c, L.n2, hi, ti, batch, pixels, true)).good()) return st;
+  return conv16(c, L.c2, ti, batch, h, w, xi, residual, true);
 }
 
 // Mid-block attention on buffer xi (in place).
@@ -270,19 +294,19 @@ Status attention(const Ctx& c, const AttentionLayer& L, int xi, int batch, int h
   if (!st.good()) return st;
   const int ch = L.norm.c;
   const int n = h * w;
-  uint16_t* x = c.b.act[xi];
-  uint16_t* t = c.b.act[(xi + 1) % 4];
-  uint16_t* qkv = c.b.act[(xi + 2) % 4];
-  uint16_t* o = c.b.act[(xi + 3) % 4];
-  if (!(st = gn(c, L.norm, x, t, batch, n, false)).good()) return st;
+  const int ti = (xi + 1) % 4, qi = (xi + 2) % 4, oi = (xi + 3) % 4;
+  if (!(st = gn(c, L.norm, xi, ti, batch, n, false)).good()) return st;
   // q|k|v for all images in one GEMM: [B*N, C] x [3C, C]^T.
-  if (!(st = conv16(c, L.qkv, t, 1, 1, batch * n, qkv)).good()) return st;
-  uint16_t* vt = t;  // the normalized input is dead after the projection
-  st = attention_core(c.dtype, qkv, qkv + ch, qkv + 2 * ch, 3 * ch, o, ch, batch, n, ch,
+  if (!(st = conv16(c, L.qkv, ti, 1, 1, batch * n, qi, nullptr, false)).good()) return st;
+  const uint16_t* qkv = c.b.act[qi];
+  uint16_t* vt = c.b.act[ti];  // the normalized input is dead after the projection
+  c.has_stats[ti] = false;
+  c.has_stats[oi] = false;
+  st = attention_core(c.dtype, qkv, qkv + ch, qkv + 2 * ch, 3 * ch, c.b.act[oi], ch, batch, n, ch,
                       c.b.scores, c.b.probs, c.b.rowsum, vt, c.s);
   if (!st.good()) return st;
   // Output projection + residual, in place.
-  return conv16(c, L.out, o, 1, 1, batch * n, x, x);
+  return conv16(c, L.out, oi, 1, 1, batch * n, xi, c.b.act[xi], true);
 }
 
 Status mid_block(const Ctx& c, const MidLayer& L, int xi, int batch, int h, int w) {
@@ -388,7 +412,8 @@ Status attention_core(int dtype, const void* q, const void* k, const void* v, lo
 Status run_conv(int dtype, const ConvLayer& L, const void* x, int in_mode, int batch, int in_h,
                 int in_w, long long in_pixel_stride, void* out, int out_mode,
                 long long out_pixel_stride, const void* residual, long long ld_res,
-                cudaStream_t s) {
+                cudaStream_t s, float* gn_part, bool* gn_done) {
+  if (gn_done) *gn_done = false;
   const int ph = in_h + L.pad + L.pad_end, pw = in_w + L.pad + L.pad_end;
   if (ph < L.k || pw < L.k)
     return Status::err(OSOR_ERR_INVALID_INPUT, "convolution input is smaller than its kernel");
@@ -424,11 +449,20 @@ Status run_conv(int dtype, const ConvLayer& L, const void* x, int in_mode, int b
     a.ld_res = ld_res;
     a.out = out;
     a.ld_out = out_pixel_stride;
+    // GroupNorm statistics in the epilogue when the output has 4, 8 or 16
+    // channels per group (Cout 128, 256, 512 with 32 groups).
+    const int cpg = L.cout % kGroups == 0 ? L.cout / kGroups : 0;
+    if (gn_part && (cpg == 4 || cpg == 8 || cpg == 16)) {
+      a.gn_part = gn_part;
+      a.gn_cpg = cpg;
+    }
     // Reads past the input edge return the TMA zero fill, which supplies
     // both the leading pad and the trailing (pad_end) pad.
     if (conv_tc_check(a) == nullptr) {
       OpScope scope(L.k == 3 ? "conv3x3_tc" : "conv1x1_tc", flops, bytes, s, 1);
-      return cuda_status(conv_tc_launch(a, s), "tensor-core conv");
+      const cudaError_t e = conv_tc_launch(a, s);
+      if (gn_done) *gn_done = e == cudaSuccess && a.gn_part != nullptr;
+      return cuda_status(e, "tensor-core conv");
     }
   }
   DirectConvArgs d;
@@ -604,9 +638,14 @@ WorkspacePlan vae_workspace_plan(const Vae& m, int op, int batch, int height, in
   for (int i = 0; i < 4; ++i)
     for (long long px : {full, full / 4, full / 16, full / 64})
       if (px > 0) g = std::max(g, gn_nhwc_plan(batch, ch[i], px, kGroups).workspace_bytes);
+  // The apply-from-tiles path keeps its per-channel coefficients there too.
+  g = std::max(g, (size_t)batch * std::max(std::max(ch[0], ch[1]), std::max(ch[2], ch[3])) * 16);
   p.gn_bytes = align256(g);
-  p.total = 4 * p.act_bytes + p.f32_bytes + p.scores_bytes + p.probs_bytes + p.rowsum_bytes +
-            p.gn_bytes;
+  // Per-tile statistics: (mean, M2) per 128-pixel tile and group, sized for
+  // the most pixels any activation has (the full resolution).
+  p.tstat_bytes = align256((size_t)batch * ((full + 127) / 128) * kGroups * 2 * sizeof(float));
+  p.total = 4 * p.act_bytes + 4 * p.tstat_bytes + p.f32_bytes + p.scores_bytes + p.probs_bytes +
+            p.rowsum_bytes + p.gn_bytes;
   return p;
 }
 
@@ -618,7 +657,8 @@ Status vae_decode(const Vae& m, const float* latents, float* image, int batch, i
   if (workspace_bytes < plan.total)
     return Status::err(OSOR_ERR_INVALID_INPUT, "decode workspace is too small");
   const Buffers b = carve(plan, workspace);
-  const Ctx c{m.dtype, b, stream, cancel};
+  bool has_stats[4] = {false, false, false, false};
+  const Ctx c{m.dtype, b, stream, cancel, has_stats};
   const Decoder& d = m.dec;
   Status st = check_cancel(cancel);
   if (!st.good()) return st;
@@ -646,14 +686,14 @@ Status vae_decode(const Vae& m, const float* latents, float* image, int batch, i
         e = upsample2x_nhwc_launch(b.act[xi], b.act[ui], batch, h, w, ch_now, stream);
       }
       if (e != cudaSuccess) return cuda_status(e, "upsample");
+      has_stats[ui] = false;
       h *= 2;
       w *= 2;
-      if (!(st = conv16(c, up.resample_conv, b.act[ui], batch, h, w, b.act[xi])).good()) return st;
+      if (!(st = conv16(c, up.resample_conv, ui, batch, h, w, xi, nullptr, true)).good()) return st;
     }
   }
   const int ti = (xi + 1) % 4;
-  if (!(st = gn(c, d.norm_out, b.act[xi], b.act[ti], batch, (long long)h * w, true)).good())
-    return st;
+  if (!(st = gn(c, d.norm_out, xi, ti, batch, (long long)h * w, true)).good()) return st;
   return run_conv(c.dtype, d.conv_out, b.act[ti], kLayoutNhwc16, batch, h, w, ch_now, image,
                   kLayoutNchwF32, 0, nullptr, 0, stream);
 }
@@ -666,7 +706,8 @@ Status vae_encode(const Vae& m, const float* image, float* moments, int batch, i
   if (workspace_bytes < plan.total)
     return Status::err(OSOR_ERR_INVALID_INPUT, "encode workspace is too small");
   const Buffers b = carve(plan, workspace);
-  const Ctx c{m.dtype, b, stream, cancel};
+  bool has_stats[4] = {false, false, false, false};
+  const Ctx c{m.dtype, b, stream, cancel, has_stats};
   const Encoder& en = m.enc;
   Status st = check_cancel(cancel);
   if (!st.good()) return st;
@@ -684,7 +725,7 @@ Status vae_encode(const Vae& m, const float* image, float* moments, int batch, i
     if (!(st = check_cancel(cancel)).good()) return st;
     if (down.resample) {
       const int di = (xi + 1) % 4;
-      if (!(st = conv16(c, down.resample_conv, b.act[xi], batch, h, w, b.act[di])).good())
+      if (!(st = conv16(c, down.resample_conv, xi, batch, h, w, di, nullptr, true)).good())
         return st;
       h /= 2;
       w /= 2;
@@ -693,8 +734,7 @@ Status vae_encode(const Vae& m, const float* image, float* moments, int batch, i
   }
   if (!(st = mid_block(c, en.mid, xi, batch, h, w)).good()) return st;
   const int ti = (xi + 1) % 4;
-  if (!(st = gn(c, en.norm_out, b.act[xi], b.act[ti], batch, (long long)h * w, true)).good())
-    return st;
+  if (!(st = gn(c, en.norm_out, xi, ti, batch, (long long)h * w, true)).good()) return st;
   st = run_conv(c.dtype, en.conv_out, b.act[ti], kLayoutNhwc16, batch, h, w, ch_now, b.f32,
                 kLayoutNchwF32, 0, nullptr, 0, stream);
   if (!st.good()) return st;

@@ -81,6 +81,7 @@ struct Encoder {
 // Per-call workspace layout (all parts 256-byte aligned).
 struct WorkspacePlan {
   size_t act_bytes = 0;      // one activation buffer
+  size_t tstat_bytes = 0;    // per-tile GroupNorm statistics of one activation buffer
   size_t f32_bytes = 0;      // thin f32 NCHW scratch
   size_t scores_bytes = 0;   // attention scores (fp32) for one image
   size_t probs_bytes = 0;    // attention probabilities (16-bit) for one image
@@ -113,10 +114,13 @@ Status vae_encode(const Vae& m, const float* image, float* moments, int batch, i
 
 // Single-op entry points shared with the C ABI. in_mode / out_mode are
 // kLayoutNhwc16 (16-bit of `dtype`) or kLayoutNchwF32.
+// With gn_part set and a tensor-core shape whose Cout has 4, 8 or 16
+// channels per group of 32, the epilogue also writes per-tile GroupNorm
+// statistics of the output to gn_part and sets *gn_done.
 Status run_conv(int dtype, const ConvLayer& L, const void* x, int in_mode, int batch, int in_h,
                 int in_w, long long in_pixel_stride, void* out, int out_mode,
                 long long out_pixel_stride, const void* residual, long long ld_res,
-                cudaStream_t s);
+                cudaStream_t s, float* gn_part = nullptr, bool* gn_done = nullptr);
 
 // softmax(q k^T) v for `batch` images of [tokens][dim] rows (stride ld);
 // scores/probs/rowsum/vt are per-image scratch reused across images.
