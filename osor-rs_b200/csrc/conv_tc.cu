@@ -58,12 +58,15 @@ struct TcParams {
   // over the tile's 128 pixels x CPG channels of that group.
   float* gn_part;
   int gn_groups;  // groups per pixel row (Cout / CPG)
+  // Thin-output mode (BLOCK_N 16): n_valid NCHW f32 planes of out_hw pixels.
+  int n_valid;
+  long long out_hw;
 };
 
 template <int BLOCK_N>
 struct TcConfig {
   static constexpr int kBBytes = BLOCK_N * kBlockK * 2;
-  static constexpr int kStages = BLOCK_N == 256 ? 4 : 6;
+  static constexpr int kStages = BLOCK_N == 256 ? 4 : (BLOCK_N == 128 ? 6 : 8);
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BLOCK_N;
   static constexpr int kStatBytes = 4 * 64 * 2 * 4;  // [warp][group in tile][mean, M2]
@@ -266,6 +269,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n_tile = tile - m_tile * p.num_n_tiles;
       const long long m = (long long)m_tile * kBlockM + row;
       const float scale = p.row_scale ? __ldg(p.row_scale + m) : 1.0f;
+      if constexpr (BLOCK_N == 16) {
+        // Thin output (Cout <= 16, weights zero-padded to 16 rows): the first
+        // n_valid channels as NCHW f32 planes; a warp writes 32 consecutive
+        // pixels of each plane.
+        uint32_t r[16];
+        tmem_load_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * 16, r);
+        tmem_wait_ld();
+        const long long img = m / p.out_hw;
+        const long long pix = m - img * p.out_hw;
+        float* o = static_cast<float*>(p.out) + img * p.n_valid * p.out_hw + pix;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (j < p.n_valid)
+            o[(long long)j * p.out_hw] =
+                __uint_as_float(r[j]) * scale + (p.bias ? __ldg(p.bias + j) : 0.0f);
+      }
 #pragma unroll 1
       for (int chunk = 0; chunk < BLOCK_N / 32; ++chunk) {
         uint32_t r[32];
@@ -460,7 +479,12 @@ const char* conv_tc_check(const ConvTcArgs& a) {
   if (a.ksize != 1 && a.ksize != 3) return "tensor-core convolution supports 1x1 and 3x3 kernels";
   if (a.stride != 1 && a.stride != 2) return "tensor-core convolution supports stride 1 and 2";
   if (a.cin <= 0 || a.cin % kBlockK != 0) return "input channels must be a multiple of 64";
-  if (a.cout <= 0 || a.cout % 128 != 0) return "output channels must be a multiple of 128";
+  if (a.out_nchw) {
+    if (a.cout <= 0 || a.cout > 16 || !a.out_f32 || a.residual || a.gn_part || a.row_scale)
+      return "thin NCHW output needs 1..16 f32 channels without residual or statistics";
+  } else if (a.cout <= 0 || a.cout % 128 != 0) {
+    return "output channels must be a multiple of 128";
+  }
   if (a.out_w <= 0 || a.out_h <= 0 || a.batch <= 0) return "empty convolution";
   const int tile_w = a.out_w >= kBlockM ? kBlockM : a.out_w;
   if (a.out_w % tile_w != 0 || kBlockM % tile_w != 0) return "output width must divide or be a multiple of 128";
@@ -471,7 +495,7 @@ const char* conv_tc_check(const ConvTcArgs& a) {
     return "operands must be 16-byte aligned";
   if (a.residual && (a.ld_res % 8 != 0 || (reinterpret_cast<uintptr_t>(a.residual) & 15)))
     return "residual must be 16-byte aligned";
-  if (a.ld_out % (a.out_f32 ? 4 : 8) != 0 || (reinterpret_cast<uintptr_t>(a.out) & 15))
+  if (!a.out_nchw && (a.ld_out % (a.out_f32 ? 4 : 8) != 0 || (reinterpret_cast<uintptr_t>(a.out) & 15)))
     return "output must be 16-byte aligned";
   if (a.bias && (reinterpret_cast<uintptr_t>(a.bias) & 15)) return "bias must be 16-byte aligned";
   if ((long long)a.batch * a.out_h * a.out_w > 0x7fffffffLL) return "problem too large";
@@ -487,7 +511,7 @@ cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
   if (!encode) return cudaErrorNotSupported;
   const int tile_w = a.out_w >= kBlockM ? kBlockM : a.out_w;
   const int tile_h = kBlockM / tile_w;
-  const int block_n = (a.cout % 256 == 0) ? 256 : 128;
+  const int block_n = a.out_nchw ? 16 : ((a.cout % 256 == 0) ? 256 : 128);
   const CUtensorMapDataType tdt =
       a.dtype == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
 
@@ -508,7 +532,8 @@ cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
   }
   {
     const int k_total = a.ksize * a.ksize * a.cin;
-    cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)a.cout};
+    // Thin outputs read 16 weight rows (the caller pads them with zeros).
+    cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)(a.out_nchw ? 16 : a.cout)};
     cuuint64_t strides[1] = {(cuuint64_t)a.ldw * 2};
     cuuint32_t box[2] = {(cuuint32_t)kBlockK, (cuuint32_t)block_n};
     cuuint32_t estr[2] = {1, 1};
@@ -524,7 +549,7 @@ cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
   p.tiles_x = a.out_w / tile_w;
   p.tiles_y = a.out_h / tile_h;
   p.num_m_tiles = a.batch * p.tiles_x * p.tiles_y;
-  p.num_n_tiles = a.cout / block_n;
+  p.num_n_tiles = a.out_nchw ? 1 : a.cout / block_n;
   p.c_blocks = a.cin / kBlockK;
   p.k_blocks = a.ksize * a.ksize * p.c_blocks;
   p.ksize = a.ksize;
@@ -541,6 +566,11 @@ cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
   const int cpg = a.gn_part ? a.gn_cpg : 0;
   p.gn_part = a.gn_part;
   p.gn_groups = cpg ? a.cout / cpg : 0;
+  p.n_valid = a.cout;
+  p.out_hw = (long long)a.out_h * a.out_w;
+  if (a.out_nchw)
+    return a.dtype == kF16 ? launch_typed<16, kF16, 0>(ta, tb, p, stream)
+                           : launch_typed<16, kBf16, 0>(ta, tb, p, stream);
   if (a.dtype == kF16)
     return block_n == 256 ? launch_cpg<256, kF16>(cpg, ta, tb, p, stream)
                           : launch_cpg<128, kF16>(cpg, ta, tb, p, stream);

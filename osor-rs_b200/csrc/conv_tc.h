@@ -34,6 +34,10 @@ struct ConvTcArgs {
   // and group of gn_cpg channels (gn_cpg 4, 8 or 16).
   float* gn_part = nullptr;
   int gn_cpg = 0;
+  // Thin output: Cout <= 16 channels written as NCHW f32 planes
+  // out[b][c][oy][ox] (out_f32 must be set); the weight buffer holds 16 rows,
+  // rows >= cout zero.
+  int out_nchw = 0;
 };
 
 // nullptr when the tensor-core kernel supports the shape, else a reason.

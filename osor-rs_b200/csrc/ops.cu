@@ -294,6 +294,52 @@ __global__ void nhwc16_to_nchw_f32_kernel(const uint16_t* __restrict__ xb, float
   }
 }
 
+// Column matrix of a thin-input convolution: for output pixel (b, oy, ox),
+// column j < k*k*cin holds input channel j % cin at tap j / cin = (ky, kx)
+// (zero outside the image), columns up to 64 are zero. With pre_w, every input
+// pixel first goes through a 1x1 convolution pre_w [cin][cin] + pre_b (the
+// decoder's post_quant_conv), and padding stays zero as in the reference
+// (the second convolution pads the first one's output). One thread per pixel.
+template <int D>
+__global__ void thin_columns_kernel(const float* __restrict__ x, uint4* __restrict__ cols,
+                                    int batch, int cin, int h, int w, int k, int pad,
+                                    const float* __restrict__ pre_w,
+                                    const float* __restrict__ pre_b) {
+  const long long pix = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long total = (long long)batch * h * w;
+  if (pix >= total) return;
+  const int ox = (int)(pix % w);
+  const int oy = (int)((pix / w) % h);
+  const long long b = pix / ((long long)w * h);
+  const long long plane = (long long)h * w;
+  const float* xb = x + b * cin * plane;
+  const int used = k * k * cin;
+#pragma unroll 1
+  for (int j0 = 0; j0 < 64; j0 += 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = j0 + u;
+      float val = 0.0f;
+      if (j < used) {
+        const int tap = j / cin, ci = j - tap * cin;
+        const int iy = oy + tap / k - pad, ix = ox + tap % k - pad;
+        if (iy >= 0 && iy < h && ix >= 0 && ix < w) {
+          const long long off = (long long)iy * w + ix;
+          if (pre_w) {
+            val = pre_b[ci];
+            for (int c = 0; c < cin; ++c) val += pre_w[ci * cin + c] * __ldg(xb + c * plane + off);
+          } else {
+            val = __ldg(xb + ci * plane + off);
+          }
+        }
+      }
+      v[u] = val;
+    }
+    cols[pix * 8 + j0 / 8] = pack8<D>(v);
+  }
+}
+
 // moments [B,8,h,w] -> sample [B,4,h,w] = (mean + exp(0.5*clamp(logvar,-30,20)) * noise) * scale
 __global__ void posterior_sample_kernel(const float* __restrict__ moments,
                                         const float* __restrict__ noise, float* __restrict__ out,
@@ -399,6 +445,20 @@ cudaError_t nhwc16_to_nchw_f32_launch(int dtype, const void* x, float* y, int ba
     nhwc16_to_nchw_f32_kernel<kF16><<<blocks_for(total, 256), 256, 0, s>>>(xb, y, c, hw, total);
   else
     nhwc16_to_nchw_f32_kernel<kBf16><<<blocks_for(total, 256), 256, 0, s>>>(xb, y, c, hw, total);
+  return cudaGetLastError();
+}
+
+cudaError_t thin_columns_launch(int dtype, const float* x, void* cols, int batch, int cin, int h,
+                                int w, int k, int pad, const float* pre_w, const float* pre_b,
+                                cudaStream_t s) {
+  if (k * k * cin > 64) return cudaErrorInvalidValue;
+  const long long total = (long long)batch * h * w;
+  const unsigned grid = (unsigned)((total + 127) / 128);
+  uint4* c = static_cast<uint4*>(cols);
+  if (dtype == kF16)
+    thin_columns_kernel<kF16><<<grid, 128, 0, s>>>(x, c, batch, cin, h, w, k, pad, pre_w, pre_b);
+  else
+    thin_columns_kernel<kBf16><<<grid, 128, 0, s>>>(x, c, batch, cin, h, w, k, pad, pre_w, pre_b);
   return cudaGetLastError();
 }
 

@@ -89,9 +89,11 @@ class Loader {
     if (!(s = tensor(prefix + ".bias", {cout}, &b)).good()) return s;
     return conv_from(w->data, b->data, cin, cout, k, stride, pad, L);
   }
+  // rows: allocated weight rows (>= cout, zero beyond cout).
   Status conv_from(const float* w, const float* b, int cin, int cout, int k, int stride, int pad,
-                   ConvLayer* L) {
-    std::vector<uint16_t> packed((size_t)cout * k * k * cin);
+                   ConvLayer* L, int rows = 0) {
+    rows = std::max(rows, cout);
+    std::vector<uint16_t> packed((size_t)rows * k * k * cin, to_bits(0.0f, model_->dtype));
     for (int co = 0; co < cout; ++co)
       for (int ci = 0; ci < cin; ++ci)
         for (int ky = 0; ky < k; ++ky)
@@ -104,9 +106,52 @@ class Loader {
     L->stride = stride;
     L->pad = pad;
     L->pad_end = pad;
+    L->w_rows = rows;
     Status s = upload(packed, &L->w);
     if (!s.good()) return s;
     return upload(std::vector<float>(b, b + cout), &L->bias);
+  }
+  // A thin-output convolution (Cout <= 16): weights padded to 16 rows so the
+  // tensor-core kernel's 16-wide output tile can read them.
+  Status thin_out_conv(const std::string& prefix, int cin, int cout, int k, int pad, ConvLayer* L) {
+    const osor_tensor *w, *b;
+    Status s = tensor(prefix + ".weight", {cout, cin, k, k}, &w);
+    if (!s.good()) return s;
+    if (!(s = tensor(prefix + ".bias", {cout}, &b)).good()) return s;
+    return conv_from(w->data, b->data, cin, cout, k, 1, pad, L, 16);
+  }
+  // A thin-input convolution as a 64-column 1x1 layer: column j < k*k*cin
+  // holds tap j / cin, channel j % cin (thin_columns_launch's order).
+  Status thin_in_conv(const std::string& prefix, int cin, int cout, int k, int pad,
+                      ThinInputLayer* L) {
+    const osor_tensor *w, *b;
+    Status s = tensor(prefix + ".weight", {cout, cin, k, k}, &w);
+    if (!s.good()) return s;
+    if (!(s = tensor(prefix + ".bias", {cout}, &b)).good()) return s;
+    if (k * k * cin > 64)
+      return Status::err(OSOR_ERR_INVALID_ARTIFACT, "thin input convolution has too many taps");
+    std::vector<float> cols((size_t)cout * 64, 0.0f);
+    for (int co = 0; co < cout; ++co)
+      for (int ci = 0; ci < cin; ++ci)
+        for (int ky = 0; ky < k; ++ky)
+          for (int kx = 0; kx < k; ++kx)
+            cols[(size_t)co * 64 + (ky * k + kx) * cin + ci] =
+                w->data[(((size_t)co * cin + ci) * k + ky) * k + kx];
+    L->cin = cin;
+    L->k = k;
+    L->pad = pad;
+    return conv_from(cols.data(), b->data, 64, cout, 1, 1, 0, &L->cols);
+  }
+  // The decoder's post_quant_conv (1x1, c -> c) kept in f32 as the thin
+  // input's per-pixel pre-convolution.
+  Status pre_conv(const std::string& prefix, int c, ThinInputLayer* L) {
+    const osor_tensor *w, *b;
+    Status s = tensor(prefix + ".weight", {c, c, 1, 1}, &w);
+    if (!s.good()) return s;
+    if (!(s = tensor(prefix + ".bias", {c}, &b)).good()) return s;
+    if (!(s = upload(std::vector<float>(w->data, w->data + (size_t)c * c), &L->pre_w)).good())
+      return s;
+    return upload(std::vector<float>(b->data, b->data + c), &L->pre_b);
   }
   Status norm(const std::string& prefix, int c, NormLayer* L) {
     if (c % kGroups != 0)
@@ -269,6 +314,22 @@ Status conv16(const Ctx& c, const ConvLayer& L, int xi, int batch, int h, int w,
                        want_stats ? c.b.tstat[oi] : nullptr, &produced);
   c.has_stats[oi] = produced;
   return st;
+}
+
+// Thin-input convolution of NCHW f32 x: its 64-column matrix goes to buffer
+// ci, the 1x1 tensor-core GEMM writes buffer oi (with GroupNorm statistics).
+Status thin_input(const Ctx& c, const ThinInputLayer& L, const float* x, int batch, int h, int w,
+                  int ci, int oi) {
+  cudaError_t e;
+  {
+    OpScope scope("thin_columns", 0.0, 4.0 * batch * h * w * L.cin + 128.0 * batch * h * w, c.s,
+                  1);
+    e = thin_columns_launch(c.dtype, x, c.b.act[ci], batch, L.cin, h, w, L.k, L.pad, L.pre_w,
+                            L.pre_b, c.s);
+  }
+  if (e != cudaSuccess) return cuda_status(e, "thin input columns");
+  c.has_stats[ci] = false;
+  return conv16(c, L.cols, ci, batch, h, w, oi, nullptr, true);
 }
 
 // x (buffer xi) -> resnet output written back into buffer xi.
@@ -465,6 +526,34 @@ Status run_conv(int dtype, const ConvLayer& L, const void* x, int in_mode, int b
       return cuda_status(e, "tensor-core conv");
     }
   }
+  if (in_mode == kLayoutNhwc16 && out_mode == kLayoutNchwF32 && L.cout <= 16 && L.w_rows >= 16 &&
+      !residual) {
+    // Thin output (the VAEs' conv_out): a 16-wide tensor-core tile, NCHW f32 planes.
+    ConvTcArgs a;
+    a.dtype = dtype;
+    a.x = x;
+    a.batch = batch;
+    a.in_h = in_h;
+    a.in_w = in_w;
+    a.cin = L.cin;
+    a.pixel_stride = in_pixel_stride;
+    a.ksize = L.k;
+    a.stride = L.stride;
+    a.pad = L.pad;
+    a.out_h = out_h;
+    a.out_w = out_w;
+    a.cout = L.cout;
+    a.w = L.w;
+    a.ldw = (long long)L.k * L.k * L.cin;
+    a.bias = L.bias;
+    a.out = out;
+    a.out_f32 = 1;
+    a.out_nchw = 1;
+    if (conv_tc_check(a) == nullptr) {
+      OpScope scope("conv_thin_tc", flops, bytes, s, 1);
+      return cuda_status(conv_tc_launch(a, s), "tensor-core thin conv");
+    }
+  }
   DirectConvArgs d;
   d.batch = batch;
   d.in_h = in_h;
@@ -531,8 +620,9 @@ Status vae_create(const osor_tensor* tensors, size_t count, const osor_vae_confi
     m->has_decoder = true;
     Decoder& d = m->dec;
     const int last = ch[3];
-    s = ld.conv("post_quant_conv", 4, 4, 1, 1, 0, &d.post_quant);
-    if (s.good()) s = ld.conv("decoder.conv_in", 4, last, 3, 1, 1, &d.conv_in);
+    // post_quant_conv (1x1, f32) + conv_in (3x3, 4 -> C) as one column GEMM.
+    s = ld.pre_conv("post_quant_conv", 4, &d.conv_in_thin);
+    if (s.good()) s = ld.thin_in_conv("decoder.conv_in", 4, last, 3, 1, &d.conv_in_thin);
     if (s.good()) s = ld.mid("decoder.mid_block", last, &d.mid);
     const int rev[4] = {ch[3], ch[2], ch[1], ch[0]};
     for (int i = 0; s.good() && i < 4; ++i) {
@@ -551,12 +641,12 @@ Status vae_create(const osor_tensor* tensors, size_t count, const osor_vae_confi
       d.up.push_back(st);
     }
     if (s.good()) s = ld.norm("decoder.conv_norm_out", ch[0], &d.norm_out);
-    if (s.good()) s = ld.conv("decoder.conv_out", ch[0], 3, 3, 1, 1, &d.conv_out);
+    if (s.good()) s = ld.thin_out_conv("decoder.conv_out", ch[0], 3, 3, 1, &d.conv_out);
   }
   if (s.good() && (parts & OSOR_PART_ENCODER)) {
     m->has_encoder = true;
     Encoder& en = m->enc;
-    s = ld.conv("encoder.conv_in", 3, ch[0], 3, 1, 1, &en.conv_in);
+    s = ld.thin_in_conv("encoder.conv_in", 3, ch[0], 3, 1, &en.conv_in_thin);
     for (int i = 0; s.good() && i < 4; ++i) {
       StageLayer st;
       const int in = i == 0 ? ch[0] : ch[i - 1];
@@ -578,7 +668,7 @@ Status vae_create(const osor_tensor* tensors, size_t count, const osor_vae_confi
     }
     if (s.good()) s = ld.mid("encoder.mid_block", ch[3], &en.mid);
     if (s.good()) s = ld.norm("encoder.conv_norm_out", ch[3], &en.norm_out);
-    if (s.good()) s = ld.conv("encoder.conv_out", ch[3], 8, 3, 1, 1, &en.conv_out);
+    if (s.good()) s = ld.thin_out_conv("encoder.conv_out", ch[3], 8, 3, 1, &en.conv_out);
     if (s.good()) s = ld.conv("quant_conv", 8, 8, 1, 1, 0, &en.quant);
   }
   cudaSetDevice(prev);
@@ -662,16 +752,10 @@ Status vae_decode(const Vae& m, const float* latents, float* image, int batch, i
   const Decoder& d = m.dec;
   Status st = check_cancel(cancel);
   if (!st.good()) return st;
-  // post_quant_conv (NCHW f32 -> NCHW f32), conv_in (NCHW f32 -> NHWC 16-bit).
-  st = run_conv(c.dtype, d.post_quant, latents, kLayoutNchwF32, batch, h, w, 0, b.f32,
-                kLayoutNchwF32, 0, nullptr, 0, stream);
-  if (!st.good()) return st;
   int xi = 0;
-  st = run_conv(c.dtype, d.conv_in, b.f32, kLayoutNchwF32, batch, h, w, 0, b.act[xi],
-                kLayoutNhwc16, d.conv_in.cout, nullptr, 0, stream);
-  if (!st.good()) return st;
+  if (!(st = thin_input(c, d.conv_in_thin, latents, batch, h, w, 1, xi)).good()) return st;
   if (!(st = mid_block(c, d.mid, xi, batch, h, w)).good()) return st;
-  int ch_now = d.conv_in.cout;
+  int ch_now = d.conv_in_thin.cols.cout;
   for (const StageLayer& up : d.up) {
     for (const ResnetLayer& r : up.resnets) {
       if (!(st = resnet(c, r, xi, batch, h, w)).good()) return st;
@@ -713,10 +797,8 @@ Status vae_encode(const Vae& m, const float* image, float* moments, int batch, i
   if (!st.good()) return st;
   int xi = 0;
   int h = height, w = width;
-  st = run_conv(c.dtype, en.conv_in, image, kLayoutNchwF32, batch, h, w, 0, b.act[xi],
-                kLayoutNhwc16, en.conv_in.cout, nullptr, 0, stream);
-  if (!st.good()) return st;
-  int ch_now = en.conv_in.cout;
+  if (!(st = thin_input(c, en.conv_in_thin, image, batch, h, w, 1, xi)).good()) return st;
+  int ch_now = en.conv_in_thin.cols.cout;
   for (const StageLayer& down : en.down) {
     for (const ResnetLayer& r : down.resnets) {
       if (!(st = resnet(c, r, xi, batch, h, w)).good()) return st;

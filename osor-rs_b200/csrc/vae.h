@@ -28,8 +28,20 @@ struct Status {
 struct ConvLayer {
   int cin = 0, cout = 0, k = 1, stride = 1, pad = 0;
   int pad_end = 0;           // zero padding after the last row / column (encoder downsample: 1)
-  const uint16_t* w = nullptr;  // 16-bit [cout][k*k*cin], (ky, kx, ci)
+  const uint16_t* w = nullptr;  // 16-bit [w_rows][k*k*cin], (ky, kx, ci)
   const float* bias = nullptr;  // [cout]
+  int w_rows = 0;               // allocated weight rows (>= cout; 16 for thin outputs)
+};
+
+// A convolution whose input has few channels (the image or the latent): run
+// as a column matrix of 64 K-columns (thin_columns_launch) times `cols`, a
+// 1x1 layer with Cin = 64. `pre_w`/`pre_b` (nullable) is a 1x1 convolution
+// applied to every input pixel first (the decoder's post_quant_conv).
+struct ThinInputLayer {
+  int cin = 0, k = 3, pad = 1;
+  ConvLayer cols;
+  const float* pre_w = nullptr;
+  const float* pre_b = nullptr;
 };
 
 struct NormLayer {
@@ -63,7 +75,7 @@ struct StageLayer {
 };
 
 struct Decoder {
-  ConvLayer post_quant, conv_in;
+  ThinInputLayer conv_in_thin;  // post_quant_conv + conv_in as one column GEMM
   MidLayer mid;
   std::vector<StageLayer> up;
   NormLayer norm_out;
@@ -71,7 +83,7 @@ struct Decoder {
 };
 
 struct Encoder {
-  ConvLayer conv_in;
+  ThinInputLayer conv_in_thin;
   std::vector<StageLayer> down;
   MidLayer mid;
   NormLayer norm_out;
