@@ -173,6 +173,95 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+CONV_SHAPES = [(4, 512, 512, 128, 128), (4, 512, 512, 256, 256), (4, 256, 256, 512, 512),
+               (4, 128, 128, 1024, 1024), (1, 128, 3, 1024, 1024)]
+GN_SHAPES = [(4, 512, 128, 128), (4, 512, 256, 256), (4, 256, 512, 512), (4, 128, 1024, 1024)]
+
+
+def _timed(fn, steps, warmup, flush):
+    """Mean device ms of fn() over `steps` calls, CUDA events on the current
+    stream, an L2 flush between calls outside the events."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    total = 0.0
+    for i in range(steps):
+        flush.fill_(i & 0xFF)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        total += s.elapsed_time(e)
+    return total / steps
+
+
+def run_ops(args):
+    """Standalone op benchmarks on the BASELINE shapes (one JSON line each):
+    conv3x3 + bias + residual (bf16 NHWC, fp32 accumulate) in TFLOP/s and
+    fused NCHW GroupNorm+SiLU (bf16) in GB/s of one read + one write."""
+    import numpy as np
+    import torch
+    from osor_b200 import ops, workloads
+    from osor_b200.model import device_status
+    tflops_sus, tflops_burst, hbm, src = _peaks()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    if args.op == "conv3x3":
+        shapes = [tuple(int(v) for v in args.shape.split(","))] if args.shape else CONV_SHAPES
+        for b, cin, cout, h, w in shapes:
+            x, wt, bias, res = workloads.conv_inputs(b, cin, cout, h, w, seed=5)
+            conv = ops.BandedConv2d(wt, bias, stride=1, padding=1, dtype=torch.bfloat16)
+            xt = ops.nchw_to_nhwc(torch.from_numpy(x).to(dev))
+            rt = ops.nchw_to_nhwc(torch.from_numpy(res).to(dev))
+            ms = _timed(lambda: conv.forward_checked(xt, residual=rt), args.steps, args.warmup, flush)
+            flop = 2.0 * b * h * w * cout * 9 * cin
+            nbytes = 2.0 * b * h * w * (cin + 2 * cout) + 2.0 * cout * 9 * cin
+            tf = flop / (ms / 1e3) / 1e12
+            path = "tcgen05 implicit GEMM" if cin % 64 == 0 and cout % 128 == 0 else "CUDA-core direct"
+            print(json.dumps({"op": "conv3x3+bias+residual", "shape": [b, cin, cout, h, w],
+                              "dtype": "bf16", "path": path, "ms": round(ms, 4),
+                              "tflops": round(tf, 1), "frac_of_sustained_peak": round(tf / tflops_sus, 4),
+                              "gbs_min_bytes": round(nbytes / (ms / 1e3) / 1e9, 1),
+                              "frac_of_hbm": round(nbytes / (ms / 1e3) / 1e9 / hbm, 4),
+                              "peak_source": src}), flush=True)
+    elif args.op == "groupnorm":
+        shapes = [tuple(int(v) for v in args.shape.split(","))] if args.shape else GN_SHAPES
+        for shape in shapes:
+            x, gamma, beta = workloads.groupnorm_inputs(shape, seed=3)
+            norm = ops.StableGroupNorm(gamma, beta)
+            xt = torch.from_numpy(x).to(torch.bfloat16).to(dev)
+            ms = _timed(lambda: norm.forward_silu(xt), args.steps, args.warmup, flush)
+            nbytes = 4.0 * xt.numel()
+            gbs = nbytes / (ms / 1e3) / 1e9
+            print(json.dumps({"op": "groupnorm32+silu (NCHW, fused)", "shape": list(shape),
+                              "dtype": "bf16", "ms": round(ms, 4), "gbs": round(gbs, 1),
+                              "frac_of_hbm": round(gbs / hbm, 4), "peak_source": src}), flush=True)
+    elif args.op == "encode":
+        from osor_b200.model import NativeModel
+        from osor_b200.weights import random_vae_weights
+        model = NativeModel(random_vae_weights(0), device=0, parts=("encoder",), dtype=args.dtype)
+        img, noise = workloads.encoder_image(4, 1024, 1024, seed=7)
+        it = torch.from_numpy(img).to(dev)
+        nt = torch.from_numpy(noise).to(dev)
+        out = torch.empty((4, 8, 128, 128), dtype=torch.float32, device=dev)
+
+        def step():
+            m = model.encode_moments(it, out=out)
+            mean, logvar = m[:, :4], m[:, 4:].clamp(-30.0, 20.0)
+            return mean + torch.exp(0.5 * logvar) * nt
+
+        ms = _timed(step, args.steps, args.warmup, flush)
+        print(json.dumps({"op": "vae encode (moments + posterior sample)", "shape": [4, 3, 1024, 1024],
+                          "dtype": args.dtype, "ms": round(ms, 3),
+                          "mpx_per_s": round(4 * 1024 * 1024 / 1e6 / (ms / 1e3), 1),
+                          "tflops": round(19.52 / (ms / 1e3), 1)}), flush=True)
+    if device_status(0) != 0:
+        raise SystemExit("device status reported a kernel wait timeout")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -181,6 +270,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--dtype", default="f16", choices=["f16", "bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op", default="decode", choices=["decode", "conv3x3", "groupnorm", "encode"],
+                    help="decode: the headline line; others: standalone op lines")
+    ap.add_argument("--shape", default=None, help="comma-separated shape for --op conv3x3/groupnorm")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -190,6 +282,9 @@ def main():
 
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.op != "decode":
+        run_ops(args)
         return
 
     import numpy as np

@@ -61,6 +61,13 @@ struct TcParams {
   // Thin-output mode (BLOCK_N 16): n_valid NCHW f32 planes of out_hw pixels.
   int n_valid;
   long long out_hw;
+  // Fused nearest-2x upsample (phases == 4): the tile grid runs over the
+  // low_h x low_w input, each tile is computed for the four output phases
+  // with weight rows [phase * cout_total, ...), and results land on the
+  // 2*low_h x 2*low_w output. phases == 1: plain convolution.
+  int phases;
+  int low_h, low_w;
+  int cout_total;  // weight rows per phase (0 when phases == 1)
 };
 
 template <int BLOCK_N>
@@ -147,7 +154,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
-  const int num_tiles = p.num_m_tiles * p.num_n_tiles;
+  // Tile order: m_tile (outer), upsample phase, n_tile (inner), so CTAs that
+  // run together share input rows in L2.
+  const int tiles_per_m = p.phases * p.num_n_tiles;
+  const int num_tiles = p.num_m_tiles * tiles_per_m;
   const int tiles_per_image = p.tiles_x * p.tiles_y;
 
   if (warp == 0) {
@@ -157,14 +167,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m_tile = tile / p.num_n_tiles;
-        const int n_tile = tile - m_tile * p.num_n_tiles;
+        const int m_tile = tile / tiles_per_m;
+        const int mrem = tile - m_tile * tiles_per_m;
+        const int ph = mrem / p.num_n_tiles;
+        const int n_tile = mrem - ph * p.num_n_tiles;
         const int img = m_tile / tiles_per_image;
         const int rem = m_tile - img * tiles_per_image;
         const int ty = rem / p.tiles_x;
         const int tx = rem - ty * p.tiles_x;
-        const int ox = tx * p.tile_w * p.stride - p.pad;
-        const int oy = ty * p.tile_h * p.stride - p.pad;
+        // Upsample phase (a, b) = (ph >> 1, ph & 1): a 2x2 conv on the
+        // low-res input starting one row / column up-left for a / b = 0.
+        const int pad_y = p.phases == 4 ? 1 - (ph >> 1) : p.pad;
+        const int pad_x = p.phases == 4 ? 1 - (ph & 1) : p.pad;
+        const int ox = tx * p.tile_w * p.stride - pad_x;
+        const int oy = ty * p.tile_h * p.stride - pad_y;
+        const int b_row = ph * p.cout_total + n_tile * BLOCK_N;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
             ok = false;
@@ -177,8 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
           tma_load_4d(smem_a + stage * kABytes, &tmap_a, &full[stage], cb * kBlockK, ox + kx,
                       oy + ky, img);
-          tma_load_2d(smem_b + stage * Cfg::kBBytes, &tmap_b, &full[stage], kb * kBlockK,
-                      n_tile * BLOCK_N);
+          tma_load_2d(smem_b + stage * Cfg::kBBytes, &tmap_b, &full[stage], kb * kBlockK, b_row);
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
@@ -265,10 +281,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       // below use a named barrier that all of them must reach.
       if (!epilogue_all(mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;
       tc_fence_after();
-      const int m_tile = tile / p.num_n_tiles;
-      const int n_tile = tile - m_tile * p.num_n_tiles;
+      const int m_tile = tile / tiles_per_m;
+      const int mrem = tile - m_tile * tiles_per_m;
+      const int ph = mrem / p.num_n_tiles;
+      const int n_tile = mrem - ph * p.num_n_tiles;
       const long long m = (long long)m_tile * kBlockM + row;
       const float scale = p.row_scale ? __ldg(p.row_scale + m) : 1.0f;
+      // Output row of pixel m: itself, or for an upsample phase (a, b) the
+      // high-res pixel (img, 2i + a, 2j + b) of low-res pixel (img, i, j).
+      long long orow = m;
+      // GroupNorm partial slot: tiles of one image stay contiguous (phase-major
+      // within the image for the upsampled output).
+      int stat_slot = m_tile;
+      if (p.phases == 4) {
+        const long long low_hw = (long long)p.low_h * p.low_w;
+        const long long img = m / low_hw;
+        const long long rem = m - img * low_hw;
+        const long long i = rem / p.low_w, j = rem - (rem / p.low_w) * p.low_w;
+        orow = (img * 2 * p.low_h + 2 * i + (ph >> 1)) * (2LL * p.low_w) + 2 * j + (ph & 1);
+        const int mt_img = m_tile / tiles_per_image;
+        stat_slot = (mt_img * 4 + ph) * tiles_per_image + (m_tile - mt_img * tiles_per_image);
+      }
       if constexpr (BLOCK_N == 16) {
         // Thin output (Cout <= 16, weights zero-padded to 16 rows): the first
         // n_valid channels as NCHW f32 planes; a warp writes 32 consecutive
@@ -309,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (p.residual) {
           const uint4* r4 = reinterpret_cast<const uint4*>(
-              static_cast<const uint16_t*>(p.residual) + m * p.ld_res + n0);
+              static_cast<const uint16_t*>(p.residual) + orow * p.ld_res + n0);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             float f[8];
@@ -319,13 +352,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (p.out_f32) {
-          float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) + m * p.ld_out + n0);
+          float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) + orow * p.ld_out + n0);
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         } else {
           uint4* o4 =
-              reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + m * p.ld_out + n0);
+              reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + orow * p.ld_out + n0);
           uint32_t pk[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) pk[j] = Elem<D>::pack(v[2 * j], v[2 * j + 1]);
@@ -386,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             merge_equal(ma, qa, stat_smem[(1 * 64 + t) * 2], stat_smem[(1 * 64 + t) * 2 + 1], n);
             merge_equal(mb, qb, stat_smem[(3 * 64 + t) * 2], stat_smem[(3 * 64 + t) * 2 + 1], n);
             merge_equal(ma, qa, mb, qb, 2.0f * n);
-            float* dst = p.gn_part + ((long long)m_tile * p.gn_groups + n_tile * kG + t) * 2;
+            float* dst = p.gn_part + ((long long)stat_slot * p.gn_groups + n_tile * kG + t) * 2;
             dst[0] = ma;
             dst[1] = qa;
           }
@@ -456,7 +489,7 @@ cudaError_t launch_typed(const CUtensorMap& ta, const CUtensorMap& tb, const TcP
     if (e != cudaSuccess) return e;
     configured[device] = true;
   }
-  const int tiles = p.num_m_tiles * p.num_n_tiles;
+  const int tiles = p.num_m_tiles * p.phases * p.num_n_tiles;
   const int grid = tiles < sm_count(device) ? tiles : sm_count(device);
   conv_tc_kernel<BLOCK_N, D, CPG><<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
   return cudaGetLastError();
@@ -476,7 +509,13 @@ cudaError_t launch_cpg(int cpg, const CUtensorMap& ta, const CUtensorMap& tb, co
 }  // namespace
 
 const char* conv_tc_check(const ConvTcArgs& a) {
-  if (a.ksize != 1 && a.ksize != 3) return "tensor-core convolution supports 1x1 and 3x3 kernels";
+  if (a.upsample) {
+    if (a.ksize != 2 || a.stride != 1 || a.out_nchw || a.out_f32)
+      return "the fused upsample convolution takes 2x2 phase weights and a 16-bit output";
+    if (a.out_h != a.in_h || a.out_w != a.in_w) return "upsample tile grid must be the input grid";
+  } else if (a.ksize != 1 && a.ksize != 3) {
+    return "tensor-core convolution supports 1x1 and 3x3 kernels";
+  }
   if (a.stride != 1 && a.stride != 2) return "tensor-core convolution supports stride 1 and 2";
   if (a.cin <= 0 || a.cin % kBlockK != 0) return "input channels must be a multiple of 64";
   if (a.out_nchw) {
@@ -533,7 +572,10 @@ cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
   {
     const int k_total = a.ksize * a.ksize * a.cin;
     // Thin outputs read 16 weight rows (the caller pads them with zeros).
-    cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)(a.out_nchw ? 16 : a.cout)};
+    // Weight rows: 16 for a thin output (zero-padded by the caller), four
+    // phase blocks of cout for the fused upsample, else cout.
+    const int rows = a.out_nchw ? 16 : (a.upsample ? 4 * a.cout : a.cout);
+    cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)a.ldw * 2};
     cuuint32_t box[2] = {(cuuint32_t)kBlockK, (cuuint32_t)block_n};
     cuuint32_t estr[2] = {1, 1};
@@ -568,6 +610,10 @@ cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
   p.gn_groups = cpg ? a.cout / cpg : 0;
   p.n_valid = a.cout;
   p.out_hw = (long long)a.out_h * a.out_w;
+  p.phases = a.upsample ? 4 : 1;
+  p.low_h = a.in_h;
+  p.low_w = a.in_w;
+  p.cout_total = a.upsample ? a.cout : 0;
   if (a.out_nchw)
     return a.dtype == kF16 ? launch_typed<16, kF16, 0>(ta, tb, p, stream)
                            : launch_typed<16, kBf16, 0>(ta, tb, p, stream);

@@ -38,6 +38,12 @@ struct ConvTcArgs {
   // out[b][c][oy][ox] (out_f32 must be set); the weight buffer holds 16 rows,
   // rows >= cout zero.
   int out_nchw = 0;
+  // Fused nearest-2x upsample + 3x3 conv: x is the low-res input
+  // [batch][in_h][in_w], out is [batch][2 in_h][2 in_w][cout] (ld_out), ksize
+  // is 2 and w holds the four phase weights [4 * cout][2 * 2 * cin] (phase
+  // (a, b) = rows [(2a + b) * cout, ...)); out_h / out_w equal in_h / in_w.
+  // GroupNorm partials (gn_part) are written per phase tile, image-major.
+  int upsample = 0;
 };
 
 // nullptr when the tensor-core kernel supports the shape, else a reason.

@@ -35,7 +35,8 @@ namespace osor {
 namespace {
 
 // 32768 chunk partials (3 floats each) plus 1024 group counters: enough for
-// batch 8 of the largest standalone shape, [*, 128, 1024, 1024] in 16-bit.
+// batch 4 of the largest standalone shape, [*, 128, 1024, 1024] in 16-bit
+// (4 * 32 groups * 171 chunks of 48 KiB = 21888 partials).
 constexpr size_t kNoAllocScratchBytes = 32768 * 3 * sizeof(float) + 1024 * sizeof(int);
 
 static __device__ __align__(256) unsigned char g_gn_noalloc_scratch[kNoAllocScratchBytes];

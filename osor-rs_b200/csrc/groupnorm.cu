@@ -28,6 +28,25 @@ namespace {
 
 __device__ __forceinline__ float silu_f(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
+// SiLU for 16-bit outputs: x * sigmoid(x) = h + h * tanh(h) with h = x / 2,
+// one MUFU tanh.approx (max relative error about 2^-11, below the 16-bit
+// output rounding) instead of an exponential and a reciprocal.
+__device__ __forceinline__ float silu_16(float v) {
+  const float h = 0.5f * v;
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
+  return fmaf(h, t, h);
+}
+
+template <typename T>
+__device__ __forceinline__ float silu_t(float v) {
+  if constexpr (sizeof(T) == 2) {
+    return silu_16(v);
+  } else {
+    return silu_f(v);
+  }
+}
+
 // Element access for the standalone kernel: float, bf16 or f16 storage.
 template <typename T>
 struct Scalar;
@@ -104,40 +123,56 @@ __global__ void __launch_bounds__(kFusedThreads)
                          const FusedParams p) {
   using S = Scalar<T>;
   constexpr int V = S::V;
+  // Two chunk buffers: the bulk load of the next item runs while this item's
+  // statistics, group wait and normalization proceed.
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  T* buf = reinterpret_cast<T*>(smem_raw);
+  T* bufs[2] = {reinterpret_cast<T*>(smem_raw), reinterpret_cast<T*>(smem_raw) + p.chunk};
   __shared__ float red[8];
-  __shared__ float stat[2];
-  __shared__ __align__(8) uint64_t bar;
+  __shared__ __align__(8) uint64_t bars[2];
   __shared__ int abort_flag;
   if (threadIdx.x == 0) {
-    mbar_init(&bar, 1);
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
     abort_flag = 0;
     fence_mbarrier_init();
   }
   __syncthreads();
-  uint32_t bar_phase = 0;
+  uint32_t bar_phase[2] = {0, 0};
   const int cpg = p.channels / p.groups;
   const long long items = (long long)p.groups_total * p.chunks_per_group;
-  for (long long item = blockIdx.x; item < items; item += gridDim.x) {
+  // Issues the bulk load of `it` into buffer `b` (thread 0, aligned path).
+  auto issue = [&](long long it, int b) {
+    const int g = (int)(it / p.chunks_per_group);
+    const long long beg = (it - (long long)g * p.chunks_per_group) * p.chunk;
+    const uint32_t bytes = (uint32_t)min(p.chunk, p.count - beg) * (uint32_t)sizeof(T);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(x + (long long)g * p.count + beg);
+    mbar_arrive_expect_tx(&bars[b], bytes);
+    for (uint32_t off = 0; off < bytes; off += 65536u)
+      bulk_load(reinterpret_cast<uint8_t*>(bufs[b]) + off, src + off, min(65536u, bytes - off),
+                &bars[b]);
+  };
+  bool pending[2] = {false, false};  // thread 0: a bulk load into buffer b is in flight
+  if (p.use_bulk && threadIdx.x == 0 && (long long)blockIdx.x < items) {
+    issue(blockIdx.x, 0);
+    pending[0] = true;
+  }
+  int cur = 0;
+  for (long long item = blockIdx.x; item < items; item += gridDim.x, cur ^= 1) {
+    T* buf = bufs[cur];
     const int group = (int)(item / p.chunks_per_group);
     const int ci = (int)(item - (long long)group * p.chunks_per_group);
     const long long begin = (long long)ci * p.chunk;
     const int n = (int)min(p.chunk, p.count - begin);
     const long long base = (long long)group * p.count + begin;
-    // ---- load the chunk into shared memory
+    // ---- the chunk in shared memory
     if (p.use_bulk) {
-      if (threadIdx.x == 0) {
-        const uint32_t bytes = (uint32_t)n * (uint32_t)sizeof(T);
-        mbar_arrive_expect_tx(&bar, bytes);
-        for (uint32_t off = 0; off < bytes; off += 65536u) {
-          const uint32_t len = min(65536u, bytes - off);
-          bulk_load(reinterpret_cast<uint8_t*>(buf) + off,
-                    reinterpret_cast<const uint8_t*>(x + base) + off, len, &bar);
-        }
+      // The other buffer was released by the previous item's final barrier.
+      if (threadIdx.x == 0 && item + gridDim.x < items) {
+        issue(item + gridDim.x, cur ^ 1);
+        pending[cur ^ 1] = true;
       }
-      mbar_wait(&bar, bar_phase, &abort_flag);
-      bar_phase ^= 1;
+      if (mbar_wait(&bars[cur], bar_phase[cur], &abort_flag)) pending[cur] = false;
+      bar_phase[cur] ^= 1;
       __syncthreads();
       if (abort_flag) break;
     } else {
@@ -195,35 +230,30 @@ __global__ void __launch_bounds__(kFusedThreads)
         }
       }
       __threadfence();
-      if (ok) {
-        // Chan merge of the group's partials in chunk order.
-        const volatile float* part = p.partials + (long long)group * p.chunks_per_group * 3;
-        float cnt = part[0];
-        float mean = part[1];
-        float M2 = part[2];
-        for (int c = 1; c < p.chunks_per_group; ++c) {
-          const float nb = part[3 * c + 0], mb = part[3 * c + 1], m2b = part[3 * c + 2];
-          const float tot = cnt + nb;
-          const float delta = mb - mean;
-          mean += delta * (nb / tot);
-          M2 += m2b + delta * delta * (cnt * (nb / tot));
-          cnt = tot;
-        }
-        const float var = M2 / (float)p.count;
-        stat[0] = mean;
-        stat[1] = 1.0f / sqrtf(var + p.eps);
-        if (ci == 0 && p.stats_out) {
-          p.stats_out[2 * group] = mean;
-          p.stats_out[2 * group + 1] = var;
-        }
-      } else {
-        abort_flag = 1;
-      }
+      if (!ok) abort_flag = 1;
     }
     __syncthreads();
     if (abort_flag) break;
-    const float mean = stat[0];
-    const float rstd = stat[1];
+    // ---- merge the group's chunk partials, all threads at once:
+    //   mean = sum(n_c mean_c) / N,  M2 = sum(M2_c) + sum(n_c (mean_c - mean)^2).
+    // Every CTA of the group reduces the same values in the same order, so all
+    // derive identical statistics. Loads go to L2 (__ldcg): other CTAs wrote them.
+    const float* part = p.partials + (long long)group * p.chunks_per_group * 3;
+    float s1 = 0.0f;
+    for (int c = threadIdx.x; c < p.chunks_per_group; c += kFusedThreads)
+      s1 += __ldcg(part + 3 * c) * __ldcg(part + 3 * c + 1);
+    const float mean = block_sum_256(s1, red) / (float)p.count;
+    float s2 = 0.0f;
+    for (int c = threadIdx.x; c < p.chunks_per_group; c += kFusedThreads) {
+      const float d = __ldcg(part + 3 * c + 1) - mean;
+      s2 += __ldcg(part + 3 * c + 2) + __ldcg(part + 3 * c) * d * d;
+    }
+    const float var = block_sum_256(s2, red) / (float)p.count;
+    const float rstd = 1.0f / sqrtf(var + p.eps);
+    if (threadIdx.x == 0 && ci == 0 && p.stats_out) {
+      p.stats_out[2 * group] = mean;
+      p.stats_out[2 * group + 1] = var;
+    }
     // ---- normalize from shared memory, one channel run at a time
     const int g = group % p.groups;
     const long long first = (long long)g * cpg * p.spatial + begin;  // offset inside the image
@@ -241,7 +271,7 @@ __global__ void __launch_bounds__(kFusedThreads)
 #pragma unroll
           for (int j = 0; j < V; ++j) {
             float v = (f[j] - mean) * a + bsh;
-            if (p.silu) v = silu_f(v);
+            if (p.silu) v = silu_t<T>(v);
             f[j] = v;
           }
           S::store(y + base + i, f);
@@ -249,7 +279,7 @@ __global__ void __launch_bounds__(kFusedThreads)
       } else {
         for (int i = pos + threadIdx.x; i < end; i += kFusedThreads) {
           float v = (S::to_f(buf[i]) - mean) * a + bsh;
-          if (p.silu) v = silu_f(v);
+          if (p.silu) v = silu_t<T>(v);
           y[base + i] = S::from_f(v);
         }
       }
@@ -258,6 +288,16 @@ __global__ void __launch_bounds__(kFusedThreads)
       seg_end += p.spatial;
     }
     __syncthreads();  // the buffer is reused by the next item
+  }
+  // After an abandoned wait, let loads still in flight land before exiting.
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; ++b) {
+      if (!pending[b]) continue;
+      const uint32_t addr = smem_u32(&bars[b]);
+      const uint64_t t0 = global_timer_ns();
+      while (!mbar_try_wait(addr, bar_phase[b]) && global_timer_ns() - t0 < kWaitLimitNs) {
+      }
+    }
   }
 }
 
@@ -458,7 +498,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       float a = (f[j] - mu[j]) * sc[j] + sh[j];
-      if (silu) a = silu_f(a);
+      if (silu) a = silu_16(a);
       f[j] = a;
     }
     return pack8<D>(f);
@@ -524,7 +564,8 @@ GnFusedPlan gn_fused_plan(int batch, int channels, long long spatial, int groups
   plan.count = (long long)(channels / groups) * spatial;
   plan.grid = num_sms() * kGnFusedCtasPerSm;
   // Chunk capacity: fits kGnFusedSmemBytes, multiple of 16 bytes.
-  const long long cap = kGnFusedSmemBytes / elem_bytes;
+  // Chunk capacity: half of the shared memory (two buffers).
+  const long long cap = kGnFusedSmemBytes / 2 / elem_bytes;
   long long chunks = (plan.count + cap - 1) / cap;
   if (chunks < 1) chunks = 1;
   const long long align = 16 / elem_bytes;
@@ -575,7 +616,7 @@ cudaError_t gn_fused_launch(const T* x, T* y, const float* gamma, const float* b
     if (e != cudaSuccess) return e;
     configured[device] = true;
   }
-  const int smem = (int)(plan.chunk * sizeof(T));
+  const int smem = (int)(2 * plan.chunk * sizeof(T));
   const long long items = (long long)plan.groups_total * plan.chunks_per_group;
   int grid = plan.grid;
   if (items < grid) grid = (int)items;

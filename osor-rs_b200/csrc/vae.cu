@@ -111,6 +111,33 @@ class Loader {
     if (!s.good()) return s;
     return upload(std::vector<float>(b, b + cout), &L->bias);
   }
+  // The conv of an UpBlock's upsampler (3x3 after a nearest 2x upsample).
+  // Output pixel (2i + a, 2j + b) reads upsampled rows 2i + a - 1 .. 2i + a + 1,
+  // i.e. low-res rows i - 1 + a + {0, 1}: tap ky lands on low-res tap
+  // ty = a ? (ky == 2) : (ky != 0) (same for columns). Summing the taps that
+  // land on the same low-res pixel gives four 2x2 kernels with 4/9 of the
+  // work; the reference upsamples then convolves (vae_decoder.rs:38-49).
+  Status upsample_conv(const std::string& prefix, int c, ConvLayer* L) {
+    Status s = conv(prefix, c, c, 3, 1, 1, L);
+    if (!s.good()) return s;
+    const osor_tensor* w;
+    if (!(s = tensor(prefix + ".weight", {c, c, 3, 3}, &w)).good()) return s;
+    std::vector<float> acc((size_t)4 * c * 4 * c, 0.0f);
+    for (int a = 0; a < 2; ++a)
+      for (int b = 0; b < 2; ++b)
+        for (int co = 0; co < c; ++co)
+          for (int ci = 0; ci < c; ++ci)
+            for (int ky = 0; ky < 3; ++ky)
+              for (int kx = 0; kx < 3; ++kx) {
+                const int ty = a ? (ky == 2) : (ky != 0);
+                const int tx = b ? (kx == 2) : (kx != 0);
+                acc[((size_t)(a * 2 + b) * c + co) * 4 * c + (ty * 2 + tx) * c + ci] +=
+                    w->data[(((size_t)co * c + ci) * 3 + ky) * 3 + kx];
+              }
+    std::vector<uint16_t> packed(acc.size());
+    for (size_t i = 0; i < acc.size(); ++i) packed[i] = to_bits(acc[i], model_->dtype);
+    return upload(packed, &L->w_up);
+  }
   // A thin-output convolution (Cout <= 16): weights padded to 16 rows so the
   // tensor-core kernel's 16-wide output tile can read them.
   Status thin_out_conv(const std::string& prefix, int cin, int cout, int k, int pad, ConvLayer* L) {
@@ -314,6 +341,52 @@ Status conv16(const Ctx& c, const ConvLayer& L, int xi, int batch, int h, int w,
                        want_stats ? c.b.tstat[oi] : nullptr, &produced);
   c.has_stats[oi] = produced;
   return st;
+}
+
+// Nearest 2x upsample + 3x3 conv of buffer xi (low-res h x w) into buffer oi
+// (2h x 2w) as one tensor-core launch over the four phase kernels, with the
+// output's GroupNorm statistics. *fused = false (and nothing runs) when the
+// shape does not tile; the caller then upsamples and convolves separately.
+Status upsample_conv(const Ctx& c, const ConvLayer& L, int xi, int batch, int h, int w, int oi,
+                     bool* fused) {
+  *fused = false;
+  if (!L.w_up) return Status::ok();
+  ConvTcArgs a;
+  a.dtype = c.dtype;
+  a.x = c.b.act[xi];
+  a.batch = batch;
+  a.in_h = h;
+  a.in_w = w;
+  a.cin = L.cin;
+  a.pixel_stride = L.cin;
+  a.ksize = 2;
+  a.stride = 1;
+  a.pad = 0;
+  a.out_h = h;
+  a.out_w = w;
+  a.cout = L.cout;
+  a.w = L.w_up;
+  a.ldw = 4LL * L.cin;
+  a.bias = L.bias;
+  a.out = c.b.act[oi];
+  a.ld_out = L.cout;
+  a.upsample = 1;
+  const int cpg = L.cout / kGroups;
+  if (L.cout % kGroups == 0 && (cpg == 4 || cpg == 8 || cpg == 16)) {
+    a.gn_part = c.b.tstat[oi];
+    a.gn_cpg = cpg;
+  }
+  if (conv_tc_check(a) != nullptr) return Status::ok();
+  const double px = 4.0 * batch * h * w;
+  // Algorithmic work of the reference's upsample + 3x3 conv; the phase
+  // kernels do 4/9 of it.
+  OpScope scope("upconv_tc", 2.0 * px * L.cout * 9 * L.cin,
+                2.0 * batch * h * w * L.cin + 2.0 * px * L.cout, c.s, 1);
+  const cudaError_t e = conv_tc_launch(a, c.s);
+  if (e != cudaSuccess) return cuda_status(e, "upsample convolution");
+  c.has_stats[oi] = a.gn_part != nullptr;
+  *fused = true;
+  return Status::ok();
 }
 
 // Thin-input convolution of NCHW f32 x: its 64-column matrix goes to buffer
@@ -636,8 +709,8 @@ Status vae_create(const osor_tensor* tensors, size_t count, const osor_vae_confi
       }
       st.resample = i + 1 < 4;
       if (s.good() && st.resample)
-        s = ld.conv("decoder.up_blocks." + std::to_string(i) + ".upsamplers.0.conv", rev[i],
-                    rev[i], 3, 1, 1, &st.resample_conv);
+        s = ld.upsample_conv("decoder.up_blocks." + std::to_string(i) + ".upsamplers.0.conv",
+                             rev[i], &st.resample_conv);
       d.up.push_back(st);
     }
     if (s.good()) s = ld.norm("decoder.conv_norm_out", ch[0], &d.norm_out);
@@ -764,16 +837,28 @@ Status vae_decode(const Vae& m, const float* latents, float* image, int batch, i
     if (!(st = check_cancel(cancel)).good()) return st;
     if (up.resample) {
       const int ui = (xi + 1) % 4;
-      cudaError_t e;
-      {
-        OpScope scope("upsample", 0.0, 10.0 * batch * h * w * ch_now, stream, 1);
-        e = upsample2x_nhwc_launch(b.act[xi], b.act[ui], batch, h, w, ch_now, stream);
+      // Fused path: four 2x2 phase convolutions of the low-res input straight
+      // into the high-res output (buffer ui), then the buffers swap roles.
+      bool fused = false;
+      if (!(st = upsample_conv(c, up.resample_conv, xi, batch, h, w, ui, &fused)).good())
+        return st;
+      if (fused) {
+        xi = ui;
+        h *= 2;
+        w *= 2;
+      } else {
+        cudaError_t e;
+        {
+          OpScope scope("upsample", 0.0, 10.0 * batch * h * w * ch_now, stream, 1);
+          e = upsample2x_nhwc_launch(b.act[xi], b.act[ui], batch, h, w, ch_now, stream);
+        }
+        if (e != cudaSuccess) return cuda_status(e, "upsample");
+        has_stats[ui] = false;
+        h *= 2;
+        w *= 2;
+        if (!(st = conv16(c, up.resample_conv, ui, batch, h, w, xi, nullptr, true)).good())
+          return st;
       }
-      if (e != cudaSuccess) return cuda_status(e, "upsample");
-      has_stats[ui] = false;
-      h *= 2;
-      w *= 2;
-      if (!(st = conv16(c, up.resample_conv, ui, batch, h, w, xi, nullptr, true)).good()) return st;
     }
   }
   const int ti = (xi + 1) % 4;

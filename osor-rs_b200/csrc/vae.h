@@ -31,6 +31,10 @@ struct ConvLayer {
   const uint16_t* w = nullptr;  // 16-bit [w_rows][k*k*cin], (ky, kx, ci)
   const float* bias = nullptr;  // [cout]
   int w_rows = 0;               // allocated weight rows (>= cout; 16 for thin outputs)
+  // For a 3x3 conv that follows a nearest 2x upsample: the four 2x2 phase
+  // convolutions on the low-res input, [4 * cout][2][2][cin] (see
+  // ConvTcArgs::upsample); nullptr otherwise.
+  const uint16_t* w_up = nullptr;
 };
 
 // A convolution whose input has few channels (the image or the latent): run
