@@ -220,7 +220,12 @@ def run_ops(args):
             flop = 2.0 * b * h * w * cout * 9 * cin
             nbytes = 2.0 * b * h * w * (cin + 2 * cout) + 2.0 * cout * 9 * cin
             tf = flop / (ms / 1e3) / 1e12
-            path = "tcgen05 implicit GEMM" if cin % 64 == 0 and cout % 128 == 0 else "CUDA-core direct"
+            if cin % 64 == 0 and cout == 128 and os.environ.get("OSOR_PAIR_CONV", "1") != "0":
+                path = "tcgen05 implicit GEMM, CTA pairs (cta_group::2)"
+            elif cin % 64 == 0 and cout % 128 == 0:
+                path = "tcgen05 implicit GEMM"
+            else:
+                path = "CUDA-core direct"
             print(json.dumps({"op": "conv3x3+bias+residual", "shape": [b, cin, cout, h, w],
                               "dtype": "bf16", "path": path, "ms": round(ms, 4),
                               "tflops": round(tf, 1), "frac_of_sustained_peak": round(tf / tflops_sus, 4),

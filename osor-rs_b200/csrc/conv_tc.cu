@@ -22,6 +22,8 @@
 // (src/native/conv.rs:54-112) with its bias add (:116-145) and the residual
 // add of Resnet::forward_checked (src/native/vae_encoder.rs:150), and the
 // score / value matmuls of attend (src/native/attention.rs:23).
+#include <cstdlib>
+
 #include "common.cuh"
 #include "conv_tc.h"
 
@@ -546,6 +548,14 @@ const char* conv_tc_check(const ConvTcArgs& a) {
 }
 
 cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
+  // Cout = 128 layers whose weights fit in shared memory run on CTA pairs
+  // (conv_tc2.cu). OSOR_PAIR_CONV=0 in the environment keeps them on this
+  // kernel, for comparing the two.
+  static const bool pair_enabled = [] {
+    const char* v = getenv("OSOR_PAIR_CONV");
+    return !(v && v[0] == '0');
+  }();
+  if (pair_enabled && conv_tc2_check(a) == nullptr) return conv_tc2_launch(a, stream);
   EncodeTiledFn encode = encode_fn();
   if (!encode) return cudaErrorNotSupported;
   const int tile_w = a.out_w >= kBlockM ? kBlockM : a.out_w;

@@ -50,4 +50,10 @@ struct ConvTcArgs {
 const char* conv_tc_check(const ConvTcArgs& a);
 cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream);
 
+// Cout = 128 variant on CTA pairs with the weights resident in shared memory
+// (plain 16-bit output, K <= 1152, an even number of 128-pixel tiles).
+// conv_tc_launch dispatches to it when conv_tc2_check passes.
+const char* conv_tc2_check(const ConvTcArgs& a);
+cudaError_t conv_tc2_launch(const ConvTcArgs& a, cudaStream_t stream);
+
 }  // namespace osor

@@ -1,0 +1,547 @@
+// Implicit-GEMM convolution for Cout = 128 on CTA pairs (2-SM tcgen05 MMA).
+//
+// With Cout = 128 the one-CTA kernel (conv_tc.cu) re-fetches the whole weight
+// matrix for every 128-pixel tile and its 128x128 MMAs read both operands
+// from one SM's shared memory; on the 1024^2 VAE layers that leaves the
+// tensor pipe under half busy. Here two CTAs of a cluster cooperate on 256
+// pixels: `tcgen05.mma.cta_group::2` with M = 256, N = 128 takes A rows
+// 0..127 from the even CTA and 128..255 from the odd one, and B rows
+// (output channels) 0..63 / 64..127 likewise, so each SM holds only half of
+// the weights. When that half fits (K <= 1152) it is loaded once per CTA and
+// stays resident in shared memory for every tile the pair computes, and the
+// pipeline stages carry only the A (input) tiles; otherwise each stage also
+// carries the weight slices it needs.
+//
+// Row-shift mode (3x3, stride 1, tiles of one 128-pixel output row): a stage
+// holds 130 consecutive input pixels of one input row and channel block, and
+// the three horizontal taps read it as views starting one pixel (one 128-byte
+// swizzle row) apart, so a tile loads 3 * Cin / 64 stages instead of 9 *.
+//
+// Roles per CTA (320 threads): warp 0 TMA producer, warp 1 TMEM allocator
+// (both CTAs) and MMA issuer (even CTA only), warps 2..9 epilogue (two per
+// TMEM lane quadrant, 64 columns each). The even CTA's barriers gate the
+// MMAs: both CTAs' TMA loads complete on them, the MMA commits arrive on both
+// CTAs' barriers (multicast commit), and both CTAs' epilogues release the
+// accumulators on the even CTA's barrier. No TMA load uses cluster multicast.
+//
+// Reference counterpart: the same convolution as conv_tc.cu
+// (BandedConv2d::forward_checked, src/native/conv.rs:54-145).
+#include <cstdlib>
+
+#include "common.cuh"
+#include "conv_epilogue.cuh"
+#include "conv_tc.h"
+
+namespace osor {
+namespace {
+
+constexpr int kM = 128;           // pixels per CTA
+constexpr int kN = 128;           // output channels of the pair
+constexpr int kBK = 64;           // K block (one 128-byte swizzle row)
+constexpr int kEpiWarps = 8;      // two per TMEM lane quadrant
+constexpr int kThreads2 = 64 + 32 * kEpiWarps;
+constexpr int kAB = kM * kBK * 2;            // A tile bytes (16 KB)
+constexpr int kShiftRows = kM + 2;           // row-shift stage: 130 pixels
+constexpr int kShiftAB = 17 * 1024;          // row-shift A bytes in a stage (>= 130 x 128 B)
+constexpr int kBB = (kN / 2) * kBK * 2;      // B bytes per K block per CTA (8 KB)
+constexpr int kMaxStages = 12;
+constexpr int kMaxResidentKBlocks = 18;      // resident weights: K <= 1152
+constexpr int kStat2 = 4 * 64 * 2 * 4;
+constexpr int kTail2 = 256;                  // barriers, TMEM address, abort flag
+constexpr int kSmem2 = 225 * 1024;
+constexpr int kSmemBudget = kSmem2 - 1024 - kTail2 - kStat2;  // stages + resident weights
+
+struct Tc2Params {
+  int num_m_tiles;         // even
+  int k_blocks, c_blocks;
+  int ksize, stride, pad;
+  int tiles_x, tiles_y, tile_w, tile_h;
+  int row_shift;           // 1: row-shift stages (see above)
+  int units;               // stages per tile: k_blocks, or 3 * c_blocks in row-shift mode
+  int b_resident;          // 1: weight half loaded once; 0: streamed with each stage
+  int stages;              // pipeline depth (<= kMaxStages)
+  int stage_bytes;         // A bytes + streamed B bytes, 1 KB multiple
+  int a_bytes;             // A bytes reserved at the start of a stage
+  uint32_t a_tx;           // A bytes one CTA's load writes
+  uint32_t b_tx;           // streamed B bytes one CTA's loads write per stage
+  const float* bias;
+  const void* residual;
+  long long ld_res;
+  void* out;
+  long long ld_out;
+  const float* row_scale;
+  float* gn_part;
+  int gn_groups;
+};
+
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ bool epi_all(bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, 256, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"((uint32_t)ok)
+      : "memory");
+  return r != 0;
+}
+template <int D, int CPG>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
+    conv_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                    const __grid_constant__ CUtensorMap tmap_b, const Tc2Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* stages = smem;
+  uint8_t* smem_b = smem + p.stages * p.stage_bytes;  // resident weight half
+  uint8_t* tail = smem_b + (p.b_resident ? p.k_blocks * kBB : 0);
+  uint64_t* full = reinterpret_cast<uint64_t*>(tail);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* tfull = empty + kMaxStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* bfull = tempty + 2;
+  uint64_t* drain = bfull + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* stat_smem = reinterpret_cast<float*>(tail + kTail2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * kEpiWarps);  // every epilogue warp of both CTAs
+    }
+    mbar_init(bfull, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, 2 * kN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int pairs = p.num_m_tiles / 2;
+  const int cluster_id = blockIdx.x >> 1;
+  const int clusters = gridDim.x >> 1;
+  const int tiles_per_image = p.tiles_x * p.tiles_y;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      if (p.b_resident) {
+        // Weight half: rows [rank * 64, rank * 64 + 64), all K blocks.
+        if (leader) mbar_arrive_expect_tx(bfull, 2u * p.k_blocks * kBB);
+        for (int kb = 0; kb < p.k_blocks; ++kb)
+          tma_load_2d_pair(smem_b + kb * kBB, &tmap_b, map_to_rank(smem_u32(bfull), 0), kb * kBK,
+                           (int)rank * (kN / 2));
+      }
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int pt = cluster_id; pt < pairs && ok; pt += clusters) {
+        const int m_tile = 2 * pt + (int)rank;
+        const int img = m_tile / tiles_per_image;
+        const int rem = m_tile - img * tiles_per_image;
+        const int ty = rem / p.tiles_x;
+        const int tx = rem - ty * p.tiles_x;
+        const int ox = tx * p.tile_w * p.stride - p.pad;
+        const int oy = ty * p.tile_h * p.stride - p.pad;
+        for (int u = 0; u < p.units; ++u) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          int ky, kx, cb;
+          if (p.row_shift) {
+            ky = u / p.c_blocks;
+            cb = u - ky * p.c_blocks;
+            kx = 0;
+          } else {
+            const int tap = u / p.c_blocks;
+            cb = u - tap * p.c_blocks;
+            ky = tap / p.ksize;
+            kx = tap - ky * p.ksize;
+          }
+          uint8_t* st = stages + stage * p.stage_bytes;
+          const uint32_t bar = map_to_rank(smem_u32(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2u * (p.a_tx + p.b_tx));
+          tma_load_4d_pair(st, &tmap_a, bar, cb * kBK, ox + kx, oy + ky, img);
+          if (!p.b_resident) {
+            // The weight slices of this stage's taps: one, or the three kx
+            // taps of row ky in row-shift mode.
+            const int taps = p.row_shift ? 3 : 1;
+            for (int t = 0; t < taps; ++t) {
+              const int kb = p.row_shift ? (ky * 3 + t) * p.c_blocks + cb : u;
+              tma_load_2d_pair(st + p.a_bytes + t * kBB, &tmap_b, bar, kb * kBK,
+                               (int)rank * (kN / 2));
+            }
+          }
+          if (++stage == p.stages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc = umma_idesc_f32acc(2 * kM, kN, Elem<D>::kUmmaFormat);
+      bool ok = !p.b_resident || mbar_wait(bfull, 0, abort_flag);
+      bool issued = false;
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int pt = cluster_id; pt < pairs && ok; pt += clusters) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kN;
+        for (int u = 0; u < p.units; ++u) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(stages + stage * p.stage_bytes);
+          if (p.row_shift) {
+            // Unit (ky, cb); tap kx reads the stage from pixel row kx on (the
+            // 128-byte swizzle follows the address bits, so a view may start
+            // on any row of a swizzle atom).
+            const int ky = u / p.c_blocks;
+            const int cb = u - ky * p.c_blocks;
+#pragma unroll
+            for (int kx = 0; kx < 3; ++kx) {
+              const uint32_t b_addr =
+                  p.b_resident ? smem_u32(smem_b + ((ky * 3 + kx) * p.c_blocks + cb) * kBB)
+                               : a_addr + p.a_bytes + kx * kBB;
+#pragma unroll
+              for (int k = 0; k < kBK / 16; ++k)
+                umma_bf16_pair(d_tmem, sw128_kmajor_desc(a_addr + kx * 128 + k * 32),
+                               sw128_kmajor_desc(b_addr + k * 32), idesc, (u | kx | k) != 0);
+            }
+          } else {
+            const uint32_t b_addr =
+                p.b_resident ? smem_u32(smem_b + u * kBB) : a_addr + p.a_bytes;
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k)
+              umma_bf16_pair(d_tmem, sw128_kmajor_desc(a_addr + k * 32),
+                             sw128_kmajor_desc(b_addr + k * 32), idesc, (u | k) != 0);
+          }
+          issued = true;
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == p.stages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (!ok && issued) {
+        umma_commit_pair(drain, 0x1);
+        const uint32_t addr = smem_u32(drain);
+        const uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(addr, 0) && global_timer_ns() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;           // TMEM lanes quad*32 .. quad*32+31
+    const int col_half = (warp - 2) >> 2;  // columns col_half*64 .. +63
+    const int row = quad * 32 + lane;
+    const uint32_t tempty_leader[2] = {map_to_rank(smem_u32(&tempty[0]), 0),
+                                       map_to_rank(smem_u32(&tempty[1]), 0)};
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int pt = cluster_id; pt < pairs; pt += clusters) {
+      const int m_tile = 2 * pt + (int)rank;
+      const long long m = (long long)m_tile * kM + row;
+      // The residual does not depend on the accumulator: start its loads
+      // before waiting for the MMAs.
+      uint4 res[8];
+      if (p.residual) {
+        const uint4* r4 = reinterpret_cast<const uint4*>(
+            static_cast<const uint16_t*>(p.residual) + m * p.ld_res + col_half * 64);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) res[j] = __ldg(r4 + j);
+      }
+      if (!epi_all(mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;
+      tc_fence_after();
+      const float scale = p.row_scale ? __ldg(p.row_scale + m) : 1.0f;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int chunk = 2 * col_half + c;
+        uint32_t r[32];
+        tmem_load_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * kN + chunk * 32, r);
+        tmem_wait_ld();
+        const int n0 = chunk * 32;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * scale;
+        if (p.bias) {
+          const float4* b4 = reinterpret_cast<const float4*>(p.bias + n0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 b = __ldg(b4 + j);
+            v[4 * j + 0] += b.x;
+            v[4 * j + 1] += b.y;
+            v[4 * j + 2] += b.z;
+            v[4 * j + 3] += b.w;
+          }
+        }
+        if (p.residual) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float f[8];
+            unpack8<D>(res[4 * c + j], f);
+#pragma unroll
+            for (int t = 0; t < 8; ++t) v[8 * j + t] += f[t];
+          }
+        }
+        uint4* o4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + m * p.ld_out + n0);
+        uint32_t pk[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) pk[j] = Elem<D>::pack(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          o4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+        if constexpr (CPG > 0) {
+          // Statistics of the stored (rounded) values.
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float2 f = Elem<D>::unpack(pk[j]);
+            v[2 * j] = f.x;
+            v[2 * j + 1] = f.y;
+          }
+          gn_chunk_stats<CPG>(v, lane, stat_smem + (quad * 64 + chunk * (32 / CPG)) * 2);
+        }
+      }
+      // Accumulator drained by this warp: release it on the even CTA.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
+      if constexpr (CPG > 0) {
+        epi_sync();
+        constexpr int kG = kN / CPG;
+        const int t = threadIdx.x - 64;
+        if (t < kG) {
+          const float n = 32.0f * CPG;
+          float ma = stat_smem[(0 * 64 + t) * 2], qa = stat_smem[(0 * 64 + t) * 2 + 1];
+          float mb = stat_smem[(2 * 64 + t) * 2], qb = stat_smem[(2 * 64 + t) * 2 + 1];
+          merge_equal_counts(ma, qa, stat_smem[(1 * 64 + t) * 2], stat_smem[(1 * 64 + t) * 2 + 1], n);
+          merge_equal_counts(mb, qb, stat_smem[(3 * 64 + t) * 2], stat_smem[(3 * 64 + t) * 2 + 1], n);
+          merge_equal_counts(ma, qa, mb, qb, 2.0f * n);
+          float* dst = p.gn_part + ((long long)m_tile * p.gn_groups + t) * 2;
+          dst[0] = ma;
+          dst[1] = qa;
+        }
+        epi_sync();
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the pair's MMAs or arrivals are pending
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 2 * kN);
+  }
+}
+
+typedef CUresult (*EncodeTiledFn2)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn2 encode_fn2() {
+  static EncodeTiledFn2 fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<EncodeTiledFn2>(ptr);
+    return static_cast<EncodeTiledFn2>(nullptr);
+  }();
+  return fn;
+}
+
+template <int D, int CPG>
+cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Params& p,
+                    cudaStream_t stream) {
+  // Per device: the shared-memory opt-in and how many pairs fit on the GPU at
+  // once (not every SM need have a partner in its cluster-capable group, so
+  // this can be below SMs / 2). The persistent grid never exceeds it: a pair
+  // that had to wait for another to finish would double the kernel's time.
+  static int resident_pairs[64] = {0};
+  int device = 0;
+  cudaGetDevice(&device);
+  if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
+  if (resident_pairs[device] == 0) {
+    cudaError_t e = cudaFuncSetAttribute(conv_tc2_kernel<D, CPG>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2);
+    if (e != cudaSuccess) return e;
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
+    cfg.blockDim = dim3(kThreads2, 1, 1);
+    cfg.dynamicSmemBytes = kSmem2;
+    cfg.stream = stream;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, conv_tc2_kernel<D, CPG>, &cfg);
+    if (e != cudaSuccess) return e;
+    if (n <= 0) return cudaErrorNotSupported;
+    resident_pairs[device] = n < sms / 2 ? n : sms / 2;
+  }
+  const int pairs = p.num_m_tiles / 2;
+  int clusters = resident_pairs[device];
+  if (clusters > pairs) clusters = pairs;
+  conv_tc2_kernel<D, CPG><<<2 * clusters, kThreads2, kSmem2, stream>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+const char* conv_tc2_check(const ConvTcArgs& a) {
+  if (a.upsample || a.out_nchw || a.out_f32) return "pair kernel: plain 16-bit output only";
+  if (a.cout != kN) return "pair kernel: Cout must be 128";
+  if (a.ksize != 1 && a.ksize != 3) return "pair kernel: 1x1 or 3x3";
+  if (a.stride != 1 && a.stride != 2) return "pair kernel: stride 1 or 2";
+  if (a.cin <= 0 || a.cin % kBK != 0) return "pair kernel: Cin % 64";
+  if (a.out_w <= 0 || a.out_h <= 0 || a.batch <= 0) return "empty convolution";
+  const int tile_w = a.out_w >= kM ? kM : a.out_w;
+  if (a.out_w % tile_w != 0 || kM % tile_w != 0) return "pair kernel: tile width";
+  const int tile_h = kM / tile_w;
+  if (a.out_h % tile_h != 0) return "pair kernel: tile rows";
+  const long long m_tiles = (long long)a.batch * (a.out_w / tile_w) * (a.out_h / tile_h);
+  if (m_tiles % 2 != 0) return "pair kernel: odd tile count";
+  if (a.stride == 2 && 2 * tile_w > 256) return "pair kernel: stride-2 tile too wide";
+  if (a.pixel_stride % 8 != 0 || a.ldw % 8 != 0 || a.ld_out % 8 != 0) return "strides";
+  if ((reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.w) |
+       reinterpret_cast<uintptr_t>(a.out)) & 15)
+    return "alignment";
+  if (a.residual && (a.ld_res % 8 != 0 || (reinterpret_cast<uintptr_t>(a.residual) & 15)))
+    return "residual alignment";
+  if (a.bias && (reinterpret_cast<uintptr_t>(a.bias) & 15)) return "bias alignment";
+  if (a.gn_part && a.gn_cpg != 4 && a.gn_cpg != 8 && a.gn_cpg != 16) return "statistics";
+  if (a.dtype != kBf16 && a.dtype != kF16) return "dtype";
+  if (m_tiles * kM > 0x7fffffffLL) return "problem too large";
+  return nullptr;
+}
+
+cudaError_t conv_tc2_launch(const ConvTcArgs& a, cudaStream_t stream) {
+  EncodeTiledFn2 encode = encode_fn2();
+  if (!encode) return cudaErrorNotSupported;
+  const int tile_w = a.out_w >= kM ? kM : a.out_w;
+  const int tile_h = kM / tile_w;
+  static const bool row_shift_enabled = [] {
+    const char* v = getenv("OSOR_ROW_SHIFT");
+    return !(v && v[0] == '0');
+  }();
+  const bool row_shift = row_shift_enabled && a.ksize == 3 && a.stride == 1 && tile_h == 1;
+  const CUtensorMapDataType tdt =
+      a.dtype == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap ta, tb;
+  {
+    const cuuint64_t ps = (cuuint64_t)a.pixel_stride * 2;
+    cuuint64_t dims[4] = {(cuuint64_t)a.cin, (cuuint64_t)a.in_w, (cuuint64_t)a.in_h,
+                          (cuuint64_t)a.batch};
+    cuuint64_t strides[3] = {ps, ps * a.in_w, ps * a.in_w * a.in_h};
+    cuuint32_t box[4] = {(cuuint32_t)kBK, (cuuint32_t)(tile_w * a.stride),
+                         (cuuint32_t)(tile_h * a.stride), 1};
+    if (row_shift) box[1] = kShiftRows;
+    cuuint32_t estr[4] = {1, (cuuint32_t)a.stride, (cuuint32_t)a.stride, 1};
+    if (encode(&ta, tdt, 4, const_cast<void*>(a.x), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  {
+    const int k_total = a.ksize * a.ksize * a.cin;
+    cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)kN};
+    cuuint64_t strides[1] = {(cuuint64_t)a.ldw * 2};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)(kN / 2)};
+    cuuint32_t estr[2] = {1, 1};
+    if (encode(&tb, tdt, 2, const_cast<void*>(a.w), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  Tc2Params p;
+  p.tile_w = tile_w;
+  p.tile_h = tile_h;
+  p.tiles_x = a.out_w / tile_w;
+  p.tiles_y = a.out_h / tile_h;
+  p.num_m_tiles = a.batch * p.tiles_x * p.tiles_y;
+  p.c_blocks = a.cin / kBK;
+  p.k_blocks = a.ksize * a.ksize * p.c_blocks;
+  p.ksize = a.ksize;
+  p.stride = a.stride;
+  p.pad = a.pad;
+  p.row_shift = row_shift ? 1 : 0;
+  p.units = row_shift ? 3 * p.c_blocks : p.k_blocks;
+  p.b_resident = p.k_blocks <= kMaxResidentKBlocks ? 1 : 0;
+  p.a_bytes = row_shift ? kShiftAB : kAB;
+  p.a_tx = row_shift ? kShiftRows * kBK * 2 : kAB;
+  p.b_tx = p.b_resident ? 0 : (row_shift ? 3 : 1) * kBB;
+  p.stage_bytes = p.a_bytes + (int)p.b_tx;
+  const int resident = p.b_resident ? p.k_blocks * kBB : 0;
+  p.stages = (kSmemBudget - resident) / p.stage_bytes;
+  if (p.stages > kMaxStages) p.stages = kMaxStages;
+  if (p.stages < 2) return cudaErrorInvalidValue;
+  p.bias = a.bias;
+  p.residual = a.residual;
+  p.ld_res = a.ld_res;
+  p.out = a.out;
+  p.ld_out = a.ld_out;
+  p.row_scale = a.row_scale;
+  const int cpg = a.gn_part ? a.gn_cpg : 0;
+  p.gn_part = a.gn_part;
+  p.gn_groups = cpg ? kN / cpg : 0;
+  if (a.dtype == kF16) {
+    switch (cpg) {
+      case 4: return launch2<kF16, 4>(ta, tb, p, stream);
+      case 8: return launch2<kF16, 8>(ta, tb, p, stream);
+      case 16: return launch2<kF16, 16>(ta, tb, p, stream);
+      default: return launch2<kF16, 0>(ta, tb, p, stream);
+    }
+  }
+  switch (cpg) {
+    case 4: return launch2<kBf16, 4>(ta, tb, p, stream);
+    case 8: return launch2<kBf16, 8>(ta, tb, p, stream);
+    case 16: return launch2<kBf16, 16>(ta, tb, p, stream);
+    default: return launch2<kBf16, 0>(ta, tb, p, stream);
+  }
+}
+
+}  // namespace osor

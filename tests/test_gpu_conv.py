@@ -66,6 +66,13 @@ TC_CASES = [
     (1, 64, 16, 32, 128, 1, 1, 0),     # 1x1
     (2, 64, 16, 64, 128, 3, 2, 0),     # encoder downsample: right/bottom pad, stride 2
     (1, 64, 8, 256, 128, 3, 2, 0),     # encoder downsample, 128-px output rows
+    # Cout 128 on CTA pairs: weights resident (K <= 1152) or streamed, 128-px
+    # output rows (row-shift stages) or shorter rows (one stage per tap)
+    (4, 128, 128, 128, 128, 3, 1, 1),  # resident, row shift, several tile pairs per cluster
+    (1, 256, 16, 64, 128, 3, 1, 1),    # streamed, per-tap stages
+    (2, 256, 4, 128, 128, 3, 1, 1),    # streamed, row shift
+    (2, 256, 8, 128, 128, 1, 1, 0),    # 1x1, resident, deep pipeline
+    (3, 64, 8, 16, 128, 3, 1, 1),      # odd number of tiles: one-CTA kernel
 ]
 
 
