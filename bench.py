@@ -278,6 +278,9 @@ def main():
     ap.add_argument("--op", default="decode", choices=["decode", "conv3x3", "groupnorm", "encode"],
                     help="decode: the headline line; others: standalone op lines")
     ap.add_argument("--shape", default=None, help="comma-separated shape for --op conv3x3/groupnorm")
+    ap.add_argument("--batch", type=int, default=BATCH,
+                    help="images per GPU for --op decode (the headline workload is 4; smaller "
+                         "batches are for profiler captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -309,9 +312,9 @@ def main():
 
     weights = random_vae_weights(0, parts=("decoder", "encoder"))
     model = NativeModel(weights, device=local, parts=("decoder",), dtype=args.dtype)
-    lat_host = workloads.decoder_latents(BATCH, LATENT, LATENT, seed=42 + rank)
+    lat_host = workloads.decoder_latents(args.batch, LATENT, LATENT, seed=42 + rank)
     lat = torch.from_numpy(lat_host).to(dev)
-    out = torch.empty((BATCH, 3, IMAGE, IMAGE), dtype=torch.float32, device=dev)
+    out = torch.empty((args.batch, 3, IMAGE, IMAGE), dtype=torch.float32, device=dev)
     flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -348,7 +351,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
-    mpx = BATCH * IMAGE * IMAGE / 1e6
+    mpx = args.batch * IMAGE * IMAGE / 1e6
     value = world * mpx / (ms_per_step / 1e3)
     if device_status(local) != 0:
         raise SystemExit("device status reported a kernel wait timeout")
@@ -374,7 +377,7 @@ def main():
 
     # ------------------------------------------------------------ e2e (host buffers)
     h_lat = torch.from_numpy(lat_host).pin_memory()
-    h_out = torch.empty((BATCH, 3, IMAGE, IMAGE), dtype=torch.float32).pin_memory()
+    h_out = torch.empty((args.batch, 3, IMAGE, IMAGE), dtype=torch.float32).pin_memory()
     d_lat = torch.empty_like(lat)
     for _ in range(2):
         d_lat.copy_(h_lat, non_blocking=True)
@@ -412,8 +415,8 @@ def main():
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": args.dtype,
             "data": "synthetic: N(0,1)/0.13025 latents (seed 42 + rank), random-init weights (seed 0)",
-            "config": {"workload": "SDXL AutoencoderKL decoder [4,4,128,128] -> [4,3,1024,1024] per GPU",
-                       "global_batch": BATCH * world, "latent": [LATENT, LATENT],
+            "config": {"workload": f"SDXL AutoencoderKL decoder [{args.batch},4,128,128] -> [{args.batch},3,1024,1024] per GPU",
+                       "global_batch": args.batch * world, "latent": [LATENT, LATENT],
                        "image": [IMAGE, IMAGE], "parallelism": f"batch split x{world} (no collective)",
                        "l2": "512 MiB L2 flush between timed steps; activations 2.1 GB per buffer",
                        "algorithmic_tflop_per_step": round(total_flops / 1e12, 2)},

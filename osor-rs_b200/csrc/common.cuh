@@ -200,8 +200,12 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
 }
+// Arrive on an mbarrier of any CTA of the cluster. Release at CTA scope: the
+// callers only order their own completed tcgen05 loads (fenced with
+// tcgen05.fence::before_thread_sync) before the arrival, so no cluster-wide
+// fence on their global stores is needed.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+  asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
 }
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* holder, uint32_t ncols) {

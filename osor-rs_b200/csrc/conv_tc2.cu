@@ -38,7 +38,7 @@ namespace {
 constexpr int kM = 128;           // pixels per CTA
 constexpr int kN = 128;           // output channels of the pair
 constexpr int kBK = 64;           // K block (one 128-byte swizzle row)
-constexpr int kEpiWarps = 8;      // two per TMEM lane quadrant
+constexpr int kEpiWarps = 16;     // four per TMEM lane quadrant, 32 columns each
 constexpr int kThreads2 = 64 + 32 * kEpiWarps;
 constexpr int kAB = kM * kBK * 2;            // A tile bytes (16 KB)
 constexpr int kShiftRows = kM + 2;           // row-shift stage: 130 pixels
@@ -46,7 +46,7 @@ constexpr int kShiftAB = 17 * 1024;          // row-shift A bytes in a stage (>=
 constexpr int kBB = (kN / 2) * kBK * 2;      // B bytes per K block per CTA (8 KB)
 constexpr int kMaxStages = 12;
 constexpr int kMaxResidentKBlocks = 18;      // resident weights: K <= 1152
-constexpr int kStat2 = 4 * 64 * 2 * 4;
+constexpr int kStat2 = 2 * 4 * 64 * 2 * 4;  // per accumulator: [quad][group](mean, M2)
 constexpr int kTail2 = 256;                  // barriers, TMEM address, abort flag
 constexpr int kSmem2 = 225 * 1024;
 constexpr int kSmemBudget = kSmem2 - 1024 - kTail2 - kStat2;  // stages + resident weights
@@ -74,19 +74,25 @@ struct Tc2Params {
   int gn_groups;
 };
 
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-__device__ __forceinline__ bool epi_all(bool ok) {
+// The four epilogue warps of one 32-column chunk (one per TMEM lane quadrant)
+// synchronise on named barrier 2 + chunk, 128 threads; warps of different
+// chunks never wait for each other.
+__device__ __forceinline__ void chunk_sync(int bar) {
+  asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool chunk_all(int bar, bool ok) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, 1, 256, p;\n\t"
+      "setp.ne.u32 p, %2, 0;\n\t"
+      "bar.red.and.pred q, %1, 128, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}\n"
       : "=r"(r)
-      : "r"((uint32_t)ok)
+      : "r"(bar), "r"((uint32_t)ok)
       : "memory");
   return r != 0;
 }
+
 template <int D, int CPG>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
     conv_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -271,7 +277,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;           // TMEM lanes quad*32 .. quad*32+31
-    const int col_half = (warp - 2) >> 2;  // columns col_half*64 .. +63
+    const int chunk = (warp - 2) >> 2;   // columns chunk*32 .. +31
+    const int cbar = 2 + chunk;
     const int row = quad * 32 + lane;
     const uint32_t tempty_leader[2] = {map_to_rank(smem_u32(&tempty[0]), 0),
                                        map_to_rank(smem_u32(&tempty[1]), 0)};
@@ -282,84 +289,85 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
       const long long m = (long long)m_tile * kM + row;
       // The residual does not depend on the accumulator: start its loads
       // before waiting for the MMAs.
-      uint4 res[8];
+      uint4 res[4];
       if (p.residual) {
         const uint4* r4 = reinterpret_cast<const uint4*>(
-            static_cast<const uint16_t*>(p.residual) + m * p.ld_res + col_half * 64);
+            static_cast<const uint16_t*>(p.residual) + m * p.ld_res + chunk * 32);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) res[j] = __ldg(r4 + j);
+        for (int j = 0; j < 4; ++j) res[j] = __ldg(r4 + j);
       }
-      if (!epi_all(mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;
+      if (!chunk_all(cbar, mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;
       tc_fence_after();
       const float scale = p.row_scale ? __ldg(p.row_scale + m) : 1.0f;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int chunk = 2 * col_half + c;
-        uint32_t r[32];
-        tmem_load_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * kN + chunk * 32, r);
-        tmem_wait_ld();
-        const int n0 = chunk * 32;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * scale;
-        if (p.bias) {
-          const float4* b4 = reinterpret_cast<const float4*>(p.bias + n0);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float4 b = __ldg(b4 + j);
-            v[4 * j + 0] += b.x;
-            v[4 * j + 1] += b.y;
-            v[4 * j + 2] += b.z;
-            v[4 * j + 3] += b.w;
-          }
-        }
-        if (p.residual) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float f[8];
-            unpack8<D>(res[4 * c + j], f);
-#pragma unroll
-            for (int t = 0; t < 8; ++t) v[8 * j + t] += f[t];
-          }
-        }
-        uint4* o4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + m * p.ld_out + n0);
-        uint32_t pk[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) pk[j] = Elem<D>::pack(v[2 * j], v[2 * j + 1]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          o4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-        if constexpr (CPG > 0) {
-          // Statistics of the stored (rounded) values.
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float2 f = Elem<D>::unpack(pk[j]);
-            v[2 * j] = f.x;
-            v[2 * j + 1] = f.y;
-          }
-          gn_chunk_stats<CPG>(v, lane, stat_smem + (quad * 64 + chunk * (32 / CPG)) * 2);
-        }
-      }
-      // Accumulator drained by this warp: release it on the even CTA.
+      uint32_t r[32];
+      tmem_load_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * kN + chunk * 32, r);
+      tmem_wait_ld();
+      // This warp's part of the accumulator is in registers: release it on
+      // the even CTA so the next tile's MMAs can start.
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
+      const int n0 = chunk * 32;
+      float v[32];
+      if (p.bias) {
+        const float4* b4 = reinterpret_cast<const float4*>(p.bias + n0);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 b = __ldg(b4 + j);
+          v[4 * j + 0] = fmaf(__uint_as_float(r[4 * j + 0]), scale, b.x);
+          v[4 * j + 1] = fmaf(__uint_as_float(r[4 * j + 1]), scale, b.y);
+          v[4 * j + 2] = fmaf(__uint_as_float(r[4 * j + 2]), scale, b.z);
+          v[4 * j + 3] = fmaf(__uint_as_float(r[4 * j + 3]), scale, b.w);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * scale;
+      }
+      if (p.residual) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float f[8];
+          unpack8<D>(res[j], f);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) v[8 * j + t] += f[t];
+        }
+      }
+      uint4* o4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + m * p.ld_out + n0);
+      uint32_t pk[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) pk[j] = Elem<D>::pack(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        o4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
       if constexpr (CPG > 0) {
-        epi_sync();
-        constexpr int kG = kN / CPG;
-        const int t = threadIdx.x - 64;
-        if (t < kG) {
+        // Statistics of the stored (rounded) values.
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float2 f = Elem<D>::unpack(pk[j]);
+          v[2 * j] = f.x;
+          v[2 * j + 1] = f.y;
+        }
+        // Per-quadrant statistics into this accumulator's half of stat_smem;
+        // the chunk's first warp merges the four quadrants. The halves
+        // alternate with the accumulators, and a warp reaches tile i + 2's
+        // writes only after the merging warp has passed tile i + 1's
+        // barrier, i.e. finished reading tile i's half.
+        constexpr int G = 32 / CPG;
+        float* st = stat_smem + acc * (4 * 64 * 2);
+        gn_chunk_stats<CPG>(v, lane, st + (quad * 64 + chunk * G) * 2);
+        chunk_sync(cbar);
+        if (((warp - 2) & 3) == 0 && lane < G) {
+          const int g = chunk * G + lane;
           const float n = 32.0f * CPG;
-          float ma = stat_smem[(0 * 64 + t) * 2], qa = stat_smem[(0 * 64 + t) * 2 + 1];
-          float mb = stat_smem[(2 * 64 + t) * 2], qb = stat_smem[(2 * 64 + t) * 2 + 1];
-          merge_equal_counts(ma, qa, stat_smem[(1 * 64 + t) * 2], stat_smem[(1 * 64 + t) * 2 + 1], n);
-          merge_equal_counts(mb, qb, stat_smem[(3 * 64 + t) * 2], stat_smem[(3 * 64 + t) * 2 + 1], n);
+          float ma = st[(0 * 64 + g) * 2], qa = st[(0 * 64 + g) * 2 + 1];
+          float mb = st[(2 * 64 + g) * 2], qb = st[(2 * 64 + g) * 2 + 1];
+          merge_equal_counts(ma, qa, st[(1 * 64 + g) * 2], st[(1 * 64 + g) * 2 + 1], n);
+          merge_equal_counts(mb, qb, st[(3 * 64 + g) * 2], st[(3 * 64 + g) * 2 + 1], n);
           merge_equal_counts(ma, qa, mb, qb, 2.0f * n);
-          float* dst = p.gn_part + ((long long)m_tile * p.gn_groups + t) * 2;
+          float* dst = p.gn_part + ((long long)m_tile * p.gn_groups + g) * 2;
           dst[0] = ma;
           dst[1] = qa;
         }
-        epi_sync();
       }
       if (++acc == 2) {
         acc = 0;
