@@ -25,6 +25,7 @@
 #include <cstdlib>
 
 #include "common.cuh"
+#include "conv_epilogue.cuh"
 #include "conv_tc.h"
 
 #include <cstdio>
@@ -38,7 +39,6 @@ namespace {
 
 constexpr int kBlockM = 128;
 constexpr int kBlockK = 64;  // 64 bf16 = 128 bytes = one swizzle row
-constexpr int kThreads = 192;
 constexpr int kABytes = kBlockM * kBlockK * 2;
 
 struct TcParams {
@@ -78,39 +78,39 @@ struct TcConfig {
   static constexpr int kStages = BLOCK_N == 256 ? 4 : (BLOCK_N == 128 ? 6 : 8);
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BLOCK_N;
-  static constexpr int kStatBytes = 4 * 64 * 2 * 4;  // [warp][group in tile][mean, M2]
+  // Epilogue warps: four (one per TMEM lane quadrant) for the thin output;
+  // otherwise sixteen, four per quadrant, each owning BLOCK_N / 128
+  // 32-column chunks.
+  static constexpr int kEpiWarps = BLOCK_N == 16 ? 4 : 16;
+  static constexpr int kChunksPerWarp = BLOCK_N == 16 ? 1 : BLOCK_N / 128;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  // GroupNorm tile statistics, one half per accumulator: [quad][group][mean, M2].
+  static constexpr int kStatBytes = 2 * 4 * 64 * 2 * 4;
   static constexpr int kSmemBytes =
       kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ + kStatBytes;
 };
 
-// Named barrier over the 128 epilogue threads (warps 2..5); id 0 is __syncthreads.
-__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
-// AND of `ok` over the 128 epilogue threads (a barrier with a reduction), so
-// that the four warps always take the same branch.
-__device__ __forceinline__ bool epilogue_all(bool ok) {
+// The four epilogue warps of one column slot (one per TMEM lane quadrant)
+// synchronise on named barrier 2 + slot, 128 threads; id 0 is __syncthreads.
+__device__ __forceinline__ void slot_sync(int bar) {
+  asm volatile("bar.sync %0, 128;" ::"r"(bar) : "memory");
+}
+// AND of `ok` over the slot's four warps, so that they take the same branch.
+__device__ __forceinline__ bool slot_all(int bar, bool ok) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, 1, 128, p;\n\t"
+      "setp.ne.u32 p, %2, 0;\n\t"
+      "bar.red.and.pred q, %1, 128, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}\n"
       : "=r"(r)
-      : "r"((uint32_t)ok)
+      : "r"(bar), "r"((uint32_t)ok)
       : "memory");
   return r != 0;
 }
 
-// Merge (mean, M2) of two halves with equal counts n: Chan's formula.
-__device__ __forceinline__ void merge_equal(float& mean, float& m2, float mean_o, float m2_o,
-                                            float n) {
-  const float d = mean_o - mean;
-  m2 = m2 + m2_o + d * d * (0.5f * n);
-  mean = 0.5f * (mean + mean_o);
-}
-
 template <int BLOCK_N, int D, int CPG>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(TcConfig<BLOCK_N>::kThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b, const TcParams p) {
   using Cfg = TcConfig<BLOCK_N>;
@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], Cfg::kEpiWarps);  // lane 0 of every epilogue warp
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -274,21 +274,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quad = warp & 3;
+    const int quad = warp & 3;           // TMEM lanes quad*32 .. quad*32+31
+    const int slot = (warp - 2) >> 2;    // column slot (0 for the thin output)
+    const int sbar = 2 + slot;
     const int row = quad * 32 + lane;
+    constexpr int CPW = Cfg::kChunksPerWarp;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      // The four epilogue warps leave together: the per-tile statistics
-      // below use a named barrier that all of them must reach.
-      if (!epilogue_all(mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;
-      tc_fence_after();
       const int m_tile = tile / tiles_per_m;
       const int mrem = tile - m_tile * tiles_per_m;
       const int ph = mrem / p.num_n_tiles;
       const int n_tile = mrem - ph * p.num_n_tiles;
       const long long m = (long long)m_tile * kBlockM + row;
-      const float scale = p.row_scale ? __ldg(p.row_scale + m) : 1.0f;
       // Output row of pixel m: itself, or for an upsample phase (a, b) the
       // high-res pixel (img, 2i + a, 2j + b) of low-res pixel (img, i, j).
       long long orow = m;
@@ -304,6 +302,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int mt_img = m_tile / tiles_per_image;
         stat_slot = (mt_img * 4 + ph) * tiles_per_image + (m_tile - mt_img * tiles_per_image);
       }
+      // The residual does not depend on the accumulator: start its loads
+      // before waiting for the MMAs.
+      uint4 res[CPW][4];
+      if (BLOCK_N != 16 && p.residual) {
+#pragma unroll
+        for (int c = 0; c < CPW; ++c) {
+          const uint4* r4 = reinterpret_cast<const uint4*>(
+              static_cast<const uint16_t*>(p.residual) + orow * p.ld_res + n_tile * BLOCK_N +
+              (slot * CPW + c) * 32);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) res[c][j] = __ldg(r4 + j);
+        }
+      }
+      // The slot's four warps leave together: the statistics below use a
+      // named barrier that all of them must reach.
+      if (!slot_all(sbar, mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;
+      tc_fence_after();
+      const float scale = p.row_scale ? __ldg(p.row_scale + m) : 1.0f;
       if constexpr (BLOCK_N == 16) {
         // Thin output (Cout <= 16, weights zero-padded to 16 rows): the first
         // n_valid channels as NCHW f32 planes; a warp writes 32 consecutive
@@ -311,6 +327,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t r[16];
         tmem_load_32x32b_x16(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * 16, r);
         tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
         const long long img = m / p.out_hw;
         const long long pix = m - img * p.out_hw;
         float* o = static_cast<float*>(p.out) + img * p.n_valid * p.out_hw + pix;
@@ -319,117 +338,101 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (j < p.n_valid)
             o[(long long)j * p.out_hw] =
                 __uint_as_float(r[j]) * scale + (p.bias ? __ldg(p.bias + j) : 0.0f);
-      }
-#pragma unroll 1
-      for (int chunk = 0; chunk < BLOCK_N / 32; ++chunk) {
-        uint32_t r[32];
-        tmem_load_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BLOCK_N +
-                                 chunk * 32,
-                             r);
-        tmem_wait_ld();
-        const int n0 = n_tile * BLOCK_N + chunk * 32;
-        float v[32];
+      } else {
+        float* st = stat_smem + acc * (4 * 64 * 2);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * scale;
-        if (p.bias) {
-          const float4* b4 = reinterpret_cast<const float4*>(p.bias + n0);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float4 b = __ldg(b4 + j);
-            v[4 * j + 0] += b.x;
-            v[4 * j + 1] += b.y;
-            v[4 * j + 2] += b.z;
-            v[4 * j + 3] += b.w;
+        for (int c = 0; c < CPW; ++c) {
+          const int chunk = slot * CPW + c;
+          uint32_t r[32];
+          tmem_load_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BLOCK_N +
+                                   chunk * 32,
+                               r);
+          tmem_wait_ld();
+          if (c == CPW - 1) {
+            // This warp's columns are all in registers: release the
+            // accumulator so the next tile's MMAs can start.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
           }
-        }
-        if (p.residual) {
-          const uint4* r4 = reinterpret_cast<const uint4*>(
-              static_cast<const uint16_t*>(p.residual) + orow * p.ld_res + n0);
+          const int n0 = n_tile * BLOCK_N + chunk * 32;
+          float v[32];
+          if (p.bias) {
+            const float4* b4 = reinterpret_cast<const float4*>(p.bias + n0);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float f[8];
-            unpack8<D>(__ldg(r4 + j), f);
-#pragma unroll
-            for (int t = 0; t < 8; ++t) v[8 * j + t] += f[t];
-          }
-        }
-        if (p.out_f32) {
-          float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) + orow * p.ld_out + n0);
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        } else {
-          uint4* o4 =
-              reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + orow * p.ld_out + n0);
-          uint32_t pk[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) pk[j] = Elem<D>::pack(v[2 * j], v[2 * j + 1]);
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            o4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-          if constexpr (CPG > 0) {
-            // Statistics of the stored (rounded) values: per group of CPG
-            // channels, exact two-pass (mean, M2) of this pixel, then a
-            // butterfly of equal-count Chan merges over the warp's 32 pixels.
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const float2 f = Elem<D>::unpack(pk[j]);
-              v[2 * j] = f.x;
-              v[2 * j + 1] = f.y;
+            for (int j = 0; j < 8; ++j) {
+              const float4 b = __ldg(b4 + j);
+              v[4 * j + 0] = fmaf(__uint_as_float(r[4 * j + 0]), scale, b.x);
+              v[4 * j + 1] = fmaf(__uint_as_float(r[4 * j + 1]), scale, b.y);
+              v[4 * j + 2] = fmaf(__uint_as_float(r[4 * j + 2]), scale, b.z);
+              v[4 * j + 3] = fmaf(__uint_as_float(r[4 * j + 3]), scale, b.w);
             }
-            constexpr int kGroupsPerChunk = 32 / CPG;
+          } else {
 #pragma unroll
-            for (int gi = 0; gi < kGroupsPerChunk; ++gi) {
-              float mean = 0.0f;
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * scale;
+          }
+          if (p.residual) {
 #pragma unroll
-              for (int c = 0; c < CPG; ++c) mean += v[gi * CPG + c];
-              mean *= 1.0f / CPG;
-              float m2 = 0.0f;
+            for (int j = 0; j < 4; ++j) {
+              float f[8];
+              unpack8<D>(res[c][j], f);
 #pragma unroll
-              for (int c = 0; c < CPG; ++c) {
-                const float d = v[gi * CPG + c] - mean;
-                m2 += d * d;
+              for (int t = 0; t < 8; ++t) v[8 * j + t] += f[t];
+            }
+          }
+          if (p.out_f32) {
+            float4* o4 =
+                reinterpret_cast<float4*>(static_cast<float*>(p.out) + orow * p.ld_out + n0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          } else {
+            uint4* o4 =
+                reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + orow * p.ld_out + n0);
+            uint32_t pk[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) pk[j] = Elem<D>::pack(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              o4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+            if constexpr (CPG > 0) {
+              // Statistics of the stored (rounded) values, per quadrant into
+              // this accumulator's half of stat_smem.
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float2 f = Elem<D>::unpack(pk[j]);
+                v[2 * j] = f.x;
+                v[2 * j + 1] = f.y;
               }
-              float n = (float)CPG;
-#pragma unroll
-              for (int o = 1; o < 32; o <<= 1) {
-                const float mo = __shfl_xor_sync(0xffffffffu, mean, o);
-                const float qo = __shfl_xor_sync(0xffffffffu, m2, o);
-                merge_equal(mean, m2, mo, qo, n);
-                n *= 2.0f;
-              }
-              if (lane == 0) {
-                float* s = stat_smem + (quad * 64 + chunk * kGroupsPerChunk + gi) * 2;
-                s[0] = mean;
-                s[1] = m2;
-              }
+              gn_chunk_stats<CPG>(v, lane, st + (quad * 64 + chunk * (32 / CPG)) * 2);
             }
           }
         }
-      }
-      if constexpr (CPG > 0) {
-        if (!p.out_f32) {
-          // Merge the four warps (quadrants 0..3 in a fixed order) and publish
-          // one (mean, M2) per group of this tile.
-          epilogue_sync();
-          constexpr int kG = BLOCK_N / CPG;
-          const int t = threadIdx.x - 64;
-          if (t < kG) {
-            const float n = 32.0f * CPG;
-            float ma = stat_smem[(0 * 64 + t) * 2], qa = stat_smem[(0 * 64 + t) * 2 + 1];
-            float mb = stat_smem[(2 * 64 + t) * 2], qb = stat_smem[(2 * 64 + t) * 2 + 1];
-            merge_equal(ma, qa, stat_smem[(1 * 64 + t) * 2], stat_smem[(1 * 64 + t) * 2 + 1], n);
-            merge_equal(mb, qb, stat_smem[(3 * 64 + t) * 2], stat_smem[(3 * 64 + t) * 2 + 1], n);
-            merge_equal(ma, qa, mb, qb, 2.0f * n);
-            float* dst = p.gn_part + ((long long)stat_slot * p.gn_groups + n_tile * kG + t) * 2;
-            dst[0] = ma;
-            dst[1] = qa;
+        if constexpr (CPG > 0) {
+          if (!p.out_f32) {
+            // The slot's first warp merges the four quadrants of the slot's
+            // groups and publishes one (mean, M2) per group of this tile. The
+            // stat_smem halves alternate with the accumulators; a warp reaches
+            // tile i + 2's writes only after the merging warp has passed tile
+            // i + 1's barrier, i.e. finished reading tile i's half.
+            slot_sync(sbar);
+            constexpr int G = 32 / CPG;
+            constexpr int kG = BLOCK_N / CPG;
+            if (((warp - 2) & 3) == 0 && lane < CPW * G) {
+              const int g = slot * CPW * G + lane;
+              const float n = 32.0f * CPG;
+              float ma = st[(0 * 64 + g) * 2], qa = st[(0 * 64 + g) * 2 + 1];
+              float mb = st[(2 * 64 + g) * 2], qb = st[(2 * 64 + g) * 2 + 1];
+              merge_equal_counts(ma, qa, st[(1 * 64 + g) * 2], st[(1 * 64 + g) * 2 + 1], n);
+              merge_equal_counts(mb, qb, st[(3 * 64 + g) * 2], st[(3 * 64 + g) * 2 + 1], n);
+              merge_equal_counts(ma, qa, mb, qb, 2.0f * n);
+              float* dst = p.gn_part + ((long long)stat_slot * p.gn_groups + n_tile * kG + g) * 2;
+              dst[0] = ma;
+              dst[1] = qa;
+            }
           }
-          epilogue_sync();
         }
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
@@ -493,7 +496,7 @@ cudaError_t launch_typed(const CUtensorMap& ta, const CUtensorMap& tb, const TcP
   }
   const int tiles = p.num_m_tiles * p.phases * p.num_n_tiles;
   const int grid = tiles < sm_count(device) ? tiles : sm_count(device);
-  conv_tc_kernel<BLOCK_N, D, CPG><<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  conv_tc_kernel<BLOCK_N, D, CPG><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
   return cudaGetLastError();
 }
 
