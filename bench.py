@@ -220,7 +220,10 @@ def run_ops(args):
             flop = 2.0 * b * h * w * cout * 9 * cin
             nbytes = 2.0 * b * h * w * (cin + 2 * cout) + 2.0 * cout * 9 * cin
             tf = flop / (ms / 1e3) / 1e12
-            if cin % 64 == 0 and cout == 128 and os.environ.get("OSOR_PAIR_CONV", "1") != "0":
+            if (cin % 64 == 0 and cout in (64, 128) and w % 256 == 0
+                    and os.environ.get("OSOR_PIXEL_N_CONV", "1") != "0"):
+                path = "tcgen05 implicit GEMM, pixels on N (M=Cout 128, N=256 pixels)"
+            elif cin % 64 == 0 and cout == 128 and os.environ.get("OSOR_PAIR_CONV", "1") != "0":
                 path = "tcgen05 implicit GEMM, CTA pairs (cta_group::2)"
             elif cin % 64 == 0 and cout % 128 == 0:
                 path = "tcgen05 implicit GEMM"

@@ -107,6 +107,32 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
+// Tiled TMA store shared -> global of a 2D box (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0,
+                                             int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until at most N committed bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA, tensor core reads).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Untiled bulk copy global -> shared (16-byte aligned addresses, size % 16 == 0).
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
                                           uint64_t* bar) {
@@ -322,12 +348,47 @@ struct Elem<kF16> {
     return __half22float2(*reinterpret_cast<const __half2*>(&w));
   }
   __device__ static __forceinline__ uint32_t pack(float a, float b) {
-    __half2 h = __floats2half2_rn(sat(a), sat(b));
-    return *reinterpret_cast<uint32_t*>(&h);
+    // Round to nearest with finite saturation in one conversion (lower
+    // half = a).
+    uint32_t r;
+    asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+    return r;
   }
   __device__ static __forceinline__ float to_f(T v) { return __half2float(v); }
   __device__ static __forceinline__ T from_f(float v) { return __float2half_rn(sat(v)); }
 };
+
+// SiLU for 16-bit outputs: x * sigmoid(x) = h + h * tanh(h) with h = x / 2,
+// one MUFU tanh.approx (max relative error about 2^-11, below the 16-bit
+// output rounding) instead of an exponential and a reciprocal.
+__device__ __forceinline__ float silu_16(float v) {
+  const float h = 0.5f * v;
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
+  return fmaf(h, t, h);
+}
+
+// GroupNorm apply, shared by the streaming apply kernel and the convolutions
+// that normalise their input tiles in shared memory, so both produce the same
+// 16-bit value. Per channel, gn_coef_prepare folds (mean, rstd * gamma, beta)
+// into y = x * a + b, pre-halved when SiLU follows, so that
+// silu(y) = h + h * tanh(h) with h = y / 2 costs two FMAs and one MUFU op.
+__device__ __forceinline__ void gn_coef_prepare(float mean, float scale, float shift, bool silu,
+                                                float& a, float& b) {
+  a = scale;
+  b = fmaf(-mean, scale, shift);
+  if (silu) {
+    a *= 0.5f;
+    b *= 0.5f;
+  }
+}
+__device__ __forceinline__ float gn_apply_prepared(float x, float a, float b, bool silu) {
+  const float h = fmaf(x, a, b);
+  if (!silu) return h;
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
+  return fmaf(h, t, h);
+}
 
 // Unpack / pack 8 values held in one 16-byte vector.
 template <int D>

@@ -23,8 +23,11 @@ __device__ __forceinline__ void merge_equal_counts(float& mean, float& m2, float
 // groups it still carries to its partner and merges the other half, so the
 // groups spread over the lanes (32 / CPG groups, 32 * CPG values each) with
 // five merge steps of one or a few groups instead of one butterfly per group.
+// The merge itself: afterwards lane l holds (mean, m2) of group l / CPG of
+// the chunk (32 * CPG values).
 template <int CPG>
-__device__ __forceinline__ void gn_chunk_stats(const float (&v)[32], int lane, float* out) {
+__device__ __forceinline__ void gn_chunk_merge(const float (&v)[32], int lane, float& mean_out,
+                                               float& m2_out) {
   constexpr int G = 32 / CPG;
   float mean[G], m2[G];
 #pragma unroll
@@ -69,12 +72,19 @@ __device__ __forceinline__ void gn_chunk_stats(const float (&v)[32], int lane, f
     }
     n *= 2.0f;
   }
-  // Lane l now holds group l / (32 / G); the first lane of each run writes it.
-  constexpr int kLanesPerGroup = 32 / G;
-  if ((lane & (kLanesPerGroup - 1)) == 0) {
-    const int g = lane / kLanesPerGroup;
-    out[2 * g] = mean[0];
-    out[2 * g + 1] = m2[0];
+  mean_out = mean[0];
+  m2_out = m2[0];
+}
+
+template <int CPG>
+__device__ __forceinline__ void gn_chunk_stats(const float (&v)[32], int lane, float* out) {
+  float mean, m2;
+  gn_chunk_merge<CPG>(v, lane, mean, m2);
+  // Lane l holds group l / CPG; the first lane of each run writes it.
+  if ((lane & (CPG - 1)) == 0) {
+    const int g = lane / CPG;
+    out[2 * g] = mean;
+    out[2 * g + 1] = m2;
   }
 }
 

@@ -513,7 +513,25 @@ cudaError_t launch_cpg(int cpg, const CUtensorMap& ta, const CUtensorMap& tb, co
 
 }  // namespace
 
+namespace {
+// OSOR_PIXEL_N_CONV=0 / OSOR_PAIR_CONV=0 in the environment keep layers off
+// the pixel-N and CTA-pair kernels, for comparing against this one.
+bool env_enabled(const char* name) {
+  const char* v = getenv(name);
+  return !(v && v[0] == '0');
+}
+bool tcn_enabled() {
+  static const bool on = env_enabled("OSOR_PIXEL_N_CONV");
+  return on;
+}
+bool pair_enabled() {
+  static const bool on = env_enabled("OSOR_PAIR_CONV");
+  return on;
+}
+}  // namespace
+
 const char* conv_tc_check(const ConvTcArgs& a) {
+  if (tcn_enabled() && conv_tcn_check(a) == nullptr) return nullptr;
   if (a.upsample) {
     if (a.ksize != 2 || a.stride != 1 || a.out_nchw || a.out_f32)
       return "the fused upsample convolution takes 2x2 phase weights and a 16-bit output";
@@ -526,6 +544,7 @@ const char* conv_tc_check(const ConvTcArgs& a) {
   if (a.out_nchw) {
     if (a.cout <= 0 || a.cout > 16 || !a.out_f32 || a.residual || a.gn_part || a.row_scale)
       return "thin NCHW output needs 1..16 f32 channels without residual or statistics";
+    if (a.w_rows < 16) return "the 16-wide thin tile reads 16 weight rows";
   } else if (a.cout <= 0 || a.cout % 128 != 0) {
     return "output channels must be a multiple of 128";
   }
@@ -551,14 +570,11 @@ const char* conv_tc_check(const ConvTcArgs& a) {
 }
 
 cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
-  // Cout = 128 layers whose weights fit in shared memory run on CTA pairs
-  // (conv_tc2.cu). OSOR_PAIR_CONV=0 in the environment keeps them on this
-  // kernel, for comparing the two.
-  static const bool pair_enabled = [] {
-    const char* v = getenv("OSOR_PAIR_CONV");
-    return !(v && v[0] == '0');
-  }();
-  if (pair_enabled && conv_tc2_check(a) == nullptr) return conv_tc2_launch(a, stream);
+  // 3x3 layers with Cout <= 128 on rows of 256 pixels run with the pixels on
+  // the MMA's N side (conv_tcn.cu); other Cout = 128 layers on CTA pairs
+  // (conv_tc2.cu).
+  if (tcn_enabled() && conv_tcn_check(a) == nullptr) return conv_tcn_launch(a, stream);
+  if (pair_enabled() && conv_tc2_check(a) == nullptr) return conv_tc2_launch(a, stream);
   EncodeTiledFn encode = encode_fn();
   if (!encode) return cudaErrorNotSupported;
   const int tile_w = a.out_w >= kBlockM ? kBlockM : a.out_w;

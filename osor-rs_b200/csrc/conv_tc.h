@@ -22,6 +22,7 @@ struct ConvTcArgs {
   int out_h = 0, out_w = 0, cout = 0;
   const void* w = nullptr;
   long long ldw = 0;
+  int w_rows = 0;  // weight rows allocated (>= cout; the thin one-CTA tile reads 16)
   const float* bias = nullptr;
   const void* residual = nullptr;
   long long ld_res = 0;
@@ -49,6 +50,12 @@ struct ConvTcArgs {
 // nullptr when the tensor-core kernel supports the shape, else a reason.
 const char* conv_tc_check(const ConvTcArgs& a);
 cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream);
+
+// 3x3 stride-1 convolution with Cout 64 / 128 (16-bit NHWC) or <= 16 (thin
+// NCHW f32) and width % 256 == 0, with the pixels on the MMA's N side (256
+// per tile). conv_tc_launch dispatches to it first.
+const char* conv_tcn_check(const ConvTcArgs& a);
+cudaError_t conv_tcn_launch(const ConvTcArgs& a, cudaStream_t stream);
 
 // Cout = 128 variant on CTA pairs with the weights resident in shared memory
 // (plain 16-bit output, K <= 1152, an even number of 128-pixel tiles).

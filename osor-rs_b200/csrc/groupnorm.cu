@@ -28,15 +28,6 @@ namespace {
 
 __device__ __forceinline__ float silu_f(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
-// SiLU for 16-bit outputs: x * sigmoid(x) = h + h * tanh(h) with h = x / 2,
-// one MUFU tanh.approx (max relative error about 2^-11, below the 16-bit
-// output rounding) instead of an exponential and a reciprocal.
-__device__ __forceinline__ float silu_16(float v) {
-  const float h = 0.5f * v;
-  float t;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
-  return fmaf(h, t, h);
-}
 
 template <typename T>
 __device__ __forceinline__ float silu_t(float v) {
@@ -479,14 +470,12 @@ __global__ void __launch_bounds__(256)
   const int r0 = threadIdx.x / vc;
   if (r0 >= rows) return;
   const int b = blockIdx.y;
-  float mu[8], sc[8], sh[8];
+  float ca[8], cb[8];
   const float4* cf = reinterpret_cast<const float4*>(coef + ((long long)b * channels + col * 8) * 4);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float4 c = __ldg(cf + j);
-    mu[j] = c.x;
-    sc[j] = c.y;
-    sh[j] = c.z;
+    gn_coef_prepare(c.x, c.y, c.z, silu != 0, ca[j], cb[j]);
   }
   const uint4* src = x + (long long)b * pixels * vc + col;
   uint4* dst = y + (long long)b * pixels * vc + col;
@@ -496,11 +485,7 @@ __global__ void __launch_bounds__(256)
     float f[8];
     unpack8<D>(q, f);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float a = (f[j] - mu[j]) * sc[j] + sh[j];
-      if (silu) a = silu_16(a);
-      f[j] = a;
-    }
+    for (int j = 0; j < 8; ++j) f[j] = gn_apply_prepared(f[j], ca[j], cb[j], silu != 0);
     return pack8<D>(f);
   };
   for (; pix + 3 * stride < pixels; pix += 4 * stride) {

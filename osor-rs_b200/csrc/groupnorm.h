@@ -38,6 +38,7 @@ struct GnNhwcPlan {
 };
 GnNhwcPlan gn_nhwc_plan(int batch, int channels, long long pixels, int groups);
 
+
 // NHWC 16-bit (dtype kBf16 / kF16) GroupNorm(+SiLU): stats, finalize and
 // apply kernels.
 cudaError_t gn_nhwc_launch(int dtype, const void* x, void* y, const float* gamma, const float* beta,

@@ -343,6 +343,19 @@ Status conv16(const Ctx& c, const ConvLayer& L, int xi, int batch, int h, int w,
   return st;
 }
 
+// GroupNorm(+SiLU) of buffer xi into buffer ti, then convolution L of ti into
+// buffer oi (16-bit NHWC, with tile statistics) or, with oi < 0, into
+// ext_out in out_mode.
+Status gn_conv(const Ctx& c, const NormLayer& N, bool silu, const ConvLayer& L, int xi, int ti,
+               int batch, int h, int w, int oi, void* ext_out, int out_mode,
+               const void* residual) {
+  Status st = gn(c, N, xi, ti, batch, (long long)h * w, silu);
+  if (!st.good()) return st;
+  if (oi >= 0) return conv16(c, L, ti, batch, h, w, oi, residual, true);
+  return run_conv(c.dtype, L, c.b.act[ti], kLayoutNhwc16, batch, h, w, L.cin, ext_out, out_mode,
+                  out_mode == kLayoutNhwc16 ? L.cout : 0, residual, L.cout, c.s);
+}
+
 // Nearest 2x upsample + 3x3 conv of buffer xi (low-res h x w) into buffer oi
 // (2h x 2w) as one tensor-core launch over the four phase kernels, with the
 // output's GroupNorm statistics. *fused = false (and nothing runs) when the
@@ -409,17 +422,17 @@ Status thin_input(const Ctx& c, const ThinInputLayer& L, const float* x, int bat
 Status resnet(const Ctx& c, const ResnetLayer& L, int xi, int batch, int h, int w) {
   Status st = check_cancel(c.cancel);
   if (!st.good()) return st;
-  const long long pixels = (long long)h * w;
   const int ti = (xi + 1) % 4, hi = (xi + 2) % 4, si = (xi + 3) % 4;
   const uint16_t* residual = c.b.act[xi];
   if (L.has_shortcut) {
     if (!(st = conv16(c, L.shortcut, xi, batch, h, w, si, nullptr, false)).good()) return st;
     residual = c.b.act[si];
   }
-  if (!(st = gn(c, L.n1, xi, ti, batch, pixels, true)).good()) return st;
-  if (!(st = conv16(c, L.c1, ti, batch, h, w, hi, nullptr, true)).good()) return st;
-  if (!(st = gn(c, L.n2, hi, ti, batch, pixels, true)).good()) return st;
-  return conv16(c, L.c2, ti, batch, h, w, xi, residual, true);
+  if (!(st = gn_conv(c, L.n1, true, L.c1, xi, ti, batch, h, w, hi, nullptr, kLayoutNhwc16,
+                     nullptr))
+           .good())
+    return st;
+  return gn_conv(c, L.n2, true, L.c2, hi, ti, batch, h, w, xi, nullptr, kLayoutNhwc16, residual);
 }
 
 // Mid-block attention on buffer xi (in place).
@@ -543,6 +556,46 @@ Status attention_core(int dtype, const void* q, const void* k, const void* v, lo
   return Status::ok();
 }
 
+namespace {
+
+// Tensor-core arguments of a convolution: NHWC 16-bit input, and a 16-bit
+// NHWC output or a thin (Cout <= 16) NCHW f32 one. False for other layouts.
+bool tc_args(ConvTcArgs* a, int dtype, const ConvLayer& L, const void* x, int in_mode, int batch,
+             int in_h, int in_w, long long in_pixel_stride, int out_h, int out_w, void* out,
+             int out_mode, long long out_pixel_stride, const void* residual, long long ld_res) {
+  if (in_mode != kLayoutNhwc16) return false;
+  const bool thin = out_mode == kLayoutNchwF32;
+  if (thin && (L.cout > 16 || residual)) return false;
+  a->dtype = dtype;
+  a->x = x;
+  a->batch = batch;
+  a->in_h = in_h;
+  a->in_w = in_w;
+  a->cin = L.cin;
+  a->pixel_stride = in_pixel_stride;
+  a->ksize = L.k;
+  a->stride = L.stride;
+  a->pad = L.pad;
+  a->out_h = out_h;
+  a->out_w = out_w;
+  a->cout = L.cout;
+  a->w = L.w;
+  a->ldw = (long long)L.k * L.k * L.cin;
+  a->w_rows = L.w_rows > L.cout ? L.w_rows : L.cout;
+  a->bias = L.bias;
+  a->residual = residual;
+  a->ld_res = ld_res;
+  a->out = out;
+  a->ld_out = out_pixel_stride;
+  if (thin) {
+    a->out_f32 = 1;
+    a->out_nchw = 1;
+  }
+  return true;
+}
+
+}  // namespace
+
 Status run_conv(int dtype, const ConvLayer& L, const void* x, int in_mode, int batch, int in_h,
                 int in_w, long long in_pixel_stride, void* out, int out_mode,
                 long long out_pixel_stride, const void* residual, long long ld_res,
@@ -561,70 +614,25 @@ Status run_conv(int dtype, const ConvLayer& L, const void* x, int in_mode, int b
   const double out_bytes = out_px * L.cout * (out_mode == kLayoutNchwF32 ? 4 : 2);
   const double bytes = in_bytes + out_bytes + (residual ? out_px * L.cout * 2 : 0.0) +
                        2.0 * L.cout * L.k * L.k * L.cin;
-  if (in_mode == kLayoutNhwc16 && out_mode == kLayoutNhwc16) {
-    ConvTcArgs a;
-    a.dtype = dtype;
-    a.x = x;
-    a.batch = batch;
-    a.in_h = in_h;
-    a.in_w = in_w;
-    a.cin = L.cin;
-    a.pixel_stride = in_pixel_stride;
-    a.ksize = L.k;
-    a.stride = L.stride;
-    a.pad = L.pad;
-    a.out_h = out_h;
-    a.out_w = out_w;
-    a.cout = L.cout;
-    a.w = L.w;
-    a.ldw = (long long)L.k * L.k * L.cin;
-    a.bias = L.bias;
-    a.residual = residual;
-    a.ld_res = ld_res;
-    a.out = out;
-    a.ld_out = out_pixel_stride;
+  ConvTcArgs a;
+  if (tc_args(&a, dtype, L, x, in_mode, batch, in_h, in_w, in_pixel_stride, out_h, out_w, out,
+              out_mode, out_pixel_stride, residual, ld_res)) {
     // GroupNorm statistics in the epilogue when the output has 4, 8 or 16
     // channels per group (Cout 128, 256, 512 with 32 groups).
     const int cpg = L.cout % kGroups == 0 ? L.cout / kGroups : 0;
-    if (gn_part && (cpg == 4 || cpg == 8 || cpg == 16)) {
+    if (gn_part && out_mode == kLayoutNhwc16 && (cpg == 4 || cpg == 8 || cpg == 16)) {
       a.gn_part = gn_part;
       a.gn_cpg = cpg;
     }
     // Reads past the input edge return the TMA zero fill, which supplies
     // both the leading pad and the trailing (pad_end) pad.
     if (conv_tc_check(a) == nullptr) {
-      OpScope scope(L.k == 3 ? "conv3x3_tc" : "conv1x1_tc", flops, bytes, s, 1);
+      const char* kind = out_mode == kLayoutNchwF32 ? "conv_thin_tc"
+                                                    : (L.k == 3 ? "conv3x3_tc" : "conv1x1_tc");
+      OpScope scope(kind, flops, bytes, s, 1);
       const cudaError_t e = conv_tc_launch(a, s);
       if (gn_done) *gn_done = e == cudaSuccess && a.gn_part != nullptr;
       return cuda_status(e, "tensor-core conv");
-    }
-  }
-  if (in_mode == kLayoutNhwc16 && out_mode == kLayoutNchwF32 && L.cout <= 16 && L.w_rows >= 16 &&
-      !residual) {
-    // Thin output (the VAEs' conv_out): a 16-wide tensor-core tile, NCHW f32 planes.
-    ConvTcArgs a;
-    a.dtype = dtype;
-    a.x = x;
-    a.batch = batch;
-    a.in_h = in_h;
-    a.in_w = in_w;
-    a.cin = L.cin;
-    a.pixel_stride = in_pixel_stride;
-    a.ksize = L.k;
-    a.stride = L.stride;
-    a.pad = L.pad;
-    a.out_h = out_h;
-    a.out_w = out_w;
-    a.cout = L.cout;
-    a.w = L.w;
-    a.ldw = (long long)L.k * L.k * L.cin;
-    a.bias = L.bias;
-    a.out = out;
-    a.out_f32 = 1;
-    a.out_nchw = 1;
-    if (conv_tc_check(a) == nullptr) {
-      OpScope scope("conv_thin_tc", flops, bytes, s, 1);
-      return cuda_status(conv_tc_launch(a, s), "tensor-core thin conv");
     }
   }
   DirectConvArgs d;
@@ -862,9 +870,8 @@ Status vae_decode(const Vae& m, const float* latents, float* image, int batch, i
     }
   }
   const int ti = (xi + 1) % 4;
-  if (!(st = gn(c, d.norm_out, xi, ti, batch, (long long)h * w, true)).good()) return st;
-  return run_conv(c.dtype, d.conv_out, b.act[ti], kLayoutNhwc16, batch, h, w, ch_now, image,
-                  kLayoutNchwF32, 0, nullptr, 0, stream);
+  return gn_conv(c, d.norm_out, true, d.conv_out, xi, ti, batch, h, w, -1, image, kLayoutNchwF32,
+                 nullptr);
 }
 
 Status vae_encode(const Vae& m, const float* image, float* moments, int batch, int height,

@@ -73,6 +73,10 @@ TC_CASES = [
     (2, 256, 4, 128, 128, 3, 1, 1),    # streamed, row shift
     (2, 256, 8, 128, 128, 1, 1, 0),    # 1x1, resident, deep pipeline
     (3, 64, 8, 16, 128, 3, 1, 1),      # odd number of tiles: one-CTA kernel
+    # Pixels on the MMA's N side (3x3, Cout <= 128, width % 256 == 0)
+    (1, 128, 4, 256, 128, 3, 1, 1),    # two channel blocks
+    (2, 64, 3, 512, 64, 3, 1, 1),      # Cout 64: weight rows past Cout read as zeros
+    (1, 256, 2, 256, 128, 3, 1, 1),    # four channel blocks, two image rows
 ]
 
 
@@ -143,3 +147,16 @@ def test_upsample_matches_oracle(cuda_device):
     x = bf16(rng.standard_normal((2, 16, 5, 7)))
     got = ops.nhwc_to_nchw(ops.upsample_2x(ops.nchw_to_nhwc(torch.from_numpy(x).cuda(), DT))).cpu()
     np.testing.assert_array_equal(got.numpy(), oracle.upsample_2x(x))
+
+
+def test_pixel_n_thin_nchw_output_exact(cuda_device):
+    """conv_out shape class: 16-bit NHWC in, Cout 3 NCHW f32 out, pixels on N."""
+    b, cin, h, w, cout = 1, 128, 3, 256, 3
+    x = dyadic((b, cin, h, w), 13, 41, 20, 1 / 16).reshape(b, cin, h, w)
+    wt = dyadic((cout, cin, 3, 3), 7, 11, 5, 1 / 32).reshape(cout, cin, 3, 3) / np.float32(8)
+    bias = np.array([-0.125, 0.0625, 0.25], np.float32)
+    conv = ops.BandedConv2d(wt, bias, stride=1, padding=1, dtype=DT)
+    xt = ops.nchw_to_nhwc(torch.from_numpy(x).cuda(), DT)
+    got = conv.forward_checked(xt, out_layout=LAYOUT_NCHW)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(got.cpu().numpy(), oracle.conv2d(x, wt, bias, stride=1, padding=1))
