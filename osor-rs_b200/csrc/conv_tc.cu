@@ -70,6 +70,9 @@ struct TcParams {
   int phases;
   int low_h, low_w;
   int cout_total;  // weight rows per phase (0 when phases == 1)
+  // 16-bit outputs leave through TMA stores of 32 consecutive tile pixels,
+  // except for an upsampled output with low_w % 32 != 0 (direct stores).
+  int direct_store;
 };
 
 template <int BLOCK_N>
@@ -86,8 +89,11 @@ struct TcConfig {
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   // GroupNorm tile statistics, one half per accumulator: [quad][group][mean, M2].
   static constexpr int kStatBytes = 2 * 4 * 64 * 2 * 4;
-  static constexpr int kSmemBytes =
-      kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ + kStatBytes;
+  // Output staging for the TMA stores: 1 KB per epilogue warp (32 pixels x
+  // 32 bytes: 16 channels of a 16-bit output or 8 of an f32 one).
+  static constexpr int kOutStageBytes = BLOCK_N == 16 ? 0 : kEpiWarps * 1024;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ +
+                                    kStatBytes + kOutStageBytes;
 };
 
 // The four epilogue warps of one column slot (one per TMEM lane quadrant)
@@ -112,7 +118,8 @@ __device__ __forceinline__ bool slot_all(int bar, bool ok) {
 template <int BLOCK_N, int D, int CPG>
 __global__ void __launch_bounds__(TcConfig<BLOCK_N>::kThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                   const __grid_constant__ CUtensorMap tmap_b, const TcParams p) {
+                   const __grid_constant__ CUtensorMap tmap_b,
+                   const __grid_constant__ CUtensorMap tmap_out, const TcParams p) {
   using Cfg = TcConfig<BLOCK_N>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -128,6 +135,7 @@ __global__ void __launch_bounds__(TcConfig<BLOCK_N>::kThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* stat_smem = reinterpret_cast<float*>(smem + S * Cfg::kStageBytes + 256);
+  uint8_t* out_stage = smem + S * Cfg::kStageBytes + 256 + Cfg::kStatBytes;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -293,6 +301,7 @@ __global__ void __launch_bounds__(TcConfig<BLOCK_N>::kThreads, 1)
       // GroupNorm partial slot: tiles of one image stay contiguous (phase-major
       // within the image for the upsampled output).
       int stat_slot = m_tile;
+      int up_j = 0, up_row = 0;  // upsample: first low-res column of this warp's pixels, image row
       if (p.phases == 4) {
         const long long low_hw = (long long)p.low_h * p.low_w;
         const long long img = m / low_hw;
@@ -301,6 +310,11 @@ __global__ void __launch_bounds__(TcConfig<BLOCK_N>::kThreads, 1)
         orow = (img * 2 * p.low_h + 2 * i + (ph >> 1)) * (2LL * p.low_w) + 2 * j + (ph & 1);
         const int mt_img = m_tile / tiles_per_image;
         stat_slot = (mt_img * 4 + ph) * tiles_per_image + (m_tile - mt_img * tiles_per_image);
+        // The warp's 32 pixels are consecutive columns of one low-res row.
+        const long long m_first = m - lane;
+        const long long rem0 = m_first - img * low_hw;
+        up_j = (int)(rem0 % p.low_w);
+        up_row = (int)(img * p.low_h + rem0 / p.low_w);
       }
       // The residual does not depend on the accumulator: start its loads
       // before waiting for the MMAs.
@@ -380,21 +394,57 @@ __global__ void __launch_bounds__(TcConfig<BLOCK_N>::kThreads, 1)
               for (int t = 0; t < 8; ++t) v[8 * j + t] += f[t];
             }
           }
+          // Stores leave through TMA from a 1 KB staging tile per warp
+          // (pixel row = lane, 32 bytes each): one lane per pixel would make
+          // every store instruction touch 32 cache lines.
+          uint8_t* sb = out_stage + (warp - 2) * 1024;
+          uint4* sdst = reinterpret_cast<uint4*>(sb + lane * 32);
           if (p.out_f32) {
-            float4* o4 =
-                reinterpret_cast<float4*>(static_cast<float*>(p.out) + orow * p.ld_out + n0);
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              o4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            for (int q4 = 0; q4 < 4; ++q4) {
+              if (lane == 0) bulk_wait_group_read<0>();
+              __syncwarp();
+              sdst[0] = make_uint4(__float_as_uint(v[8 * q4]), __float_as_uint(v[8 * q4 + 1]),
+                                   __float_as_uint(v[8 * q4 + 2]), __float_as_uint(v[8 * q4 + 3]));
+              sdst[1] = make_uint4(__float_as_uint(v[8 * q4 + 4]), __float_as_uint(v[8 * q4 + 5]),
+                                   __float_as_uint(v[8 * q4 + 6]), __float_as_uint(v[8 * q4 + 7]));
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&tmap_out, sb, n0 + 8 * q4, (int)(m - lane));
+                bulk_commit_group();
+              }
+            }
           } else {
-            uint4* o4 =
-                reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + orow * p.ld_out + n0);
             uint32_t pk[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) pk[j] = Elem<D>::pack(v[2 * j], v[2 * j + 1]);
+            if (p.direct_store) {
+              // Upsampled output narrower than 32 low-res columns: a warp's
+              // pixels span several output rows, store them lane by lane.
+              uint4* o4 =
+                  reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + orow * p.ld_out + n0);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              o4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+              for (int j = 0; j < 4; ++j)
+                o4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+            } else {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              if (lane == 0) bulk_wait_group_read<0>();
+              __syncwarp();
+              sdst[0] = make_uint4(pk[8 * h], pk[8 * h + 1], pk[8 * h + 2], pk[8 * h + 3]);
+              sdst[1] = make_uint4(pk[8 * h + 4], pk[8 * h + 5], pk[8 * h + 6], pk[8 * h + 7]);
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                if (p.phases == 4)
+                  tma_store_5d(&tmap_out, sb, n0 + 16 * h, ph & 1, up_j, ph >> 1, up_row);
+                else
+                  tma_store_2d(&tmap_out, sb, n0 + 16 * h, (int)(m - lane));
+                bulk_commit_group();
+              }
+            }
+            }
             if constexpr (CPG > 0) {
               // Statistics of the stored (rounded) values, per quadrant into
               // this accumulator's half of stat_smem.
@@ -438,6 +488,7 @@ __global__ void __launch_bounds__(TcConfig<BLOCK_N>::kThreads, 1)
         acc_phase ^= 1;
       }
     }
+    if (BLOCK_N != 16 && lane == 0) bulk_wait_group<0>();
   }
 
   tc_fence_before();
@@ -481,7 +532,8 @@ int sm_count(int device) {
 }
 
 template <int BLOCK_N, int D, int CPG>
-cudaError_t launch_typed(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p,
+cudaError_t launch_typed(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                         const TcParams& p,
                          cudaStream_t stream) {
   using Cfg = TcConfig<BLOCK_N>;
   static bool configured[64] = {false};
@@ -496,18 +548,18 @@ cudaError_t launch_typed(const CUtensorMap& ta, const CUtensorMap& tb, const TcP
   }
   const int tiles = p.num_m_tiles * p.phases * p.num_n_tiles;
   const int grid = tiles < sm_count(device) ? tiles : sm_count(device);
-  conv_tc_kernel<BLOCK_N, D, CPG><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  conv_tc_kernel<BLOCK_N, D, CPG><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, to, p);
   return cudaGetLastError();
 }
 
 template <int BLOCK_N, int D>
-cudaError_t launch_cpg(int cpg, const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p,
-                       cudaStream_t stream) {
+cudaError_t launch_cpg(int cpg, const CUtensorMap& ta, const CUtensorMap& tb,
+                       const CUtensorMap& to, const TcParams& p, cudaStream_t stream) {
   switch (cpg) {
-    case 4: return launch_typed<BLOCK_N, D, 4>(ta, tb, p, stream);
-    case 8: return launch_typed<BLOCK_N, D, 8>(ta, tb, p, stream);
-    case 16: return launch_typed<BLOCK_N, D, 16>(ta, tb, p, stream);
-    default: return launch_typed<BLOCK_N, D, 0>(ta, tb, p, stream);
+    case 4: return launch_typed<BLOCK_N, D, 4>(ta, tb, to, p, stream);
+    case 8: return launch_typed<BLOCK_N, D, 8>(ta, tb, to, p, stream);
+    case 16: return launch_typed<BLOCK_N, D, 16>(ta, tb, to, p, stream);
+    default: return launch_typed<BLOCK_N, D, 0>(ta, tb, to, p, stream);
   }
 }
 
@@ -643,14 +695,44 @@ cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
   p.low_h = a.in_h;
   p.low_w = a.in_w;
   p.cout_total = a.upsample ? a.cout : 0;
+  p.direct_store = a.upsample && a.in_w % 32 != 0;
+  // Output tensor map for the epilogue's TMA stores (unused by the thin
+  // NCHW output, which stores directly).
+  CUtensorMap to = tb;
+  if (!a.out_nchw) {
+    CUresult r;
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    if (a.upsample) {
+      // Output pixel (img, 2i + a, 2j + b) of phase (a, b) and low-res pixel
+      // (img, i, j) as dims (channel, b, j, a, img * low_h + i).
+      const cuuint64_t row = (cuuint64_t)a.ld_out * 2;
+      cuuint64_t dims[5] = {(cuuint64_t)a.cout, 2, (cuuint64_t)a.in_w, 2,
+                            (cuuint64_t)a.batch * a.in_h};
+      cuuint64_t strides[4] = {row, 2 * row, 2 * (cuuint64_t)a.in_w * row,
+                               4 * (cuuint64_t)a.in_w * row};
+      cuuint32_t box[5] = {16, 1, 32, 1, 1};
+      r = encode(&to, tdt, 5, a.out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                 CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+      const int esize = a.out_f32 ? 4 : 2;
+      cuuint64_t dims[2] = {(cuuint64_t)a.cout, (cuuint64_t)p.num_m_tiles * kBlockM};
+      cuuint64_t strides[1] = {(cuuint64_t)a.ld_out * esize};
+      cuuint32_t box[2] = {(cuuint32_t)(32 / esize), 32};
+      r = encode(&to, a.out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : tdt, 2, a.out, dims, strides,
+                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                 CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  }
   if (a.out_nchw)
-    return a.dtype == kF16 ? launch_typed<16, kF16, 0>(ta, tb, p, stream)
-                           : launch_typed<16, kBf16, 0>(ta, tb, p, stream);
+    return a.dtype == kF16 ? launch_typed<16, kF16, 0>(ta, tb, to, p, stream)
+                           : launch_typed<16, kBf16, 0>(ta, tb, to, p, stream);
   if (a.dtype == kF16)
-    return block_n == 256 ? launch_cpg<256, kF16>(cpg, ta, tb, p, stream)
-                          : launch_cpg<128, kF16>(cpg, ta, tb, p, stream);
-  return block_n == 256 ? launch_cpg<256, kBf16>(cpg, ta, tb, p, stream)
-                        : launch_cpg<128, kBf16>(cpg, ta, tb, p, stream);
+    return block_n == 256 ? launch_cpg<256, kF16>(cpg, ta, tb, to, p, stream)
+                          : launch_cpg<128, kF16>(cpg, ta, tb, to, p, stream);
+  return block_n == 256 ? launch_cpg<256, kBf16>(cpg, ta, tb, to, p, stream)
+                        : launch_cpg<128, kBf16>(cpg, ta, tb, to, p, stream);
 }
 
 }  // namespace osor

@@ -28,7 +28,6 @@ namespace {
 
 __device__ __forceinline__ float silu_f(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
-
 template <typename T>
 __device__ __forceinline__ float silu_t(float v) {
   if constexpr (sizeof(T) == 2) {
