@@ -379,23 +379,41 @@ def main():
     total_flops = sum(v["flops"] for v in kinds.values()) / args.steps
 
     # ------------------------------------------------------------ e2e (host buffers)
+    # Every step copies its latents in from pinned host memory and its image
+    # back out; the device->host copy of step i runs on a copy stream while
+    # step i + 1 decodes (two device output buffers, as a serving loop would).
     h_lat = torch.from_numpy(lat_host).pin_memory()
-    h_out = torch.empty((args.batch, 3, IMAGE, IMAGE), dtype=torch.float32).pin_memory()
+    h_outs = [torch.empty((args.batch, 3, IMAGE, IMAGE), dtype=torch.float32).pin_memory()
+              for _ in range(2)]
+    outs = [out, torch.empty_like(out)]
     d_lat = torch.empty_like(lat)
-    for _ in range(2):
-        d_lat.copy_(h_lat, non_blocking=True)
-        model.decode(d_lat, out=out)
-        h_out.copy_(out, non_blocking=True)
+    copy_stream = torch.cuda.Stream(dev)
+
+    def e2e_steps(n):
+        done = [None, None]
+        for i in range(n):
+            j = i % 2
+            d_lat.copy_(h_lat, non_blocking=True)
+            if done[j] is not None:
+                stream.wait_event(done[j])  # outs[j]'s previous copy has finished
+            model.decode(d_lat, out=outs[j])
+            ready = torch.cuda.Event()
+            ready.record(stream)
+            copy_stream.wait_event(ready)
+            with torch.cuda.stream(copy_stream):
+                h_outs[j].copy_(outs[j], non_blocking=True)
+            done[j] = torch.cuda.Event()
+            done[j].record(copy_stream)
+        stream.wait_stream(copy_stream)
+
+    e2e_steps(2)
     torch.cuda.synchronize(dev)
     e_start = torch.cuda.Event(enable_timing=True)
     e_end = torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize(dev)
     e_start.record(stream)
-    for _ in range(args.steps):
-        d_lat.copy_(h_lat, non_blocking=True)
-        model.decode(d_lat, out=out)
-        h_out.copy_(out, non_blocking=True)
+    e2e_steps(args.steps)
     e_end.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = e_start.elapsed_time(e_end) / args.steps
@@ -403,6 +421,7 @@ def main():
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = float(te.item())
+    h_out = h_outs[(args.steps - 1) % 2]
     if not np.all(np.isfinite(h_out.numpy()[:, :, ::64, ::64])):
         raise SystemExit("non-finite decoder output")
 

@@ -51,9 +51,9 @@ struct ConvTcArgs {
 const char* conv_tc_check(const ConvTcArgs& a);
 cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream);
 
-// 3x3 stride-1 convolution with Cout 64 / 128 (16-bit NHWC) or <= 16 (thin
-// NCHW f32) and width % 256 == 0, with the pixels on the MMA's N side (256
-// per tile). conv_tc_launch dispatches to it first.
+// 3x3 (pad 1) or 1x1 stride-1 convolution with Cout 64 / 128 (16-bit NHWC)
+// or <= 16 (thin NCHW f32) and width % 256 == 0, with the pixels on the
+// MMA's N side (256 per tile). conv_tc_launch dispatches to it first.
 const char* conv_tcn_check(const ConvTcArgs& a);
 cudaError_t conv_tcn_launch(const ConvTcArgs& a, cudaStream_t stream);
 

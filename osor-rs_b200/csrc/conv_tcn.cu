@@ -1,4 +1,4 @@
-// Implicit-GEMM 3x3 convolution with the pixels on the MMA's N side.
+// Implicit-GEMM 3x3 (or 1x1) convolution with the pixels on the MMA's N side.
 //
 // For Cout <= 128 this kernel swaps the GEMM operands so that every
 // tcgen05.mma is a full M = 128, N = 256 instruction:
@@ -467,7 +467,8 @@ cudaError_t launch_n(const CUtensorMap& tx, const CUtensorMap& tw, const CUtenso
 
 const char* conv_tcn_check(const ConvTcArgs& a) {
   if (a.upsample || a.row_scale) return "pixel-N kernel: plain convolution only";
-  if (a.ksize != 3 || a.stride != 1 || a.pad != 1) return "pixel-N kernel: 3x3, stride 1, pad 1";
+  if (!((a.ksize == 3 && a.pad == 1) || (a.ksize == 1 && a.pad == 0)) || a.stride != 1)
+    return "pixel-N kernel: 3x3 pad 1 or 1x1, stride 1";
   if (a.out_h != a.in_h || a.out_w != a.in_w) return "pixel-N kernel: same-size output";
   if (a.out_w <= 0 || a.out_h <= 0 || a.batch <= 0) return "empty convolution";
   if (a.out_w % kNN != 0) return "pixel-N kernel: width must be a multiple of 256";
@@ -512,9 +513,11 @@ cudaError_t conv_tcn_launch(const ConvTcArgs& a, cudaStream_t stream) {
       return cudaErrorInvalidValue;
   }
   {
-    // Rows past Cout are outside the tensor: the box reads them as zeros.
+    // Weight rows past Cout: the caller's zero padding when it allocated 128
+    // rows, else outside the tensor (the box reads them as zeros).
     const int k_total = a.ksize * a.ksize * a.cin;
-    cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)a.cout};
+    const int rows = a.w_rows >= kNM ? kNM : a.cout;
+    cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)a.ldw * 2};
     cuuint32_t box[2] = {(cuuint32_t)kNK, (cuuint32_t)kNM};
     cuuint32_t estr[2] = {1, 1};

@@ -504,9 +504,121 @@ int num_sms() {
   return c > 0 ? c : 148;
 }
 
+// Bulk-copy apply: each CTA streams 16 KB chunks (2048 16-byte vectors) of
+// one image through a ring of kApplyStages shared-memory buffers: a bulk
+// load lands the chunk, the 256 threads normalise it in place (each thread
+// always the same 8 channels, since 256 is a multiple of C / 8), and a bulk
+// store writes it back. kApplyStages - 1 loads stay in flight per CTA.
+constexpr int kApplyChunk = 16384;  // bytes
+constexpr int kApplyStages = 4;
+
+template <int D>
+__global__ void __launch_bounds__(256)
+    gn_nhwc_apply_bulk_kernel(const uint8_t* __restrict__ x, uint8_t* __restrict__ y,
+                              const float* __restrict__ coef, int channels,
+                              int chunks_per_image, long long chunks_total, int silu) {
+  extern __shared__ __align__(128) uint8_t abuf[];
+  __shared__ __align__(8) uint64_t full[kApplyStages];
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kApplyStages; ++s) mbar_init(&full[s], 1);
+    abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  const int vc = channels / 8;
+  const int octet = threadIdx.x % vc;
+  long long issued = 0, consumed = 0;  // thread 0: loads issued / iterations finished
+  auto load = [&](long long it) {
+    const long long chunk = blockIdx.x + it * gridDim.x;
+    if (chunk >= chunks_total) return;
+    issued = it + 1;
+    const int b = (int)(it % kApplyStages);
+    mbar_arrive_expect_tx(&full[b], kApplyChunk);
+    bulk_load(abuf + b * kApplyChunk, x + chunk * kApplyChunk, kApplyChunk, &full[b]);
+  };
+  if (threadIdx.x == 0)
+    for (int it = 0; it < kApplyStages - 1; ++it) load(it);
+  int img = -1;
+  float ca[8], cb[8];
+  for (long long it = 0;; ++it) {
+    const long long chunk = blockIdx.x + it * gridDim.x;
+    if (chunk >= chunks_total) break;
+    const int b = (int)(it % kApplyStages);
+    const int ci = (int)(chunk / chunks_per_image);
+    if (ci != img) {
+      img = ci;
+      const float4* cf =
+          reinterpret_cast<const float4*>(coef + ((long long)img * channels + octet * 8) * 4);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 c = __ldg(cf + j);
+        gn_coef_prepare(c.x, c.y, c.z, silu != 0, ca[j], cb[j]);
+      }
+    }
+    const bool ok = mbar_wait(&full[b], (uint32_t)((it / kApplyStages) & 1), &abort_flag);
+    __syncthreads();
+    if (!ok || abort_flag) break;
+    consumed = it + 1;
+    uint4* v = reinterpret_cast<uint4*>(abuf + b * kApplyChunk);
+#pragma unroll
+    for (int k = 0; k < kApplyChunk / 16 / 256; ++k) {
+      float f[8];
+      unpack8<D>(v[threadIdx.x + k * 256], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = gn_apply_prepared(f[j], ca[j], cb[j], silu != 0);
+      v[threadIdx.x + k * 256] = pack8<D>(f);
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      bulk_store(y + chunk * kApplyChunk, abuf + b * kApplyChunk, kApplyChunk);
+      bulk_commit_group();
+      // The previous iteration's store has finished reading its buffer, which
+      // now takes the load kApplyStages - 1 chunks ahead.
+      bulk_wait_group_read<1>();
+      load(it + kApplyStages - 1);
+    }
+  }
+  if (threadIdx.x == 0) {
+    bulk_wait_group<0>();
+    // After an abort, let the loads still in flight (iterations consumed ..
+    // issued - 1) land before the CTA leaves.
+    for (long long it = consumed; it < issued; ++it) {
+      const uint32_t addr = smem_u32(&full[it % kApplyStages]);
+      const uint32_t parity = (uint32_t)((it / kApplyStages) & 1);
+      const uint64_t t0 = global_timer_ns();
+      while (!mbar_try_wait(addr, parity) && global_timer_ns() - t0 < kWaitLimitNs) {
+      }
+    }
+  }
+}
+
 template <int D>
 cudaError_t apply_launch(const void* x, void* y, const float* coef, int batch, int channels,
                          long long pixels, int silu, cudaStream_t stream) {
+  const long long image_bytes = pixels * channels * 2;
+  if (256 % (channels / 8) == 0 && image_bytes % kApplyChunk == 0 &&
+      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0) {
+    const int smem = kApplyStages * kApplyChunk;
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(gn_nhwc_apply_bulk_kernel<D>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      configured[dev] = true;
+    }
+    const int per_image = (int)(image_bytes / kApplyChunk);
+    const long long total = (long long)per_image * batch;
+    long long grid = (long long)num_sms() * 3;
+    if (grid > total) grid = total;
+    gn_nhwc_apply_bulk_kernel<D><<<(unsigned)grid, 256, smem, stream>>>(
+        static_cast<const uint8_t*>(x), static_cast<uint8_t*>(y), coef, channels, per_image, total,
+        silu);
+    return cudaGetLastError();
+  }
   const int vc = channels / 8;
   const int rows = 256 / vc;
   const int threads = rows * vc;

@@ -145,7 +145,10 @@ class Loader {
     Status s = tensor(prefix + ".weight", {cout, cin, k, k}, &w);
     if (!s.good()) return s;
     if (!(s = tensor(prefix + ".bias", {cout}, &b)).good()) return s;
-    return conv_from(w->data, b->data, cin, cout, k, 1, pad, L, 16);
+    // 128 zero-padded weight rows: the pixel-N kernel reads a full M = 128
+    // weight tile (zeros from memory stream faster than the TMA's
+    // out-of-bounds fill), the 16-wide one-CTA tile the first 16.
+    return conv_from(w->data, b->data, cin, cout, k, 1, pad, L, 128);
   }
   // A thin-input convolution as a 64-column 1x1 layer: column j < k*k*cin
   // holds tap j / cin, channel j % cin (thin_columns_launch's order).
