@@ -19,6 +19,7 @@
 #include <string>
 #include <unordered_map>
 
+#include "attn_fa.h"
 #include "common.cuh"
 #include "conv_tc.h"
 #include "groupnorm.h"
@@ -466,6 +467,20 @@ Status mid_block(const Ctx& c, const MidLayer& L, int xi, int batch, int h, int 
   return st;
 }
 
+// The fused kernel (attn_fa.cu) runs when OSOR_FUSED_ATTENTION=1 is set in
+// the environment. By default attention takes the three-kernel path (scores
+// GEMM with TMA stores, softmax, P V), which measured faster at the VAE's
+// D = 512: TMEM holds one 256-key score tile and one half of the 128 x 512
+// output, so the fused kernel computes Q K^T once per output half and its
+// S tile cannot be double buffered.
+bool fused_attention_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("OSOR_FUSED_ATTENTION");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+
 bool attention_tc_ok(int tokens, int dim) {
   return tokens % 128 == 0 && dim % 128 == 0 && dim <= 512 && tokens <= 16384;
 }
@@ -488,6 +503,22 @@ Status attention_core(int dtype, const void* q, const void* k, const void* v, lo
       if (e != cudaSuccess) return cuda_status(e, "attention");
     }
     return Status::ok();
+  }
+  if (fused_attention_enabled() && attn_fused_ok(tokens, dim, ld, ld_out, q, k, vt, out)) {
+    // V^T of every image, then one fused launch over all images: the scores
+    // stay in TMEM / shared memory.
+    cudaError_t e;
+    for (int bi = 0; bi < batch; ++bi) {
+      const long long off = (long long)bi * tokens;
+      OpScope scope("attn_transpose", 0.0, 4.0 * tokens * dim, s, 1);
+      e = transpose16_launch(vb + off * ld, ld, static_cast<uint16_t*>(vt) + off * dim, tokens,
+                             tokens, dim, s);
+      if (e != cudaSuccess) return cuda_status(e, "attention transpose");
+    }
+    const double nn = (double)tokens * tokens;
+    OpScope scope("attn_fused", 4.0 * batch * nn * dim, 8.0 * batch * tokens * dim, s, 1);
+    return cuda_status(attn_fused_launch(dtype, q, k, ld, vt, out, ld_out, batch, tokens, dim, s),
+                       "fused attention");
   }
   for (int bi = 0; bi < batch; ++bi) {
     const long long off = (long long)bi * tokens;

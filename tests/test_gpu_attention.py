@@ -3,6 +3,10 @@ F32 attention (src/native/attention.rs:27-84) on bf16-representable inputs.
 Shapes cover the tensor-core path (tokens % 128 == 0) and the CUDA-core path
 the reference's own small shapes take (vae_encoder.rs:497: 5x7 and 11x13
 tokens, 32 channels)."""
+import os
+import subprocess
+import sys
+
 import numpy as np
 import pytest
 import torch
@@ -16,8 +20,10 @@ pytestmark = pytest.mark.gpu
 
 
 CASES = [
-    (1, 256, 512),    # tensor-core scores / values, VAE width
-    (2, 384, 128),
+    (1, 256, 512),    # fused kernel, one 256-key tile, VAE width
+    (2, 1024, 512),   # fused kernel, four key tiles, two channel halves
+    (1, 512, 256),    # fused kernel, one channel half
+    (2, 384, 128),    # three-kernel tensor-core path
     (2, 35, 32),      # reference batch test shapes, CUDA-core path
     (4, 143, 32),
 ]
@@ -43,3 +49,41 @@ def test_attend_matches_oracle(case, dt, cuda_device):
     # bf16 probabilities (relative 2^-9) and bf16 output rounding.
     assert err.max() <= 2e-2, err.max()
     assert np.sqrt((err ** 2).mean()) <= 3e-3
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+def test_fused_attention_rescales_growing_maxima(dt, cuda_device):
+    """Logits that grow along the keys (up to ~40 in natural units) for every
+    other query row and shrink for the rest, so within each warp some rows'
+    running maximum jumps by more than 2^8 across key tiles (the fused kernel
+    rescales their output accumulator) while the others keep theirs."""
+    b, n, d = 1, 1024, 512
+    rng = np.random.default_rng(3)
+
+    def half(a):
+        return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dt)
+
+    e = rng.standard_normal(d)
+    e /= np.linalg.norm(e)
+    sign = np.where(np.arange(n) % 2 == 0, 1.0, -1.0)[None, :, None]
+    q = half(sign * e * 2.0 + 0.05 * rng.standard_normal((b, n, d)))
+    ramp = (np.arange(n) / n * 20.0)[None, :, None]
+    k = half(e[None, None, :] * ramp + 0.05 * rng.standard_normal((b, n, d)))
+    v = half(rng.standard_normal((b, n, d)))
+    got = ops.attend(q.cuda(), k.cuda(), v.cuda()).float().cpu().numpy()
+    qf, kf, vf = q.float().numpy(), k.float().numpy(), v.float().numpy()
+    want = oracle.attend(qf, np.ascontiguousarray(kf.transpose(0, 2, 1)), vf)
+    err = np.abs(got - want)
+    assert np.all(np.isfinite(got))
+    assert err.max() <= 2e-2, err.max()
+
+
+def test_fused_kernel_runs_the_same_cases(cuda_device):
+    """The fused attention kernel is opt-in (OSOR_FUSED_ATTENTION=1, read once
+    per process): run this file's oracle cases again in a child process with
+    it selected. Shapes with tokens % 256 == 0 and D of 256 or 512 take it."""
+    env = dict(os.environ, OSOR_FUSED_ATTENTION="1")
+    r = subprocess.run([sys.executable, "-m", "pytest", __file__, "-q", "-p", "no:cacheprovider",
+                        "-k", "attend_matches_oracle or rescales_growing_maxima"],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
