@@ -224,6 +224,22 @@ int osor_conv2d(const void* x, void* y, const void* weight_packed, const float* 
                                out_mode, cout, residual, cout, static_cast<cudaStream_t>(stream)));
 }
 
+namespace {
+// The L2-resident NCHW GroupNorm takes 16-byte-aligned tensors whose H * W is
+// a multiple of the vector width; OSOR_GN_NCHW_L2=0 in the environment keeps
+// the shared-memory-resident kernel, for comparing.
+bool nchw_l2_ok(const void* x, const void* y, int batch, int channels, long long spatial,
+                int dtype) {
+  static const bool on = [] {
+    const char* v = getenv("OSOR_GN_NCHW_L2");
+    return !(v && v[0] == '0');
+  }();
+  const int eb = dtype == OSOR_DTYPE_F32 ? 4 : 2;
+  return on && aligned16(x) && aligned16(y) &&
+         osor::gn_nchw_l2_plan(batch, channels, spatial, 32, eb).feasible;
+}
+}  // namespace
+
 size_t osor_group_norm_workspace_size(int batch, int channels, int height, int width, int layout,
                                       int dtype) {
   if (batch <= 0 || channels <= 0 || channels % 32 != 0 || height <= 0 || width <= 0) return 0;
@@ -234,8 +250,14 @@ size_t osor_group_norm_workspace_size(int batch, int channels, int height, int w
   }
   if (layout != OSOR_LAYOUT_NCHW || (!is16(dtype) && dtype != OSOR_DTYPE_F32)) return 0;
   const int eb = dtype == OSOR_DTYPE_F32 ? 4 : 2;
+  // Room for either NCHW kernel: the L2-resident two-pass one (16-byte
+  // vectors along H * W) and the shared-memory-resident one.
   const osor::GnFusedPlan p = osor::gn_fused_plan(batch, channels, spatial, 32, eb);
-  return p.feasible ? p.workspace_bytes : 0;
+  const osor::GnL2Plan q = osor::gn_nchw_l2_plan(batch, channels, spatial, 32, eb);
+  size_t need = 0;
+  if (p.feasible) need = p.workspace_bytes;
+  if (q.feasible && q.workspace_bytes > need) need = q.workspace_bytes;
+  return need;
 }
 
 int osor_group_norm_silu(const void* x, void* y, const float* gamma, const float* beta, int batch,
@@ -258,6 +280,21 @@ int osor_group_norm_silu(const void* x, void* y, const float* gamma, const float
       return fail(OSOR_ERR_INVALID_INPUT, "NHWC tensors must be 16-byte aligned");
     e = osor::gn_nhwc_launch(internal_dtype(dtype), x, y, gamma, beta, batch, channels, spatial, 32,
                              eps, silu, workspace, stats, s);
+  } else if (nchw_l2_ok(x, y, batch, channels, spatial, dtype)) {
+    // One HBM read and write per element; chunks re-read from L2.
+    if (dtype == OSOR_DTYPE_F32)
+      e = osor::gn_nchw_l2_launch<float>(static_cast<const float*>(x), static_cast<float*>(y),
+                                         gamma, beta, batch, channels, spatial, 32, eps, silu,
+                                         workspace, stats, s);
+    else if (dtype == OSOR_DTYPE_BF16)
+      e = osor::gn_nchw_l2_launch<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x),
+                                                 static_cast<__nv_bfloat16*>(y), gamma, beta,
+                                                 batch, channels, spatial, 32, eps, silu,
+                                                 workspace, stats, s);
+    else
+      e = osor::gn_nchw_l2_launch<__half>(static_cast<const __half*>(x), static_cast<__half*>(y),
+                                          gamma, beta, batch, channels, spatial, 32, eps, silu,
+                                          workspace, stats, s);
   } else if (dtype == OSOR_DTYPE_F32) {
     e = osor::gn_fused_launch<float>(static_cast<const float*>(x), static_cast<float*>(y), gamma,
                                      beta, batch, channels, spatial, 32, eps, silu, workspace, stats,

@@ -43,6 +43,12 @@ struct Scalar;
 template <>
 struct Scalar<float> {
   static constexpr int V = 4;  // elements per 16-byte vector
+  __device__ static void unpack(const uint4& q, float (&f)[4]) {
+    f[0] = __uint_as_float(q.x);
+    f[1] = __uint_as_float(q.y);
+    f[2] = __uint_as_float(q.z);
+    f[3] = __uint_as_float(q.w);
+  }
   __device__ static float to_f(float v) { return v; }
   __device__ static float from_f(float v) { return v; }
   __device__ static void load(const float* p, float (&f)[4]) {
@@ -65,6 +71,7 @@ struct Scalar16 {
   __device__ static void load(const T* p, float (&f)[8]) {
     unpack8<D>(*reinterpret_cast<const uint4*>(p), f);
   }
+  __device__ static void unpack(const uint4& q, float (&f)[8]) { unpack8<D>(q, f); }
   __device__ static void store(T* p, const float (&f)[8]) {
     *reinterpret_cast<uint4*>(p) = pack8<D>(f);
   }
@@ -652,7 +659,264 @@ cudaError_t gn_nhwc_typed(const void* x, void* y, const float* gamma, const floa
 
 }  // namespace
 
+// ---------------------------------------------------------------- NCHW, L2-resident
+// Standalone NCHW GroupNorm(+SiLU) with one HBM read and one HBM write per
+// element. A group (CPG channels x H x W, contiguous in NCHW) is split into P
+// chunks of up to kL2Chunk bytes handled by co-resident CTAs. Per chunk, one
+// read from HBM accumulates sums of (x - a) and (x - a)^2 with the anchor a =
+// the chunk's first element (the reference Metal kernel's anchoring), turned
+// into the chunk's (n, mean, M2) and published with a counter; once all P
+// chunks of the group have published (Chan merge in chunk order), the chunk
+// is read again - from L2 - normalised and written. Each CTA normalises a
+// chunk kL2Lag iterations after publishing it, so the group wait overlaps
+// later chunks' reads and a group may span consecutive waves of the
+// persistent grid (the L2 keeps kL2Lag + 1 chunks per CTA). Waits are
+// bounded.
+constexpr int kL2Threads = 512;
+constexpr int kL2CtasPerSm = 2;
+constexpr long long kL2Chunk = 64 * 1024;  // bytes
+constexpr int kL2Unroll = 4;               // 16-byte loads in flight per thread
+constexpr int kL2Lag = 2;                  // iterations between a chunk's statistics and its store
+
+struct L2Params {
+  long long count;  // elements per group
+  long long chunk;  // elements per chunk (16-byte multiple); the last is shorter
+  int P;            // chunks per group
+  int groups_total, groups, channels;
+  long long spatial;
+  float eps;
+  int silu;
+  float* partials;  // [groups_total * P][3] (n, mean, M2)
+  int* arrive;      // [groups_total]
+  float* stats_out;
+};
+
+__device__ __forceinline__ float block_sum_512(float v, float* scratch) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float t = lane < kL2Threads / 32 ? scratch[lane] : 0.0f;
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  return __shfl_sync(0xffffffffu, t, 0);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kL2Threads, kL2CtasPerSm)
+    gn_nchw_l2_kernel(const T* __restrict__ x, T* __restrict__ y, const float* __restrict__ gamma,
+                      const float* __restrict__ beta, const L2Params p) {
+  using S = Scalar<T>;
+  constexpr int V = S::V;
+  __shared__ float red[2][kL2Threads / 32];
+  __shared__ int failed;
+  if (threadIdx.x == 0) failed = 0;
+  const long long items = (long long)p.groups_total * p.P;
+  const int cpg = p.channels / p.groups;
+  constexpr long long kStep = (long long)kL2Threads * V;
+
+  auto pass1 = [&](long long item) {
+    const int g = (int)(item / p.P);
+    const int c = (int)(item - (long long)g * p.P);
+    const long long begin = (long long)c * p.chunk;
+    const long long n = min(p.chunk, p.count - begin);
+    const T* src = x + (long long)g * p.count + begin;
+    const float a = S::to_f(src[0]);
+    float s1 = 0.0f, s2 = 0.0f;
+    for (long long i0 = (long long)threadIdx.x * V; i0 < n; i0 += kStep * kL2Unroll) {
+      uint4 raw[kL2Unroll];
+#pragma unroll
+      for (int u = 0; u < kL2Unroll; ++u)
+        if (i0 + u * kStep < n) raw[u] = __ldcg(reinterpret_cast<const uint4*>(src + i0 + u * kStep));
+#pragma unroll
+      for (int u = 0; u < kL2Unroll; ++u)
+        if (i0 + u * kStep < n) {
+          float f[V];
+          S::unpack(raw[u], f);
+#pragma unroll
+          for (int j = 0; j < V; ++j) {
+            const float d = f[j] - a;
+            s1 += d;
+            s2 = fmaf(d, d, s2);
+          }
+        }
+    }
+    // Both sums in one block reduction.
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) {
+      red[0][warp] = s1;
+      red[1][warp] = s2;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t1 = 0.0f, t2 = 0.0f;
+      for (int w = 0; w < kL2Threads / 32; ++w) {
+        t1 += red[0][w];
+        t2 += red[1][w];
+      }
+      const float nf = (float)n;
+      const float d = t1 / nf;  // mean - a
+      float* dst = p.partials + item * 3;
+      dst[0] = nf;
+      dst[1] = a + d;
+      dst[2] = fmaxf(t2 - t1 * d, 0.0f);
+      __threadfence();
+      atomicAdd(&p.arrive[g], 1);
+    }
+  };
+
+  auto pass2 = [&](long long item) {
+    const int g = (int)(item / p.P);
+    const int c = (int)(item - (long long)g * p.P);
+    if (threadIdx.x == 0) {
+      const volatile int* ar = p.arrive + g;
+      const uint64_t t0 = global_timer_ns();
+      while (*ar < p.P) {
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+          record_device_error(kDevWaitTimeout);
+          failed = 1;
+          break;
+        }
+      }
+      __threadfence();
+    }
+    __syncthreads();
+    if (failed) return;
+    const float* part = p.partials + (long long)g * p.P * 3;
+    float sm = 0.0f;
+    for (int k = threadIdx.x; k < p.P; k += kL2Threads)
+      sm += __ldcg(part + k * 3) * __ldcg(part + k * 3 + 1);
+    const float mean = block_sum_512(sm, red[0]) / (float)p.count;
+    float sq = 0.0f;
+    for (int k = threadIdx.x; k < p.P; k += kL2Threads) {
+      const float nk = __ldcg(part + k * 3), mk = __ldcg(part + k * 3 + 1);
+      const float d = mk - mean;
+      sq += __ldcg(part + k * 3 + 2) + nk * d * d;
+    }
+    const float var = fmaxf(block_sum_512(sq, red[0]) / (float)p.count, 0.0f);
+    const float rstd = rsqrtf(var + p.eps);
+    if (threadIdx.x == 0 && c == 0 && p.stats_out) {
+      p.stats_out[g * 2] = mean;
+      p.stats_out[g * 2 + 1] = var;
+    }
+    const long long begin = (long long)c * p.chunk;
+    const long long n = min(p.chunk, p.count - begin);
+    const long long base = (long long)g * p.count + begin;
+    const int gi = g % p.groups;
+    for (long long i0 = (long long)threadIdx.x * V; i0 < n; i0 += kStep * kL2Unroll) {
+      uint4 raw[kL2Unroll];
+#pragma unroll
+      for (int u = 0; u < kL2Unroll; ++u)
+        if (i0 + u * kStep < n)
+          raw[u] = __ldcg(reinterpret_cast<const uint4*>(x + base + i0 + u * kStep));
+#pragma unroll
+      for (int u = 0; u < kL2Unroll; ++u) {
+        const long long i = i0 + u * kStep;
+        if (i < n) {
+          // V consecutive elements never straddle a channel (spatial % V == 0).
+          const int ch = gi * cpg + (int)((begin + i) / p.spatial);
+          const float sc = rstd * __ldg(gamma + ch);
+          const float sh = __ldg(beta + ch);
+          float f[V];
+          S::unpack(raw[u], f);
+#pragma unroll
+          for (int j = 0; j < V; ++j) {
+            float v = (f[j] - mean) * sc + sh;
+            if (p.silu) v = silu_t<T>(v);
+            f[j] = v;
+          }
+          S::store(y + base + i, f);
+        }
+      }
+    }
+  };
+
+  // Normalise the chunk published kL2Lag iterations earlier: by then its
+  // group has normally completed, so the wait rarely spins.
+  for (long long it = 0;; ++it) {
+    const long long item = blockIdx.x + it * gridDim.x;
+    const long long prev = item - (long long)kL2Lag * gridDim.x;
+    if (item < items) pass1(item);
+    if (prev >= 0 && prev < items) pass2(prev);
+    if (prev >= items || failed) break;
+  }
+}
+
 // ------------------------------------------------------------ host wrappers
+
+GnL2Plan gn_nchw_l2_plan(int batch, int channels, long long spatial, int groups, int elem_bytes) {
+  GnL2Plan plan{};
+  const int vec = 16 / elem_bytes;
+  plan.feasible = spatial % vec == 0 && channels % groups == 0;
+  plan.groups_total = batch * groups;
+  plan.count = (long long)(channels / groups) * spatial;
+  plan.grid = num_sms() * kL2CtasPerSm;
+  long long chunk = kL2Chunk / elem_bytes;
+  // Every group must fit in one wave of the grid (P <= grid); chunks hold
+  // whole 16-byte vectors and at most kL2Chunk bytes (one ring buffer).
+  if ((plan.count + chunk - 1) / chunk > plan.grid) {
+    chunk = (plan.count + plan.grid - 1) / plan.grid;
+    chunk = (chunk + vec - 1) / vec * vec;
+    if (chunk * elem_bytes > kL2Chunk) plan.feasible = false;
+  }
+  chunk = (chunk + vec - 1) / vec * vec;
+  plan.chunk = chunk;
+  plan.P = (int)((plan.count + chunk - 1) / chunk);
+  plan.workspace_bytes = ((size_t)plan.groups_total * sizeof(int) + 255) / 256 * 256 +
+                         (size_t)plan.groups_total * plan.P * 3 * sizeof(float);
+  return plan;
+}
+
+template <typename T>
+cudaError_t gn_nchw_l2_launch(const T* x, T* y, const float* gamma, const float* beta, int batch,
+                              int channels, long long spatial, int groups, float eps, int silu,
+                              void* workspace, float* stats_out, cudaStream_t stream) {
+  const GnL2Plan plan = gn_nchw_l2_plan(batch, channels, spatial, groups, (int)sizeof(T));
+  if (!plan.feasible) return cudaErrorInvalidValue;
+  L2Params p;
+  p.count = plan.count;
+  p.chunk = plan.chunk;
+  p.P = plan.P;
+  p.groups_total = plan.groups_total;
+  p.groups = groups;
+  p.channels = channels;
+  p.spatial = spatial;
+  p.eps = eps;
+  p.silu = silu;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.arrive = reinterpret_cast<int*>(ws);
+  p.partials = reinterpret_cast<float*>(ws + ((size_t)plan.groups_total * sizeof(int) + 255) / 256 * 256);
+  p.stats_out = stats_out;
+  cudaError_t e = cudaMemsetAsync(p.arrive, 0, (size_t)plan.groups_total * sizeof(int), stream);
+  if (e != cudaSuccess) return e;
+  const long long items = (long long)plan.groups_total * plan.P;
+  int grid = plan.grid;
+  if (items < grid) grid = (int)items;
+  void* args[] = {(void*)&x, (void*)&y, (void*)&gamma, (void*)&beta, (void*)&p};
+  // A cooperative launch guarantees that all CTAs are resident, which the
+  // cross-CTA group wait needs.
+  return cudaLaunchCooperativeKernel(reinterpret_cast<void*>(gn_nchw_l2_kernel<T>), dim3(grid),
+                                     dim3(kL2Threads), args, 0, stream);
+}
+
+template cudaError_t gn_nchw_l2_launch<float>(const float*, float*, const float*, const float*,
+                                              int, int, long long, int, float, int, void*, float*,
+                                              cudaStream_t);
+template cudaError_t gn_nchw_l2_launch<__nv_bfloat16>(const __nv_bfloat16*, __nv_bfloat16*,
+                                                      const float*, const float*, int, int,
+                                                      long long, int, float, int, void*, float*,
+                                                      cudaStream_t);
+template cudaError_t gn_nchw_l2_launch<__half>(const __half*, __half*, const float*, const float*,
+                                               int, int, long long, int, float, int, void*, float*,
+                                               cudaStream_t);
 
 GnFusedPlan gn_fused_plan(int batch, int channels, long long spatial, int groups, int elem_bytes) {
   GnFusedPlan plan{};

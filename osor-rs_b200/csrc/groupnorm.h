@@ -11,6 +11,24 @@ namespace osor {
 constexpr int kGnFusedSmemBytes = 96 * 1024;
 constexpr int kGnFusedCtasPerSm = 2;
 
+// Standalone NCHW GroupNorm(+SiLU) with one HBM read and write per element
+// (chunks re-read from L2): gn_nchw_l2_launch. Workspace: group counters (zeroed by the launch) and
+// chunk partials.
+struct GnL2Plan {
+  int groups_total;
+  long long count;
+  long long chunk;
+  int P;
+  int grid;
+  bool feasible;  // H * W a multiple of the 16-byte vector width, groups fit one wave
+  size_t workspace_bytes;
+};
+GnL2Plan gn_nchw_l2_plan(int batch, int channels, long long spatial, int groups, int elem_bytes);
+template <typename T>
+cudaError_t gn_nchw_l2_launch(const T* x, T* y, const float* gamma, const float* beta, int batch,
+                              int channels, long long spatial, int groups, float eps, int silu,
+                              void* workspace, float* stats_out, cudaStream_t stream);
+
 struct GnFusedPlan {
   int groups_total;
   long long count;

@@ -104,7 +104,10 @@ def test_constant_groups_return_bias(cuda_device):
 
 # Standalone-op workload of the benchmark config (seed 3: x ~ N(0.5, 2),
 # gamma ~ N(1, 0.1), beta ~ N(0, 0.1)) at sizes the oracle finishes quickly.
-HALF_SHAPES = [(2, 512, 32, 32), (1, 256, 64, 64), (1, 128, 128, 128), (2, 64, 15, 17)]
+# The last two run the NCHW kernels over several waves of their persistent
+# grids (more group chunks than resident CTAs).
+HALF_SHAPES = [(2, 512, 32, 32), (1, 256, 64, 64), (1, 128, 128, 128), (2, 64, 15, 17),
+               (4, 128, 256, 256), (2, 256, 256, 256)]
 
 
 @pytest.mark.parametrize("shape", HALF_SHAPES)
@@ -128,3 +131,17 @@ def test_half_matches_oracle(shape, layout, dt, cuda_device):
     np.testing.assert_allclose(s[..., 1], var, rtol=1e-4)
     err = np.abs(y - ref)
     assert np.all(err <= 2 ** -8 * np.abs(ref) + 1e-3), err.max()
+
+
+def test_shared_memory_nchw_kernel_matches_oracle(cuda_device):
+    """The NCHW op takes the L2-resident two-pass kernel when its vectors fit;
+    OSOR_GN_NCHW_L2=0 (read once per process) selects the shared-memory-
+    resident one, checked here on the same cases in a child process."""
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ, OSOR_GN_NCHW_L2="0")
+    r = subprocess.run([sys.executable, "-m", "pytest", __file__, "-q", "-p", "no:cacheprovider",
+                        "-k", "test_half_matches_oracle and nchw"],
+                       env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]

@@ -57,11 +57,13 @@ def test_noalloc_matches_workspace_entry_point_twice(shape, dt, cuda_device):
         _lib.check(lb.osor_group_norm_silu_noalloc(_p(xt), _p(out), _p(g), _p(b), b_, c, h, w,
                                                    code, 1e-6, 1, _p(stats), _stream()))
         torch.cuda.synchronize()
-        # Same kernel and plan: identical values; the tolerance is the one
-        # the GroupNorm parity tests use for 16-bit outputs.
+        # The workspace entry point may take the L2-resident NCHW kernel, whose
+        # chunking differs from the shared-memory-resident one that the fixed
+        # scratch serves: statistics agree to rounding, outputs to one ulp of
+        # the 16-bit type (bf16: 2^-7 relative).
         got, want = out.float().cpu().numpy(), ref.float().cpu().numpy()
         assert np.all(np.isfinite(got))
-        assert np.all(np.abs(got - want) <= 2 ** -8 * np.abs(want) + 1e-3)
+        assert np.all(np.abs(got - want) <= 2 ** -7 * np.abs(want) + 1e-3)
         np.testing.assert_allclose(stats.cpu().numpy(), ref_stats.cpu().numpy(), rtol=1e-4,
                                    atol=1e-6)
     assert _lib.lib().osor_device_status(0, 1) == 0
