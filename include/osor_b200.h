@@ -181,6 +181,27 @@ int osor_group_norm_silu_noalloc(const void* x, void* y, const float* gamma, con
                                  int batch, int channels, int height, int width, int dtype,
                                  float eps, int silu, float* stats, void* stream);
 
+/* The statistics half of StableGroupNorm::forward_reference
+ * (src/native/vae_encoder.rs:55-75) on 16-bit NHWC x: stats (device f32
+ * [B][32][2]) receives each group's (mean, biased variance). With
+ * osor_group_norm_apply it lets several GPUs that each hold a row band of one
+ * image normalize it together: every band's statistics are gathered and merged
+ * by the apply. workspace: osor_group_norm_workspace_size(..., NHWC, dtype). */
+int osor_group_norm_stats(const void* x, int batch, int channels, int height, int width,
+                          int dtype, float* stats, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/* The normalization half (vae_encoder.rs:76-80, plus SiLU when `silu`, :103)
+ * on 16-bit NHWC x -> y with statistics merged from `parts` sets part_stats
+ * (device f32 [parts][B][32][2], each set over the same number of elements,
+ * as osor_group_norm_stats writes them for equal bands): mean = mean of the
+ * means, variance = mean of the variances + mean squared deviation of the
+ * means. workspace: at least B * C * 16 bytes. */
+int osor_group_norm_apply(const void* x, void* y, const float* gamma, const float* beta,
+                          const float* part_stats, int parts, int batch, int channels, int height,
+                          int width, int dtype, float eps, int silu, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
 /* Nearest 2x upsample of 16-bit NHWC [B][H][W][C] -> [B][2H][2W][C], C % 8 == 0.
  * Replaces upsample_2x (src/native/vae_decoder.rs:18-35). */
 int osor_upsample_2x(const void* x, void* y, int batch, int height, int width, int channels,
@@ -197,6 +218,18 @@ size_t osor_attention_workspace_size(int batch, int tokens, int dim);
 int osor_attention(const void* q, const void* k, const void* v, void* out, int batch, int tokens,
                    int dim, long long ld, int dtype, void* workspace, size_t workspace_bytes,
                    void* stream);
+
+/* Device workspace for osor_attention_kv. */
+size_t osor_attention_kv_workspace_size(int batch, int n_q, int n_kv, int dim);
+
+/* out = softmax(q k^T) v per batch entry with n_q query rows (row stride ld_q)
+ * against n_kv key / value rows (row stride ld_kv); out: [B][n_q][D]
+ * contiguous. The row band of one image on one GPU attends to the keys and
+ * values gathered from every band. Replaces attend (src/native/attention.rs
+ * :10-25), whose q and k already allow different row counts. */
+int osor_attention_kv(const void* q, long long ld_q, const void* k, const void* v, long long ld_kv,
+                      void* out, int batch, int n_q, int n_kv, int dim, int dtype,
+                      void* workspace, size_t workspace_bytes, void* stream);
 
 /* One profiled op: kind ("conv_tc", "conv_direct", "groupnorm", ...),
  * algorithmic FLOPs and bytes, device time between the CUDA events recorded

@@ -6,6 +6,7 @@
 #include "conv_tc.h"
 #include "groupnorm.h"
 #include "ops.h"
+#include "profile.h"
 #include "vae.h"
 
 struct osor_vae {
@@ -280,7 +281,9 @@ int osor_group_norm_silu(const void* x, void* y, const float* gamma, const float
       return fail(OSOR_ERR_INVALID_INPUT, "NHWC tensors must be 16-byte aligned");
     e = osor::gn_nhwc_launch(internal_dtype(dtype), x, y, gamma, beta, batch, channels, spatial, 32,
                              eps, silu, workspace, stats, s);
+    osor::note_launches(3);
   } else if (nchw_l2_ok(x, y, batch, channels, spatial, dtype)) {
+    osor::note_launches(1);
     // One HBM read and write per element; chunks re-read from L2.
     if (dtype == OSOR_DTYPE_F32)
       e = osor::gn_nchw_l2_launch<float>(static_cast<const float*>(x), static_cast<float*>(y),
@@ -296,19 +299,67 @@ int osor_group_norm_silu(const void* x, void* y, const float* gamma, const float
                                           gamma, beta, batch, channels, spatial, 32, eps, silu,
                                           workspace, stats, s);
   } else if (dtype == OSOR_DTYPE_F32) {
+    osor::note_launches(1);
     e = osor::gn_fused_launch<float>(static_cast<const float*>(x), static_cast<float*>(y), gamma,
                                      beta, batch, channels, spatial, 32, eps, silu, workspace, stats,
                                      s);
   } else if (dtype == OSOR_DTYPE_BF16) {
+    osor::note_launches(1);
     e = osor::gn_fused_launch<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x),
                                              static_cast<__nv_bfloat16*>(y), gamma, beta, batch,
                                              channels, spatial, 32, eps, silu, workspace, stats, s);
   } else {
+    osor::note_launches(1);
     e = osor::gn_fused_launch<__half>(static_cast<const __half*>(x), static_cast<__half*>(y), gamma,
                                       beta, batch, channels, spatial, 32, eps, silu, workspace,
                                       stats, s);
   }
   return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "group norm");
+}
+
+int osor_group_norm_stats(const void* x, int batch, int channels, int height, int width,
+                          int dtype, float* stats, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  if (!x || !stats) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (batch <= 0 || height <= 0 || width <= 0 || channels <= 0 || channels % 32 != 0)
+    return fail(OSOR_ERR_INVALID_INPUT, "VAE group normalization requires channels divisible by 32");
+  const size_t need =
+      osor_group_norm_workspace_size(batch, channels, height, width, OSOR_LAYOUT_NHWC, dtype);
+  if (need == 0) return fail(OSOR_ERR_INVALID_INPUT, "unsupported group-norm shape or dtype");
+  if (!workspace || workspace_bytes < need)
+    return fail(OSOR_ERR_INVALID_INPUT, "group-norm workspace is too small");
+  if (!aligned16(x)) return fail(OSOR_ERR_INVALID_INPUT, "NHWC tensors must be 16-byte aligned");
+  DeviceOf dev(x);
+  cudaError_t e = osor::gn_nhwc_stats_launch(internal_dtype(dtype), x, batch, channels,
+                                             (long long)height * width, 32, workspace, stats,
+                                             static_cast<cudaStream_t>(stream));
+  osor::note_launches(2);
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "group-norm statistics");
+}
+
+int osor_group_norm_apply(const void* x, void* y, const float* gamma, const float* beta,
+                          const float* part_stats, int parts, int batch, int channels, int height,
+                          int width, int dtype, float eps, int silu, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  if (!x || !y || !gamma || !beta || !part_stats)
+    return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (parts <= 0) return fail(OSOR_ERR_INVALID_INPUT, "at least one statistics set is needed");
+  if (batch <= 0 || height <= 0 || width <= 0 || channels <= 0 || channels % 32 != 0)
+    return fail(OSOR_ERR_INVALID_INPUT, "VAE group normalization requires channels divisible by 32");
+  const size_t need =
+      osor_group_norm_workspace_size(batch, channels, height, width, OSOR_LAYOUT_NHWC, dtype);
+  if (need == 0) return fail(OSOR_ERR_INVALID_INPUT, "unsupported group-norm shape or dtype");
+  if (!workspace || workspace_bytes < (size_t)batch * channels * 4 * sizeof(float))
+    return fail(OSOR_ERR_INVALID_INPUT, "group-norm workspace is too small");
+  if (!aligned16(x) || !aligned16(y))
+    return fail(OSOR_ERR_INVALID_INPUT, "NHWC tensors must be 16-byte aligned");
+  DeviceOf dev(x);
+  cudaError_t e = osor::gn_nhwc_apply_stats_launch(
+      internal_dtype(dtype), x, y, gamma, beta, part_stats, parts, batch, channels,
+      (long long)height * width, 32, eps, silu, static_cast<float*>(workspace),
+      static_cast<cudaStream_t>(stream));
+  osor::note_launches(2);
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "group-norm apply");
 }
 
 int osor_upsample_2x(const void* x, void* y, int batch, int height, int width, int channels,
@@ -321,51 +372,63 @@ int osor_upsample_2x(const void* x, void* y, int batch, int height, int width, i
   DeviceOf dev(x);
   cudaError_t e = osor::upsample2x_nhwc_launch(x, y, batch, height, width, channels,
                                                static_cast<cudaStream_t>(stream));
+  osor::note_launches(1);
   return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "upsample");
 }
 
-size_t osor_attention_workspace_size(int batch, int tokens, int dim) {
+size_t osor_attention_kv_workspace_size(int batch, int n_q, int n_kv, int dim) {
   (void)batch;
-  if (tokens <= 0 || dim <= 0) return 0;
-  const size_t a = ((size_t)tokens * tokens * 4 + 255) / 256 * 256;
-  const size_t b = ((size_t)tokens * tokens * 2 + 255) / 256 * 256;
-  const size_t c = ((size_t)tokens * 4 + 255) / 256 * 256;
-  const size_t d = ((size_t)tokens * dim * 2 + 255) / 256 * 256;
+  if (n_q <= 0 || n_kv <= 0 || dim <= 0) return 0;
+  const size_t a = ((size_t)n_q * n_kv * 4 + 255) / 256 * 256;
+  const size_t b = ((size_t)n_q * n_kv * 2 + 255) / 256 * 256;
+  const size_t c = ((size_t)n_q * 4 + 255) / 256 * 256;
+  const size_t d = ((size_t)n_kv * dim * 2 + 255) / 256 * 256;
   return a + b + c + d;
 }
 
-int osor_attention(const void* q, const void* k, const void* v, void* out, int batch, int tokens,
-                   int dim, long long ld, int dtype, void* workspace, size_t workspace_bytes,
-                   void* stream) {
+size_t osor_attention_workspace_size(int batch, int tokens, int dim) {
+  return osor_attention_kv_workspace_size(batch, tokens, tokens, dim);
+}
+
+int osor_attention_kv(const void* q, long long ld_q, const void* k, const void* v, long long ld_kv,
+                      void* out, int batch, int n_q, int n_kv, int dim, int dtype,
+                      void* workspace, size_t workspace_bytes, void* stream) {
   if (!q || !k || !v || !out) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
-  if (batch <= 0 || tokens <= 0 || dim <= 0 || dim > 512 || ld < dim)
+  if (batch <= 0 || n_q <= 0 || n_kv <= 0 || dim <= 0 || dim > 512 || ld_q < dim || ld_kv < dim)
     return fail(OSOR_ERR_INVALID_INPUT, "attention tensor shapes are incompatible");
   if (!is16(dtype)) return fail(OSOR_ERR_INVALID_INPUT, "attention dtype must be BF16 or F16");
-  const size_t need = osor_attention_workspace_size(batch, tokens, dim);
+  const size_t need = osor_attention_kv_workspace_size(batch, n_q, n_kv, dim);
   if (!workspace || workspace_bytes < need)
     return fail(OSOR_ERR_INVALID_INPUT, "attention workspace is too small");
   DeviceOf dev(q);
   uint8_t* w = static_cast<uint8_t*>(workspace);
   float* scores = reinterpret_cast<float*>(w);
-  w += ((size_t)tokens * tokens * 4 + 255) / 256 * 256;
+  w += ((size_t)n_q * n_kv * 4 + 255) / 256 * 256;
   void* probs = w;
-  w += ((size_t)tokens * tokens * 2 + 255) / 256 * 256;
+  w += ((size_t)n_q * n_kv * 2 + 255) / 256 * 256;
   float* rowsum = reinterpret_cast<float*>(w);
-  w += ((size_t)tokens * 4 + 255) / 256 * 256;
+  w += ((size_t)n_q * 4 + 255) / 256 * 256;
   void* vt = w;
-  // Batch entries are [N][D] blocks of stride N*ld inside q/k/v.
+  // Batch entries are [n][D] blocks of stride n*ld inside q/k/v.
   osor::Status s;
   const uint16_t* qb = static_cast<const uint16_t*>(q);
   const uint16_t* kb = static_cast<const uint16_t*>(k);
   const uint16_t* vb = static_cast<const uint16_t*>(v);
   uint16_t* ob = static_cast<uint16_t*>(out);
   for (int b = 0; b < batch && s.good(); ++b) {
-    const long long off = (long long)b * tokens * ld;
-    s = osor::attention_core(internal_dtype(dtype), qb + off, kb + off, vb + off, ld,
-                             ob + (long long)b * tokens * dim, dim, 1, tokens, dim, scores, probs,
+    const long long oq = (long long)b * n_q * ld_q, okv = (long long)b * n_kv * ld_kv;
+    s = osor::attention_core(internal_dtype(dtype), qb + oq, ld_q, kb + okv, vb + okv, ld_kv,
+                             ob + (long long)b * n_q * dim, dim, 1, n_q, n_kv, dim, scores, probs,
                              rowsum, vt, static_cast<cudaStream_t>(stream));
   }
   return report(s);
+}
+
+int osor_attention(const void* q, const void* k, const void* v, void* out, int batch, int tokens,
+                   int dim, long long ld, int dtype, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  return osor_attention_kv(q, ld, k, v, ld, out, batch, tokens, tokens, dim, dtype, workspace,
+                           workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -408,18 +408,53 @@ __global__ void __launch_bounds__(256)
   float var = (float)(s2 / count) - dm * dm;
   var = fmaxf(var, 0.0f);
   const float rstd = 1.0f / sqrtf(var + eps);
-  for (int i = threadIdx.x; i < cpg; i += blockDim.x) {
-    const int c = g * cpg + i;
-    float* o = coef + ((long long)b * channels + c) * 4;
-    o[0] = mean;
-    o[1] = rstd * gamma[c];
-    o[2] = beta[c];
-    o[3] = 0.0f;
+  if (gamma) {
+    for (int i = threadIdx.x; i < cpg; i += blockDim.x) {
+      const int c = g * cpg + i;
+      float* o = coef + ((long long)b * channels + c) * 4;
+      o[0] = mean;
+      o[1] = rstd * gamma[c];
+      o[2] = beta[c];
+      o[3] = 0.0f;
+    }
   }
   if (threadIdx.x == 0 && stats_out) {
     stats_out[((long long)b * groups + g) * 2] = mean;
     stats_out[((long long)b * groups + g) * 2 + 1] = var;
   }
+}
+
+// coef[b][c] = (mean, rstd * gamma[c], beta[c], 0) from `parts` given
+// per-(image, group) (mean, var) sets, part_stats[p][b][g][2], each over the
+// same number of elements (e.g. equal row bands of one image held by several
+// GPUs). The merge of equal counts is the mean of the means and
+// var = mean(var_p) + mean((mean_p - mean)^2).
+__global__ void gn_coef_from_stats_kernel(const float* __restrict__ part_stats, int parts,
+                                          int batch, int channels, int groups,
+                                          const float* __restrict__ gamma,
+                                          const float* __restrict__ beta, float eps,
+                                          float* __restrict__ coef) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // b * channels + c
+  if (i >= batch * channels) return;
+  const int b = i / channels, c = i - b * channels;
+  const int g = c / (channels / groups);
+  const long long set = (long long)batch * groups * 2;
+  const float* ps = part_stats + ((long long)b * groups + g) * 2;
+  float mean = 0.0f;
+  for (int p = 0; p < parts; ++p) mean += ps[p * set];
+  mean /= (float)parts;
+  float var = 0.0f;
+  for (int p = 0; p < parts; ++p) {
+    const float d = ps[p * set] - mean;
+    var += fmaxf(ps[p * set + 1], 0.0f) + d * d;
+  }
+  var /= (float)parts;
+  const float rstd = 1.0f / sqrtf(var + eps);
+  float* o = coef + (long long)i * 4;
+  o[0] = mean;
+  o[1] = rstd * gamma[c];
+  o[2] = beta[c];
+  o[3] = 0.0f;
 }
 
 // grid (groups, batch): combine the per-tile (mean, M2) partials that the
@@ -1023,6 +1058,42 @@ cudaError_t gn_nhwc_apply_tiles_launch(int dtype, const void* x, void* y, const 
   const float tile_count = 128.0f * (float)(channels / groups);
   gn_tiles_finalize_kernel<<<dim3(groups, batch), 256, 0, stream>>>(
       tile_part, tiles, tile_count, channels, groups, gamma, beta, eps, coef, stats_out);
+  if (dtype == kF16) return apply_launch<kF16>(x, y, coef, batch, channels, pixels, silu, stream);
+  return apply_launch<kBf16>(x, y, coef, batch, channels, pixels, silu, stream);
+}
+
+cudaError_t gn_nhwc_stats_launch(int dtype, const void* x, int batch, int channels,
+                                 long long pixels, int groups, void* workspace, float* mean_var,
+                                 cudaStream_t stream) {
+  const GnNhwcPlan plan = gn_nhwc_plan(batch, channels, pixels, groups);
+  float* partials = static_cast<float*>(workspace);
+  const int vc = channels / 8;
+  const int rows = plan.threads / vc;
+  const size_t sred = (size_t)rows * vc * 16 * sizeof(float);
+  const uint16_t* xs = static_cast<const uint16_t*>(x);
+  if (dtype == kF16) {
+    gn_nhwc_stats_kernel<kF16><<<dim3(plan.chunks, batch), plan.threads, sred, stream>>>(
+        xs, partials, channels, pixels, plan.pix_per_chunk, groups);
+    gn_nhwc_finalize_kernel<kF16><<<dim3(groups, batch), 256, 0, stream>>>(
+        xs, partials, plan.chunks, channels, pixels, groups, nullptr, nullptr, 0.0f, nullptr,
+        mean_var);
+  } else {
+    gn_nhwc_stats_kernel<kBf16><<<dim3(plan.chunks, batch), plan.threads, sred, stream>>>(
+        xs, partials, channels, pixels, plan.pix_per_chunk, groups);
+    gn_nhwc_finalize_kernel<kBf16><<<dim3(groups, batch), 256, 0, stream>>>(
+        xs, partials, plan.chunks, channels, pixels, groups, nullptr, nullptr, 0.0f, nullptr,
+        mean_var);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t gn_nhwc_apply_stats_launch(int dtype, const void* x, void* y, const float* gamma,
+                                       const float* beta, const float* part_stats, int parts,
+                                       int batch, int channels, long long pixels, int groups,
+                                       float eps, int silu, float* coef, cudaStream_t stream) {
+  const int total = batch * channels;
+  gn_coef_from_stats_kernel<<<(total + 255) / 256, 256, 0, stream>>>(
+      part_stats, parts, batch, channels, groups, gamma, beta, eps, coef);
   if (dtype == kF16) return apply_launch<kF16>(x, y, coef, batch, channels, pixels, silu, stream);
   return apply_launch<kBf16>(x, y, coef, batch, channels, pixels, silu, stream);
 }

@@ -67,6 +67,18 @@ cudaError_t gn_nhwc_launch(int dtype, const void* x, void* y, const float* gamma
 // tensor-core convolution (ConvTcArgs::gn_part): finalize from the per-tile
 // (mean, M2) partials, then the streaming apply. pixels % 128 == 0. `coef` is
 // batch * channels * 4 floats of scratch.
+// Statistics only: mean_var[b][g] = (mean, var) of 16-bit NHWC x (workspace
+// as gn_nhwc_plan's partials).
+cudaError_t gn_nhwc_stats_launch(int dtype, const void* x, int batch, int channels,
+                                 long long pixels, int groups, void* workspace, float* mean_var,
+                                 cudaStream_t stream);
+// Apply only, from `parts` sets of per-(image, group) (mean, var) over equal
+// element counts, part_stats[p][b][g][2], merged in the kernel; coef is
+// scratch of batch * channels * 4 floats.
+cudaError_t gn_nhwc_apply_stats_launch(int dtype, const void* x, void* y, const float* gamma,
+                                       const float* beta, const float* part_stats, int parts,
+                                       int batch, int channels, long long pixels, int groups,
+                                       float eps, int silu, float* coef, cudaStream_t stream);
 cudaError_t gn_nhwc_apply_tiles_launch(int dtype, const void* x, void* y, const float* gamma,
                                        const float* beta, int batch, int channels,
                                        long long pixels, int groups, float eps, int silu,

@@ -215,13 +215,14 @@ __global__ void transpose16_kernel(const uint16_t* __restrict__ in, long long ld
 
 // ------------------------------------------------------------ CUDA-core attention
 // One warp per query row, online softmax over keys, fp32. q already scaled.
-// q/k/v rows have stride ld (elements); out rows stride ld_out.
+// q rows have stride ld_q, k/v rows stride ld_kv, out rows stride ld_out
+// (elements).
 template <int D>
-__global__ void attention_rows_kernel(const uint16_t* __restrict__ qb,
+__global__ void attention_rows_kernel(const uint16_t* __restrict__ qb, long long ld_q,
                                       const uint16_t* __restrict__ kb,
                                       const uint16_t* __restrict__ vb, long long ld,
-                                      uint16_t* __restrict__ ob, long long ld_out, int tokens,
-                                      int dim) {
+                                      uint16_t* __restrict__ ob, long long ld_out, int n_q,
+                                      int tokens, int dim) {
   using E = Elem<D>;
   using T = typename E::T;
   const T* q = reinterpret_cast<const T*>(qb);
@@ -231,9 +232,9 @@ __global__ void attention_rows_kernel(const uint16_t* __restrict__ qb,
   extern __shared__ float qs[];  // [warps][dim]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
-  if (row >= tokens) return;
+  if (row >= n_q) return;
   float* qrow = qs + warp * dim;
-  for (int c = lane; c < dim; c += 32) qrow[c] = E::to_f(q[row * ld + c]);
+  for (int c = lane; c < dim; c += 32) qrow[c] = E::to_f(q[row * ld_q + c]);
   __syncwarp();
   constexpr int kMaxPer = 16;  // dim <= 512
   float acc[kMaxPer];
@@ -408,21 +409,23 @@ cudaError_t transpose16_launch(const void* in, long long ld_in, void* out, long 
   return cudaGetLastError();
 }
 
-cudaError_t attention_rows_launch(int dtype, const void* q, const void* k, const void* v,
-                                  long long ld, void* out, long long ld_out, int tokens, int dim,
-                                  cudaStream_t s) {
+cudaError_t attention_rows_launch(int dtype, const void* q, long long ld_q, const void* k,
+                                  const void* v, long long ld_kv, void* out, long long ld_out,
+                                  int n_q, int n_kv, int dim, cudaStream_t s) {
   if (dim > 512) return cudaErrorInvalidValue;
   const int warps = 4;
-  const dim3 grid((tokens + warps - 1) / warps);
+  const dim3 grid((n_q + warps - 1) / warps);
   const size_t smem = (size_t)warps * dim * sizeof(float);
   const uint16_t* qb = static_cast<const uint16_t*>(q);
   const uint16_t* kb = static_cast<const uint16_t*>(k);
   const uint16_t* vb = static_cast<const uint16_t*>(v);
   uint16_t* ob = static_cast<uint16_t*>(out);
   if (dtype == kF16)
-    attention_rows_kernel<kF16><<<grid, warps * 32, smem, s>>>(qb, kb, vb, ld, ob, ld_out, tokens, dim);
+    attention_rows_kernel<kF16><<<grid, warps * 32, smem, s>>>(qb, ld_q, kb, vb, ld_kv, ob, ld_out,
+                                                               n_q, n_kv, dim);
   else
-    attention_rows_kernel<kBf16><<<grid, warps * 32, smem, s>>>(qb, kb, vb, ld, ob, ld_out, tokens, dim);
+    attention_rows_kernel<kBf16><<<grid, warps * 32, smem, s>>>(qb, ld_q, kb, vb, ld_kv, ob,
+                                                                ld_out, n_q, n_kv, dim);
   return cudaGetLastError();
 }
 

@@ -34,10 +34,11 @@ cudaError_t softmax_rows_launch(int dtype, const float* scores, void* probs, flo
 cudaError_t transpose16_launch(const void* in, long long ld_in, void* out, long long ld_out,
                                int rows, int cols, cudaStream_t s);
 
-// softmax(q k^T) v on CUDA cores, one warp per query (dim <= 512).
-cudaError_t attention_rows_launch(int dtype, const void* q, const void* k, const void* v,
-                                  long long ld, void* out, long long ld_out, int tokens, int dim,
-                                  cudaStream_t s);
+// softmax(q k^T) v on CUDA cores, one warp per query (dim <= 512): n_q query
+// rows of stride ld_q against n_kv key / value rows of stride ld_kv.
+cudaError_t attention_rows_launch(int dtype, const void* q, long long ld_q, const void* k,
+                                  const void* v, long long ld_kv, void* out, long long ld_out,
+                                  int n_q, int n_kv, int dim, cudaStream_t s);
 
 cudaError_t nchw_f32_to_nhwc16_launch(int dtype, const float* x, void* y, int batch, int c,
                                       long long hw, cudaStream_t s);

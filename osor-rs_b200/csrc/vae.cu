@@ -453,8 +453,8 @@ Status attention(const Ctx& c, const AttentionLayer& L, int xi, int batch, int h
   uint16_t* vt = c.b.act[ti];  // the normalized input is dead after the projection
   c.has_stats[ti] = false;
   c.has_stats[oi] = false;
-  st = attention_core(c.dtype, qkv, qkv + ch, qkv + 2 * ch, 3 * ch, c.b.act[oi], ch, batch, n, ch,
-                      c.b.scores, c.b.probs, c.b.rowsum, vt, c.s);
+  st = attention_core(c.dtype, qkv, 3 * ch, qkv + ch, qkv + 2 * ch, 3 * ch, c.b.act[oi], ch, batch,
+                      n, n, ch, c.b.scores, c.b.probs, c.b.rowsum, vt, c.s);
   if (!st.good()) return st;
   // Output projection + residual, in place.
   return conv16(c, L.out, oi, 1, 1, batch * n, xi, c.b.act[xi], true);
@@ -487,102 +487,107 @@ bool attention_tc_ok(int tokens, int dim) {
 
 }  // namespace
 
-Status attention_core(int dtype, const void* q, const void* k, const void* v, long long ld,
-                      void* out, long long ld_out, int batch, int tokens, int dim, float* scores,
-                      void* probs, float* rowsum, void* vt, cudaStream_t s) {
+Status attention_core(int dtype, const void* q, long long ld_q, const void* k, const void* v,
+                      long long ld_kv, void* out, long long ld_out, int batch, int n_q, int n_kv,
+                      int dim, float* scores, void* probs, float* rowsum, void* vt,
+                      cudaStream_t s) {
   const uint16_t* qb = static_cast<const uint16_t*>(q);
   const uint16_t* kb = static_cast<const uint16_t*>(k);
   const uint16_t* vb = static_cast<const uint16_t*>(v);
   uint16_t* ob = static_cast<uint16_t*>(out);
-  if (!attention_tc_ok(tokens, dim)) {
+  if (!attention_tc_ok(n_q, dim) || !attention_tc_ok(n_kv, dim)) {
     for (int bi = 0; bi < batch; ++bi) {
-      const long long off = (long long)bi * tokens;
-      OpScope scope("attn_cuda_core", 4.0 * tokens * tokens * dim, 8.0 * tokens * dim, s, 1);
-      cudaError_t e = attention_rows_launch(dtype, qb + off * ld, kb + off * ld, vb + off * ld, ld,
-                                            ob + off * ld_out, ld_out, tokens, dim, s);
+      const long long oq = (long long)bi * n_q, okv = (long long)bi * n_kv;
+      OpScope scope("attn_cuda_core", 4.0 * n_q * n_kv * dim, 4.0 * (n_q + n_kv) * dim, s, 1);
+      cudaError_t e = attention_rows_launch(dtype, qb + oq * ld_q, ld_q, kb + okv * ld_kv,
+                                            vb + okv * ld_kv, ld_kv, ob + oq * ld_out, ld_out,
+                                            n_q, n_kv, dim, s);
       if (e != cudaSuccess) return cuda_status(e, "attention");
     }
     return Status::ok();
   }
-  if (fused_attention_enabled() && attn_fused_ok(tokens, dim, ld, ld_out, q, k, vt, out)) {
+  if (n_q == n_kv && ld_q == ld_kv && fused_attention_enabled() &&
+      attn_fused_ok(n_q, dim, ld_q, ld_out, q, k, vt, out)) {
     // V^T of every image, then one fused launch over all images: the scores
     // stay in TMEM / shared memory.
+    const int tokens = n_q;
     cudaError_t e;
     for (int bi = 0; bi < batch; ++bi) {
       const long long off = (long long)bi * tokens;
       OpScope scope("attn_transpose", 0.0, 4.0 * tokens * dim, s, 1);
-      e = transpose16_launch(vb + off * ld, ld, static_cast<uint16_t*>(vt) + off * dim, tokens,
-                             tokens, dim, s);
+      e = transpose16_launch(vb + off * ld_kv, ld_kv, static_cast<uint16_t*>(vt) + off * dim,
+                             tokens, tokens, dim, s);
       if (e != cudaSuccess) return cuda_status(e, "attention transpose");
     }
     const double nn = (double)tokens * tokens;
     OpScope scope("attn_fused", 4.0 * batch * nn * dim, 8.0 * batch * tokens * dim, s, 1);
-    return cuda_status(attn_fused_launch(dtype, q, k, ld, vt, out, ld_out, batch, tokens, dim, s),
-                       "fused attention");
+    return cuda_status(
+        attn_fused_launch(dtype, q, k, ld_q, vt, out, ld_out, batch, tokens, dim, s),
+        "fused attention");
   }
   for (int bi = 0; bi < batch; ++bi) {
-    const long long off = (long long)bi * tokens;
-    // scores = q k^T (fp32)
+    const long long oq = (long long)bi * n_q, okv = (long long)bi * n_kv;
+    // scores = q k^T (fp32), [n_q][n_kv]
     ConvTcArgs a;
     a.dtype = dtype;
-    a.x = qb + off * ld;
+    a.x = qb + oq * ld_q;
     a.batch = 1;
     a.in_h = 1;
-    a.in_w = tokens;
+    a.in_w = n_q;
     a.cin = dim;
-    a.pixel_stride = ld;
+    a.pixel_stride = ld_q;
     a.ksize = 1;
     a.stride = 1;
     a.pad = 0;
     a.out_h = 1;
-    a.out_w = tokens;
-    a.cout = tokens;
-    a.w = kb + off * ld;
-    a.ldw = ld;
+    a.out_w = n_q;
+    a.cout = n_kv;
+    a.w = kb + okv * ld_kv;
+    a.ldw = ld_kv;
     a.out = scores;
-    a.ld_out = tokens;
+    a.ld_out = n_kv;
     a.out_f32 = 1;
     if (const char* why = conv_tc_check(a)) return Status::err(OSOR_ERR_INVALID_INPUT, why);
-    const double nn = (double)tokens * tokens;
+    const double nn = (double)n_q * n_kv;
     cudaError_t e;
     {
-      OpScope scope("attn_scores", 2.0 * nn * dim, 4.0 * tokens * dim + 4.0 * nn, s, 1);
+      OpScope scope("attn_scores", 2.0 * nn * dim, 2.0 * (n_q + n_kv) * dim + 4.0 * nn, s, 1);
       e = conv_tc_launch(a, s);
     }
     if (e != cudaSuccess) return cuda_status(e, "attention scores");
     {
       OpScope scope("attn_softmax", 0.0, 6.0 * nn, s, 1);
-      e = softmax_rows_launch(dtype, scores, probs, rowsum, tokens, tokens, tokens, tokens, s);
+      e = softmax_rows_launch(dtype, scores, probs, rowsum, n_q, n_kv, n_kv, n_kv, s);
     }
     if (e != cudaSuccess) return cuda_status(e, "attention softmax");
     {
-      OpScope scope("attn_transpose", 0.0, 4.0 * tokens * dim, s, 1);
-      e = transpose16_launch(vb + off * ld, ld, vt, tokens, tokens, dim, s);
+      OpScope scope("attn_transpose", 0.0, 4.0 * n_kv * dim, s, 1);
+      e = transpose16_launch(vb + okv * ld_kv, ld_kv, vt, n_kv, n_kv, dim, s);
     }
     if (e != cudaSuccess) return cuda_status(e, "attention transpose");
-    // out = (P / rowsum) V, with V^T [dim][tokens] as the K-major B operand.
+    // out = (P / rowsum) V, with V^T [dim][n_kv] as the K-major B operand.
     ConvTcArgs pv;
     pv.dtype = dtype;
     pv.x = probs;
     pv.batch = 1;
     pv.in_h = 1;
-    pv.in_w = tokens;
-    pv.cin = tokens;
-    pv.pixel_stride = tokens;
+    pv.in_w = n_q;
+    pv.cin = n_kv;
+    pv.pixel_stride = n_kv;
     pv.ksize = 1;
     pv.stride = 1;
     pv.pad = 0;
     pv.out_h = 1;
-    pv.out_w = tokens;
+    pv.out_w = n_q;
     pv.cout = dim;
     pv.w = vt;
-    pv.ldw = tokens;
-    pv.out = ob + off * ld_out;
+    pv.ldw = n_kv;
+    pv.out = ob + oq * ld_out;
     pv.ld_out = ld_out;
     pv.row_scale = rowsum;
     if (const char* why = conv_tc_check(pv)) return Status::err(OSOR_ERR_INVALID_INPUT, why);
     {
-      OpScope scope("attn_values", 2.0 * nn * dim, 2.0 * nn + 4.0 * tokens * dim, s, 1);
+      OpScope scope("attn_values", 2.0 * nn * dim, 2.0 * nn + 2.0 * (n_q + n_kv) * dim, s, 1);
       e = conv_tc_launch(pv, s);
     }
     if (e != cudaSuccess) return cuda_status(e, "attention values");

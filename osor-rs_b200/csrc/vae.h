@@ -138,10 +138,13 @@ Status run_conv(int dtype, const ConvLayer& L, const void* x, int in_mode, int b
                 long long out_pixel_stride, const void* residual, long long ld_res,
                 cudaStream_t s, float* gn_part = nullptr, bool* gn_done = nullptr);
 
-// softmax(q k^T) v for `batch` images of [tokens][dim] rows (stride ld);
-// scores/probs/rowsum/vt are per-image scratch reused across images.
-Status attention_core(int dtype, const void* q, const void* k, const void* v, long long ld,
-                      void* out, long long ld_out, int batch, int tokens, int dim, float* scores,
-                      void* probs, float* rowsum, void* vt, cudaStream_t s);
+// softmax(q k^T) v for `batch` images: n_q query rows (stride ld_q) against
+// n_kv key / value rows (stride ld_kv) per image. scores [n_q][n_kv] f32,
+// probs [n_q][n_kv] 16-bit, rowsum [n_q] and vt [dim][n_kv] are per-image
+// scratch reused across images.
+Status attention_core(int dtype, const void* q, long long ld_q, const void* k, const void* v,
+                      long long ld_kv, void* out, long long ld_out, int batch, int n_q, int n_kv,
+                      int dim, float* scores, void* probs, float* rowsum, void* vt,
+                      cudaStream_t s);
 
 }  // namespace osor

@@ -101,9 +101,14 @@ SIGNATURES = {
                                   _sz, _vp]),
     "osor_group_norm_silu_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _i, _vp,
                                           _vp]),
+    "osor_group_norm_stats": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp]),
+    "osor_group_norm_apply": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _i, _vp,
+                                   _sz, _vp]),
     "osor_upsample_2x": (_i, [_vp, _vp, _i, _i, _i, _i, _vp]),
     "osor_attention_workspace_size": (_sz, [_i, _i, _i]),
     "osor_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _ll, _i, _vp, _sz, _vp]),
+    "osor_attention_kv_workspace_size": (_sz, [_i, _i, _i, _i]),
+    "osor_attention_kv": (_i, [_vp, _ll, _vp, _vp, _ll, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
     "osor_profile_begin": (None, []),
     "osor_profile_end": (_i, [_vp, _i, ctypes.POINTER(_i)]),
     "osor_launch_count": (_ll, []),

@@ -1,0 +1,255 @@
+"""Row-band split of the VAE decoder over the ranks of a process group.
+
+The reference bounds memory by running each convolution over horizontal row
+bands of its output, one after the other (src/native/conv.rs:98-108,
+src/native/columns.rs:335-362). Here the same row-band geometry is spread over
+GPUs: each of the K ranks of a band group owns a contiguous range of
+R = H / K rows of every activation of one image (H the latent height;
+upsampling doubles R with the image), so one image decodes on K GPUs at once.
+
+Activations are held as *extended* NHWC tensors ``[1, R + 2, W, C]``: rows
+1..R are the band, rows 0 and R + 1 are halo rows. Three exchanges keep the
+result equal to the one-GPU decode:
+
+* halo: before every 3x3 convolution each rank sends its first band row to the
+  rank above and its last band row to the rank below (torch.distributed
+  point-to-point, NCCL over NVLink on GPUs) into their halo rows; the image's
+  top and bottom halo rows are zeros, the convolution's zero padding. The
+  convolution runs over all R + 2 rows with padding 1, and rows 1..R of its
+  output are exact (rows 0 and R + 1 are overwritten by the next exchange).
+* GroupNorm: each rank computes its band's per-group (mean, variance) over
+  rows 1..R (``osor_group_norm_stats``), the ranks all-gather them, and the
+  apply kernel merges the K equal-count sets before normalizing the band
+  (``osor_group_norm_apply``).
+* attention: the ranks all-gather the band's q|k|v projection, and each
+  attends its own queries against every key and value of the image
+  (``osor_attention_kv``).
+
+The block order is the decoder's (src/native/vae_decoder.rs:104-114, the mid
+block src/native/vae_encoder.rs:367-375, resnets :134-151, attention
+:320-339). ``BandDecoder`` drives an op backend: ``CudaBandOps`` calls the
+library's C ABI on this rank's GPU; a CPU backend with the same methods runs
+the same band logic in the multi-process tests.
+"""
+from __future__ import annotations
+
+from typing import Dict, Optional
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import ops
+from ._lib import InvalidInput, LAYOUT_NCHW
+from .weights import SDXL_CHANNELS, SDXL_LAYERS
+
+GROUPS = 32
+
+
+class CudaBandOps:
+    """The decoder's layers on one CUDA device through the C ABI: 16-bit NHWC
+    activations, f32 NCHW at the latent input and the RGB output."""
+
+    def __init__(self, weights: Dict[str, np.ndarray], device="cuda", dtype=torch.float16):
+        if dtype not in ops.HALF_TYPES:
+            raise InvalidInput("band decoder dtype must be bfloat16 or float16")
+        self.w = weights
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self._convs: Dict[str, ops.BandedConv2d] = {}
+        self._norms: Dict[str, ops.StableGroupNorm] = {}
+
+    # -- layers, built on first use
+    def _conv(self, name: str) -> ops.BandedConv2d:
+        c = self._convs.get(name)
+        if c is None:
+            weight = self.w[name + ".weight"]
+            if weight.ndim == 2:
+                weight = weight.reshape(weight.shape[0], weight.shape[1], 1, 1)
+            k = weight.shape[-1]
+            c = ops.BandedConv2d(weight, self.w[name + ".bias"], stride=1, padding=k // 2,
+                                 device=self.device, dtype=self.dtype)
+            self._convs[name] = c
+        return c
+
+    def _qkv(self, prefix: str) -> ops.BandedConv2d:
+        """q|k|v as one 1x1 convolution [3C, C], q and k scaled by C^-1/4
+        (vae_encoder.rs:320-327 scales each of q and k)."""
+        name = prefix + "#qkv"
+        c = self._convs.get(name)
+        if c is None:
+            ws, bs = [], []
+            for part in ("to_q", "to_k", "to_v"):
+                w = np.asarray(self.w[f"{prefix}.{part}.weight"], np.float32)
+                w = w.reshape(w.shape[0], w.shape[1])
+                b = np.asarray(self.w[f"{prefix}.{part}.bias"], np.float32)
+                scale = np.float32(w.shape[1] ** -0.25) if part != "to_v" else np.float32(1)
+                ws.append(w * scale)
+                bs.append(b * scale)
+            weight = np.concatenate(ws)[:, :, None, None]
+            c = ops.BandedConv2d(weight, np.concatenate(bs), stride=1, padding=0,
+                                 device=self.device, dtype=self.dtype)
+            self._convs[name] = c
+        return c
+
+    def _norm(self, name: str) -> ops.StableGroupNorm:
+        n = self._norms.get(name)
+        if n is None:
+            n = ops.StableGroupNorm(self.w[name + ".weight"], self.w[name + ".bias"],
+                                    device=self.device)
+            self._norms[name] = n
+        return n
+
+    # -- the backend methods BandDecoder uses
+    def empty(self, shape, f32: bool = False) -> torch.Tensor:
+        return torch.empty(shape, dtype=torch.float32 if f32 else self.dtype, device=self.device)
+
+    def zeros(self, shape, f32: bool = False) -> torch.Tensor:
+        return torch.zeros(shape, dtype=torch.float32 if f32 else self.dtype, device=self.device)
+
+    def conv(self, name, x, residual=None, out=None, out_nchw=False):
+        layout = LAYOUT_NCHW if out_nchw else ops._lib.LAYOUT_NHWC
+        return self._conv(name).forward_checked(x, residual=residual, out_layout=layout, out=out)
+
+    def qkv(self, prefix, h):
+        return self._qkv(prefix).forward_checked(h)
+
+    def upsample(self, x):
+        return ops.upsample_2x(x)
+
+    def gn_stats(self, name, x):
+        return self._norm(name).stats(x)
+
+    def gn_apply(self, name, x, part_stats, silu, out):
+        return self._norm(name).apply(x, part_stats, silu, out=out)
+
+    def attend(self, q, k, v):
+        return ops.attend_kv(q, k, v)
+
+
+class BandDecoder:
+    """VaeDecoder::forward (src/native/vae_decoder.rs:104-114) on the rank's
+    row band of one image. ``group`` is the band group (default: the whole
+    world); rank r of K owns latent rows [r R, (r + 1) R), R = h / K."""
+
+    def __init__(self, backend, channels=SDXL_CHANNELS, layers: int = SDXL_LAYERS,
+                 group: Optional[dist.ProcessGroup] = None):
+        self.ops = backend
+        self.channels = tuple(channels)
+        self.layers = int(layers)
+        self.group = group
+        self.k = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self._nccl = dist.is_initialized() and dist.get_backend(group) == "nccl"
+
+    def _peer(self, local: int) -> int:
+        return dist.get_global_rank(self.group, local) if self.group is not None else local
+
+    # -- exchanges
+    def halo(self, x: torch.Tensor) -> torch.Tensor:
+        """Fill the halo rows of extended x [1, R + 2, W, C] from the neighbours
+        (zeros at the image's top and bottom)."""
+        r = x.shape[1] - 2
+        p2p = []
+        if self.rank > 0:
+            up = self._peer(self.rank - 1)
+            p2p.append(dist.P2POp(dist.isend, x[:, 1], up, self.group))
+            p2p.append(dist.P2POp(dist.irecv, x[:, 0], up, self.group))
+        if self.rank + 1 < self.k:
+            down = self._peer(self.rank + 1)
+            p2p.append(dist.P2POp(dist.isend, x[:, r], down, self.group))
+            p2p.append(dist.P2POp(dist.irecv, x[:, r + 1], down, self.group))
+        if p2p:
+            for req in dist.batch_isend_irecv(p2p):
+                req.wait()
+        if self.rank == 0:
+            x[:, 0].zero_()
+        if self.rank + 1 == self.k:
+            x[:, r + 1].zero_()
+        return x
+
+    def gather(self, t: torch.Tensor) -> torch.Tensor:
+        """[K, *t.shape]: every rank's t in rank order."""
+        if self.k == 1:
+            return t.unsqueeze(0)
+        out = torch.empty((self.k,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        if self._nccl:
+            dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+        else:
+            dist.all_gather(list(out.unbind(0)), t.contiguous(), group=self.group)
+        return out
+
+    # -- blocks
+    def group_norm(self, name: str, x: torch.Tensor, silu: bool) -> torch.Tensor:
+        """GroupNorm (+ SiLU) of extended x's band into a new extended tensor
+        whose halo rows are filled."""
+        r = x.shape[1] - 2
+        band = x[:, 1:r + 1]
+        stats = self.gather(self.ops.gn_stats(name, band))
+        y = self.ops.empty(x.shape)
+        self.ops.gn_apply(name, band, stats, silu, y[:, 1:r + 1])
+        return self.halo(y)
+
+    def resnet(self, prefix: str, x: torch.Tensor) -> torch.Tensor:
+        h = self.ops.conv(prefix + ".conv1", self.group_norm(prefix + ".norm1", x, True))
+        h = self.group_norm(prefix + ".norm2", h, True)
+        shortcut = x
+        if prefix + ".conv_shortcut.weight" in self.ops.w:
+            shortcut = self.ops.conv(prefix + ".conv_shortcut", x)
+        return self.ops.conv(prefix + ".conv2", h, residual=shortcut)
+
+    def attention(self, prefix: str, x: torch.Tensor) -> torch.Tensor:
+        _, rr, w, c = x.shape
+        r = rr - 2
+        band = x[:, 1:r + 1]
+        stats = self.gather(self.ops.gn_stats(prefix + ".group_norm", band))
+        h = self.ops.gn_apply(prefix + ".group_norm", band, stats, False, None)
+        qkv = self.ops.qkv(prefix, h).reshape(1, r * w, 3 * c)
+        every = self.gather(qkv).reshape(1, self.k * r * w, 3 * c)
+        o = self.ops.attend(qkv[:, :, :c], every[:, :, c:2 * c], every[:, :, 2 * c:])
+        y = self.ops.zeros(x.shape)
+        self.ops.conv(prefix + ".to_out.0", o.reshape(1, r, w, c), residual=band,
+                      out=y[:, 1:r + 1])
+        return y
+
+    def upsample(self, name: str, x: torch.Tensor) -> torch.Tensor:
+        """conv3x3(upsample_2x(x)) (vae_decoder.rs:38-49): rows 1..2R + 2 of the
+        upsampled extended band are the high-resolution band with its halo."""
+        r = x.shape[1] - 2
+        u = self.ops.upsample(self.halo(x))
+        return self.ops.conv(name, u[:, 1:2 * r + 3])
+
+    def decode(self, latents: torch.Tensor) -> torch.Tensor:
+        """Unscaled latents [1, 4, h, w] (the whole image, on every rank) ->
+        this rank's rows of the raw RGB image, f32 NCHW [1, 3, 8 h / K, 8 w]."""
+        if latents.ndim != 4 or latents.shape[0] != 1 or latents.shape[1] != 4:
+            raise InvalidInput("band decode takes one image's latents [1, 4, h, w]")
+        _, _, h, w = latents.shape
+        if h % self.k:
+            raise InvalidInput("latent height must divide evenly into the band group")
+        r = h // self.k
+        r0 = self.rank * r
+        lat = self.ops.zeros((1, 4, r + 2, w), f32=True)
+        lo, hi = max(r0 - 1, 0), min(r0 + r + 1, h)
+        lat[:, :, lo - (r0 - 1):hi - (r0 - 1)] = latents[:, :, lo:hi]
+        z = self.ops.conv("post_quant_conv", lat, out_nchw=True)
+        # conv_in's zero padding applies to post_quant_conv's output.
+        if self.rank == 0:
+            z[:, :, 0].zero_()
+        if self.rank + 1 == self.k:
+            z[:, :, r + 1].zero_()
+        x = self.ops.conv("decoder.conv_in", z)
+        mid = "decoder.mid_block"
+        x = self.resnet(mid + ".resnets.0", x)
+        x = self.attention(mid + ".attentions.0", x)
+        x = self.resnet(mid + ".resnets.1", x)
+        rev = list(reversed(self.channels))
+        for i in range(len(rev)):
+            for j in range(self.layers + 1):
+                x = self.resnet(f"decoder.up_blocks.{i}.resnets.{j}", x)
+            if i + 1 < len(rev):
+                x = self.upsample(f"decoder.up_blocks.{i}.upsamplers.0.conv", x)
+        x = self.group_norm("decoder.conv_norm_out", x, True)
+        y = self.ops.conv("decoder.conv_out", x, out_nchw=True)
+        rows = y.shape[2] - 2
+        return y[:, :, 1:rows + 1].contiguous()

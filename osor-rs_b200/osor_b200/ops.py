@@ -7,6 +7,8 @@ on torch CUDA tensors (torch is only the allocator / stream provider here):
   StableGroupNorm.forward(_silu) src/native/vae_encoder.rs:37-105
   upsample_2x                    src/native/vae_decoder.rs:18-35
   attend                         src/native/attention.rs:10-25
+  attend_kv                      src/native/attention.rs:10-25 (n_q != n_kv)
+  StableGroupNorm.stats / .apply src/native/vae_encoder.rs:55-80, split in two
 
 Activations between ops are NHWC ``[B, H, W, C]`` 16-bit (bf16 or f16) device
 tensors, the library's internal layout; ``nchw_to_nhwc`` / ``nhwc_to_nchw``
@@ -107,8 +109,11 @@ class BandedConv2d:
 
     def forward_checked(self, x: torch.Tensor, checkpoint: Checkpoint = None,
                         residual: Optional[torch.Tensor] = None,
-                        out_layout: int = _lib.LAYOUT_NHWC) -> torch.Tensor:
-        """x: NHWC [B, H, W, Cin] of this conv's dtype, or NCHW f32 [B, Cin, H, W]."""
+                        out_layout: int = _lib.LAYOUT_NHWC,
+                        out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """x: NHWC [B, H, W, Cin] of this conv's dtype, or NCHW f32 [B, Cin, H, W].
+        ``out`` (optional) receives the result; it must be contiguous and of
+        the output's shape and type."""
         if checkpoint:
             checkpoint()
         _require_cuda(x, "convolution input")
@@ -124,9 +129,16 @@ class BandedConv2d:
             raise InvalidInput("convolution input channels do not match the weight")
         oh, ow = self.out_shape(h, w)
         if out_layout == _lib.LAYOUT_NHWC:
-            y = torch.empty((b, oh, ow, self.cout), dtype=self.dtype, device=x.device)
+            shape, dt = (b, oh, ow, self.cout), self.dtype
         else:
-            y = torch.empty((b, self.cout, oh, ow), dtype=torch.float32, device=x.device)
+            shape, dt = (b, self.cout, oh, ow), torch.float32
+        if out is None:
+            y = torch.empty(shape, dtype=dt, device=x.device)
+        else:
+            _require_cuda(out, "convolution output")
+            if tuple(out.shape) != shape or out.dtype != dt or out.device != x.device:
+                raise InvalidInput("convolution output tensor does not match the result")
+            y = out
         if residual is not None:
             _require_cuda(residual, "residual")
             if residual.shape != y.shape or residual.dtype != self.dtype:
@@ -185,6 +197,62 @@ class StableGroupNorm:
     def forward(self, x, layout=_lib.LAYOUT_NCHW, eps=EPS, stats=None):
         return self._run(x, False, layout, eps, stats)
 
+    def _nhwc_workspace(self, x: torch.Tensor) -> torch.Tensor:
+        _require_cuda(x, "group-norm input")
+        if x.ndim != 4 or x.dtype not in HALF_TYPES:
+            raise InvalidInput("group-norm statistics / apply take 16-bit NHWC [B, H, W, C]")
+        b, h, w, c = x.shape
+        if c != self.channels or b == 0 or h == 0 or w == 0:
+            raise InvalidInput("invalid VAE group normalization input shape")
+        need = _lib.lib().osor_group_norm_workspace_size(b, c, h, w, _lib.LAYOUT_NHWC,
+                                                         dtype_code(x.dtype))
+        if need == 0:
+            raise InvalidInput("unsupported group-norm shape, layout or dtype")
+        key = (x.device, need)
+        ws = self._workspace.get(key)
+        if ws is None:
+            ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+            self._workspace = {key: ws}
+        return ws
+
+    def stats(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Per-(image, group) (mean, biased variance) of 16-bit NHWC x, f32 [B, 32, 2]."""
+        ws = self._nhwc_workspace(x)
+        b, h, w, c = x.shape
+        if out is None:
+            out = torch.empty((b, GROUPS, 2), dtype=torch.float32, device=x.device)
+        elif out.shape != (b, GROUPS, 2) or out.dtype != torch.float32 or not out.is_contiguous():
+            raise InvalidInput("statistics output must be contiguous f32 [B, 32, 2]")
+        check(_lib.lib().osor_group_norm_stats(_ptr(x), b, c, h, w, dtype_code(x.dtype),
+                                               _ptr(out), _ptr(ws), ws.numel(),
+                                               _stream(x.device)))
+        return out
+
+    def apply(self, x: torch.Tensor, part_stats: torch.Tensor, silu: bool, eps=EPS,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Normalize 16-bit NHWC x with the merge of ``part_stats`` f32
+        [P, B, 32, 2]: P statistics sets over equal element counts (the row
+        bands of the same images)."""
+        ws = self._nhwc_workspace(x)
+        b, h, w, c = x.shape
+        _require_cuda(part_stats, "group-norm statistics")
+        if (part_stats.ndim != 4 or tuple(part_stats.shape[1:]) != (b, GROUPS, 2)
+                or part_stats.dtype != torch.float32):
+            raise InvalidInput("statistics must be f32 [P, B, 32, 2]")
+        if out is None:
+            out = torch.empty_like(x)
+        else:
+            _require_cuda(out, "group-norm output")
+            if out.shape != x.shape or out.dtype != x.dtype:
+                raise InvalidInput("group-norm output must match the input")
+        check(_lib.lib().osor_group_norm_apply(_ptr(x), _ptr(out), _ptr(self.weight),
+                                               _ptr(self.bias), _ptr(part_stats),
+                                               part_stats.shape[0], b, c, h, w,
+                                               dtype_code(x.dtype), float(eps),
+                                               1 if silu else 0, _ptr(ws), ws.numel(),
+                                               _stream(x.device)))
+        return out
+
     def forward_silu(self, x, layout=_lib.LAYOUT_NCHW, eps=EPS, stats=None):
         return self._run(x, True, layout, eps, stats)
 
@@ -218,4 +286,41 @@ def attend(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
     out = torch.empty_like(q)
     check(lb.osor_attention(_ptr(q), _ptr(k), _ptr(v), _ptr(out), b, n, d, d,
                             dtype_code(q.dtype), _ptr(ws), need, _stream(q.device)))
+    return out
+
+
+def _rows_view(t: torch.Tensor, what: str):
+    """[B, N, D] (or [N, D]) view whose last dim is contiguous -> (B, N, D, row
+    stride). Batch entries must follow one another at N rows."""
+    if not t.is_cuda:
+        raise InvalidInput(f"{what} must be a CUDA tensor")
+    if t.ndim == 2:
+        t = t.unsqueeze(0)
+    if t.ndim != 3 or t.dtype not in HALF_TYPES or t.stride(2) != 1:
+        raise InvalidInput("attention tensors must be 16-bit [B, N, D] rows")
+    b, n, d = t.shape
+    ld = t.stride(1)
+    if ld < d or (b > 1 and t.stride(0) != n * ld):
+        raise InvalidInput(f"{what} rows are not evenly strided")
+    return b, n, d, ld
+
+
+def attend_kv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """softmax(q k^T) v with n_q query rows against n_kv key / value rows
+    (attention.rs:10-25 allows different row counts). q [B, n_q, D], k and v
+    [B, n_kv, D]: row-strided views (e.g. column slices of one q|k|v
+    projection); out: contiguous [B, n_q, D]."""
+    bq, nq, d, ldq = _rows_view(q, "query")
+    bk, nk, dk, ldk = _rows_view(k, "key")
+    bv, nv, dv, ldv = _rows_view(v, "value")
+    if (bq, d) != (bk, dk) or (bk, nk, dk) != (bv, nv, dv) or ldk != ldv:
+        raise InvalidInput("attention tensor shapes are incompatible")
+    if q.dtype != k.dtype or k.dtype != v.dtype:
+        raise InvalidInput("attention tensors must be one 16-bit type")
+    lb = _lib.lib()
+    need = lb.osor_attention_kv_workspace_size(bq, nq, nk, d)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    out = torch.empty((bq, nq, d), dtype=q.dtype, device=q.device)
+    check(lb.osor_attention_kv(_ptr(q), ldq, _ptr(k), _ptr(v), ldk, _ptr(out), bq, nq, nk, d,
+                               dtype_code(q.dtype), _ptr(ws), need, _stream(q.device)))
     return out

@@ -1,0 +1,143 @@
+"""Row-band decoding on the GPU: the band entry points of the C ABI against
+the oracle, and the band decoder itself against the oracle's whole-image
+decode (one rank on one GPU; two ranks over NCCL when two GPUs are visible).
+
+* osor_group_norm_stats + osor_group_norm_apply over the row bands of one
+  image, with the bands' statistics merged by the apply, equal the oracle's
+  whole-image GroupNorm (src/native/vae_encoder.rs:55-81) to 16-bit output
+  rounding.
+* osor_attention_kv (n_q query rows against n_kv keys / values, strided
+  column slices of one q|k|v projection) equals the oracle's attention
+  (src/native/attention.rs:27-84) to 16-bit rounding, on the tensor-core path
+  (row counts multiples of 128) and the CUDA-core path.
+* BandDecoder's RGB meets the decoder's acceptance bounds against the oracle.
+"""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.dirname(HERE), os.path.join(os.path.dirname(HERE), "osor-rs_b200")):
+    if _p not in sys.path:  # also run as a script, one rank of the two-GPU check
+        sys.path.insert(0, _p)
+
+import oracle
+import oracle.vae as ovae
+from osor_b200 import ops, workloads
+from osor_b200.bands import BandDecoder, CudaBandOps
+from osor_b200.model import device_status
+from osor_b200.weights import random_vae_weights
+
+pytestmark = pytest.mark.gpu
+
+# RGB acceptance per dtype, as for the whole-image decoder (bf16's 8-bit
+# mantissa sets its worst pixel near 4e-2 on random-init weights).
+MAX_ABS = {torch.float16: 2e-2, torch.bfloat16: 8e-2}
+
+
+def _round(a, dt):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dt).float().numpy()
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+@pytest.mark.parametrize("bands,h,w,c", [(2, 64, 64, 128), (4, 32, 256, 256), (3, 24, 40, 64)])
+def test_group_norm_band_statistics_merge(cuda_device, dt, bands, h, w, c):
+    rng = np.random.default_rng(bands)
+    x = _round(rng.standard_normal((1, c, h, w)) * 2.0 + 0.5, dt)
+    gamma = rng.uniform(0.5, 1.5, c).astype(np.float32)
+    beta = rng.uniform(-0.2, 0.2, c).astype(np.float32)
+    want = oracle.group_norm(x, gamma, beta, silu=True)
+    gn = ops.StableGroupNorm(gamma, beta)
+    xt = ops.nchw_to_nhwc(torch.from_numpy(x).cuda(), dt)
+    r = h // bands
+    parts = torch.stack([gn.stats(xt[:, i * r:(i + 1) * r].contiguous()) for i in range(bands)])
+    got = torch.cat([gn.apply(xt[:, i * r:(i + 1) * r].contiguous(), parts, True)
+                     for i in range(bands)], dim=1)
+    torch.cuda.synchronize()
+    got = ops.nhwc_to_nchw(got).cpu().numpy()
+    # 16-bit output rounding (bf16: relative 2^-8) plus statistics order.
+    err = np.abs(got - want)
+    assert np.all(err <= 2 ** -8 * np.abs(want) + 1e-3), err.max()
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16], ids=["f16", "bf16"])
+@pytest.mark.parametrize("n_q,n_kv,d", [(256, 1024, 512), (128, 512, 128), (32, 96, 64)])
+def test_attention_kv_matches_oracle(cuda_device, dt, n_q, n_kv, d):
+    rng = np.random.default_rng(n_q + d)
+    scale = float(d) ** -0.25
+    qkv = _round(rng.standard_normal((n_kv, 3 * d)) * scale * 2.0, dt)
+    q0 = 3 * (n_kv - n_q) // 4 // 8 * 8  # a band in the middle of the keys
+    q = qkv[q0:q0 + n_q, :d]
+    k, v = qkv[:, d:2 * d], qkv[:, 2 * d:]
+    want = oracle.attend(q[None], np.ascontiguousarray(k.T)[None], v[None])[0]
+    t = torch.from_numpy(qkv).to(dt).cuda()
+    got = ops.attend_kv(t[None, q0:q0 + n_q, :d], t[None, :, d:2 * d], t[None, :, 2 * d:])
+    torch.cuda.synchronize()
+    got = got[0].float().cpu().numpy()
+    # 16-bit probabilities and output, fp32 statistics (the square-attention bounds).
+    err = np.abs(got - want)
+    assert err.max() <= 2e-2, err.max()
+    assert np.sqrt((err ** 2).mean()) <= 3e-3
+
+
+def _weights():
+    return random_vae_weights(0, parts=("decoder",))
+
+
+def test_band_decoder_one_rank_matches_oracle(cuda_device):
+    weights = _weights()
+    lat = workloads.decoder_latents(1, 16, 16, seed=42)
+    dec = BandDecoder(CudaBandOps(weights, dtype=torch.float16))
+    got = dec.decode(torch.from_numpy(lat).cuda())
+    assert device_status(0) == 0
+    got = got.cpu().numpy()
+    want = ovae.decode(weights, lat)
+    assert np.all(np.isfinite(got))
+    assert np.abs(got - want).max() <= MAX_ABS[torch.float16]
+    assert workloads.psnr(got, want) >= 40.0
+
+
+def _rank_main(out_path: str) -> None:
+    """One rank of the two-GPU check (run under torch.distributed.run)."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    try:
+        lat = workloads.decoder_latents(1, 16, 16, seed=42)
+        dec = BandDecoder(CudaBandOps(_weights(), device=f"cuda:{local}",
+                                      dtype=torch.float16))
+        band = dec.decode(torch.from_numpy(lat).cuda())
+        every = torch.empty((dist.get_world_size(),) + tuple(band.shape), device=band.device)
+        dist.all_gather_into_tensor(every, band)
+        if dist.get_rank() == 0:
+            np.save(out_path, torch.cat(list(every), dim=2).cpu().numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_band_decoder_two_gpus_matches_oracle(tmp_path):
+    out = str(tmp_path / "bands.npy")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1",
+           "--master-port=29531", __file__, out]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=os.path.dirname(HERE))
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    got = np.load(out)
+    lat = workloads.decoder_latents(1, 16, 16, seed=42)
+    want = ovae.decode(_weights(), lat)
+    assert got.shape == want.shape
+    assert np.abs(got - want).max() <= MAX_ABS[torch.float16]
+    assert workloads.psnr(got, want) >= 40.0
+
+
+if __name__ == "__main__":
+    _rank_main(sys.argv[1])
