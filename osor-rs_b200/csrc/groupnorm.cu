@@ -702,16 +702,23 @@ cudaError_t gn_nhwc_typed(const void* x, void* y, const float* gamma, const floa
 // the chunk's first element (the reference Metal kernel's anchoring), turned
 // into the chunk's (n, mean, M2) and published with a counter; once all P
 // chunks of the group have published (Chan merge in chunk order), the chunk
-// is read again - from L2 - normalised and written. Each CTA normalises a
-// chunk kL2Lag iterations after publishing it, so the group wait overlaps
-// later chunks' reads and a group may span consecutive waves of the
-// persistent grid (the L2 keeps kL2Lag + 1 chunks per CTA). Waits are
-// bounded.
-constexpr int kL2Threads = 512;
-constexpr int kL2CtasPerSm = 2;
-constexpr long long kL2Chunk = 64 * 1024;  // bytes
-constexpr int kL2Unroll = 4;               // 16-byte loads in flight per thread
-constexpr int kL2Lag = 2;                  // iterations between a chunk's statistics and its store
+// is read again, normalised and written. Each CTA normalises a chunk two
+// iterations after publishing it, so the group wait overlaps later chunks'
+// reads and a group may span consecutive waves of the persistent grid. The
+// second read was meant to hit L2, but the three chunks per CTA that are in
+// flight (about 110 MB over the grid) together with the output stream do not
+// stay there: profiled, the L2 hit rate is 2% and DRAM reads are twice the
+// tensor, so the kernel moves 1.5x the algorithmic bytes. Waits are bounded.
+constexpr int kL2Lag = 2;  // iterations between a chunk's statistics and its store
+
+// CTA shape: many small CTAs per SM keep loads in flight while others wait
+// on their group counters (measured against 512 x 2, 256 x 4, 256 x 3,
+// 128 x 6 and 128 x 8 threads with 16-64 KB chunks: 128 x 8 with 32 KB
+// chunks is fastest).
+constexpr int kL2Threads = 128;
+constexpr int kL2CtasPerSm = 8;
+constexpr int kL2Unroll = 4;  // 16-byte loads in flight per thread
+constexpr long long kL2Chunk = 32 * 1024;  // bytes
 
 struct L2Params {
   long long count;  // elements per group
@@ -726,16 +733,17 @@ struct L2Params {
   float* stats_out;
 };
 
-__device__ __forceinline__ float block_sum_512(float v, float* scratch) {
+template <int THREADS>
+__device__ __forceinline__ float block_sum_t(float v, float* scratch) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __syncthreads();
   if (lane == 0) scratch[warp] = v;
   __syncthreads();
-  float t = lane < kL2Threads / 32 ? scratch[lane] : 0.0f;
+  float t = lane < THREADS / 32 ? scratch[lane] : 0.0f;
 #pragma unroll
-  for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  for (int o = THREADS / 64; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
   return __shfl_sync(0xffffffffu, t, 0);
 }
 
@@ -829,14 +837,14 @@ __global__ void __launch_bounds__(kL2Threads, kL2CtasPerSm)
     float sm = 0.0f;
     for (int k = threadIdx.x; k < p.P; k += kL2Threads)
       sm += __ldcg(part + k * 3) * __ldcg(part + k * 3 + 1);
-    const float mean = block_sum_512(sm, red[0]) / (float)p.count;
+    const float mean = block_sum_t<kL2Threads>(sm, red[0]) / (float)p.count;
     float sq = 0.0f;
     for (int k = threadIdx.x; k < p.P; k += kL2Threads) {
       const float nk = __ldcg(part + k * 3), mk = __ldcg(part + k * 3 + 1);
       const float d = mk - mean;
       sq += __ldcg(part + k * 3 + 2) + nk * d * d;
     }
-    const float var = fmaxf(block_sum_512(sq, red[0]) / (float)p.count, 0.0f);
+    const float var = fmaxf(block_sum_t<kL2Threads>(sq, red[0]) / (float)p.count, 0.0f);
     const float rstd = rsqrtf(var + p.eps);
     if (threadIdx.x == 0 && c == 0 && p.stats_out) {
       p.stats_out[g * 2] = mean;
@@ -857,7 +865,7 @@ __global__ void __launch_bounds__(kL2Threads, kL2CtasPerSm)
         const long long i = i0 + u * kStep;
         if (i < n) {
           // V consecutive elements never straddle a channel (spatial % V == 0).
-          const int ch = gi * cpg + (int)((begin + i) / p.spatial);
+          const int ch = gi * cpg + (int)((unsigned)(begin + i) / (unsigned)p.spatial);
           const float sc = rstd * __ldg(gamma + ch);
           const float sh = __ldg(beta + ch);
           float f[V];
@@ -890,13 +898,15 @@ __global__ void __launch_bounds__(kL2Threads, kL2CtasPerSm)
 GnL2Plan gn_nchw_l2_plan(int batch, int channels, long long spatial, int groups, int elem_bytes) {
   GnL2Plan plan{};
   const int vec = 16 / elem_bytes;
-  plan.feasible = spatial % vec == 0 && channels % groups == 0;
   plan.groups_total = batch * groups;
+  // Offsets within a group use 32-bit arithmetic.
+  plan.feasible = spatial % vec == 0 && channels % groups == 0 &&
+                  (long long)(channels / groups) * spatial < (1LL << 31);
   plan.count = (long long)(channels / groups) * spatial;
   plan.grid = num_sms() * kL2CtasPerSm;
   long long chunk = kL2Chunk / elem_bytes;
   // Every group must fit in one wave of the grid (P <= grid); chunks hold
-  // whole 16-byte vectors and at most kL2Chunk bytes (one ring buffer).
+  // whole 16-byte vectors and at most kL2Chunk bytes.
   if ((plan.count + chunk - 1) / chunk > plan.grid) {
     chunk = (plan.count + plan.grid - 1) / plan.grid;
     chunk = (chunk + vec - 1) / vec * vec;
