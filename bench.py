@@ -276,6 +276,25 @@ def run_ops(args):
                           "dtype": args.dtype, "ms": round(ms, 3),
                           "mpx_per_s": round(4 * 1024 * 1024 / 1e6 / (ms / 1e3), 1),
                           "tflops": round(19.52 / (ms / 1e3), 1)}), flush=True)
+    elif args.op == "noise":
+        # Seeded posterior + diffusion noise for the 4 x 1024^2 job
+        # (noise.rs:107-146): 2 x 262,144 values, f64 Box-Muller per pair.
+        import time
+        import oracle
+        from osor_b200.noise import seeded_noise
+        seeded_noise(42, 4, 1024, 1024)  # the first call uploads the jump table
+        ms = _timed(lambda: seeded_noise(42, 4, 1024, 1024), args.steps, args.warmup, flush)
+        count = 2 * 4 * 4 * 128 * 128
+        t0 = time.perf_counter()
+        for stream in (0, 1):
+            oracle.seeded_noise(42, stream, count // 2)
+        cpu_ms = (time.perf_counter() - t0) * 1e3
+        print(json.dumps({"op": "seeded noise (xoshiro256** + f64 Box-Muller)",
+                          "shape": [2, 4, 4, 128, 128], "dtype": "f32", "ms": round(ms, 4),
+                          "msamples_per_s": round(count / (ms / 1e3) / 1e6, 1),
+                          "cpu_baseline": {"ms": round(cpu_ms, 3), "cores": 1, "kind": "port",
+                                           "sample": "the same 2 x 262,144 values"}}),
+              flush=True)
     if device_status(0) != 0:
         raise SystemExit("device status reported a kernel wait timeout")
 
@@ -431,7 +450,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--dtype", default="f16", choices=["f16", "bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--op", default="decode", choices=["decode", "conv3x3", "groupnorm", "encode"],
+    ap.add_argument("--op", default="decode",
+                    choices=["decode", "conv3x3", "groupnorm", "encode", "noise"],
                     help="decode: the headline line; others: standalone op lines")
     ap.add_argument("--shape", default=None, help="comma-separated shape for --op conv3x3/groupnorm")
     ap.add_argument("--bands", type=int, default=0,

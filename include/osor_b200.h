@@ -202,6 +202,17 @@ int osor_group_norm_apply(const void* x, void* y, const float* gamma, const floa
                           int width, int dtype, float eps, int silu, void* workspace,
                           size_t workspace_bytes, void* stream);
 
+/* Posterior and diffusion noise for a [batch, 3, height, width] job from a
+ * seed: device tensors [batch, 4, height/8, width/8] of `dtype` (F32, F16 or
+ * BF16), stream 0 into `posterior` and stream 1 into `diffusion`, bit-equal
+ * in F32 to the reference's stored-seed contract version 1 (xoshiro256**
+ * streams seeded by SplitMix64, Box-Muller pairs in f64 rounded to F32, NCHW
+ * order). batch 1..4; height and width multiples of 8 in 32..1024. The first
+ * call on a device copies an 88 KB jump table to it synchronously, so make it
+ * before any stream capture. Replaces seeded_noise (src/noise.rs:107-146). */
+int osor_seeded_noise(unsigned long long seed, int batch, int height, int width, int dtype,
+                      void* posterior, void* diffusion, void* stream);
+
 /* Nearest 2x upsample of 16-bit NHWC [B][H][W][C] -> [B][2H][2W][C], C % 8 == 0.
  * Replaces upsample_2x (src/native/vae_decoder.rs:18-35). */
 int osor_upsample_2x(const void* x, void* y, int batch, int height, int width, int channels,

@@ -71,6 +71,9 @@ def lib():
         l.oracle_upsample_2x.restype = None
         l.oracle_attention.argtypes = [_f32p] * 4 + [ctypes.c_int] * 4 + [ctypes.c_longlong]
         l.oracle_attention.restype = ctypes.c_int
+        l.oracle_seeded_noise.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_longlong,
+                                          _f32p]
+        l.oracle_seeded_noise.restype = None
         l.oracle_set_threads.argtypes = [ctypes.c_int]
         l.oracle_threads.restype = ctypes.c_int
         _lib = l
@@ -179,4 +182,13 @@ def attend(q, kt, v, max_score_elements=MAX_SCORE_ELEMENTS) -> np.ndarray:
                                 int(max_score_elements))
     if rc != 0:
         raise ValueError("attention score budget cannot hold one query row")
+    return out
+
+
+def seeded_noise(seed: int, stream: int, count: int) -> np.ndarray:
+    """`count` standard-normal f32 values of stream `stream` (0: posterior,
+    1: diffusion) of the reference's seeded noise, version 1
+    (src/noise.rs:1-99)."""
+    out = np.empty(int(count), np.float32)
+    lib().oracle_seeded_noise(int(seed) & (2 ** 64 - 1), int(stream), int(count), _p(out))
     return out

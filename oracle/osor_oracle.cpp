@@ -396,4 +396,47 @@ int oracle_attention(const float* q, const float* kt, const float* v, float* out
   return 0;
 }
 
+// Seeded standard-normal noise, version 1 of the reference's stored-seed
+// contract (src/noise.rs:1-99): stream `stream` is a xoshiro256** generator
+// whose four state words are the first four SplitMix64 outputs from
+// seed + stream * 0x9E3779B97F4A7C15 (noise.rs:42-66); values are Box-Muller
+// pairs in f64 - u1 = 1 - (top 53 bits of one output) * 2^-53, u2 from the
+// next output, r = sqrt(-2 ln u1), angle = 2 pi u2, (r cos, r sin) - rounded to
+// f32 (noise.rs:80-99). The published generators (SplitMix64, xoshiro256**)
+// are restated here from their definitions.
+void oracle_seeded_noise(uint64_t seed, uint64_t stream, long long count, float* out) {
+  const uint64_t kStride = 0x9E3779B97F4A7C15ull;
+  uint64_t mixer = seed + stream * kStride;
+  uint64_t st[4];
+  for (int i = 0; i < 4; ++i) {
+    mixer += kStride;
+    uint64_t z = mixer;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    st[i] = z ^ (z >> 31);
+  }
+  auto rotl = [](uint64_t v, int k) { return (v << k) | (v >> (64 - k)); };
+  auto next = [&]() {
+    const uint64_t result = rotl(st[1] * 5, 7) * 9;
+    const uint64_t t = st[1] << 17;
+    st[2] ^= st[0];
+    st[3] ^= st[1];
+    st[1] ^= st[2];
+    st[0] ^= st[3];
+    st[2] ^= t;
+    st[3] = rotl(st[3], 45);
+    return result;
+  };
+  auto unit = [&]() { return (double)(next() >> 11) * (1.0 / (double)(1ull << 53)); };
+  const double kPi = 3.14159265358979323846;
+  for (long long i = 0; i < count; i += 2) {
+    const double u1 = 1.0 - unit();
+    const double u2 = unit();
+    const double radius = std::sqrt(-2.0 * std::log(u1));
+    const double angle = 2.0 * kPi * u2;
+    out[i] = (float)(radius * std::cos(angle));
+    if (i + 1 < count) out[i + 1] = (float)(radius * std::sin(angle));
+  }
+}
+
 }  // extern "C"

@@ -5,6 +5,7 @@
 #include "common.cuh"
 #include "conv_tc.h"
 #include "groupnorm.h"
+#include "noise.h"
 #include "ops.h"
 #include "profile.h"
 #include "vae.h"
@@ -360,6 +361,23 @@ int osor_group_norm_apply(const void* x, void* y, const float* gamma, const floa
       static_cast<cudaStream_t>(stream));
   osor::note_launches(2);
   return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "group-norm apply");
+}
+
+int osor_seeded_noise(unsigned long long seed, int batch, int height, int width, int dtype,
+                      void* posterior, void* diffusion, void* stream) {
+  if (!posterior || !diffusion) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  auto valid_axis = [](int a) { return a >= 32 && a <= 1024 && a % 8 == 0; };
+  if (batch < 1 || batch > 4 || !valid_axis(height) || !valid_axis(width))
+    return fail(OSOR_ERR_INVALID_INPUT,
+                "seeded noise needs batch 1..=4 and image axes that the model admits");
+  if (dtype != OSOR_DTYPE_F32 && dtype != OSOR_DTYPE_F16 && dtype != OSOR_DTYPE_BF16)
+    return fail(OSOR_ERR_INVALID_INPUT, "seeded noise dtype must be F32, F16, or BF16");
+  DeviceOf dev(posterior);
+  const int count = batch * 4 * (height / 8) * (width / 8);
+  cudaError_t e = osor::seeded_noise_launch(seed, count, dtype, posterior, diffusion,
+                                            static_cast<cudaStream_t>(stream));
+  osor::note_launches(1);
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "seeded noise");
 }
 
 int osor_upsample_2x(const void* x, void* y, int batch, int height, int width, int channels,

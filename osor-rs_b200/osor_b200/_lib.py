@@ -104,6 +104,7 @@ SIGNATURES = {
     "osor_group_norm_stats": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp]),
     "osor_group_norm_apply": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _i, _vp,
                                    _sz, _vp]),
+    "osor_seeded_noise": (_i, [ctypes.c_ulonglong, _i, _i, _i, _i, _vp, _vp, _vp]),
     "osor_upsample_2x": (_i, [_vp, _vp, _i, _i, _i, _i, _vp]),
     "osor_attention_workspace_size": (_sz, [_i, _i, _i]),
     "osor_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _ll, _i, _vp, _sz, _vp]),

@@ -61,6 +61,13 @@ def test_invalid_arguments_fail_before_device_work():
     assert lb.osor_group_norm_workspace_size(1, 64, 4, 4, nhwc, f32) == 0
     assert lb.osor_group_norm_workspace_size(1, 64, 4, 4, nhwc, _lib.DTYPE_F16) > 0
     assert lb.osor_vae_workspace_size(None, _lib.OP_DECODE, 1, 64, 64) == 0
+    # Seeded noise admission (noise.rs:115-126): batch 1..4, axes multiples of
+    # 8 in 32..1024, dtype F32/F16/BF16; rejected before any device work.
+    dummy = ctypes.c_void_p(256)
+    for batch, h, w, dt in [(0, 32, 32, f32), (5, 32, 32, f32), (1, 33, 32, f32),
+                            (1, 32, 1032, f32), (1, 24, 32, f32), (1, 32, 32, 7)]:
+        assert lb.osor_seeded_noise(1, batch, h, w, dt, dummy, dummy, None) == \
+            _lib.OSOR_ERR_INVALID_INPUT
 
 
 def test_device_check_reports_unavailable_without_gpu():
