@@ -213,6 +213,59 @@ int osor_group_norm_apply(const void* x, void* y, const float* gamma, const floa
 int osor_seeded_noise(unsigned long long seed, int batch, int height, int width, int dtype,
                       void* posterior, void* diffusion, void* stream);
 
+/* DDPM scheduler (src/scheduler.rs:128-340) and the latent-space stages of
+ * the inference pipeline around the VAE (src/pipeline.rs:720-860), in F32.
+ * Products and sums are rounded one by one, as the reference evaluates them.
+ *
+ * osor_scheduler_alphas: host function; alphas_cumprod receives
+ * num_train_timesteps cumulative alphas (beta_schedule 0 = linear,
+ * 1 = scaled_linear; trained_betas nullable) computed as Scheduler::new does
+ * (scheduler.rs:128-221). */
+int osor_scheduler_alphas(int num_train_timesteps, double beta_start, double beta_end,
+                          int beta_schedule, const double* trained_betas, float* alphas_cumprod);
+
+/* original * sqrt(a) + noise * sqrt(1 - a) over n device floats
+ * (Scheduler::add_noise, scheduler.rs:278-297). */
+int osor_scheduler_add_noise(const float* original, const float* noise, float* out, long long n,
+                             float alpha_t, void* stream);
+
+/* Predicted original sample (scheduler.rs:299-339); prediction_type 0 =
+ * epsilon, 1 = sample, 2 = v_prediction; clamped to +-clip_range when
+ * clip_sample. */
+int osor_scheduler_predicted_original(const float* noisy, const float* model_output, float* out,
+                                      long long n, float alpha_t, int prediction_type,
+                                      int clip_sample, float clip_range, void* stream);
+
+/* The encoder's input: normalized = image * 2 - 1 over [B][3][H][W]
+ * (pipeline.rs:721). */
+int osor_pipeline_normalize_image(const float* image, float* normalized, int batch, int height,
+                                  int width, void* stream);
+
+/* Stages before the denoiser (pipeline.rs:733-771): from the encoder's
+ * moments [B][8][h][w], posterior / diffusion noise [B][4][h][w] and the mask
+ * [B][1][H][W] (h = H/8, w = W/8), the UNet input [B][9][h][w] = (noisy
+ * latent, max-pooled mask, original latent); sample [B][4][h][w] (nullable)
+ * receives the posterior sample. alpha_t = alphas_cumprod[timestep]. */
+int osor_pipeline_prepare(const float* moments, const float* posterior_noise,
+                          const float* diffusion_noise, const float* mask, float* unet_input,
+                          float* sample, int batch, int height, int width, float alpha_t,
+                          double vae_scaling_factor, void* stream);
+
+/* Stages after the denoiser (pipeline.rs:810-836): from its output
+ * [B][5][h][w] and the UNet input, latent_alpha = sigmoid(channel 4)
+ * [B][1][h][w], the predicted original and the alpha blend (both nullable,
+ * [B][4][h][w]), and the decoder's input latents = blend / scaling. */
+int osor_pipeline_finish(const float* unet_output, const float* unet_input, float* latent_alpha,
+                         float* predicted, float* blend, float* latents, int batch, int height,
+                         int width, float alpha_t, int prediction_type, int clip_sample,
+                         float clip_range, double vae_scaling_factor, void* stream);
+
+/* Display mapping (pipeline.rs:846-856, 862-896): image = clamp(0.5 decoded
+ * + 0.5, 0, 1) [B][3][H][W]; alpha = bilinear 8x (align_corners = false) of
+ * latent_alpha, [B][1][H][W]. */
+int osor_pipeline_map(const float* decoded, const float* latent_alpha, float* image, float* alpha,
+                      int batch, int height, int width, void* stream);
+
 /* Nearest 2x upsample of 16-bit NHWC [B][H][W][C] -> [B][2H][2W][C], C % 8 == 0.
  * Replaces upsample_2x (src/native/vae_decoder.rs:18-35). */
 int osor_upsample_2x(const void* x, void* y, int batch, int height, int width, int channels,

@@ -1,4 +1,5 @@
 // extern "C" entry points declared in include/osor_b200.h.
+#include <cmath>
 #include <cstring>
 #include <string>
 
@@ -6,6 +7,7 @@
 #include "conv_tc.h"
 #include "groupnorm.h"
 #include "noise.h"
+#include "pipeline.h"
 #include "ops.h"
 #include "profile.h"
 #include "vae.h"
@@ -378,6 +380,120 @@ int osor_seeded_noise(unsigned long long seed, int batch, int height, int width,
                                             static_cast<cudaStream_t>(stream));
   osor::note_launches(1);
   return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "seeded noise");
+}
+
+int osor_scheduler_alphas(int num_train_timesteps, double beta_start, double beta_end,
+                          int beta_schedule, const double* trained_betas, float* alphas_cumprod) {
+  if (!alphas_cumprod) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  const int rc = osor::scheduler_alphas(num_train_timesteps, beta_start, beta_end, beta_schedule,
+                                        trained_betas, alphas_cumprod);
+  if (rc == 1) return fail(OSOR_ERR_INVALID_INPUT, "scheduler: invalid configuration");
+  if (rc == 2) return fail(OSOR_ERR_INVALID_INPUT, "scheduler: cumulative alpha underflowed");
+  return OSOR_OK;
+}
+
+namespace {
+bool latent_job_ok(int batch, int height, int width) {
+  auto valid_axis = [](int a) { return a >= 32 && a <= 1024 && a % 8 == 0; };
+  return batch >= 1 && batch <= 4 && valid_axis(height) && valid_axis(width);
+}
+bool alpha_ok(float a) { return std::isfinite(a) && a > 0.0f && a <= 1.0f; }
+}  // namespace
+
+int osor_pipeline_prepare(const float* moments, const float* posterior_noise,
+                          const float* diffusion_noise, const float* mask, float* unet_input,
+                          float* sample, int batch, int height, int width, float alpha_t,
+                          double vae_scaling_factor, void* stream) {
+  if (!moments || !posterior_noise || !diffusion_noise || !mask || !unet_input)
+    return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (!latent_job_ok(batch, height, width))
+    return fail(OSOR_ERR_INVALID_INPUT, "image dimensions or batch exceed limits");
+  if (!alpha_ok(alpha_t) || !(vae_scaling_factor > 0.0) || !std::isfinite(vae_scaling_factor))
+    return fail(OSOR_ERR_INVALID_INPUT, "invalid cumulative alpha or VAE scaling factor");
+  DeviceOf dev(moments);
+  cudaError_t e = osor::pipeline_prepare_launch(
+      moments, posterior_noise, diffusion_noise, mask, unet_input, sample, batch, height / 8,
+      width / 8, (float)vae_scaling_factor, alpha_t, static_cast<cudaStream_t>(stream));
+  osor::note_launches(1);
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "pipeline prepare");
+}
+
+int osor_pipeline_finish(const float* unet_output, const float* unet_input, float* latent_alpha,
+                         float* predicted, float* blend, float* latents, int batch, int height,
+                         int width, float alpha_t, int prediction_type, int clip_sample,
+                         float clip_range, double vae_scaling_factor, void* stream) {
+  if (!unet_output || !unet_input || !latent_alpha || !latents)
+    return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (!latent_job_ok(batch, height, width))
+    return fail(OSOR_ERR_INVALID_INPUT, "image dimensions or batch exceed limits");
+  if (!alpha_ok(alpha_t) || !(vae_scaling_factor > 0.0) || !std::isfinite(vae_scaling_factor))
+    return fail(OSOR_ERR_INVALID_INPUT, "invalid cumulative alpha or VAE scaling factor");
+  if (prediction_type < 0 || prediction_type > 2)
+    return fail(OSOR_ERR_INVALID_INPUT, "unsupported prediction_type");
+  if (clip_sample && !(clip_range > 0.0f && std::isfinite(clip_range)))
+    return fail(OSOR_ERR_INVALID_INPUT, "invalid clip range");
+  DeviceOf dev(unet_output);
+  cudaError_t e = osor::pipeline_finish_launch(
+      unet_output, unet_input, latent_alpha, predicted, blend, latents, batch, height / 8,
+      width / 8, alpha_t, prediction_type, clip_sample, clip_range,
+      (float)(1.0 / vae_scaling_factor), static_cast<cudaStream_t>(stream));
+  osor::note_launches(1);
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "pipeline finish");
+}
+
+int osor_pipeline_normalize_image(const float* image, float* normalized, int batch, int height,
+                                  int width, void* stream) {
+  if (!image || !normalized) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (!latent_job_ok(batch, height, width))
+    return fail(OSOR_ERR_INVALID_INPUT, "image dimensions or batch exceed limits");
+  DeviceOf dev(image);
+  cudaError_t e = osor::pipeline_normalize_launch(image, normalized, (long long)batch * 3 * height * width,
+                                                  static_cast<cudaStream_t>(stream));
+  osor::note_launches(1);
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "pipeline normalize");
+}
+
+int osor_pipeline_map(const float* decoded, const float* latent_alpha, float* image, float* alpha,
+                      int batch, int height, int width, void* stream) {
+  if (!decoded || !latent_alpha || !image || !alpha)
+    return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (!latent_job_ok(batch, height, width))
+    return fail(OSOR_ERR_INVALID_INPUT, "image dimensions or batch exceed limits");
+  DeviceOf dev(decoded);
+  cudaError_t e = osor::pipeline_map_launch(decoded, latent_alpha, image, alpha, batch, height,
+                                            width, static_cast<cudaStream_t>(stream));
+  osor::note_launches(1);
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "pipeline map");
+}
+
+int osor_scheduler_add_noise(const float* original, const float* noise, float* out, long long n,
+                             float alpha_t, void* stream) {
+  if (!original || !noise || !out) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (n <= 0 || n > 16LL * 1024 * 1024)
+    return fail(OSOR_ERR_INVALID_INPUT, "scheduler tensor exceeds safety limit");
+  if (!alpha_ok(alpha_t)) return fail(OSOR_ERR_INVALID_INPUT, "invalid cumulative alpha");
+  DeviceOf dev(original);
+  cudaError_t e = osor::scheduler_add_noise_launch(original, noise, out, n, alpha_t,
+                                                   static_cast<cudaStream_t>(stream));
+  osor::note_launches(1);
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "scheduler add_noise");
+}
+
+int osor_scheduler_predicted_original(const float* noisy, const float* model_output, float* out,
+                                      long long n, float alpha_t, int prediction_type,
+                                      int clip_sample, float clip_range, void* stream) {
+  if (!noisy || !model_output || !out) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (n <= 0 || n > 16LL * 1024 * 1024)
+    return fail(OSOR_ERR_INVALID_INPUT, "scheduler tensor exceeds safety limit");
+  if (!alpha_ok(alpha_t)) return fail(OSOR_ERR_INVALID_INPUT, "invalid cumulative alpha");
+  if (prediction_type < 0 || prediction_type > 2)
+    return fail(OSOR_ERR_INVALID_INPUT, "unsupported prediction_type");
+  DeviceOf dev(noisy);
+  cudaError_t e =
+      osor::scheduler_predicted_launch(noisy, model_output, out, n, alpha_t, prediction_type,
+                                       clip_sample, clip_range, static_cast<cudaStream_t>(stream));
+  osor::note_launches(1);
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "scheduler predicted_original");
 }
 
 int osor_upsample_2x(const void* x, void* y, int batch, int height, int width, int channels,

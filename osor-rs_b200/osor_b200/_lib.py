@@ -105,6 +105,15 @@ SIGNATURES = {
     "osor_group_norm_apply": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _i, _vp,
                                    _sz, _vp]),
     "osor_seeded_noise": (_i, [ctypes.c_ulonglong, _i, _i, _i, _i, _vp, _vp, _vp]),
+    "osor_scheduler_alphas": (_i, [_i, ctypes.c_double, ctypes.c_double, _i, _vp, _vp]),
+    "osor_scheduler_add_noise": (_i, [_vp, _vp, _vp, _ll, _f, _vp]),
+    "osor_scheduler_predicted_original": (_i, [_vp, _vp, _vp, _ll, _f, _i, _i, _f, _vp]),
+    "osor_pipeline_prepare": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f,
+                                   ctypes.c_double, _vp]),
+    "osor_pipeline_finish": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _f,
+                                  ctypes.c_double, _vp]),
+    "osor_pipeline_map": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "osor_pipeline_normalize_image": (_i, [_vp, _vp, _i, _i, _i, _vp]),
     "osor_upsample_2x": (_i, [_vp, _vp, _i, _i, _i, _i, _vp]),
     "osor_attention_workspace_size": (_sz, [_i, _i, _i]),
     "osor_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _ll, _i, _vp, _sz, _vp]),
