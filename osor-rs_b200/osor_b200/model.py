@@ -89,6 +89,15 @@ class NativeModel:
         self._handle = handle
         self._workspace: Dict[tuple, torch.Tensor] = {}
 
+    @classmethod
+    def from_safetensors(cls, path: str, device: int = 0, parts=("decoder", "encoder"),
+                         dtype: str = "f16", limits=None, **kwargs) -> "NativeModel":
+        """Load `vae.safetensors` (diffusers names) with the reference's file
+        checks (``artifact.read_safetensors``) and build the model."""
+        from .artifact import read_safetensors
+        return cls(read_safetensors(path, limits), device=device, parts=parts, dtype=dtype,
+                   **kwargs)
+
     def close(self) -> None:
         if getattr(self, "_handle", None):
             _lib.lib().osor_vae_destroy(self._handle)
