@@ -341,29 +341,6 @@ __global__ void thin_columns_kernel(const float* __restrict__ x, uint4* __restri
   }
 }
 
-// moments [B,8,h,w] -> sample [B,4,h,w] = (mean + exp(0.5*clamp(logvar,-30,20)) * noise) * scale
-__global__ void posterior_sample_kernel(const float* __restrict__ moments,
-                                        const float* __restrict__ noise, float* __restrict__ out,
-                                        long long hw, long long total, float scale) {
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long p = i % hw;
-    const long long t = i / hw;
-    const int c = (int)(t % 4);
-    const long long b = t / 4;
-    const float mean = moments[(b * 8 + c) * hw + p];
-    const float logvar = fminf(fmaxf(moments[(b * 8 + 4 + c) * hw + p], -30.0f), 20.0f);
-    out[i] = (mean + expf(0.5f * logvar) * noise[i]) * scale;
-  }
-}
-
-__global__ void scale_f32_kernel(const float* __restrict__ x, float* __restrict__ y, float s,
-                                 long long n) {
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x)
-    y[i] = x[i] * s;
-}
-
 int blocks_for(long long n, int threads) {
   long long b = (n + threads - 1) / threads;
   const long long cap = 148LL * 32;
@@ -462,19 +439,6 @@ cudaError_t thin_columns_launch(int dtype, const float* x, void* cols, int batch
     thin_columns_kernel<kF16><<<grid, 128, 0, s>>>(x, c, batch, cin, h, w, k, pad, pre_w, pre_b);
   else
     thin_columns_kernel<kBf16><<<grid, 128, 0, s>>>(x, c, batch, cin, h, w, k, pad, pre_w, pre_b);
-  return cudaGetLastError();
-}
-
-cudaError_t posterior_sample_launch(const float* moments, const float* noise, float* out,
-                                    int batch, long long hw, float scale, cudaStream_t s) {
-  const long long total = (long long)batch * 4 * hw;
-  posterior_sample_kernel<<<blocks_for(total, 256), 256, 0, s>>>(moments, noise, out, hw, total,
-                                                                 scale);
-  return cudaGetLastError();
-}
-
-cudaError_t scale_f32_launch(const float* x, float* y, float scale, long long n, cudaStream_t s) {
-  scale_f32_kernel<<<blocks_for(n, 256), 256, 0, s>>>(x, y, scale, n);
   return cudaGetLastError();
 }
 

@@ -50,8 +50,5 @@ cudaError_t nhwc16_to_nchw_f32_launch(int dtype, const void* x, float* y, int ba
 cudaError_t thin_columns_launch(int dtype, const float* x, void* cols, int batch, int cin, int h,
                                 int w, int k, int pad, const float* pre_w, const float* pre_b,
                                 cudaStream_t s);
-cudaError_t posterior_sample_launch(const float* moments, const float* noise, float* out,
-                                    int batch, long long hw, float scale, cudaStream_t s);
-cudaError_t scale_f32_launch(const float* x, float* y, float scale, long long n, cudaStream_t s);
 
 }  // namespace osor
