@@ -1,11 +1,12 @@
-"""Row-band split of the VAE decoder over the ranks of a process group.
+"""Row-band split of the VAE decoder and encoder over the ranks of a process group.
 
 The reference bounds memory by running each convolution over horizontal row
 bands of its output, one after the other (src/native/conv.rs:98-108,
 src/native/columns.rs:335-362). Here the same row-band geometry is spread over
 GPUs: each of the K ranks of a band group owns a contiguous range of
-R = H / K rows of every activation of one image (H the latent height;
-upsampling doubles R with the image), so one image decodes on K GPUs at once.
+R = H / K rows of every activation of one image (upsampling doubles R with
+the image, the encoder's stride-2 downsampling halves it), so one image is
+decoded or encoded on K GPUs at once.
 
 Activations are held as *extended* NHWC tensors ``[1, R + 2, W, C]``: rows
 1..R are the band, rows 0 and R + 1 are halo rows. Three exchanges keep the
@@ -27,9 +28,11 @@ result equal to the one-GPU decode:
 
 The block order is the decoder's (src/native/vae_decoder.rs:104-114, the mid
 block src/native/vae_encoder.rs:367-375, resnets :134-151, attention
-:320-339). ``BandDecoder`` drives an op backend: ``CudaBandOps`` calls the
-library's C ABI on this rank's GPU; a CPU backend with the same methods runs
-the same band logic in the multi-process tests.
+:320-339) or the encoder's (vae_encoder.rs:414-424); the encoder's stride-2
+downsamplers halve the band and read one halo row below it. ``BandDecoder``
+and ``BandEncoder`` drive an op backend: ``CudaBandOps`` calls the library's
+C ABI on this rank's GPU; a CPU backend with the same methods runs the same
+band logic in the multi-process tests.
 """
 from __future__ import annotations
 
@@ -47,12 +50,12 @@ GROUPS = 32
 
 
 class CudaBandOps:
-    """The decoder's layers on one CUDA device through the C ABI: 16-bit NHWC
-    activations, f32 NCHW at the latent input and the RGB output."""
+    """The VAE's layers on one CUDA device through the C ABI: 16-bit NHWC
+    activations, f32 NCHW at the image / latent boundaries."""
 
     def __init__(self, weights: Dict[str, np.ndarray], device="cuda", dtype=torch.float16):
         if dtype not in ops.HALF_TYPES:
-            raise InvalidInput("band decoder dtype must be bfloat16 or float16")
+            raise InvalidInput("band model dtype must be bfloat16 or float16")
         self.w = weights
         self.device = torch.device(device)
         self.dtype = dtype
@@ -100,7 +103,7 @@ class CudaBandOps:
             self._norms[name] = n
         return n
 
-    # -- the backend methods BandDecoder uses
+    # -- the backend methods the band models use
     def empty(self, shape, f32: bool = False) -> torch.Tensor:
         return torch.empty(shape, dtype=torch.float32 if f32 else self.dtype, device=self.device)
 
@@ -110,6 +113,17 @@ class CudaBandOps:
     def conv(self, name, x, residual=None, out=None, out_nchw=False):
         layout = LAYOUT_NCHW if out_nchw else ops._lib.LAYOUT_NHWC
         return self._conv(name).forward_checked(x, residual=residual, out_layout=layout, out=out)
+
+    def conv_down(self, name, x, out):
+        """The encoder's downsampler (vae_encoder.rs:206-210): 3x3 stride 2 with
+        one zero row / column after the input's last (padding 0 before, 1 after)."""
+        key = name + "#down"
+        c = self._convs.get(key)
+        if c is None:
+            c = ops.BandedConv2d(self.w[name + ".weight"], self.w[name + ".bias"], stride=2,
+                                 padding=0, padding_end=1, device=self.device, dtype=self.dtype)
+            self._convs[key] = c
+        return c.forward_checked(x, out=out)
 
     def qkv(self, prefix, h):
         return self._qkv(prefix).forward_checked(h)
@@ -127,10 +141,9 @@ class CudaBandOps:
         return ops.attend_kv(q, k, v)
 
 
-class BandDecoder:
-    """VaeDecoder::forward (src/native/vae_decoder.rs:104-114) on the rank's
-    row band of one image. ``group`` is the band group (default: the whole
-    world); rank r of K owns latent rows [r R, (r + 1) R), R = h / K."""
+class _BandModel:
+    """The exchanges and the blocks shared by the band encoder and decoder.
+    ``group`` is the band group (default: the whole world)."""
 
     def __init__(self, backend, channels=SDXL_CHANNELS, layers: int = SDXL_LAYERS,
                  group: Optional[dist.ProcessGroup] = None):
@@ -212,6 +225,27 @@ class BandDecoder:
                       out=y[:, 1:r + 1])
         return y
 
+    def _band_rows(self, image: torch.Tensor, rows: int, channels: int) -> torch.Tensor:
+        """This rank's rows of an NCHW f32 tensor holding the whole image, with
+        one halo row above and below (zeros outside the image): [1, C, R + 2, W]."""
+        if image.ndim != 4 or image.shape[0] != 1 or image.shape[1] != channels:
+            raise InvalidInput(f"band split takes one image [1, {channels}, H, W]")
+        _, _, h, w = image.shape
+        if h % rows:
+            raise InvalidInput("the image height must divide evenly into the band group")
+        r = h // rows
+        r0 = self.rank * r
+        out = self.ops.zeros((1, channels, r + 2, w), f32=True)
+        lo, hi = max(r0 - 1, 0), min(r0 + r + 1, h)
+        out[:, :, lo - (r0 - 1):hi - (r0 - 1)] = image[:, :, lo:hi]
+        return out
+
+
+class BandDecoder(_BandModel):
+    """VaeDecoder::forward (src/native/vae_decoder.rs:104-114) on the rank's
+    row band of one image: rank r of K owns latent rows [r R, (r + 1) R),
+    R = h / K."""
+
     def upsample(self, name: str, x: torch.Tensor) -> torch.Tensor:
         """conv3x3(upsample_2x(x)) (vae_decoder.rs:38-49): rows 1..2R + 2 of the
         upsampled extended band are the high-resolution band with its halo."""
@@ -222,16 +256,8 @@ class BandDecoder:
     def decode(self, latents: torch.Tensor) -> torch.Tensor:
         """Unscaled latents [1, 4, h, w] (the whole image, on every rank) ->
         this rank's rows of the raw RGB image, f32 NCHW [1, 3, 8 h / K, 8 w]."""
-        if latents.ndim != 4 or latents.shape[0] != 1 or latents.shape[1] != 4:
-            raise InvalidInput("band decode takes one image's latents [1, 4, h, w]")
-        _, _, h, w = latents.shape
-        if h % self.k:
-            raise InvalidInput("latent height must divide evenly into the band group")
-        r = h // self.k
-        r0 = self.rank * r
-        lat = self.ops.zeros((1, 4, r + 2, w), f32=True)
-        lo, hi = max(r0 - 1, 0), min(r0 + r + 1, h)
-        lat[:, :, lo - (r0 - 1):hi - (r0 - 1)] = latents[:, :, lo:hi]
+        lat = self._band_rows(latents, self.k, 4)
+        r = lat.shape[2] - 2
         z = self.ops.conv("post_quant_conv", lat, out_nchw=True)
         # conv_in's zero padding applies to post_quant_conv's output.
         if self.rank == 0:
@@ -253,3 +279,43 @@ class BandDecoder:
         y = self.ops.conv("decoder.conv_out", x, out_nchw=True)
         rows = y.shape[2] - 2
         return y[:, :, 1:rows + 1].contiguous()
+
+
+class BandEncoder(_BandModel):
+    """VaeEncoder::forward (src/native/vae_encoder.rs:414-424) on the rank's row
+    band of one image: rank r of K owns image rows [r R, (r + 1) R), R = H / K,
+    and R / 2^i rows after the i-th downsampler (H a multiple of 8 K)."""
+
+    def downsample(self, name: str, x: torch.Tensor) -> torch.Tensor:
+        """Pad right / bottom by one, 3x3 stride 2 (vae_encoder.rs:206-210): output
+        row i of the band reads band rows 2i .. 2i + 2, the last of which is the
+        bottom halo row (zeros below the image)."""
+        _, rr, w, c = x.shape
+        r = rr - 2
+        if r % 2:
+            raise InvalidInput("band rows must stay even through the downsamplers")
+        self.halo(x)
+        y = self.ops.zeros((1, r // 2 + 2, w // 2, c))
+        self.ops.conv_down(name, x[:, 1:r + 2], y[:, 1:r // 2 + 1])
+        return y
+
+    def encode_moments(self, image: torch.Tensor) -> torch.Tensor:
+        """Normalized image [1, 3, H, W] (the whole image, on every rank) -> this
+        rank's rows of the posterior moments, f32 NCHW [1, 8, H / 8 / K, W / 8]."""
+        if image.ndim == 4 and image.shape[2] % (8 * self.k):
+            raise InvalidInput("image height must divide into 8 x the band group")
+        x = self.ops.conv("encoder.conv_in", self._band_rows(image, self.k, 3))
+        for i in range(len(self.channels)):
+            for j in range(self.layers):
+                x = self.resnet(f"encoder.down_blocks.{i}.resnets.{j}", x)
+            if i + 1 < len(self.channels):
+                x = self.downsample(f"encoder.down_blocks.{i}.downsamplers.0.conv", x)
+        mid = "encoder.mid_block"
+        x = self.resnet(mid + ".resnets.0", x)
+        x = self.attention(mid + ".attentions.0", x)
+        x = self.resnet(mid + ".resnets.1", x)
+        x = self.group_norm("encoder.conv_norm_out", x, True)
+        y = self.ops.conv("encoder.conv_out", x, out_nchw=True)
+        m = self.ops.conv("quant_conv", y, out_nchw=True)
+        rows = m.shape[2] - 2
+        return m[:, :, 1:rows + 1].contiguous()

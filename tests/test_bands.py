@@ -20,7 +20,7 @@ import torch.multiprocessing as mp
 
 import oracle
 from oracle import vae as ovae
-from osor_b200.bands import BandDecoder
+from osor_b200.bands import BandDecoder, BandEncoder
 from osor_b200.weights import random_vae_weights
 
 CHANNELS = (32, 32, 64, 64)
@@ -65,6 +65,12 @@ class OracleBandOps:
             out.copy_(y)
             return out
         return y
+
+    def conv_down(self, name, x, out):
+        y = oracle.conv2d(oracle.pad_right_bottom(self._nchw(x)), self.w[name + ".weight"],
+                          self.w[name + ".bias"], stride=2, padding=0)
+        out.copy_(self._nhwc(y))
+        return out
 
     def qkv(self, prefix, h):
         b, r, w, c = h.shape
@@ -146,6 +152,37 @@ def test_band_split_decode_matches_whole_image(world, h, w, tmp_path):
     want = ovae.decode(weights, latents, CHANNELS, LAYERS)
     assert got.shape == want.shape == (1, 3, 8 * h, 8 * w)
     # f32 oracle ops on bands vs the whole image: only summation order differs.
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4 * np.abs(want).max())
+
+
+def _encoder_rank_main(rank, world, port, h, w, out_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        weights = random_vae_weights(3, CHANNELS, LAYERS, parts=("encoder",))
+        rng = np.random.default_rng(12)
+        image = torch.from_numpy(rng.uniform(-1, 1, (1, 3, h, w)).astype(np.float32))
+        band = BandEncoder(OracleBandOps(weights), CHANNELS, LAYERS).encode_moments(image)
+        parts = [torch.empty_like(band) for _ in range(world)]
+        dist.all_gather(parts, band)
+        if rank == 0:
+            np.save(os.path.join(out_dir, "moments.npy"), torch.cat(parts, dim=2).numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,h,w", [(2, 64, 48), (4, 64, 32)])
+def test_band_split_encode_matches_whole_image(world, h, w, tmp_path):
+    """Band rows halve at each stride-2 downsampler, whose last output row reads
+    the halo row below the band (vae_encoder.rs:206-210)."""
+    mp.start_processes(_encoder_rank_main, args=(world, _free_port(), h, w, str(tmp_path)),
+                       nprocs=world, start_method="spawn")
+    got = np.load(tmp_path / "moments.npy")
+    weights = random_vae_weights(3, CHANNELS, LAYERS, parts=("encoder",))
+    image = np.random.default_rng(12).uniform(-1, 1, (1, 3, h, w)).astype(np.float32)
+    want = ovae.encode_moments(weights, image, CHANNELS, LAYERS)
+    assert got.shape == want.shape == (1, 8, h // 8, w // 8)
     np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4 * np.abs(want).max())
 
 

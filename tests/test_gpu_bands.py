@@ -1,6 +1,7 @@
-"""Row-band decoding on the GPU: the band entry points of the C ABI against
-the oracle, and the band decoder itself against the oracle's whole-image
-decode (one rank on one GPU; two ranks over NCCL when two GPUs are visible).
+"""Row-band decoding and encoding on the GPU: the band entry points of the C
+ABI against the oracle, and the band decoder / encoder against the oracle's
+whole-image results (one rank on one GPU; two ranks over NCCL when two GPUs
+are visible).
 
 * osor_group_norm_stats + osor_group_norm_apply over the row bands of one
   image, with the bands' statistics merged by the apply, equal the oracle's
@@ -10,7 +11,8 @@ decode (one rank on one GPU; two ranks over NCCL when two GPUs are visible).
   column slices of one q|k|v projection) equals the oracle's attention
   (src/native/attention.rs:27-84) to 16-bit rounding, on the tensor-core path
   (row counts multiples of 128) and the CUDA-core path.
-* BandDecoder's RGB meets the decoder's acceptance bounds against the oracle.
+* BandDecoder's RGB meets the decoder's acceptance bounds against the oracle,
+  and BandEncoder's moments the encoder's (relative L2 <= 1e-2).
 """
 import os
 import subprocess
@@ -28,7 +30,7 @@ for _p in (os.path.dirname(HERE), os.path.join(os.path.dirname(HERE), "osor-rs_b
 import oracle
 import oracle.vae as ovae
 from osor_b200 import ops, workloads
-from osor_b200.bands import BandDecoder, CudaBandOps
+from osor_b200.bands import BandDecoder, BandEncoder, CudaBandOps
 from osor_b200.model import device_status
 from osor_b200.weights import random_vae_weights
 
@@ -101,6 +103,16 @@ def test_band_decoder_one_rank_matches_oracle(cuda_device):
     assert workloads.psnr(got, want) >= 40.0
 
 
+def test_band_encoder_one_rank_matches_oracle(cuda_device):
+    weights = random_vae_weights(0, parts=("encoder",))
+    img, _ = workloads.encoder_image(1, 128, 128, seed=5)
+    got = BandEncoder(CudaBandOps(weights, dtype=torch.float16)).encode_moments(
+        torch.from_numpy(img).cuda())
+    assert device_status(0) == 0
+    want = ovae.encode_moments(weights, img)
+    assert workloads.rel_l2(got.cpu().numpy(), want) <= 1e-2
+
+
 def _rank_main(out_path: str) -> None:
     """One rank of the two-GPU check (run under torch.distributed.run)."""
     import torch.distributed as dist
@@ -116,8 +128,15 @@ def _rank_main(out_path: str) -> None:
         band = dec.decode(torch.from_numpy(lat).cuda())
         every = torch.empty((dist.get_world_size(),) + tuple(band.shape), device=band.device)
         dist.all_gather_into_tensor(every, band)
+        img, _ = workloads.encoder_image(1, 128, 128, seed=5)
+        enc = BandEncoder(CudaBandOps(random_vae_weights(0, parts=("encoder",)),
+                                      device=f"cuda:{local}", dtype=torch.float16))
+        mband = enc.encode_moments(torch.from_numpy(img).cuda())
+        mevery = torch.empty((dist.get_world_size(),) + tuple(mband.shape), device=mband.device)
+        dist.all_gather_into_tensor(mevery, mband)
         if dist.get_rank() == 0:
             np.save(out_path, torch.cat(list(every), dim=2).cpu().numpy())
+            np.save(out_path + ".moments.npy", torch.cat(list(mevery), dim=2).cpu().numpy())
     finally:
         dist.destroy_process_group()
 
@@ -137,6 +156,11 @@ def test_band_decoder_two_gpus_matches_oracle(tmp_path):
     assert got.shape == want.shape
     assert np.abs(got - want).max() <= MAX_ABS[torch.float16]
     assert workloads.psnr(got, want) >= 40.0
+    moments = np.load(out + ".moments.npy")
+    img, _ = workloads.encoder_image(1, 128, 128, seed=5)
+    want_m = ovae.encode_moments(random_vae_weights(0, parts=("encoder",)), img)
+    assert moments.shape == want_m.shape
+    assert workloads.rel_l2(moments, want_m) <= 1e-2
 
 
 if __name__ == "__main__":
