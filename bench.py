@@ -163,8 +163,13 @@ def run_reference(args, rank, world):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1)/0.13025 latents; random-init weights seed 0)",
-        "config": {"workload": "SDXL VAE decoder, bounded CPU sample: 1 x [4,32,32] -> [3,256,256] per step",
-                   "global_batch": 1, "parallelism": "host threads"},
+        "config": {"workload": "SDXL AutoencoderKL decoder [4,4,128,128] -> [4,3,1024,1024] per GPU",
+                   "sample_per_step": "1 x [4,32,32] -> [3,256,256]: a bounded sample of the "
+                                      "workload, the same layers at a quarter of the latent side "
+                                      "(the mid-block attention, quadratic in tokens, costs less "
+                                      "per pixel there)",
+                   "global_batch": 4, "latent": [LATENT, LATENT], "image": [IMAGE, IMAGE],
+                   "parallelism": f"host threads ({oracle.threads()})"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": oracle.threads(), "kind": "port",
                          "sample": "1 x [4,32,32] latents -> [3,256,256] per step; the reference "
                                    "(Rust/Candle CPU) cannot be built here, this is its C++ restatement"},
