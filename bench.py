@@ -178,6 +178,11 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# DRAM bytes (read + write) per 3x3 convolution launch of the decode for one
+# image, averaged over its 28 launches, from one ncu capture of the batch-1
+# decode; every layer is per image, so a launch over B images moves B times this.
+CONV3X3_DRAM_BYTES_PER_IMAGE = 253.13e6
+
 CONV_SHAPES = [(4, 512, 512, 128, 128), (4, 512, 512, 256, 256), (4, 256, 256, 512, 512),
                (4, 128, 128, 1024, 1024), (1, 128, 3, 1024, 1024)]
 GN_SHAPES = [(4, 512, 128, 128), (4, 512, 256, 256), (4, 256, 512, 512), (4, 128, 1024, 1024)]
@@ -634,7 +639,11 @@ def main():
                          "achieved": round(achieved, 1), "peak": tflops_sus, "unit": "TFLOP/s",
                          "frac": round(achieved / tflops_sus, 4),
                          "peak_source": f"{peak_src} bf16_tflops_sustained (dense cuBLAS bf16; f16 runs the same tensor-core rate)",
-                         "traffic": None,
+                         "traffic": round(CONV3X3_DRAM_BYTES_PER_IMAGE * args.batch),
+                         "traffic_unit": "bytes per launch",
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the "
+                                           "decode's 28 3x3 conv launches, one image, times the "
+                                           "batch (profiles/decode_b1_dram_traffic.md)",
                          "decode_tflops": round(total_flops / (ms_per_step / 1e3) / 1e12, 1)},
             "op_breakdown": breakdown,
             "e2e": {"value": world * mpx / (e2e_ms / 1e3), "unit": UNIT,
