@@ -510,10 +510,18 @@ int osor_upsample_2x(const void* x, void* y, int batch, int height, int width, i
   return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "upsample");
 }
 
+namespace {
+// Softmax scratch of the tensor-core attention: per-row (max, sum) partials
+// over column blocks of at least 32 and the row maxima.
+size_t attention_stats_bytes(int n_q, int n_kv) {
+  return ((size_t)n_q * ((n_kv + 31) / 32) * 8 + (size_t)n_q * 4 + 255) / 256 * 256;
+}
+}  // namespace
+
 size_t osor_attention_kv_workspace_size(int batch, int n_q, int n_kv, int dim) {
   (void)batch;
   if (n_q <= 0 || n_kv <= 0 || dim <= 0) return 0;
-  const size_t a = ((size_t)n_q * n_kv * 4 + 255) / 256 * 256;
+  const size_t a = attention_stats_bytes(n_q, n_kv);
   const size_t b = ((size_t)n_q * n_kv * 2 + 255) / 256 * 256;
   const size_t c = ((size_t)n_q * 4 + 255) / 256 * 256;
   const size_t d = ((size_t)n_kv * dim * 2 + 255) / 256 * 256;
@@ -537,7 +545,7 @@ int osor_attention_kv(const void* q, long long ld_q, const void* k, const void* 
   DeviceOf dev(q);
   uint8_t* w = static_cast<uint8_t*>(workspace);
   float* scores = reinterpret_cast<float*>(w);
-  w += ((size_t)n_q * n_kv * 4 + 255) / 256 * 256;
+  w += attention_stats_bytes(n_q, n_kv);
   void* probs = w;
   w += ((size_t)n_q * n_kv * 2 + 255) / 256 * 256;
   float* rowsum = reinterpret_cast<float*>(w);

@@ -73,6 +73,10 @@ struct TcParams {
   // 16-bit outputs leave through TMA stores of 32 consecutive tile pixels,
   // except for an upsampled output with low_w % 32 != 0 (direct stores).
   int direct_store;
+  // Two-pass row softmax (ConvTcArgs::softmax_*).
+  float* softmax_stats;
+  int softmax_stats_ld;
+  const float* softmax_max;
 };
 
 template <int BLOCK_N>
@@ -354,6 +358,7 @@ __global__ void __launch_bounds__(TcConfig<BLOCK_N>::kThreads, 1)
                 __uint_as_float(r[j]) * scale + (p.bias ? __ldg(p.bias + j) : 0.0f);
       } else {
         float* st = stat_smem + acc * (4 * 64 * 2);
+        float sm_max = 0.0f, sm_sum = 0.0f;  // softmax statistics pass
 #pragma unroll
         for (int c = 0; c < CPW; ++c) {
           const int chunk = slot * CPW + c;
@@ -393,6 +398,32 @@ __global__ void __launch_bounds__(TcConfig<BLOCK_N>::kThreads, 1)
 #pragma unroll
               for (int t = 0; t < 8; ++t) v[8 * j + t] += f[t];
             }
+          }
+          if (p.softmax_stats) {
+            // Row softmax statistics of this warp's CPW x 32 columns, merged
+            // across its chunks online; nothing is stored.
+            constexpr float kLog2e = 1.4426950408889634f;
+            float mx = v[0];
+#pragma unroll
+            for (int j = 1; j < 32; ++j) mx = fmaxf(mx, v[j]);
+            if (c > 0) mx = fmaxf(mx, sm_max);
+            float sum = c > 0 ? sm_sum * ex2_approx((sm_max - mx) * kLog2e) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sum += ex2_approx((v[j] - mx) * kLog2e);
+            sm_max = mx;
+            sm_sum = sum;
+            if (c == CPW - 1) {
+              const int block = (n_tile * BLOCK_N + slot * CPW * 32) / (CPW * 32);
+              reinterpret_cast<float2*>(p.softmax_stats)[m * p.softmax_stats_ld + block] =
+                  make_float2(sm_max, sm_sum);
+            }
+            continue;
+          }
+          if (p.softmax_max) {
+            constexpr float kLog2e = 1.4426950408889634f;
+            const float mrow = __ldg(p.softmax_max + m) * kLog2e;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = ex2_approx(fmaf(v[j], kLog2e, -mrow));
           }
           // Stores leave through TMA from a 1 KB staging tile per warp
           // (pixel row = lane, 32 bytes each): one lane per pixel would make
@@ -610,7 +641,8 @@ const char* conv_tc_check(const ConvTcArgs& a) {
     return "operands must be 16-byte aligned";
   if (a.residual && (a.ld_res % 8 != 0 || (reinterpret_cast<uintptr_t>(a.residual) & 15)))
     return "residual must be 16-byte aligned";
-  if (!a.out_nchw && (a.ld_out % (a.out_f32 ? 4 : 8) != 0 || (reinterpret_cast<uintptr_t>(a.out) & 15)))
+  if (!a.out_nchw && !a.softmax_stats &&
+      (a.ld_out % (a.out_f32 ? 4 : 8) != 0 || (reinterpret_cast<uintptr_t>(a.out) & 15)))
     return "output must be 16-byte aligned";
   if (a.bias && (reinterpret_cast<uintptr_t>(a.bias) & 15)) return "bias must be 16-byte aligned";
   if ((long long)a.batch * a.out_h * a.out_w > 0x7fffffffLL) return "problem too large";
@@ -618,7 +650,23 @@ const char* conv_tc_check(const ConvTcArgs& a) {
   if (a.dtype != kBf16 && a.dtype != kF16) return "unknown 16-bit type";
   if (a.gn_part && (a.out_f32 || (a.gn_cpg != 4 && a.gn_cpg != 8 && a.gn_cpg != 16)))
     return "fused group-norm statistics need a 16-bit output and 4, 8 or 16 channels per group";
+  if (a.softmax_stats || a.softmax_max) {
+    if (a.softmax_stats && a.softmax_max) return "one softmax pass at a time";
+    if (a.ksize != 1 || a.out_nchw || a.upsample || a.bias || a.residual || a.gn_part ||
+        a.row_scale || a.out_f32)
+      return "the softmax passes take a plain 1x1 product with a 16-bit output";
+    if (a.softmax_stats &&
+        (a.softmax_stats_ld < a.cout / conv_tc_softmax_block(a.cout) ||
+         (reinterpret_cast<uintptr_t>(a.softmax_stats) & 7)))
+      return "softmax statistics buffer is too small or misaligned";
+  }
   return nullptr;
+}
+
+int conv_tc_softmax_block(int cout) {
+  // Each epilogue warp covers BLOCK_N / 4 columns of a tile (two or one
+  // 32-column chunks).
+  return (cout % 256 == 0 ? 256 : 128) / 4;
 }
 
 cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
@@ -696,10 +744,13 @@ cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
   p.low_w = a.in_w;
   p.cout_total = a.upsample ? a.cout : 0;
   p.direct_store = a.upsample && a.in_w % 32 != 0;
+  p.softmax_stats = a.softmax_stats;
+  p.softmax_stats_ld = a.softmax_stats_ld;
+  p.softmax_max = a.softmax_max;
   // Output tensor map for the epilogue's TMA stores (unused by the thin
   // NCHW output, which stores directly).
   CUtensorMap to = tb;
-  if (!a.out_nchw) {
+  if (!a.out_nchw && !a.softmax_stats) {
     CUresult r;
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     if (a.upsample) {

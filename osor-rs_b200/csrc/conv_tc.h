@@ -45,7 +45,19 @@ struct ConvTcArgs {
   // (a, b) = rows [(2a + b) * cout, ...)); out_h / out_w equal in_h / in_w.
   // GroupNorm partials (gn_part) are written per phase tile, image-major.
   int upsample = 0;
+  // Softmax over each output row in two passes of the same product (the
+  // attention scores, 1x1, no bias / residual / statistics, Cout a multiple
+  // of 128). softmax_stats: no output is stored; for every row and every
+  // block of conv_tc_softmax_block(cout) columns, (max, sum of exp(v - max))
+  // goes to softmax_stats[row][block][2] (softmax_stats_ld blocks per row).
+  // softmax_max: the 16-bit output is exp(v - softmax_max[row]).
+  float* softmax_stats = nullptr;
+  int softmax_stats_ld = 0;
+  const float* softmax_max = nullptr;
 };
+
+// Columns per (max, sum) partial of the softmax statistics pass.
+int conv_tc_softmax_block(int cout);
 
 // nullptr when the tensor-core kernel supports the shape, else a reason.
 const char* conv_tc_check(const ConvTcArgs& a);

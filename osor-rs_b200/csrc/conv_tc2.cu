@@ -441,7 +441,8 @@ cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Param
 }  // namespace
 
 const char* conv_tc2_check(const ConvTcArgs& a) {
-  if (a.upsample || a.out_nchw || a.out_f32) return "pair kernel: plain 16-bit output only";
+  if (a.upsample || a.out_nchw || a.out_f32 || a.softmax_stats || a.softmax_max)
+    return "pair kernel: plain 16-bit output only";
   if (a.cout != kN) return "pair kernel: Cout must be 128";
   if (a.ksize != 1 && a.ksize != 3) return "pair kernel: 1x1 or 3x3";
   if (a.stride != 1 && a.stride != 2) return "pair kernel: stride 1 or 2";

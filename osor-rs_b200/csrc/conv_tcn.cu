@@ -466,7 +466,8 @@ cudaError_t launch_n(const CUtensorMap& tx, const CUtensorMap& tw, const CUtenso
 }  // namespace
 
 const char* conv_tcn_check(const ConvTcArgs& a) {
-  if (a.upsample || a.row_scale) return "pixel-N kernel: plain convolution only";
+  if (a.upsample || a.row_scale || a.softmax_stats || a.softmax_max)
+    return "pixel-N kernel: plain convolution only";
   if (!((a.ksize == 3 && a.pad == 1) || (a.ksize == 1 && a.pad == 0)) || a.stride != 1)
     return "pixel-N kernel: 3x3 pad 1 or 1x1, stride 1";
   if (a.out_h != a.in_h || a.out_w != a.in_w) return "pixel-N kernel: same-size output";

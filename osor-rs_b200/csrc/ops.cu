@@ -139,59 +139,30 @@ __global__ void upsample2x_nhwc_kernel(const uint4* __restrict__ x, uint4* __res
 }
 
 // ------------------------------------------------------------ softmax
-// One CTA per row: p = exp(s - max) stored as 16-bit, inv_sum = 1 / sum(p) in
-// fp32 (sum of the rounded values, which is what the P.V GEMM multiplies).
-constexpr int kSoftmaxThreads = 256;
-constexpr int kSoftmaxMaxVec = 16;  // rows up to 16 * 4 * 256 = 16384 columns
-
-template <int D>
-__global__ void __launch_bounds__(kSoftmaxThreads)
-    softmax_rows_kernel(const float* __restrict__ s, uint16_t* __restrict__ p,
-                        float* __restrict__ inv_sum, int cols, long long ld_s, long long ld_p) {
-  using E = Elem<D>;
-  __shared__ float red[8];
-  const long long row = blockIdx.x;
-  const float4* srow = reinterpret_cast<const float4*>(s + row * ld_s);
-  const int nv = cols / 4;
-  float4 v[kSoftmaxMaxVec];
-  float mx = -INFINITY;
+// stats[row][block] = (max, sum of exp(v - max)) over the blocks of one score
+// row -> the row's max and 1 / (sum of exp(v - row max)). One warp per row.
+__global__ void softmax_merge_kernel(const float2* __restrict__ stats, int blocks, long long ld,
+                                     int rows, float* __restrict__ row_max,
+                                     float* __restrict__ inv_sum) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float2* st = stats + row * ld;
+  float m = -INFINITY;
+  for (int b = lane; b < blocks; b += 32) m = fmaxf(m, st[b].x);
 #pragma unroll
-  for (int j = 0; j < kSoftmaxMaxVec; ++j) {
-    const int idx = threadIdx.x + j * kSoftmaxThreads;
-    if (idx < nv) {
-      v[j] = __ldcs(srow + idx);
-      mx = fmaxf(mx, fmaxf(fmaxf(v[j].x, v[j].y), fmaxf(v[j].z, v[j].w)));
-    }
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float l = 0.0f;
+  for (int b = lane; b < blocks; b += 32) {
+    const float2 v = st[b];
+    l += v.y * ex2_approx((v.x - m) * kLog2e);
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-  __syncthreads();
-  mx = red[0];
-#pragma unroll
-  for (int k = 1; k < kSoftmaxThreads / 32; ++k) mx = fmaxf(mx, red[k]);
-  __syncthreads();
-  float sum = 0.0f;
-  uint2* prow = reinterpret_cast<uint2*>(p + row * ld_p);
-#pragma unroll
-  for (int j = 0; j < kSoftmaxMaxVec; ++j) {
-    const int idx = threadIdx.x + j * kSoftmaxThreads;
-    if (idx < nv) {
-      const uint32_t a = E::pack(__expf(v[j].x - mx), __expf(v[j].y - mx));
-      const uint32_t b = E::pack(__expf(v[j].z - mx), __expf(v[j].w - mx));
-      const float2 fa = E::unpack(a), fb = E::unpack(b);
-      sum += (fa.x + fa.y) + (fb.x + fb.y);
-      prow[idx] = make_uint2(a, b);
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.0f;
-    for (int k = 0; k < kSoftmaxThreads / 32; ++k) t += red[k];
-    inv_sum[row] = 1.0f / t;
+  for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+  if (lane == 0) {
+    row_max[row] = m;
+    inv_sum[row] = 1.0f / l;
   }
 }
 
@@ -365,16 +336,11 @@ cudaError_t upsample2x_nhwc_launch(const void* x, void* y, int batch, int h, int
   return cudaGetLastError();
 }
 
-cudaError_t softmax_rows_launch(int dtype, const float* scores, void* probs, float* inv_sum,
-                                int rows, int cols, long long ld_s, long long ld_p,
-                                cudaStream_t s) {
-  if (cols % 4 != 0 || cols > kSoftmaxMaxVec * 4 * kSoftmaxThreads || ld_s % 4 || ld_p % 4)
-    return cudaErrorInvalidValue;
-  uint16_t* p = static_cast<uint16_t*>(probs);
-  if (dtype == kF16)
-    softmax_rows_kernel<kF16><<<rows, kSoftmaxThreads, 0, s>>>(scores, p, inv_sum, cols, ld_s, ld_p);
-  else
-    softmax_rows_kernel<kBf16><<<rows, kSoftmaxThreads, 0, s>>>(scores, p, inv_sum, cols, ld_s, ld_p);
+cudaError_t softmax_merge_launch(const float* stats, int blocks, long long ld, int rows,
+                                 float* row_max, float* inv_sum, cudaStream_t s) {
+  const int warps = 8;
+  softmax_merge_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, s>>>(
+      reinterpret_cast<const float2*>(stats), blocks, ld, rows, row_max, inv_sum);
   return cudaGetLastError();
 }
 

@@ -26,10 +26,10 @@ cudaError_t direct_conv_launch(int dtype, const void* x, int in_mode, const void
 cudaError_t upsample2x_nhwc_launch(const void* x, void* y, int batch, int h, int w, int c,
                                    cudaStream_t s);
 
-// probs[r][c] = 16-bit(exp(scores[r][c] - max_r)); inv_sum[r] = 1 / sum_c probs[r][c].
-cudaError_t softmax_rows_launch(int dtype, const float* scores, void* probs, float* inv_sum,
-                                int rows, int cols, long long ld_s, long long ld_p,
-                                cudaStream_t s);
+// stats [rows][ld][2] = (max, sum of exp(v - max)) for `blocks` column blocks
+// of each score row -> row_max[r] and inv_sum[r] = 1 / sum of exp(v - row_max).
+cudaError_t softmax_merge_launch(const float* stats, int blocks, long long ld, int rows,
+                                 float* row_max, float* inv_sum, cudaStream_t s);
 
 cudaError_t transpose16_launch(const void* in, long long ld_in, void* out, long long ld_out,
                                int rows, int cols, cudaStream_t s);

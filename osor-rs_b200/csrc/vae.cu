@@ -525,9 +525,16 @@ Status attention_core(int dtype, const void* q, long long ld_q, const void* k, c
         attn_fused_launch(dtype, q, k, ld_q, vt, out, ld_out, batch, tokens, dim, s),
         "fused attention");
   }
+  // Softmax in two passes of the scores GEMM, so that no f32 score matrix is
+  // written: the first pass keeps per-row (max, sum of exp) over blocks of
+  // columns, a merge gives each row's max and 1 / sum, and the second pass
+  // writes P = exp(s - max) as 16-bit; out = (P V) / sum.
+  const int blk = conv_tc_softmax_block(n_kv);
+  const int nblk = n_kv / blk;
+  float* stats = scores;                                // [n_q][nblk][2]
+  float* row_max = scores + (long long)n_q * nblk * 2;  // [n_q]
   for (int bi = 0; bi < batch; ++bi) {
     const long long oq = (long long)bi * n_q, okv = (long long)bi * n_kv;
-    // scores = q k^T (fp32), [n_q][n_kv]
     ConvTcArgs a;
     a.dtype = dtype;
     a.x = qb + oq * ld_q;
@@ -544,22 +551,34 @@ Status attention_core(int dtype, const void* q, long long ld_q, const void* k, c
     a.cout = n_kv;
     a.w = kb + okv * ld_kv;
     a.ldw = ld_kv;
-    a.out = scores;
-    a.ld_out = n_kv;
-    a.out_f32 = 1;
+    a.softmax_stats = stats;
+    a.softmax_stats_ld = nblk;
     if (const char* why = conv_tc_check(a)) return Status::err(OSOR_ERR_INVALID_INPUT, why);
     const double nn = (double)n_q * n_kv;
     cudaError_t e;
     {
-      OpScope scope("attn_scores", 2.0 * nn * dim, 2.0 * (n_q + n_kv) * dim + 4.0 * nn, s, 1);
+      OpScope scope("attn_scores", 2.0 * nn * dim, 2.0 * (n_q + n_kv) * dim + 8.0 * n_q * nblk,
+                    s, 1);
       e = conv_tc_launch(a, s);
     }
-    if (e != cudaSuccess) return cuda_status(e, "attention scores");
+    if (e != cudaSuccess) return cuda_status(e, "attention score statistics");
     {
-      OpScope scope("attn_softmax", 0.0, 6.0 * nn, s, 1);
-      e = softmax_rows_launch(dtype, scores, probs, rowsum, n_q, n_kv, n_kv, n_kv, s);
+      OpScope scope("attn_softmax", 0.0, 8.0 * n_q * nblk + 8.0 * n_q, s, 1);
+      e = softmax_merge_launch(stats, nblk, nblk, n_q, row_max, rowsum, s);
     }
-    if (e != cudaSuccess) return cuda_status(e, "attention softmax");
+    if (e != cudaSuccess) return cuda_status(e, "attention softmax merge");
+    ConvTcArgs pa = a;
+    pa.softmax_stats = nullptr;
+    pa.softmax_stats_ld = 0;
+    pa.softmax_max = row_max;
+    pa.out = probs;
+    pa.ld_out = n_kv;
+    if (const char* why = conv_tc_check(pa)) return Status::err(OSOR_ERR_INVALID_INPUT, why);
+    {
+      OpScope scope("attn_probs", 2.0 * nn * dim, 2.0 * (n_q + n_kv) * dim + 2.0 * nn, s, 1);
+      e = conv_tc_launch(pa, s);
+    }
+    if (e != cudaSuccess) return cuda_status(e, "attention probabilities");
     {
       OpScope scope("attn_transpose", 0.0, 4.0 * n_kv * dim, s, 1);
       e = transpose16_launch(vb + okv * ld_kv, ld_kv, vt, n_kv, n_kv, dim, s);
@@ -838,7 +857,8 @@ WorkspacePlan vae_workspace_plan(const Vae& m, int op, int batch, int height, in
   p.f32_bytes = align256((size_t)batch * 8 * std::max(latent, 1LL) * 4);
   const int tokens = (int)latent;
   if (attention_tc_ok(tokens, ch[3])) {
-    p.scores_bytes = align256((size_t)tokens * tokens * 4);
+    // softmax partials (max, sum) per row and 32-column block, and row maxima
+    p.scores_bytes = align256((size_t)tokens * (tokens / 32) * 8 + (size_t)tokens * 4);
     p.probs_bytes = align256((size_t)tokens * tokens * 2);
     p.rowsum_bytes = align256((size_t)tokens * 4);
   }

@@ -99,7 +99,7 @@ struct WorkspacePlan {
   size_t act_bytes = 0;      // one activation buffer
   size_t tstat_bytes = 0;    // per-tile GroupNorm statistics of one activation buffer
   size_t f32_bytes = 0;      // thin f32 NCHW scratch
-  size_t scores_bytes = 0;   // attention scores (fp32) for one image
+  size_t scores_bytes = 0;   // attention softmax partials for one image
   size_t probs_bytes = 0;    // attention probabilities (16-bit) for one image
   size_t rowsum_bytes = 0;
   size_t gn_bytes = 0;
@@ -139,9 +139,9 @@ Status run_conv(int dtype, const ConvLayer& L, const void* x, int in_mode, int b
                 cudaStream_t s, float* gn_part = nullptr, bool* gn_done = nullptr);
 
 // softmax(q k^T) v for `batch` images: n_q query rows (stride ld_q) against
-// n_kv key / value rows (stride ld_kv) per image. scores [n_q][n_kv] f32,
-// probs [n_q][n_kv] 16-bit, rowsum [n_q] and vt [dim][n_kv] are per-image
-// scratch reused across images.
+// n_kv key / value rows (stride ld_kv) per image. scores (softmax partials:
+// n_q x n_kv / 32 x 2 + n_q floats), probs [n_q][n_kv] 16-bit, rowsum [n_q]
+// and vt [dim][n_kv] are per-image scratch reused across images.
 Status attention_core(int dtype, const void* q, long long ld_q, const void* k, const void* v,
                       long long ld_kv, void* out, long long ld_out, int batch, int n_q, int n_kv,
                       int dim, float* scores, void* probs, float* rowsum, void* vt,
