@@ -70,6 +70,50 @@ def test_invalid_arguments_fail_before_device_work():
             _lib.OSOR_ERR_INVALID_INPUT
 
 
+def test_band_pipeline_and_scheduler_entry_points_validate_on_the_host():
+    """The entry points added for the band split, the pipeline stages and the
+    scheduler refuse bad arguments before any device work."""
+    lb = _lib.lib()
+    d = ctypes.c_void_p(256)
+    f16 = _lib.DTYPE_F16
+    bad = _lib.OSOR_ERR_INVALID_INPUT
+    # GroupNorm statistics / merged apply: channels % 32, parts >= 1, nulls.
+    assert lb.osor_group_norm_stats(d, 1, 48, 4, 4, f16, d, d, 1 << 20, None) == bad
+    assert lb.osor_group_norm_stats(None, 1, 64, 4, 4, f16, d, d, 1 << 20, None) == bad
+    assert lb.osor_group_norm_apply(d, d, d, d, d, 0, 1, 64, 4, 4, f16, 1e-6, 1, d, 1 << 20,
+                                    None) == bad
+    assert lb.osor_group_norm_apply(d, d, d, d, d, 2, 1, 64, 4, 4, f16, 1e-6, 1, d, 16,
+                                    None) == bad  # workspace below B * C * 16 bytes
+    # Rectangular attention: dim <= 512, strides >= dim, 16-bit only.
+    assert lb.osor_attention_kv(d, 64, d, d, 64, d, 1, 8, 16, 1024, f16, d, 1 << 30, None) == bad
+    assert lb.osor_attention_kv(d, 32, d, d, 64, d, 1, 8, 16, 64, f16, d, 1 << 30, None) == bad
+    assert lb.osor_attention_kv(d, 64, d, d, 64, d, 1, 8, 16, 64, _lib.DTYPE_F32, d, 1 << 30,
+                                None) == bad
+    assert lb.osor_attention_kv_workspace_size(1, 8, 16, 64) > 0
+    assert lb.osor_attention_kv_workspace_size(1, 0, 16, 64) == 0
+    # Pipeline stages: admission limits, cumulative alpha, prediction type.
+    assert lb.osor_pipeline_prepare(d, d, d, d, d, None, 5, 64, 64, 0.4, 0.13025, None) == bad
+    assert lb.osor_pipeline_prepare(d, d, d, d, d, None, 1, 60, 64, 0.4, 0.13025, None) == bad
+    assert lb.osor_pipeline_prepare(d, d, d, d, d, None, 1, 64, 64, 0.0, 0.13025, None) == bad
+    assert lb.osor_pipeline_prepare(d, d, d, d, d, None, 1, 64, 64, 0.4, -1.0, None) == bad
+    assert lb.osor_pipeline_finish(d, d, d, None, None, d, 1, 64, 64, 0.4, 3, 0, 1.0, 0.13025,
+                                   None) == bad
+    assert lb.osor_pipeline_finish(d, d, d, None, None, d, 1, 64, 64, 0.4, 0, 1, 0.0, 0.13025,
+                                   None) == bad
+    assert lb.osor_pipeline_map(d, d, d, None, 1, 64, 64, None) == bad
+    assert lb.osor_pipeline_normalize_image(d, d, 1, 1032, 64, None) == bad
+    # Scheduler formulas: element limit and alpha range.
+    assert lb.osor_scheduler_add_noise(d, d, d, 0, 0.4, None) == bad
+    assert lb.osor_scheduler_add_noise(d, d, d, 16 * 1024 * 1024 + 1, 0.4, None) == bad
+    assert lb.osor_scheduler_predicted_original(d, d, d, 4, 1.5, 0, 0, 1.0, None) == bad
+    # Cumulative alphas are host work: they run here.
+    out = np.empty(3, np.float32)
+    assert lb.osor_scheduler_alphas(3, 0.1, 0.2, 0, None, out.ctypes.data) == _lib.OSOR_OK
+    assert np.all(np.diff(out) < 0) and 0 < out[-1] < out[0] < 1
+    assert lb.osor_scheduler_alphas(3, 0.1, 0.2, 2, None, out.ctypes.data) == bad
+    assert lb.osor_scheduler_alphas(0, 0.1, 0.2, 0, None, out.ctypes.data) == bad
+
+
 def test_device_check_reports_unavailable_without_gpu():
     import torch
     if torch.cuda.is_available():
