@@ -295,6 +295,81 @@ int osor_attention_kv(const void* q, long long ld_q, const void* k, const void* 
                       void* out, int batch, int n_q, int n_kv, int dim, int dtype,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------- UNet
+ * Ops of the SDXL inpainting UNet (src/native.rs:112-379) beyond the VAE set.
+ * Pixel tensors are 16-bit NHWC rows (`dtype` BF16 / F16, 16-byte aligned);
+ * the convolutions, GroupNorm(+SiLU) (eps 1e-5 in resnets, 1e-6 before the
+ * transformers) and the linear projections over pixels (1x1 osor_conv2d) are
+ * the VAE entry points above. */
+
+/* features (device f32 [B][base_channels + pooled_width + 6 * time_projection])
+ * receives per batch entry the sinusoidal projection (cosines first) of
+ * `timestep`, the pooled prompt embedding (device f32 [pooled_width], the same
+ * for every entry) and the projections of the six time ids (device f32
+ * [B][6]): the inputs of the time and added embeddings of Unet::forward
+ * (src/native.rs:318-335). */
+int osor_unet_time_features(const float* time_ids, const float* pooled, int batch, int timestep,
+                            int base_channels, int time_projection, int pooled_width,
+                            float* features, void* stream);
+
+/* y[r][o] = sum_k act(x[r][k]) * w[o][k] + bias[o] + bias2[o] for 1..8 rows
+ * (act = SiLU when pre_silu, else identity); x, y device f32, w 16-bit
+ * [out][in] of `dtype`, bias / bias2 device f32 (nullable); rows * in <=
+ * 12288. Replaces the TimestepEmbedding linears and the resnets'
+ * time_emb_proj(silu(temb)) (src/native/resnet.rs:104-110): with every
+ * resnet's projection stacked in one weight, one call gives all time biases. */
+int osor_rows_linear(const float* x, int rows, int in_features, const void* weight,
+                     const float* bias, const float* bias2, int out_features, int pre_silu,
+                     int dtype, float* y, void* stream);
+
+/* LayerNorm over the last axis of [rows][channels] (channels % 8 == 0, at most
+ * 2048) with f32 statistics and f32 gamma / beta. Replaces the transformer
+ * blocks' nn::LayerNorm (src/native/spatial.rs:171-173). */
+int osor_layer_norm(const void* x, void* y, const float* gamma, const float* beta, long long rows,
+                    int channels, float eps, int dtype, void* stream);
+
+/* y[r][f] = x[r][f] * gelu_erf(x[r][features + f]) for x [rows][2 * features]
+ * (features % 8 == 0). Replaces FeedForward's exact-erf GEGLU gate
+ * (src/native/transformer.rs:17-23). */
+int osor_geglu(const void* x, void* y, long long rows, int features, int dtype, void* stream);
+
+/* y[p] = (a[p], b[p]) for NHWC a [P][ca], b [P][cb] (ca, cb % 8 == 0).
+ * Replaces Tensor::cat(&[xs, skip], 1) of the up blocks
+ * (src/native/unet_blocks.rs:214-219, src/native/cross_blocks.rs:206). */
+int osor_concat_channels(const void* a, int ca, const void* b, int cb, void* y, long long pixels,
+                         int dtype, void* stream);
+
+/* Nearest resize of NHWC [B][H][W][C] to [B][out_h][out_w][C] (C % 8 == 0),
+ * source index min(n - 1, floor(i * (n / out))) in f64. Replaces
+ * upsample_nearest2d to the next skip's size (src/native/unet_blocks.rs:222-235,
+ * src/native.rs:356-367). */
+int osor_resize_nearest(const void* x, void* y, int batch, int in_h, int in_w, int out_h,
+                        int out_w, int channels, int dtype, void* stream);
+
+/* y[b][p][c] = x[b][p][c] + image_bias[b * bias_stride + c] + residual[b][p][c]
+ * for c < channels, with x rows of stride ld_x (>= channels, % 8 == 0) and y /
+ * residual rows of `channels` (% 8 == 0); image_bias device f32 (16-byte
+ * aligned, bias_stride % 4 == 0) and residual nullable. x == y (in place)
+ * needs ld_x == channels. Adds a resnet's per-image time bias after conv1
+ * (src/native/resnet.rs:104-110), and narrows a convolution computed with
+ * zero-padded output channels. */
+int osor_channel_update(const void* x, long long ld_x, void* y, int channels, int batch,
+                        long long pixels_per_image, const float* image_bias,
+                        long long bias_stride, const void* residual, int dtype, void* stream);
+
+/* Multi-head out = softmax(q k^T) v per head with f32 scores and softmax:
+ * head h of query row i of batch entry b reads q + b*q_batch_stride + i*ld_q +
+ * h*head_dim (already scaled, e.g. by head_dim^-1/2), keys / values at
+ * k / v + b*kv_batch_stride + j*ld_kv + h*head_dim, and writes out +
+ * b*out_batch_stride + i*ld_out + h*head_dim. Strides in elements, multiples
+ * of 8; kv_batch_stride 0 shares one key / value set (the fixed prompt) across
+ * the batch. head_dim 32, 64 or 128. Replaces SelfAttention and
+ * FixedCrossAttention's attend (src/native/spatial.rs:29-46, 83-158). */
+int osor_attention_heads(const void* q, long long ld_q, long long q_batch_stride, const void* k,
+                         const void* v, long long ld_kv, long long kv_batch_stride, void* out,
+                         long long ld_out, long long out_batch_stride, int batch, int heads,
+                         int n_q, int n_kv, int head_dim, int dtype, void* stream);
+
 /* One profiled op: kind ("conv_tc", "conv_direct", "groupnorm", ...),
  * algorithmic FLOPs and bytes, device time between the CUDA events recorded
  * on its stream, and the number of kernels it launched. */

@@ -10,6 +10,7 @@
 #include "pipeline.h"
 #include "ops.h"
 #include "profile.h"
+#include "unet.h"
 #include "vae.h"
 
 struct osor_vae {
@@ -249,7 +250,9 @@ size_t osor_group_norm_workspace_size(int batch, int channels, int height, int w
   if (batch <= 0 || channels <= 0 || channels % 32 != 0 || height <= 0 || width <= 0) return 0;
   const long long spatial = (long long)height * width;
   if (layout == OSOR_LAYOUT_NHWC) {
-    if (!is16(dtype) || channels / 8 > 256) return 0;
+    // Up to 1024 16-byte vectors per pixel (C <= 8192): the wide kernels own
+    // four 8-channel columns per thread.
+    if (!is16(dtype) || channels / 8 > 1024) return 0;
     return osor::gn_nhwc_plan(batch, channels, spatial, 32).workspace_bytes;
   }
   if (layout != OSOR_LAYOUT_NCHW || (!is16(dtype) && dtype != OSOR_DTYPE_F32)) return 0;
@@ -571,6 +574,152 @@ int osor_attention(const void* q, const void* k, const void* v, void* out, int b
                    void* stream) {
   return osor_attention_kv(q, ld, k, v, ld, out, batch, tokens, tokens, dim, dtype, workspace,
                            workspace_bytes, stream);
+}
+
+// ---------------------------------------------------------------- UNet
+int osor_unet_time_features(const float* time_ids, const float* pooled, int batch, int timestep,
+                            int base_channels, int time_projection, int pooled_width,
+                            float* features, void* stream) {
+  if (!time_ids || !features || (pooled_width > 0 && !pooled))
+    return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (batch < 1 || batch > 8 || timestep < 0 || base_channels < 2 || base_channels % 2 != 0 ||
+      time_projection < 2 || time_projection % 2 != 0 || pooled_width < 0)
+    return fail(OSOR_ERR_INVALID_INPUT, "invalid time embedding shape");
+  DeviceOf dev(features);
+  osor::note_launches(1);
+  const cudaError_t e = osor::unet_time_features_launch(
+      time_ids, pooled, batch, (float)timestep, base_channels, time_projection, pooled_width,
+      features, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "time features");
+}
+
+int osor_rows_linear(const float* x, int rows, int in_features, const void* weight,
+                     const float* bias, const float* bias2, int out_features, int pre_silu,
+                     int dtype, float* y, void* stream) {
+  if (!x || !weight || !y) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (rows < 1 || rows > 8 || in_features < 1 || out_features < 1 ||
+      (long long)rows * in_features > 12288)
+    return fail(OSOR_ERR_INVALID_INPUT, "row linear takes 1..8 rows of at most 12288 values");
+  if (!is16(dtype)) return fail(OSOR_ERR_INVALID_INPUT, "linear weight dtype must be BF16 or F16");
+  if (!aligned16(weight)) return fail(OSOR_ERR_INVALID_INPUT, "linear weight must be 16-byte aligned");
+  DeviceOf dev(y);
+  osor::note_launches(1);
+  const cudaError_t e = osor::rows_linear_launch(internal_dtype(dtype), x, rows, in_features,
+                                                 weight, bias, bias2, out_features, pre_silu,
+                                                 y, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "row linear");
+}
+
+int osor_layer_norm(const void* x, void* y, const float* gamma, const float* beta, long long rows,
+                    int channels, float eps, int dtype, void* stream) {
+  if (!x || !y || !gamma || !beta) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (rows < 1 || channels < 8 || channels % 8 != 0 || channels > 2048 || !(eps >= 0.0f))
+    return fail(OSOR_ERR_INVALID_INPUT, "layer norm needs rows of 8..2048 channels (multiple of 8)");
+  if (!is16(dtype)) return fail(OSOR_ERR_INVALID_INPUT, "layer norm dtype must be BF16 or F16");
+  if (!aligned16(x) || !aligned16(y))
+    return fail(OSOR_ERR_INVALID_INPUT, "layer norm tensors must be 16-byte aligned");
+  DeviceOf dev(x);
+  osor::note_launches(1);
+  const cudaError_t e = osor::layer_norm_launch(internal_dtype(dtype), x, y, gamma, beta, rows,
+                                                channels, eps, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "layer norm");
+}
+
+int osor_geglu(const void* x, void* y, long long rows, int features, int dtype, void* stream) {
+  if (!x || !y) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (rows < 1 || features < 8 || features % 8 != 0)
+    return fail(OSOR_ERR_INVALID_INPUT, "GEGLU needs a positive multiple of 8 features");
+  if (!is16(dtype)) return fail(OSOR_ERR_INVALID_INPUT, "GEGLU dtype must be BF16 or F16");
+  if (!aligned16(x) || !aligned16(y))
+    return fail(OSOR_ERR_INVALID_INPUT, "GEGLU tensors must be 16-byte aligned");
+  DeviceOf dev(x);
+  osor::note_launches(1);
+  const cudaError_t e = osor::geglu_launch(internal_dtype(dtype), x, y, rows, features,
+                                           static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "GEGLU");
+}
+
+int osor_concat_channels(const void* a, int ca, const void* b, int cb, void* y, long long pixels,
+                         int dtype, void* stream) {
+  if (!a || !b || !y) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (pixels < 1 || ca < 8 || cb < 8 || ca % 8 != 0 || cb % 8 != 0)
+    return fail(OSOR_ERR_INVALID_INPUT, "concatenated channel counts must be multiples of 8");
+  if (!is16(dtype)) return fail(OSOR_ERR_INVALID_INPUT, "concatenation dtype must be BF16 or F16");
+  if (!aligned16(a) || !aligned16(b) || !aligned16(y))
+    return fail(OSOR_ERR_INVALID_INPUT, "concatenated tensors must be 16-byte aligned");
+  DeviceOf dev(y);
+  osor::note_launches(1);
+  const cudaError_t e =
+      osor::concat_channels_launch(a, ca, b, cb, y, pixels, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "channel concatenation");
+}
+
+int osor_resize_nearest(const void* x, void* y, int batch, int in_h, int in_w, int out_h,
+                        int out_w, int channels, int dtype, void* stream) {
+  if (!x || !y) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (batch < 1 || in_h < 1 || in_w < 1 || out_h < 1 || out_w < 1 || channels < 8 ||
+      channels % 8 != 0)
+    return fail(OSOR_ERR_INVALID_INPUT, "invalid nearest resize shape");
+  if (!is16(dtype)) return fail(OSOR_ERR_INVALID_INPUT, "resize dtype must be BF16 or F16");
+  if (!aligned16(x) || !aligned16(y))
+    return fail(OSOR_ERR_INVALID_INPUT, "resized tensors must be 16-byte aligned");
+  DeviceOf dev(x);
+  osor::note_launches(1);
+  const cudaError_t e = osor::resize_nearest_launch(x, y, batch, in_h, in_w, out_h, out_w,
+                                                    channels, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "nearest resize");
+}
+
+int osor_channel_update(const void* x, long long ld_x, void* y, int channels, int batch,
+                        long long pixels_per_image, const float* image_bias,
+                        long long bias_stride, const void* residual, int dtype, void* stream) {
+  if (!x || !y) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (batch < 1 || pixels_per_image < 1 || channels < 8 || channels % 8 != 0 || ld_x < channels ||
+      ld_x % 8 != 0)
+    return fail(OSOR_ERR_INVALID_INPUT, "invalid channel update shape");
+  if (x == y && ld_x != channels)
+    return fail(OSOR_ERR_INVALID_INPUT, "an in-place channel update needs ld_x == channels");
+  if (image_bias && (bias_stride < channels || bias_stride % 4 != 0))
+    return fail(OSOR_ERR_INVALID_INPUT, "image bias rows must hold the channels, stride % 4 == 0");
+  if (!is16(dtype)) return fail(OSOR_ERR_INVALID_INPUT, "channel update dtype must be BF16 or F16");
+  if (!aligned16(x) || !aligned16(y) || !aligned16(image_bias) || !aligned16(residual))
+    return fail(OSOR_ERR_INVALID_INPUT, "channel update tensors must be 16-byte aligned");
+  DeviceOf dev(x);
+  osor::note_launches(1);
+  const cudaError_t e = osor::channel_update_launch(internal_dtype(dtype), x, ld_x, y, channels,
+                                                    pixels_per_image, batch, image_bias,
+                                                    bias_stride, residual,
+                                                    static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "channel update");
+}
+
+int osor_attention_heads(const void* q, long long ld_q, long long q_batch_stride, const void* k,
+                         const void* v, long long ld_kv, long long kv_batch_stride, void* out,
+                         long long ld_out, long long out_batch_stride, int batch, int heads,
+                         int n_q, int n_kv, int head_dim, int dtype, void* stream) {
+  if (!q || !k || !v || !out) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (head_dim != 32 && head_dim != 64 && head_dim != 128)
+    return fail(OSOR_ERR_INVALID_INPUT, "attention head width must be 32, 64 or 128");
+  const long long width = (long long)heads * head_dim;
+  if (batch < 1 || batch > 65535 || heads < 1 || heads > 65535 || n_q < 1 || n_kv < 1 ||
+      ld_q < width || ld_kv < width || ld_out < width)
+    return fail(OSOR_ERR_INVALID_INPUT, "attention tensor shapes are incompatible");
+  if (batch > 1 && (q_batch_stride < (long long)n_q * ld_q ||
+                    out_batch_stride < (long long)n_q * ld_out ||
+                    (kv_batch_stride != 0 && kv_batch_stride < (long long)n_kv * ld_kv)))
+    return fail(OSOR_ERR_INVALID_INPUT, "attention batch strides overlap");
+  if (q_batch_stride < 0 || kv_batch_stride < 0 || out_batch_stride < 0 ||
+      ((ld_q | ld_kv | ld_out | q_batch_stride | kv_batch_stride | out_batch_stride) & 7) != 0)
+    return fail(OSOR_ERR_INVALID_INPUT, "attention strides must be non-negative multiples of 8");
+  if (!is16(dtype)) return fail(OSOR_ERR_INVALID_INPUT, "attention dtype must be BF16 or F16");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return fail(OSOR_ERR_INVALID_INPUT, "attention tensors must be 16-byte aligned");
+  DeviceOf dev(q);
+  osor::note_launches(1);
+  const cudaError_t e = osor::attention_heads_launch(
+      internal_dtype(dtype), q, ld_q, q_batch_stride, k, v, ld_kv, kv_batch_stride, out, ld_out,
+      out_batch_stride, batch, heads, n_q, n_kv, head_dim, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "multi-head attention");
 }
 
 }  // extern "C"

@@ -539,6 +539,91 @@ __global__ void __launch_bounds__(256)
   for (; pix < pixels; pix += stride) dst[pix * vc] = apply(__ldcs(src + pix * vc));
 }
 
+// Wide rows (C / 8 > 256 vectors, e.g. the 2560-channel skip concatenations
+// of the UNet): each of the 256 threads owns the columns threadIdx.x + 256 * i
+// of every pixel of its chunk, so no cross-thread reduction is needed; the
+// partials layout is the one gn_nhwc_finalize_kernel reads.
+constexpr int kWideCols = 4;  // C <= 8192
+
+template <int D>
+__global__ void __launch_bounds__(256)
+    gn_nhwc_stats_wide_kernel(const uint16_t* __restrict__ x, float* __restrict__ partials,
+                              int channels, long long pixels, long long pix_per_chunk,
+                              int groups) {
+  using E = Elem<D>;
+  const int vc = channels / 8;
+  const int cpg = channels / groups;
+  const int b = blockIdx.y;
+  const long long p_begin = (long long)blockIdx.x * pix_per_chunk;
+  const long long p_end = min(pixels, p_begin + pix_per_chunk);
+  const typename E::T* img =
+      reinterpret_cast<const typename E::T*>(x) + (long long)b * pixels * channels;
+  for (int col = threadIdx.x; col < vc; col += blockDim.x) {
+    float anchor[8], s1[8], s2[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = col * 8 + j;
+      anchor[j] = E::to_f(img[(c / cpg) * cpg]);
+      s1[j] = s2[j] = 0.0f;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(img) + col;
+    for (long long pix = p_begin; pix < p_end; ++pix) {
+      float f[8];
+      unpack8<D>(__ldcs(src + pix * vc), f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = f[j] - anchor[j];
+        s1[j] += d;
+        s2[j] += d * d;
+      }
+    }
+    float* out = partials + (((long long)b * gridDim.x + blockIdx.x) * channels + col * 8) * 2;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      out[2 * j] = s1[j];
+      out[2 * j + 1] = s2[j];
+    }
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(256)
+    gn_nhwc_apply_wide_kernel(const uint4* __restrict__ x, uint4* __restrict__ y,
+                              const float* __restrict__ coef, int channels, long long pixels,
+                              int silu) {
+  const int vc = channels / 8;
+  const int b = blockIdx.y;
+  float ca[kWideCols][8], cb[kWideCols][8];
+#pragma unroll
+  for (int i = 0; i < kWideCols; ++i) {
+    const int col = threadIdx.x + 256 * i;
+    if (col < vc) {
+      const float4* cf =
+          reinterpret_cast<const float4*>(coef + ((long long)b * channels + col * 8) * 4);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 c = __ldg(cf + j);
+        gn_coef_prepare(c.x, c.y, c.z, silu != 0, ca[i][j], cb[i][j]);
+      }
+    }
+  }
+  const uint4* src = x + (long long)b * pixels * vc;
+  uint4* dst = y + (long long)b * pixels * vc;
+  for (long long pix = blockIdx.x; pix < pixels; pix += gridDim.x) {
+#pragma unroll
+    for (int i = 0; i < kWideCols; ++i) {
+      const int col = threadIdx.x + 256 * i;
+      if (col < vc) {
+        float f[8];
+        unpack8<D>(__ldcs(src + pix * vc + col), f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = gn_apply_prepared(f[j], ca[i][j], cb[i][j], silu != 0);
+        dst[pix * vc + col] = pack8<D>(f);
+      }
+    }
+  }
+}
+
 int num_sms() {
   int dev = 0, c = 0;
   cudaGetDevice(&dev);
@@ -668,6 +753,14 @@ cudaError_t apply_launch(const void* x, void* y, const float* coef, int batch, i
     return cudaGetLastError();
   }
   const int vc = channels / 8;
+  if (vc > 256) {
+    long long bx = ((long long)num_sms() * 8 + batch - 1) / batch;
+    if (bx > pixels) bx = pixels;
+    if (bx < 1) bx = 1;
+    gn_nhwc_apply_wide_kernel<D><<<dim3((unsigned)bx, batch), 256, 0, stream>>>(
+        static_cast<const uint4*>(x), static_cast<uint4*>(y), coef, channels, pixels, silu);
+    return cudaGetLastError();
+  }
   const int rows = 256 / vc;
   const int threads = rows * vc;
   long long bx = ((long long)num_sms() * 8 + batch - 1) / batch;
@@ -679,6 +772,23 @@ cudaError_t apply_launch(const void* x, void* y, const float* coef, int batch, i
   return cudaGetLastError();
 }
 
+// Per-chunk partial sums of every channel: the row-sharing kernel for C / 8
+// <= 256 vectors, the column-owning one above that.
+template <int D>
+void stats_launch(const uint16_t* xs, float* partials, const GnNhwcPlan& plan, int batch,
+                  int channels, long long pixels, int groups, cudaStream_t stream) {
+  const int vc = channels / 8;
+  if (vc > 256) {
+    gn_nhwc_stats_wide_kernel<D><<<dim3(plan.chunks, batch), 256, 0, stream>>>(
+        xs, partials, channels, pixels, plan.pix_per_chunk, groups);
+    return;
+  }
+  const int rows = plan.threads / vc;
+  const size_t sred = (size_t)rows * vc * 16 * sizeof(float);
+  gn_nhwc_stats_kernel<D><<<dim3(plan.chunks, batch), plan.threads, sred, stream>>>(
+      xs, partials, channels, pixels, plan.pix_per_chunk, groups);
+}
+
 template <int D>
 cudaError_t gn_nhwc_typed(const void* x, void* y, const float* gamma, const float* beta, int batch,
                           int channels, long long pixels, int groups, float eps, int silu,
@@ -687,12 +797,8 @@ cudaError_t gn_nhwc_typed(const void* x, void* y, const float* gamma, const floa
   float* partials = static_cast<float*>(workspace);
   float* coef = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
                                          (plan.partial_bytes + 255) / 256 * 256);
-  const int vc = channels / 8;
-  const int rows = plan.threads / vc;
-  const size_t sred = (size_t)rows * vc * 16 * sizeof(float);
   const uint16_t* xs = static_cast<const uint16_t*>(x);
-  gn_nhwc_stats_kernel<D><<<dim3(plan.chunks, batch), plan.threads, sred, stream>>>(
-      xs, partials, channels, pixels, plan.pix_per_chunk, groups);
+  stats_launch<D>(xs, partials, plan, batch, channels, pixels, groups, stream);
   gn_nhwc_finalize_kernel<D><<<dim3(groups, batch), 256, 0, stream>>>(
       xs, partials, plan.chunks, channels, pixels, groups, gamma, beta, eps, coef, stats_out);
   return apply_launch<D>(x, y, coef, batch, channels, pixels, silu, stream);
@@ -1083,19 +1189,14 @@ cudaError_t gn_nhwc_stats_launch(int dtype, const void* x, int batch, int channe
                                  cudaStream_t stream) {
   const GnNhwcPlan plan = gn_nhwc_plan(batch, channels, pixels, groups);
   float* partials = static_cast<float*>(workspace);
-  const int vc = channels / 8;
-  const int rows = plan.threads / vc;
-  const size_t sred = (size_t)rows * vc * 16 * sizeof(float);
   const uint16_t* xs = static_cast<const uint16_t*>(x);
   if (dtype == kF16) {
-    gn_nhwc_stats_kernel<kF16><<<dim3(plan.chunks, batch), plan.threads, sred, stream>>>(
-        xs, partials, channels, pixels, plan.pix_per_chunk, groups);
+    stats_launch<kF16>(xs, partials, plan, batch, channels, pixels, groups, stream);
     gn_nhwc_finalize_kernel<kF16><<<dim3(groups, batch), 256, 0, stream>>>(
         xs, partials, plan.chunks, channels, pixels, groups, nullptr, nullptr, 0.0f, nullptr,
         mean_var);
   } else {
-    gn_nhwc_stats_kernel<kBf16><<<dim3(plan.chunks, batch), plan.threads, sred, stream>>>(
-        xs, partials, channels, pixels, plan.pix_per_chunk, groups);
+    stats_launch<kBf16>(xs, partials, plan, batch, channels, pixels, groups, stream);
     gn_nhwc_finalize_kernel<kBf16><<<dim3(groups, batch), 256, 0, stream>>>(
         xs, partials, plan.chunks, channels, pixels, groups, nullptr, nullptr, 0.0f, nullptr,
         mean_var);

@@ -119,6 +119,15 @@ SIGNATURES = {
     "osor_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _ll, _i, _vp, _sz, _vp]),
     "osor_attention_kv_workspace_size": (_sz, [_i, _i, _i, _i]),
     "osor_attention_kv": (_i, [_vp, _ll, _vp, _vp, _ll, _vp, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "osor_unet_time_features": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
+    "osor_rows_linear": (_i, [_vp, _i, _i, _vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
+    "osor_layer_norm": (_i, [_vp, _vp, _vp, _vp, _ll, _i, _f, _i, _vp]),
+    "osor_geglu": (_i, [_vp, _vp, _ll, _i, _i, _vp]),
+    "osor_concat_channels": (_i, [_vp, _i, _vp, _i, _vp, _ll, _i, _vp]),
+    "osor_resize_nearest": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
+    "osor_channel_update": (_i, [_vp, _ll, _vp, _i, _i, _ll, _vp, _ll, _vp, _i, _vp]),
+    "osor_attention_heads": (_i, [_vp, _ll, _ll, _vp, _vp, _ll, _ll, _vp, _ll, _ll, _i, _i, _i,
+                                  _i, _i, _i, _vp]),
     "osor_profile_begin": (None, []),
     "osor_profile_end": (_i, [_vp, _i, ctypes.POINTER(_i)]),
     "osor_launch_count": (_ll, []),
