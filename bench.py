@@ -305,6 +305,32 @@ def run_ops(args):
                           "cpu_baseline": {"ms": round(cpu_ms, 3), "cores": 1, "kind": "port",
                                            "sample": "the same 2 x 262,144 values"}}),
               flush=True)
+    elif args.op == "unet":
+        # One SDXL inpainting UNet call at t=400 for the 4 x 1024^2 job:
+        # [4, 9, 128, 128] latents, 77-token prompt, random-init weights.
+        from osor_b200.unet import Architecture, NativeUnet, random_unet_weights, unet_flops
+        arch = Architecture.sdxl()
+        g = torch.Generator(device=dev).manual_seed(11)
+        weights = random_unet_weights(arch, seed=0, device=dev)
+        context = torch.randn((1, 77, arch.context), generator=g, device=dev)
+        pooled = torch.randn((1, arch.pooled), generator=g, device=dev)
+        dt = torch.float16 if args.dtype == "f16" else torch.bfloat16
+        unet = NativeUnet(weights, context, pooled, arch=arch, device=0, dtype=dt)
+        del weights
+        x = torch.randn((4, 9, 128, 128), generator=g, device=dev)
+        ids = torch.tensor([[1024.0, 1024.0, 0.0, 0.0, 1024.0, 1024.0]] * 4, device=dev)
+        before = _lib.launch_count()
+        unet(x, 400, ids)
+        torch.cuda.synchronize()
+        launches = _lib.launch_count() - before
+        ms = _timed(lambda: unet(x, 400, ids), args.steps, args.warmup, flush)
+        flop = unet_flops(arch, 4, 128, 128)
+        tf = flop / (ms / 1e3) / 1e12
+        print(json.dumps({"op": "sdxl inpainting unet (one denoising call, t=400)",
+                          "shape": [4, 9, 128, 128], "dtype": args.dtype, "ms": round(ms, 2),
+                          "tflop_per_call": round(flop / 1e12, 2), "tflops": round(tf, 1),
+                          "frac_of_sustained_peak": round(tf / tflops_sus, 4),
+                          "gpu_launches": launches, "peak_source": src}), flush=True)
     if device_status(0) != 0:
         raise SystemExit("device status reported a kernel wait timeout")
 
@@ -461,7 +487,7 @@ def main():
     ap.add_argument("--dtype", default="f16", choices=["f16", "bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op", default="decode",
-                    choices=["decode", "conv3x3", "groupnorm", "encode", "noise"],
+                    choices=["decode", "conv3x3", "groupnorm", "encode", "noise", "unet"],
                     help="decode: the headline line; others: standalone op lines")
     ap.add_argument("--shape", default=None, help="comma-separated shape for --op conv3x3/groupnorm")
     ap.add_argument("--bands", type=int, default=0,

@@ -416,66 +416,3 @@ def forward(w, arch: Arch, sample, timestep: int, time_ids, context, pooled):
             xs = conv(w, f"up_blocks.{i}.upsamplers.0.conv", upsample_nearest(xs, *size))
     assert not residuals
     return conv(w, "conv_out", gn(w, "conv_norm_out", xs, RESNET_EPS, True))
-
-
-def flops(arch: Arch, batch: int, h: int, w: int, tokens: int = 77) -> float:
-    """Multiply-add FLOPs (2 per MAC) of one forward: convolutions, linear
-    layers and attention products; elementwise work is not counted."""
-    total = 0.0
-    shapes: Dict[str, Tuple[int, ...]] = dict(specs(arch))
-
-    def conv_f(name, hh, ww):
-        co, ci, k, _ = shapes[name + ".weight"]
-        return 2.0 * batch * hh * ww * co * ci * k * k
-
-    def lin_f(name, rows):
-        co, ci = shapes[name + ".weight"]
-        return 2.0 * rows * co * ci
-
-    def resnet_f(prefix, hh, ww):
-        f = conv_f(prefix + ".conv1", hh, ww) + conv_f(prefix + ".conv2", hh, ww)
-        if prefix + ".conv_shortcut.weight" in shapes:
-            f += conv_f(prefix + ".conv_shortcut", hh, ww)
-        return f
-
-    def st_f(prefix, spec, hh, ww):
-        n_tok = hh * ww
-        rows = batch * n_tok
-        c = spec.channels
-        f = 2 * lin_f(prefix + ".proj_in", rows)
-        for d in range(spec.depth):
-            t = f"{prefix}.transformer_blocks.{d}"
-            f += 4 * lin_f(t + ".attn1.to_q", rows) + 4.0 * batch * n_tok * n_tok * c
-            f += 2 * lin_f(t + ".attn2.to_q", rows) + 4.0 * batch * n_tok * tokens * c
-            f += lin_f(t + ".ff.net.0.proj", rows) + lin_f(t + ".ff.net.2", rows)
-        return f
-
-    sizes = [(h, w)]
-    for _ in range(len(arch.blocks) - 1):
-        ph, pw = sizes[-1]
-        sizes.append(((ph - 1) // 2 + 1, (pw - 1) // 2 + 1))
-    total += conv_f("conv_in", h, w)
-    n = len(arch.blocks)
-    for i, spec in enumerate(arch.blocks):
-        hh, ww = sizes[i]
-        for j in range(arch.layers):
-            total += resnet_f(f"down_blocks.{i}.resnets.{j}", hh, ww)
-            if spec.depth is not None:
-                total += st_f(f"down_blocks.{i}.attentions.{j}", spec, hh, ww)
-        if i + 1 < n:
-            total += conv_f(f"down_blocks.{i}.downsamplers.0.conv", *sizes[i + 1])
-    hh, ww = sizes[-1]
-    last = arch.blocks[-1]
-    total += resnet_f("mid_block.resnets.0", hh, ww) + resnet_f("mid_block.resnets.1", hh, ww)
-    total += st_f("mid_block.attentions.0", last, hh, ww)
-    for i in range(n):
-        spec = arch.blocks[n - 1 - i]
-        hh, ww = sizes[n - 1 - i]
-        for j in range(arch.layers + 1):
-            total += resnet_f(f"up_blocks.{i}.resnets.{j}", hh, ww)
-            if spec.depth is not None:
-                total += st_f(f"up_blocks.{i}.attentions.{j}", spec, hh, ww)
-        if i + 1 < n:
-            total += conv_f(f"up_blocks.{i}.upsamplers.0.conv", *sizes[n - 2 - i])
-    total += conv_f("conv_out", h, w)
-    return total

@@ -215,6 +215,63 @@ def random_unet_weights(arch: Architecture, seed: int = 0, device="cpu",
     return out
 
 
+
+def unet_flops(arch: Architecture, batch: int, h: int, w: int, tokens: int = 77) -> float:
+    """FLOPs (2 per multiply-add) of one forward's convolutions, linear layers
+    and attention products; elementwise work and the prompt's keys / values
+    (computed once at load) are not counted."""
+    shapes = dict(unet_specs(arch))
+
+    def conv_f(name, hh, ww):
+        co, ci, k, _ = shapes[name + ".weight"]
+        return 2.0 * batch * hh * ww * co * ci * k * k
+
+    def lin_f(name, rows):
+        co, ci = shapes[name + ".weight"]
+        return 2.0 * rows * co * ci
+
+    def resnet_f(prefix, hh, ww):
+        f = conv_f(prefix + ".conv1", hh, ww) + conv_f(prefix + ".conv2", hh, ww)
+        if prefix + ".conv_shortcut.weight" in shapes:
+            f += conv_f(prefix + ".conv_shortcut", hh, ww)
+        return f
+
+    def transformer_f(prefix, spec, hh, ww):
+        n = hh * ww
+        rows, c = batch * n, spec.channels
+        f = 2 * lin_f(prefix + ".proj_in", rows)
+        for d in range(spec.depth):
+            t = f"{prefix}.transformer_blocks.{d}"
+            f += 4 * lin_f(t + ".attn1.to_q", rows) + 4.0 * batch * n * n * c
+            f += 2 * lin_f(t + ".attn2.to_q", rows) + 4.0 * batch * n * tokens * c
+            f += lin_f(t + ".ff.net.0.proj", rows) + lin_f(t + ".ff.net.2", rows)
+        return f
+
+    n = len(arch.blocks)
+    sizes = [(h, w)]
+    for _ in range(n - 1):
+        sizes.append(((sizes[-1][0] - 1) // 2 + 1, (sizes[-1][1] - 1) // 2 + 1))
+    total = conv_f("conv_in", h, w) + conv_f("conv_out", h, w)
+    for i, spec in enumerate(arch.blocks):
+        for j in range(arch.layers):
+            total += resnet_f(f"down_blocks.{i}.resnets.{j}", *sizes[i])
+            if spec.depth is not None:
+                total += transformer_f(f"down_blocks.{i}.attentions.{j}", spec, *sizes[i])
+        if i + 1 < n:
+            total += conv_f(f"down_blocks.{i}.downsamplers.0.conv", *sizes[i + 1])
+    last = arch.blocks[-1]
+    total += resnet_f("mid_block.resnets.0", *sizes[-1]) + resnet_f("mid_block.resnets.1", *sizes[-1])
+    total += transformer_f("mid_block.attentions.0", last, *sizes[-1])
+    for i in range(n):
+        spec, size = arch.blocks[n - 1 - i], sizes[n - 1 - i]
+        for j in range(arch.layers + 1):
+            total += resnet_f(f"up_blocks.{i}.resnets.{j}", *size)
+            if spec.depth is not None:
+                total += transformer_f(f"up_blocks.{i}.attentions.{j}", spec, *size)
+        if i + 1 < n:
+            total += conv_f(f"up_blocks.{i}.upsamplers.0.conv", *sizes[n - 2 - i])
+    return total
+
 # ------------------------------------------------------------------ topology
 class UnetGraph:
     """Unet::forward (src/native.rs:276-379) over an ops backend. Tensors are
