@@ -326,11 +326,27 @@ def run_ops(args):
         ms = _timed(lambda: unet(x, 400, ids), args.steps, args.warmup, flush)
         flop = unet_flops(arch, 4, 128, 128)
         tf = flop / (ms / 1e3) / 1e12
+        # Per-kind breakdown of one call from CUDA events around each op.
+        _lib.profile_begin()
+        unet(x, 400, ids)
+        entries = _lib.profile_end()
+        kinds = {}
+        for kind, eflops, _, ems, elaunches in entries:
+            k = kinds.setdefault(kind, [0.0, 0.0, 0])
+            k[0] += ems
+            k[1] += eflops
+            k[2] += elaunches
+        total = sum(v[0] for v in kinds.values()) or 1.0
+        breakdown = {k: {"ms": round(v[0], 3), "share": round(v[0] / total, 3),
+                         "tflops": round(v[1] / (v[0] / 1e3) / 1e12, 1) if v[1] and v[0] else None,
+                         "launches": v[2]}
+                     for k, v in sorted(kinds.items(), key=lambda kv: -kv[1][0])}
         print(json.dumps({"op": "sdxl inpainting unet (one denoising call, t=400)",
                           "shape": [4, 9, 128, 128], "dtype": args.dtype, "ms": round(ms, 2),
                           "tflop_per_call": round(flop / 1e12, 2), "tflops": round(tf, 1),
                           "frac_of_sustained_peak": round(tf / tflops_sus, 4),
-                          "gpu_launches": launches, "peak_source": src}), flush=True)
+                          "gpu_launches": launches, "peak_source": src,
+                          "breakdown": breakdown}), flush=True)
     if device_status(0) != 0:
         raise SystemExit("device status reported a kernel wait timeout")
 

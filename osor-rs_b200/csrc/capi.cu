@@ -285,6 +285,7 @@ int osor_group_norm_silu(const void* x, void* y, const float* gamma, const float
   if (layout == OSOR_LAYOUT_NHWC) {
     if (!aligned16(x) || !aligned16(y))
       return fail(OSOR_ERR_INVALID_INPUT, "NHWC tensors must be 16-byte aligned");
+    osor::OpScope scope("groupnorm", 0.0, 4.0 * batch * channels * spatial, s, 3);
     e = osor::gn_nhwc_launch(internal_dtype(dtype), x, y, gamma, beta, batch, channels, spatial, 32,
                              eps, silu, workspace, stats, s);
     osor::note_launches(3);
@@ -587,6 +588,9 @@ int osor_unet_time_features(const float* time_ids, const float* pooled, int batc
     return fail(OSOR_ERR_INVALID_INPUT, "invalid time embedding shape");
   DeviceOf dev(features);
   osor::note_launches(1);
+  osor::OpScope scope("time_features", 0.0,
+                      4.0 * batch * (base_channels + pooled_width + 6 * time_projection),
+                      static_cast<cudaStream_t>(stream), 1);
   const cudaError_t e = osor::unet_time_features_launch(
       time_ids, pooled, batch, (float)timestep, base_channels, time_projection, pooled_width,
       features, static_cast<cudaStream_t>(stream));
@@ -604,6 +608,8 @@ int osor_rows_linear(const float* x, int rows, int in_features, const void* weig
   if (!aligned16(weight)) return fail(OSOR_ERR_INVALID_INPUT, "linear weight must be 16-byte aligned");
   DeviceOf dev(y);
   osor::note_launches(1);
+  osor::OpScope scope("rows_linear", 2.0 * rows * in_features * out_features,
+                      2.0 * in_features * out_features, static_cast<cudaStream_t>(stream), 1);
   const cudaError_t e = osor::rows_linear_launch(internal_dtype(dtype), x, rows, in_features,
                                                  weight, bias, bias2, out_features, pre_silu,
                                                  y, static_cast<cudaStream_t>(stream));
@@ -620,6 +626,8 @@ int osor_layer_norm(const void* x, void* y, const float* gamma, const float* bet
     return fail(OSOR_ERR_INVALID_INPUT, "layer norm tensors must be 16-byte aligned");
   DeviceOf dev(x);
   osor::note_launches(1);
+  osor::OpScope scope("layernorm", 0.0, 4.0 * rows * channels, static_cast<cudaStream_t>(stream),
+                      1);
   const cudaError_t e = osor::layer_norm_launch(internal_dtype(dtype), x, y, gamma, beta, rows,
                                                 channels, eps, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "layer norm");
@@ -634,6 +642,7 @@ int osor_geglu(const void* x, void* y, long long rows, int features, int dtype, 
     return fail(OSOR_ERR_INVALID_INPUT, "GEGLU tensors must be 16-byte aligned");
   DeviceOf dev(x);
   osor::note_launches(1);
+  osor::OpScope scope("geglu", 0.0, 6.0 * rows * features, static_cast<cudaStream_t>(stream), 1);
   const cudaError_t e = osor::geglu_launch(internal_dtype(dtype), x, y, rows, features,
                                            static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "GEGLU");
@@ -649,6 +658,8 @@ int osor_concat_channels(const void* a, int ca, const void* b, int cb, void* y, 
     return fail(OSOR_ERR_INVALID_INPUT, "concatenated tensors must be 16-byte aligned");
   DeviceOf dev(y);
   osor::note_launches(1);
+  osor::OpScope scope("concat", 0.0, 4.0 * pixels * (ca + cb), static_cast<cudaStream_t>(stream),
+                      1);
   const cudaError_t e =
       osor::concat_channels_launch(a, ca, b, cb, y, pixels, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "channel concatenation");
@@ -665,6 +676,8 @@ int osor_resize_nearest(const void* x, void* y, int batch, int in_h, int in_w, i
     return fail(OSOR_ERR_INVALID_INPUT, "resized tensors must be 16-byte aligned");
   DeviceOf dev(x);
   osor::note_launches(1);
+  osor::OpScope scope("resize", 0.0, 2.0 * batch * channels * ((double)in_h * in_w + (double)out_h * out_w),
+                      static_cast<cudaStream_t>(stream), 1);
   const cudaError_t e = osor::resize_nearest_launch(x, y, batch, in_h, in_w, out_h, out_w,
                                                     channels, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "nearest resize");
@@ -686,6 +699,9 @@ int osor_channel_update(const void* x, long long ld_x, void* y, int channels, in
     return fail(OSOR_ERR_INVALID_INPUT, "channel update tensors must be 16-byte aligned");
   DeviceOf dev(x);
   osor::note_launches(1);
+  osor::OpScope scope("channel_update", 0.0,
+                      2.0 * batch * pixels_per_image * channels * (residual ? 3.0 : 2.0),
+                      static_cast<cudaStream_t>(stream), 1);
   const cudaError_t e = osor::channel_update_launch(internal_dtype(dtype), x, ld_x, y, channels,
                                                     pixels_per_image, batch, image_bias,
                                                     bias_stride, residual,
@@ -716,6 +732,10 @@ int osor_attention_heads(const void* q, long long ld_q, long long q_batch_stride
     return fail(OSOR_ERR_INVALID_INPUT, "attention tensors must be 16-byte aligned");
   DeviceOf dev(q);
   osor::note_launches(1);
+  osor::OpScope scope("attn_heads", 4.0 * batch * n_q * (double)n_kv * width,
+                      2.0 * batch * width * (2.0 * n_q + (kv_batch_stride ? 2.0 * n_kv : 0.0)) +
+                          (kv_batch_stride ? 0.0 : 4.0 * n_kv * width),
+                      static_cast<cudaStream_t>(stream), 1);
   const cudaError_t e = osor::attention_heads_launch(
       internal_dtype(dtype), q, ld_q, q_batch_stride, k, v, ld_kv, kv_batch_stride, out, ld_out,
       out_batch_stride, batch, heads, n_q, n_kv, head_dim, static_cast<cudaStream_t>(stream));
