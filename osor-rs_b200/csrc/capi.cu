@@ -288,7 +288,6 @@ int osor_group_norm_silu(const void* x, void* y, const float* gamma, const float
     osor::OpScope scope("groupnorm", 0.0, 4.0 * batch * channels * spatial, s, 3);
     e = osor::gn_nhwc_launch(internal_dtype(dtype), x, y, gamma, beta, batch, channels, spatial, 32,
                              eps, silu, workspace, stats, s);
-    osor::note_launches(3);
   } else if (nchw_l2_ok(x, y, batch, channels, spatial, dtype)) {
     osor::note_launches(1);
     // One HBM read and write per element; chunks re-read from L2.
@@ -587,7 +586,6 @@ int osor_unet_time_features(const float* time_ids, const float* pooled, int batc
       time_projection < 2 || time_projection % 2 != 0 || pooled_width < 0)
     return fail(OSOR_ERR_INVALID_INPUT, "invalid time embedding shape");
   DeviceOf dev(features);
-  osor::note_launches(1);
   osor::OpScope scope("time_features", 0.0,
                       4.0 * batch * (base_channels + pooled_width + 6 * time_projection),
                       static_cast<cudaStream_t>(stream), 1);
@@ -607,7 +605,6 @@ int osor_rows_linear(const float* x, int rows, int in_features, const void* weig
   if (!is16(dtype)) return fail(OSOR_ERR_INVALID_INPUT, "linear weight dtype must be BF16 or F16");
   if (!aligned16(weight)) return fail(OSOR_ERR_INVALID_INPUT, "linear weight must be 16-byte aligned");
   DeviceOf dev(y);
-  osor::note_launches(1);
   osor::OpScope scope("rows_linear", 2.0 * rows * in_features * out_features,
                       2.0 * in_features * out_features, static_cast<cudaStream_t>(stream), 1);
   const cudaError_t e = osor::rows_linear_launch(internal_dtype(dtype), x, rows, in_features,
@@ -625,7 +622,6 @@ int osor_layer_norm(const void* x, void* y, const float* gamma, const float* bet
   if (!aligned16(x) || !aligned16(y))
     return fail(OSOR_ERR_INVALID_INPUT, "layer norm tensors must be 16-byte aligned");
   DeviceOf dev(x);
-  osor::note_launches(1);
   osor::OpScope scope("layernorm", 0.0, 4.0 * rows * channels, static_cast<cudaStream_t>(stream),
                       1);
   const cudaError_t e = osor::layer_norm_launch(internal_dtype(dtype), x, y, gamma, beta, rows,
@@ -641,7 +637,6 @@ int osor_geglu(const void* x, void* y, long long rows, int features, int dtype, 
   if (!aligned16(x) || !aligned16(y))
     return fail(OSOR_ERR_INVALID_INPUT, "GEGLU tensors must be 16-byte aligned");
   DeviceOf dev(x);
-  osor::note_launches(1);
   osor::OpScope scope("geglu", 0.0, 6.0 * rows * features, static_cast<cudaStream_t>(stream), 1);
   const cudaError_t e = osor::geglu_launch(internal_dtype(dtype), x, y, rows, features,
                                            static_cast<cudaStream_t>(stream));
@@ -657,7 +652,6 @@ int osor_concat_channels(const void* a, int ca, const void* b, int cb, void* y, 
   if (!aligned16(a) || !aligned16(b) || !aligned16(y))
     return fail(OSOR_ERR_INVALID_INPUT, "concatenated tensors must be 16-byte aligned");
   DeviceOf dev(y);
-  osor::note_launches(1);
   osor::OpScope scope("concat", 0.0, 4.0 * pixels * (ca + cb), static_cast<cudaStream_t>(stream),
                       1);
   const cudaError_t e =
@@ -675,7 +669,6 @@ int osor_resize_nearest(const void* x, void* y, int batch, int in_h, int in_w, i
   if (!aligned16(x) || !aligned16(y))
     return fail(OSOR_ERR_INVALID_INPUT, "resized tensors must be 16-byte aligned");
   DeviceOf dev(x);
-  osor::note_launches(1);
   osor::OpScope scope("resize", 0.0, 2.0 * batch * channels * ((double)in_h * in_w + (double)out_h * out_w),
                       static_cast<cudaStream_t>(stream), 1);
   const cudaError_t e = osor::resize_nearest_launch(x, y, batch, in_h, in_w, out_h, out_w,
@@ -698,7 +691,6 @@ int osor_channel_update(const void* x, long long ld_x, void* y, int channels, in
   if (!aligned16(x) || !aligned16(y) || !aligned16(image_bias) || !aligned16(residual))
     return fail(OSOR_ERR_INVALID_INPUT, "channel update tensors must be 16-byte aligned");
   DeviceOf dev(x);
-  osor::note_launches(1);
   osor::OpScope scope("channel_update", 0.0,
                       2.0 * batch * pixels_per_image * channels * (residual ? 3.0 : 2.0),
                       static_cast<cudaStream_t>(stream), 1);
@@ -731,7 +723,6 @@ int osor_attention_heads(const void* q, long long ld_q, long long q_batch_stride
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
     return fail(OSOR_ERR_INVALID_INPUT, "attention tensors must be 16-byte aligned");
   DeviceOf dev(q);
-  osor::note_launches(1);
   osor::OpScope scope("attn_heads", 4.0 * batch * n_q * (double)n_kv * width,
                       2.0 * batch * width * (2.0 * n_q + (kv_batch_stride ? 2.0 * n_kv : 0.0)) +
                           (kv_batch_stride ? 0.0 : 4.0 * n_kv * width),

@@ -373,6 +373,168 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
   }
 }
 
+// Head width 64 on the tensor cores (mma.sync m16n8k16, f32 accumulate),
+// flash-style: each warp owns 16 query rows with Q held as A fragments; per
+// 64-key tile, S = Q K^T lands in f32 accumulators, the online softmax runs on
+// those fragments (row max / sum across the 4 lanes of a quad), P is repacked
+// in registers as the A operand of O += P V. K and V tiles are staged in
+// shared memory as [key][dim] rows of 72 elements, which makes the B-fragment
+// loads bank-conflict free. Fragment layouts are the PTX ISA's for
+// m16n8k16: lane = 4 * group + t; A holds (row group / group + 8, cols 2t,
+// 2t + 1, +8), B (k 2t, 2t + 1, +8; n group), C (row group / group + 8,
+// cols 2t, 2t + 1).
+constexpr int kMmaWarps = 4;
+constexpr int kMmaRows = 16 * kMmaWarps;  // query rows per block
+constexpr int kMmaKeys = 64;              // keys per tile
+constexpr int kMmaLd = 72;                // shared row stride in elements
+
+template <int D>
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  if (D == kF16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+__device__ __forceinline__ uint32_t lds32(const uint16_t* p) {
+  return *reinterpret_cast<const uint32_t*>(p);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kMmaWarps * 32)
+    attention_heads64_mma_kernel(const uint16_t* __restrict__ qb, long long ld_q, long long q_bs,
+                                 const uint16_t* __restrict__ kb, const uint16_t* __restrict__ vb,
+                                 long long ld_kv, long long kv_bs, uint16_t* __restrict__ ob,
+                                 long long ld_out, long long out_bs, int n_q, int n_kv) {
+  constexpr int HD = 64;
+  __shared__ __align__(16) uint16_t ks[kMmaKeys * kMmaLd];
+  __shared__ __align__(16) uint16_t vs[kMmaKeys * kMmaLd];
+  using E = Elem<D>;
+  const int h = blockIdx.y;
+  const long long b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const long long ra = (long long)blockIdx.x * kMmaRows + warp * 16 + g;
+  const long long rb = ra + 8;
+  const bool va = ra < n_q, vb8 = rb < n_q;
+  const uint16_t* qbase = qb + b * q_bs + (long long)h * HD;
+  uint32_t qa[4][4];
+#pragma unroll
+  for (int kst = 0; kst < 4; ++kst) {
+    const int c0 = kst * 16 + 2 * t;
+    qa[kst][0] = va ? __ldg(reinterpret_cast<const uint32_t*>(qbase + ra * ld_q + c0)) : 0u;
+    qa[kst][1] = vb8 ? __ldg(reinterpret_cast<const uint32_t*>(qbase + rb * ld_q + c0)) : 0u;
+    qa[kst][2] = va ? __ldg(reinterpret_cast<const uint32_t*>(qbase + ra * ld_q + c0 + 8)) : 0u;
+    qa[kst][3] = vb8 ? __ldg(reinterpret_cast<const uint32_t*>(qbase + rb * ld_q + c0 + 8)) : 0u;
+  }
+  float o[8][4];
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  const uint16_t* kbase = kb + b * kv_bs + (long long)h * HD;
+  const uint16_t* vbase = vb + b * kv_bs + (long long)h * HD;
+  for (int j0 = 0; j0 < n_kv; j0 += kMmaKeys) {
+    __syncthreads();  // the previous tile is consumed
+    for (int i = threadIdx.x; i < kMmaKeys * (HD / 8); i += kMmaWarps * 32) {
+      const int key = i >> 3, c = i & 7;
+      const int j = j0 + key;
+      uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
+      if (j < n_kv) {
+        kv = __ldg(reinterpret_cast<const uint4*>(kbase + (long long)j * ld_kv) + c);
+        vv = __ldg(reinterpret_cast<const uint4*>(vbase + (long long)j * ld_kv) + c);
+      }
+      *reinterpret_cast<uint4*>(ks + key * kMmaLd + c * 8) = kv;
+      *reinterpret_cast<uint4*>(vs + key * kMmaLd + c * 8) = vv;
+    }
+    __syncthreads();
+    // S = Q K^T for 8 tiles of 8 keys.
+    float sc[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+      const uint16_t* kr = ks + (nt * 8 + g) * kMmaLd + 2 * t;
+#pragma unroll
+      for (int kst = 0; kst < 4; ++kst)
+        mma16816<D>(sc[nt], qa[kst], lds32(kr + kst * 16), lds32(kr + kst * 16 + 8));
+    }
+    // Mask keys past the end, then the tile's row maxima over the quad.
+    float mx0 = m0, mx1 = m1;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const int key = j0 + nt * 8 + 2 * t;
+      if (key >= n_kv) sc[nt][0] = sc[nt][2] = -INFINITY;
+      if (key + 1 >= n_kv) sc[nt][1] = sc[nt][3] = -INFINITY;
+      mx0 = fmaxf(mx0, fmaxf(sc[nt][0], sc[nt][1]));
+      mx1 = fmaxf(mx1, fmaxf(sc[nt][2], sc[nt][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float c0 = __expf(m0 - mx0), c1 = __expf(m1 - mx1);
+    m0 = mx0;
+    m1 = mx1;
+    l0 *= c0;
+    l1 *= c1;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      o[nt][0] *= c0;
+      o[nt][1] *= c0;
+      o[nt][2] *= c1;
+      o[nt][3] *= c1;
+    }
+    // P = exp(S - max) as the A fragments of the 4 key steps of P V.
+    uint32_t pa[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const float p0 = __expf(sc[nt][0] - m0), p1 = __expf(sc[nt][1] - m0);
+      const float p2 = __expf(sc[nt][2] - m1), p3 = __expf(sc[nt][3] - m1);
+      l0 += p0 + p1;
+      l1 += p2 + p3;
+      pa[nt >> 1][(nt & 1) * 2] = E::pack(p0, p1);
+      pa[nt >> 1][(nt & 1) * 2 + 1] = E::pack(p2, p3);
+    }
+    // O += P V: B fragments (keys 2t, 2t + 1 (+8) of dim column group).
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const uint16_t* vcol = vs + nt * 8 + g;
+#pragma unroll
+      for (int kst = 0; kst < 4; ++kst) {
+        const int k0 = kst * 16 + 2 * t;
+        const uint32_t b0 = (uint32_t)vcol[k0 * kMmaLd] | ((uint32_t)vcol[(k0 + 1) * kMmaLd] << 16);
+        const uint32_t b1 =
+            (uint32_t)vcol[(k0 + 8) * kMmaLd] | ((uint32_t)vcol[(k0 + 9) * kMmaLd] << 16);
+        mma16816<D>(o[nt], pa[kst], b0, b1);
+      }
+    }
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+  uint16_t* obase = ob + b * out_bs + (long long)h * HD + 2 * t;
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) {
+    if (va)
+      *reinterpret_cast<uint32_t*>(obase + ra * ld_out + nt * 8) =
+          E::pack(o[nt][0] * i0, o[nt][1] * i0);
+    if (vb8)
+      *reinterpret_cast<uint32_t*>(obase + rb * ld_out + nt * 8) =
+          E::pack(o[nt][2] * i1, o[nt][3] * i1);
+  }
+}
+
 template <int D>
 cudaError_t attention_heads_typed(const void* q, long long ld_q, long long q_bs, const void* k,
                                   const void* v, long long ld_kv, long long kv_bs, void* out,
@@ -390,7 +552,7 @@ cudaError_t attention_heads_typed(const void* q, long long ld_q, long long q_bs,
           qb, ld_q, q_bs, kb, vb, ld_kv, kv_bs, ob, ld_out, out_bs, n_q, n_kv);
       break;
     case 64:
-      attention_heads_kernel<D, 64><<<grid(4 * kAttnWarps), block, 0, s>>>(
+      attention_heads64_mma_kernel<D><<<grid(kMmaRows), dim3(kMmaWarps * 32), 0, s>>>(
           qb, ld_q, q_bs, kb, vb, ld_kv, kv_bs, ob, ld_out, out_bs, n_q, n_kv);
       break;
     case 128:
