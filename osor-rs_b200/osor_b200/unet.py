@@ -674,6 +674,16 @@ class NativeUnet:
             self.ops = CudaUnetOps(weights, self.arch, context, pooled, self.device, dtype)
         self.graph = UnetGraph(self.arch, self.ops)
 
+    @classmethod
+    def from_safetensors(cls, path: str, context, pooled, arch: Optional[Architecture] = None,
+                         device: int = 0, dtype=torch.bfloat16, limits=None) -> "NativeUnet":
+        """Load a bundle's `unet.safetensors` (diffusers names) with the
+        reference's per-file checks (``artifact.read_safetensors``,
+        src/artifact.rs:585-760) and build the UNet."""
+        from .artifact import read_safetensors
+        return cls(read_safetensors(path, limits), context, pooled, arch=arch, device=device,
+                   dtype=dtype)
+
     def denoise(self, unet_input: torch.Tensor, timestep: int, time_ids: torch.Tensor,
                 cancellation=None) -> torch.Tensor:
         def checkpoint():

@@ -353,6 +353,19 @@ def test_native_unet_validates_inputs(tiny_model, cuda_device):
         NativeUnet(w, seq[:, :, :4], pooled, arch=arch)
 
 
+def test_unet_loads_from_safetensors(tiny_model, tmp_path, cuda_device):
+    from osor_b200.artifact import write_safetensors
+    arch, w, seq, pooled = tiny_model
+    path = str(tmp_path / "unet.safetensors")
+    write_safetensors(path, w, dtype="F16")
+    loaded = NativeUnet.from_safetensors(path, seq, pooled, arch=arch, dtype=torch.float16)
+    direct = NativeUnet(w, seq, pooled, arch=arch, dtype=torch.float16)
+    x = torch.from_numpy(np.random.default_rng(6).standard_normal((1, 9, 8, 8)).astype(np.float32)).cuda()
+    ids = torch.tensor([[64, 64, 0, 0, 64, 64]], dtype=torch.float32, device="cuda")
+    # The file stores F16 tensors; the model rounds weights to f16 either way.
+    assert torch.equal(loaded(x, 400, ids), direct(x, 400, ids))
+
+
 def test_pipeline_runs_with_the_native_unet(cuda_device):
     from osor_b200.model import NativeModel
     from osor_b200.pipeline import Pipeline
