@@ -316,6 +316,7 @@ def run_ops(args):
         pooled = torch.randn((1, arch.pooled), generator=g, device=dev)
         dt = torch.float16 if args.dtype == "f16" else torch.bfloat16
         unet = NativeUnet(weights, context, pooled, arch=arch, device=0, dtype=dt)
+        replay = NativeUnet(weights, context, pooled, arch=arch, device=0, dtype=dt, graphs=True)
         del weights
         x = torch.randn((4, 9, 128, 128), generator=g, device=dev)
         ids = torch.tensor([[1024.0, 1024.0, 0.0, 0.0, 1024.0, 1024.0]] * 4, device=dev)
@@ -323,7 +324,8 @@ def run_ops(args):
         unet(x, 400, ids)
         torch.cuda.synchronize()
         launches = _lib.launch_count() - before
-        ms = _timed(lambda: unet(x, 400, ids), args.steps, args.warmup, flush)
+        eager_ms = _timed(lambda: unet(x, 400, ids), args.steps, args.warmup, flush)
+        ms = _timed(lambda: replay(x, 400, ids), args.steps, args.warmup, flush)
         flop = unet_flops(arch, 4, 128, 128)
         tf = flop / (ms / 1e3) / 1e12
         # Per-kind breakdown of one call from CUDA events around each op.
@@ -343,6 +345,7 @@ def run_ops(args):
                      for k, v in sorted(kinds.items(), key=lambda kv: -kv[1][0])}
         print(json.dumps({"op": "sdxl inpainting unet (one denoising call, t=400)",
                           "shape": [4, 9, 128, 128], "dtype": args.dtype, "ms": round(ms, 2),
+                          "mode": "CUDA graph replay", "eager_ms": round(eager_ms, 2),
                           "tflop_per_call": round(flop / 1e12, 2), "tflops": round(tf, 1),
                           "frac_of_sustained_peak": round(tf / tflops_sus, 4),
                           "gpu_launches": launches, "peak_source": src,

@@ -478,7 +478,6 @@ class CudaUnetOps:
         self.temb_w = torch.cat([w[p + ".time_emb_proj.weight"] for p in self.resnets]) \
             .to(dtype).contiguous()
         self.temb_b = torch.cat([w[p + ".time_emb_proj.bias"] for p in self.resnets]).contiguous()
-        self._gn_ws: Dict[int, torch.Tensor] = {}
         del w
 
     def _heads_of(self, prefix: str) -> int:
@@ -556,10 +555,9 @@ class CudaUnetOps:
         need = self.lib.osor_group_norm_workspace_size(b, c, h, w, _lib.LAYOUT_NHWC, self.dt)
         if need == 0:
             raise InvalidInput("unsupported group-norm shape")
-        ws = self._gn_ws.get(need)
-        if ws is None:
-            ws = torch.empty(need, dtype=torch.uint8, device=x.device)
-            self._gn_ws = {need: ws}
+        # Per call (the caching allocator makes this cheap): a captured graph
+        # keeps every buffer it uses.
+        ws = torch.empty(need, dtype=torch.uint8, device=x.device)
         y = torch.empty_like(x)
         check(self.lib.osor_group_norm_silu(_ptr(x), _ptr(y), _ptr(gamma), _ptr(beta), b, c, h,
                                             w, _lib.LAYOUT_NHWC, self.dt, float(eps),
@@ -665,7 +663,12 @@ class NativeUnet:
     (src/native.rs:503-519)."""
 
     def __init__(self, weights: Mapping[str, object], context, pooled,
-                 arch: Optional[Architecture] = None, device: int = 0, dtype=torch.bfloat16):
+                 arch: Optional[Architecture] = None, device: int = 0, dtype=torch.bfloat16,
+                 graphs: bool = False):
+        """``graphs``: replay each (batch, h, w, timestep) call as one CUDA graph
+        captured on its first use (about 1,100 launches become one); the
+        cancellation token is then polled before the call only, since a graph
+        runs its blocks without returning to the host."""
         self.arch = arch or Architecture.sdxl()
         self.device = torch.device("cuda", device)
         if not torch.cuda.is_available():
@@ -673,6 +676,8 @@ class NativeUnet:
         with torch.cuda.device(self.device):
             self.ops = CudaUnetOps(weights, self.arch, context, pooled, self.device, dtype)
         self.graph = UnetGraph(self.arch, self.ops)
+        self.graphs = graphs
+        self._captured: Dict[Tuple[int, int, int, int], tuple] = {}
 
     @classmethod
     def from_safetensors(cls, path: str, context, pooled, arch: Optional[Architecture] = None,
@@ -707,6 +712,32 @@ class NativeUnet:
             raise InvalidInput("timestep must be non-negative")
         ids = time_ids.to(torch.float32).contiguous()
         with torch.cuda.device(self.device):
-            return self.graph.forward(unet_input, int(timestep), ids, checkpoint)
+            if not self.graphs:
+                return self.graph.forward(unet_input, int(timestep), ids, checkpoint)
+            checkpoint()
+            key = (b, h, w, int(timestep))
+            entry = self._captured.get(key)
+            if entry is None:
+                entry = self._capture(unet_input, int(timestep), ids)
+                self._captured[key] = entry
+            g, static_in, static_ids, static_out = entry
+            static_in.copy_(unet_input)
+            static_ids.copy_(ids)
+            g.replay()
+            return static_out.clone()
+
+    def _capture(self, unet_input, timestep, ids):
+        static_in, static_ids = unet_input.clone(), ids.clone()
+        # One eager call on a side stream first, so that every lazy set-up
+        # (kernel attributes, descriptors) happens outside the capture.
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self.graph.forward(static_in, timestep, static_ids)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            static_out = self.graph.forward(static_in, timestep, static_ids)
+        return g, static_in, static_ids, static_out
 
     __call__ = denoise

@@ -353,6 +353,19 @@ def test_native_unet_validates_inputs(tiny_model, cuda_device):
         NativeUnet(w, seq[:, :, :4], pooled, arch=arch)
 
 
+def test_graph_replay_matches_eager(tiny_model, cuda_device):
+    arch, w, seq, pooled = tiny_model
+    eager = NativeUnet(w, seq, pooled, arch=arch, dtype=torch.float16)
+    replay = NativeUnet(w, seq, pooled, arch=arch, dtype=torch.float16, graphs=True)
+    rng = np.random.default_rng(8)
+    ids = torch.tensor([[64, 64, 0, 0, 64, 64]] * 2, dtype=torch.float32, device="cuda")
+    for _ in range(2):  # capture, then replay with new inputs
+        x = torch.from_numpy(rng.standard_normal((2, 9, 8, 8)).astype(np.float32)).cuda()
+        assert torch.equal(replay(x, 400, ids), eager(x, 400, ids))
+    assert torch.equal(replay(x, 401, ids), eager(x, 401, ids))
+    assert len(replay._captured) == 2
+
+
 def test_unet_loads_from_safetensors(tiny_model, tmp_path, cuda_device):
     from osor_b200.artifact import write_safetensors
     arch, w, seq, pooled = tiny_model
