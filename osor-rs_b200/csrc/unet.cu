@@ -126,7 +126,8 @@ __global__ void __launch_bounds__(256)
 // ------------------------------------------------------------ LayerNorm
 constexpr int kLnMaxVec = 8;  // 8-channel vectors per lane: channels <= 2048
 
-template <int D>
+// VPL: 8-channel vectors per lane held in registers (ceil(C / 256) or more).
+template <int D, int VPL>
 __global__ void __launch_bounds__(256)
     layer_norm_kernel(const uint4* __restrict__ x, uint4* __restrict__ y,
                       const float* __restrict__ gamma, const float* __restrict__ beta,
@@ -136,10 +137,10 @@ __global__ void __launch_bounds__(256)
   if (row >= rows) return;
   const int vc = channels / 8;
   const uint4* src = x + row * vc;
-  float v[kLnMaxVec][8];
+  float v[VPL][8];
   float s = 0.0f;
 #pragma unroll
-  for (int j = 0; j < kLnMaxVec; ++j) {
+  for (int j = 0; j < VPL; ++j) {
     const int c8 = lane + 32 * j;
     if (c8 < vc) {
       unpack8<D>(__ldg(src + c8), v[j]);
@@ -150,7 +151,7 @@ __global__ void __launch_bounds__(256)
   const float mean = warp_sum(s) / (float)channels;
   float q = 0.0f;
 #pragma unroll
-  for (int j = 0; j < kLnMaxVec; ++j) {
+  for (int j = 0; j < VPL; ++j) {
     const int c8 = lane + 32 * j;
     if (c8 < vc) {
 #pragma unroll
@@ -163,7 +164,7 @@ __global__ void __launch_bounds__(256)
   const float rstd = 1.0f / sqrtf(warp_sum(q) / (float)channels + eps);
   uint4* dst = y + row * vc;
 #pragma unroll
-  for (int j = 0; j < kLnMaxVec; ++j) {
+  for (int j = 0; j < VPL; ++j) {
     const int c8 = lane + 32 * j;
     if (c8 < vc) {
       float o[8];
@@ -378,8 +379,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
 // 64-key tile, S = Q K^T lands in f32 accumulators, the online softmax runs on
 // those fragments (row max / sum across the 4 lanes of a quad), P is repacked
 // in registers as the A operand of O += P V. K and V tiles are staged in
-// shared memory as [key][dim] rows of 72 elements, which makes the B-fragment
-// loads bank-conflict free. Fragment layouts are the PTX ISA's for
+// shared memory as [key][dim] rows of 72 elements (144 bytes: the eight rows of
+// an ldmatrix phase fall in distinct banks); B fragments come from ldmatrix,
+// transposed for V. Fragment layouts are the PTX ISA's for
 // m16n8k16: lane = 4 * group + t; A holds (row group / group + 8, cols 2t,
 // 2t + 1, +8), B (k 2t, 2t + 1, +8; n group), C (row group / group + 8,
 // cols 2t, 2t + 1).
@@ -406,8 +408,19 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
   }
 }
 
-__device__ __forceinline__ uint32_t lds32(const uint16_t* p) {
-  return *reinterpret_cast<const uint32_t*>(p);
+// Four 8 x 8 16-bit matrices from shared memory; lanes 8m .. 8m + 7 give the
+// row addresses of matrix m, and r[m] receives the lane's element pair of it:
+// (row lane / 4, cols 2 (lane % 4), +1), or with .trans (rows 2 (lane % 4), +1,
+// col lane / 4), i.e. a B fragment of the transposed storage.
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const uint16_t* row) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(row)));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const uint16_t* row) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(row)));
 }
 
 template <int D>
@@ -457,15 +470,20 @@ __global__ void __launch_bounds__(kMmaWarps * 32)
       *reinterpret_cast<uint4*>(vs + key * kMmaLd + c * 8) = vv;
     }
     __syncthreads();
-    // S = Q K^T for 8 tiles of 8 keys.
+    // S = Q K^T for 8 tiles of 8 keys. One ldmatrix gives the B fragments of
+    // two key steps: matrices (dims 32 kp + 0, 8, 16, 24) of the tile's 8 keys.
+    const int lrow = lane & 7, lmat = lane >> 3;
     float sc[8][4];
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
       sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
-      const uint16_t* kr = ks + (nt * 8 + g) * kMmaLd + 2 * t;
 #pragma unroll
-      for (int kst = 0; kst < 4; ++kst)
-        mma16816<D>(sc[nt], qa[kst], lds32(kr + kst * 16), lds32(kr + kst * 16 + 8));
+      for (int kp = 0; kp < 2; ++kp) {
+        uint32_t bk[4];
+        ldsm_x4(bk, ks + (nt * 8 + lrow) * kMmaLd + 32 * kp + 8 * lmat);
+        mma16816<D>(sc[nt], qa[2 * kp], bk[0], bk[1]);
+        mma16816<D>(sc[nt], qa[2 * kp + 1], bk[2], bk[3]);
+      }
     }
     // Mask keys past the end, then the tile's row maxima over the quad.
     float mx0 = m0, mx1 = m1;
@@ -504,17 +522,16 @@ __global__ void __launch_bounds__(kMmaWarps * 32)
       pa[nt >> 1][(nt & 1) * 2] = E::pack(p0, p1);
       pa[nt >> 1][(nt & 1) * 2 + 1] = E::pack(p2, p3);
     }
-    // O += P V: B fragments (keys 2t, 2t + 1 (+8) of dim column group).
+    // O += P V: transposed ldmatrix of [key][dim] rows gives the B fragments
+    // (keys 2t, 2t + 1 of dim column g) of two key steps per load.
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
-      const uint16_t* vcol = vs + nt * 8 + g;
 #pragma unroll
-      for (int kst = 0; kst < 4; ++kst) {
-        const int k0 = kst * 16 + 2 * t;
-        const uint32_t b0 = (uint32_t)vcol[k0 * kMmaLd] | ((uint32_t)vcol[(k0 + 1) * kMmaLd] << 16);
-        const uint32_t b1 =
-            (uint32_t)vcol[(k0 + 8) * kMmaLd] | ((uint32_t)vcol[(k0 + 9) * kMmaLd] << 16);
-        mma16816<D>(o[nt], pa[kst], b0, b1);
+      for (int kp = 0; kp < 2; ++kp) {
+        uint32_t bv[4];
+        ldsm_x4_trans(bv, vs + (32 * kp + 8 * lmat + lrow) * kMmaLd + nt * 8);
+        mma16816<D>(o[nt], pa[2 * kp], bv[0], bv[1]);
+        mma16816<D>(o[nt], pa[2 * kp + 1], bv[2], bv[3]);
       }
     }
   }
@@ -597,10 +614,21 @@ cudaError_t layer_norm_launch(int dtype, const void* x, void* y, const float* ga
   const unsigned grid = (unsigned)((rows + 7) / 8);
   const uint4* xv = static_cast<const uint4*>(x);
   uint4* yv = static_cast<uint4*>(y);
-  if (dtype == kF16)
-    layer_norm_kernel<kF16><<<grid, 256, 0, s>>>(xv, yv, gamma, beta, rows, channels, eps);
-  else
-    layer_norm_kernel<kBf16><<<grid, 256, 0, s>>>(xv, yv, gamma, beta, rows, channels, eps);
+  const int vpl = (channels / 8 + 31) / 32;
+  auto launch = [&](auto kernel) {
+    kernel<<<grid, 256, 0, s>>>(xv, yv, gamma, beta, rows, channels, eps);
+  };
+  if (dtype == kF16) {
+    if (vpl <= 2) launch(layer_norm_kernel<kF16, 2>);
+    else if (vpl <= 3) launch(layer_norm_kernel<kF16, 3>);
+    else if (vpl <= 5) launch(layer_norm_kernel<kF16, 5>);
+    else launch(layer_norm_kernel<kF16, kLnMaxVec>);
+  } else {
+    if (vpl <= 2) launch(layer_norm_kernel<kBf16, 2>);
+    else if (vpl <= 3) launch(layer_norm_kernel<kBf16, 3>);
+    else if (vpl <= 5) launch(layer_norm_kernel<kBf16, 5>);
+    else launch(layer_norm_kernel<kBf16, kLnMaxVec>);
+  }
   return cudaGetLastError();
 }
 
