@@ -308,7 +308,8 @@ def run_ops(args):
     elif args.op == "unet":
         # One SDXL inpainting UNet call at t=400 for the 4 x 1024^2 job:
         # [4, 9, 128, 128] latents, 77-token prompt, random-init weights.
-        from osor_b200.unet import Architecture, NativeUnet, random_unet_weights, unet_flops
+        from osor_b200.unet import (Architecture, NativeUnet, UnetExecutor, random_unet_weights,
+                                    unet_flops)
         arch = Architecture.sdxl()
         g = torch.Generator(device=dev).manual_seed(11)
         weights = random_unet_weights(arch, seed=0, device=dev)
@@ -317,6 +318,7 @@ def run_ops(args):
         dt = torch.float16 if args.dtype == "f16" else torch.bfloat16
         unet = NativeUnet(weights, context, pooled, arch=arch, device=0, dtype=dt)
         replay = NativeUnet(weights, context, pooled, arch=arch, device=0, dtype=dt, graphs=True)
+        native = UnetExecutor(weights, context, pooled, arch=arch, device=0, dtype=dt)
         del weights
         x = torch.randn((4, 9, 128, 128), generator=g, device=dev)
         ids = torch.tensor([[1024.0, 1024.0, 0.0, 0.0, 1024.0, 1024.0]] * 4, device=dev)
@@ -325,6 +327,7 @@ def run_ops(args):
         torch.cuda.synchronize()
         launches = _lib.launch_count() - before
         eager_ms = _timed(lambda: unet(x, 400, ids), args.steps, args.warmup, flush)
+        native_ms = _timed(lambda: native(x, 400, ids), args.steps, args.warmup, flush)
         ms = _timed(lambda: replay(x, 400, ids), args.steps, args.warmup, flush)
         flop = unet_flops(arch, 4, 128, 128)
         tf = flop / (ms / 1e3) / 1e12
@@ -346,6 +349,7 @@ def run_ops(args):
         print(json.dumps({"op": "sdxl inpainting unet (one denoising call, t=400)",
                           "shape": [4, 9, 128, 128], "dtype": args.dtype, "ms": round(ms, 2),
                           "mode": "CUDA graph replay", "eager_ms": round(eager_ms, 2),
+                          "native_executor_ms": round(native_ms, 2),
                           "tflop_per_call": round(flop / 1e12, 2), "tflops": round(tf, 1),
                           "frac_of_sustained_peak": round(tf / tflops_sus, 4),
                           "gpu_launches": launches, "peak_source": src,

@@ -370,6 +370,45 @@ int osor_attention_heads(const void* q, long long ld_q, long long q_batch_stride
                          long long ld_out, long long out_batch_stride, int batch, int heads,
                          int n_q, int n_kv, int head_dim, int dtype, void* stream);
 
+/* The UNet as one handle: weights packed and the prompt's cross-attention
+ * keys / values computed at create, one call per denoising step. */
+typedef struct osor_unet osor_unet;
+
+/* Architecture fields of the UNet (src/native.rs:51-98; SDXL: channels {320,
+ * 640, 1280}, depth {0, 2, 10} (0: a block without transformers), heads {5,
+ * 10, 20}, context 2048, pooled 1280, time_projection 256, layers 2) and the
+ * model dtype. */
+typedef struct osor_unet_config {
+  int channels[3];
+  int depth[3];
+  int heads[3];
+  int context;
+  int pooled;
+  int time_projection;
+  int layers;
+  int dtype;
+} osor_unet_config;
+
+/* Builds the UNet from host float32 tensors with diffusers names and the fixed
+ * prompt conditioning: `context` host f32 [tokens][config->context] (1..1024
+ * tokens) and `pooled` host f32 [config->pooled]. A missing or misshaped
+ * tensor returns OSOR_ERR_INVALID_ARTIFACT. Replaces Unet::new
+ * (src/native.rs:127-258) inside NativeModel::new. */
+int osor_unet_create(const osor_tensor* tensors, size_t count, const osor_unet_config* config,
+                     const float* context, int tokens, const float* pooled, int device,
+                     osor_unet** out);
+void osor_unet_destroy(osor_unet* unet);
+
+/* One denoising call: input [B][9][h][w] f32 (device), time_ids [B][6] f32
+ * (device) -> output [B][5][h][w] f32 (device); B 1..4, h and w 4..128.
+ * Activations come from a stream-ordered memory pool owned by the handle;
+ * `cancel` (nullable host flag) is polled between blocks and transformer
+ * layers. Replaces ModelBackend::denoise / NativeModel::denoise_checked
+ * (src/pipeline.rs:54-68, src/native.rs:503-519). */
+int osor_unet_denoise(const osor_unet* unet, const float* input, int timestep,
+                      const float* time_ids, float* output, int batch, int height, int width,
+                      void* stream, const volatile int* cancel);
+
 /* One profiled op: kind ("conv_tc", "conv_direct", "groupnorm", ...),
  * algorithmic FLOPs and bytes, device time between the CUDA events recorded
  * on its stream, and the number of kernels it launched. */

@@ -11,10 +11,15 @@
 #include "ops.h"
 #include "profile.h"
 #include "unet.h"
+#include "unet_model.h"
 #include "vae.h"
 
 struct osor_vae {
   osor::Vae* impl;
+};
+
+struct osor_unet {
+  osor::Unet* impl;
 };
 
 namespace {
@@ -731,6 +736,34 @@ int osor_attention_heads(const void* q, long long ld_q, long long q_batch_stride
       internal_dtype(dtype), q, ld_q, q_batch_stride, k, v, ld_kv, kv_batch_stride, out, ld_out,
       out_batch_stride, batch, heads, n_q, n_kv, head_dim, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "multi-head attention");
+}
+
+int osor_unet_create(const osor_tensor* tensors, size_t count, const osor_unet_config* config,
+                     const float* context, int tokens, const float* pooled, int device,
+                     osor_unet** out) {
+  if (!tensors || !config || !context || !pooled || !out)
+    return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  *out = nullptr;
+  if (osor_device_check(device) != OSOR_OK) return OSOR_ERR_UNAVAILABLE;
+  osor::Unet* impl = nullptr;
+  osor::Status s = osor::unet_create(tensors, count, config, context, tokens, pooled, device, &impl);
+  if (!s.good()) return report(s);
+  *out = new osor_unet{impl};
+  return OSOR_OK;
+}
+
+void osor_unet_destroy(osor_unet* unet) {
+  if (!unet) return;
+  osor::unet_destroy(unet->impl);
+  delete unet;
+}
+
+int osor_unet_denoise(const osor_unet* unet, const float* input, int timestep,
+                      const float* time_ids, float* output, int batch, int height, int width,
+                      void* stream, const volatile int* cancel) {
+  if (!unet || !unet->impl) return fail(OSOR_ERR_INVALID_INPUT, "null UNet handle");
+  return report(osor::unet_denoise(*unet->impl, input, timestep, time_ids, output, batch, height,
+                                   width, static_cast<cudaStream_t>(stream), cancel));
 }
 
 }  // extern "C"

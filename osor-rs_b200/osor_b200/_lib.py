@@ -75,6 +75,13 @@ class OsorVaeConfig(ctypes.Structure):
                 ("dtype", ctypes.c_int)]
 
 
+class OsorUnetConfig(ctypes.Structure):
+    _fields_ = [("channels", ctypes.c_int * 3), ("depth", ctypes.c_int * 3),
+                ("heads", ctypes.c_int * 3), ("context", ctypes.c_int), ("pooled", ctypes.c_int),
+                ("time_projection", ctypes.c_int), ("layers", ctypes.c_int),
+                ("dtype", ctypes.c_int)]
+
+
 _vp = ctypes.c_void_p
 _i = ctypes.c_int
 _sz = ctypes.c_size_t
@@ -128,6 +135,10 @@ SIGNATURES = {
     "osor_channel_update": (_i, [_vp, _ll, _vp, _i, _i, _ll, _vp, _ll, _vp, _i, _vp]),
     "osor_attention_heads": (_i, [_vp, _ll, _ll, _vp, _vp, _ll, _ll, _vp, _ll, _ll, _i, _i, _i,
                                   _i, _i, _i, _vp]),
+    "osor_unet_create": (_i, [ctypes.POINTER(OsorTensor), _sz, ctypes.POINTER(OsorUnetConfig),
+                              _vp, _i, _vp, _i, ctypes.POINTER(_vp)]),
+    "osor_unet_destroy": (None, [_vp]),
+    "osor_unet_denoise": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "osor_profile_begin": (None, []),
     "osor_profile_end": (_i, [_vp, _i, ctypes.POINTER(_i)]),
     "osor_launch_count": (_ll, []),

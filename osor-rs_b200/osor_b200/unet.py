@@ -741,3 +741,92 @@ class NativeUnet:
         return g, static_in, static_ids, static_out
 
     __call__ = denoise
+
+
+class UnetExecutor:
+    """The UNet as one C-ABI handle (``osor_unet_create`` /
+    ``osor_unet_denoise``): the C++ runtime a compiled host binds in place of
+    NativeModel::denoise (src/native.rs:503-519). It runs the same kernels in
+    the same order as ``NativeUnet`` and gives the same bits; activations come
+    from a memory pool owned by the handle. Callable as the pipeline's
+    denoiser."""
+
+    def __init__(self, weights: Mapping[str, object], context, pooled,
+                 arch: Optional[Architecture] = None, device: int = 0, dtype=torch.bfloat16):
+        self.arch = arch or Architecture.sdxl()
+        self.device = torch.device("cuda", device)
+        if dtype not in HALF_TYPES:
+            raise InvalidInput("UNet dtype must be bfloat16 or float16")
+        arrays = {}
+        for name, _ in unet_specs(self.arch):
+            t = weights.get(name) if hasattr(weights, "get") else weights[name]
+            if t is None:
+                raise InvalidArtifact(f"native model tensor missing or incompatible: {name}")
+            a = t.detach().to(torch.float32).cpu().numpy() if torch.is_tensor(t) else t
+            arrays[name] = np.ascontiguousarray(a, np.float32)
+        table = (_lib.OsorTensor * len(arrays))()
+        names = []
+        for i, (name, a) in enumerate(arrays.items()):
+            if a.ndim > 4:
+                raise InvalidArtifact(f"native model tensor missing or incompatible: {name}")
+            names.append(name.encode())
+            table[i].name = names[-1]
+            table[i].data = a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+            table[i].ndim = a.ndim
+            for d in range(4):
+                table[i].shape[d] = a.shape[d] if d < a.ndim else 0
+        ctx = torch.as_tensor(context).detach().to(torch.float32).cpu().numpy()
+        pool = torch.as_tensor(pooled).detach().to(torch.float32).cpu().numpy()
+        if ctx.ndim != 3 or ctx.shape[0] != 1 or ctx.shape[2] != self.arch.context \
+                or pool.shape != (1, self.arch.pooled):
+            raise InvalidInput(f"fixed conditioning must be [1, 1..=1024, {self.arch.context}] "
+                               f"and [1, {self.arch.pooled}]")
+        ctx = np.ascontiguousarray(ctx[0])
+        pool = np.ascontiguousarray(pool[0])
+        blocks = self.arch.blocks
+        cfg = _lib.OsorUnetConfig()
+        for i, blk in enumerate(blocks):
+            cfg.channels[i] = blk.channels
+            cfg.depth[i] = blk.depth or 0
+            cfg.heads[i] = blk.heads
+        cfg.context, cfg.pooled = self.arch.context, self.arch.pooled
+        cfg.time_projection, cfg.layers = self.arch.time_projection, self.arch.layers
+        cfg.dtype = dtype_code(dtype)
+        handle = ctypes.c_void_p()
+        check(_lib.lib().osor_unet_create(table, len(arrays), ctypes.byref(cfg),
+                                          ctx.ctypes.data, ctx.shape[0], pool.ctypes.data,
+                                          device, ctypes.byref(handle)))
+        self._handle = handle
+
+    def close(self) -> None:
+        if getattr(self, "_handle", None):
+            _lib.lib().osor_unet_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def denoise(self, unet_input: torch.Tensor, timestep: int, time_ids: torch.Tensor,
+                cancellation=None) -> torch.Tensor:
+        if not torch.is_tensor(unet_input) or unet_input.ndim != 4 \
+                or unet_input.shape[1] != IN_CHANNELS:
+            raise InvalidInput("UNet input must have shape [batch,9,height,width]")
+        b, _, h, w = unet_input.shape
+        if unet_input.dtype != torch.float32 or unet_input.device != self.device \
+                or not unet_input.is_contiguous():
+            raise InvalidInput("UNet input must be contiguous f32 on the model device")
+        if not torch.is_tensor(time_ids) or tuple(time_ids.shape) != (b, 6) \
+                or time_ids.device != self.device:
+            raise InvalidInput("time_ids must have shape [batch, 6] on the UNet input device")
+        ids = time_ids.to(torch.float32).contiguous()
+        out = torch.empty((b, OUT_CHANNELS, h, w), dtype=torch.float32, device=self.device)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        flag = cancellation.pointer() if cancellation is not None else None
+        check(_lib.lib().osor_unet_denoise(self._handle, _ptr(unet_input), int(timestep),
+                                           _ptr(ids), _ptr(out), b, h, w, stream, flag))
+        return out
+
+    __call__ = denoise

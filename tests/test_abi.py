@@ -114,6 +114,18 @@ def test_band_pipeline_and_scheduler_entry_points_validate_on_the_host():
     assert lb.osor_scheduler_alphas(0, 0.1, 0.2, 0, None, out.ctypes.data) == bad
 
 
+def test_unet_handle_entry_points_validate_on_the_host():
+    lb = _lib.lib()
+    bad = _lib.OSOR_ERR_INVALID_INPUT
+    cfg = _lib.OsorUnetConfig()
+    out = ctypes.c_void_p()
+    one = np.zeros(8, np.float32)
+    assert lb.osor_unet_create(None, 0, ctypes.byref(cfg), one.ctypes.data, 1, one.ctypes.data, 0,
+                               ctypes.byref(out)) == bad
+    assert lb.osor_unet_denoise(None, None, 400, None, None, 1, 8, 8, None, None) == bad
+    lb.osor_unet_destroy(None)
+
+
 def test_device_check_reports_unavailable_without_gpu():
     import torch
     if torch.cuda.is_available():

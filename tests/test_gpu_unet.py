@@ -21,7 +21,8 @@ import torch
 from oracle import unet as U
 from osor_b200 import _lib
 from osor_b200._lib import InvalidInput, check, dtype_code
-from osor_b200.unet import Architecture, BlockSpec, NativeUnet, random_unet_weights
+from osor_b200.unet import (Architecture, BlockSpec, NativeUnet, UnetExecutor,
+                            random_unet_weights)
 
 pytestmark = pytest.mark.gpu
 
@@ -364,6 +365,56 @@ def test_graph_replay_matches_eager(tiny_model, cuda_device):
         assert torch.equal(replay(x, 400, ids), eager(x, 400, ids))
     assert torch.equal(replay(x, 401, ids), eager(x, 401, ids))
     assert len(replay._captured) == 2
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16])
+def test_native_executor_matches_the_python_host(tiny_model, dt, cuda_device):
+    """osor_unet_create / osor_unet_denoise run the same launches as NativeUnet."""
+    arch, w, seq, pooled = tiny_model
+    host = NativeUnet(w, seq, pooled, arch=arch, dtype=dt)
+    native = UnetExecutor(w, seq, pooled, arch=arch, dtype=dt)
+    rng = np.random.default_rng(12)
+    for shape in ((2, 9, 8, 8), (1, 9, 5, 7)):
+        x = torch.from_numpy(rng.standard_normal(shape).astype(np.float32)).cuda()
+        ids = torch.tensor([[64, 56, 0, 0, 64, 56]] * shape[0], dtype=torch.float32, device="cuda")
+        assert torch.equal(native(x, 400, ids), host(x, 400, ids))
+    native.close()
+
+
+def test_native_executor_at_sdxl_widths(cuda_device):
+    arch = Architecture((BlockSpec(320, None, 5), BlockSpec(640, 1, 10), BlockSpec(1280, 1, 20)),
+                        context=64, pooled=32, time_projection=32, layers=1)
+    w = {k: v.numpy() for k, v in random_unet_weights(arch, seed=7).items()}
+    rng = np.random.default_rng(2)
+    seq = rng.standard_normal((1, 77, 64)).astype(np.float32)
+    pooled = rng.standard_normal((1, 32)).astype(np.float32)
+    x = torch.from_numpy(rng.standard_normal((1, 9, 16, 16)).astype(np.float32)).cuda()
+    ids = torch.tensor([[128, 128, 0, 0, 128, 128]], dtype=torch.float32, device="cuda")
+    native = UnetExecutor(w, seq, pooled, arch=arch, dtype=torch.bfloat16)
+    host = NativeUnet(w, seq, pooled, arch=arch, dtype=torch.bfloat16)
+    assert torch.equal(native(x, 400, ids), host(x, 400, ids))
+
+
+def test_native_executor_cancels_and_validates(tiny_model, cuda_device):
+    from osor_b200.model import CancellationToken
+    arch, w, seq, pooled = tiny_model
+    native = UnetExecutor(w, seq, pooled, arch=arch, dtype=torch.float16)
+    x = torch.zeros((1, 9, 8, 8), device="cuda")
+    ids = torch.zeros((1, 6), device="cuda")
+    token = CancellationToken()
+    token.cancel()
+    with pytest.raises(_lib.Cancelled):
+        native(x, 400, ids, cancellation=token)
+    with pytest.raises(InvalidInput):
+        native(torch.zeros((1, 9, 200, 8), device="cuda"), 400, ids)
+    with pytest.raises(InvalidInput):
+        native(torch.zeros((5, 9, 8, 8), device="cuda"), 400, torch.zeros((5, 6), device="cuda"))
+    out = native(x, 400, ids)
+    assert torch.isfinite(out).all()
+    bad = dict(w)
+    bad["conv_out.weight"] = np.zeros((5, 64, 1, 1), np.float32)
+    with pytest.raises(_lib.InvalidArtifact):
+        UnetExecutor(bad, seq, pooled, arch=arch)
 
 
 def test_unet_loads_from_safetensors(tiny_model, tmp_path, cuda_device):
