@@ -824,7 +824,7 @@ class UnetExecutor:
         ids = time_ids.to(torch.float32).contiguous()
         out = torch.empty((b, OUT_CHANNELS, h, w), dtype=torch.float32, device=self.device)
         stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
-        flag = cancellation.pointer() if cancellation is not None else None
+        flag = cancellation.pointer if cancellation is not None else None
         check(_lib.lib().osor_unet_denoise(self._handle, _ptr(unet_input), int(timestep),
                                            _ptr(ids), _ptr(out), b, h, w, stream, flag))
         return out
