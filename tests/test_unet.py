@@ -8,8 +8,8 @@ import torch
 
 from oracle import unet as U
 from osor_b200 import _lib
-from osor_b200.unet import (Architecture, BlockSpec, NativeUnet, UnetGraph, random_unet_weights,
-                            resnet_prefixes, unet_specs)
+from osor_b200.unet import (Architecture, BlockSpec, NativeUnet, UnetExecutor, UnetGraph,
+                            random_unet_weights, resnet_prefixes, unet_specs)
 
 
 def _oracle_arch(arch: Architecture) -> U.Arch:
@@ -175,3 +175,16 @@ def test_native_unet_requires_a_cuda_device():
     with pytest.raises(_lib.Unavailable):
         NativeUnet(random_unet_weights(arch), np.zeros((1, 2, 8), np.float32),
                    np.zeros((1, 8), np.float32), arch=arch)
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the CPU-only refusal")
+def test_native_runtime_handle_requires_a_cuda_device():
+    """The wrapper marshals every tensor and the configuration into the C ABI,
+    which refuses without an sm_100 device."""
+    arch = Architecture.tiny()
+    with pytest.raises(_lib.Unavailable):
+        UnetExecutor(random_unet_weights(arch), np.zeros((1, 2, 8), np.float32),
+                     np.zeros((1, 8), np.float32), arch=arch)
+    with pytest.raises(_lib.InvalidInput):  # prompt width does not match the architecture
+        UnetExecutor(random_unet_weights(arch), np.zeros((1, 2, 4), np.float32),
+                     np.zeros((1, 8), np.float32), arch=arch)
