@@ -165,21 +165,43 @@ int osor_group_norm_silu(const void* x, void* y, const float* gamma, const float
                          int silu, float* stats, void* workspace, size_t workspace_bytes,
                          void* stream);
 
-/* The NCHW case of osor_group_norm_silu (same kernel, same results) for
- * callers that cannot allocate device memory where they run the op, such as
- * a host framework's enqueue callback that owns all allocations or a serving
- * loop that must not call the allocator. It takes no workspace: the scratch
- * lives in one fixed device array of 397312 bytes (32768 chunk partials plus
- * 1024 group counters) that every GPU loading the library keeps until exit;
- * shapes that need more return OSOR_ERR_INVALID_INPUT before any device work.
- * The first call on a device looks up the array's address with that device
- * current, so make that first call before any stream capture. All calls share
- * the array (each call clears its counters first); calls that overlap on the
- * GPU race and must not be issued. It calls no cudaMalloc / cudaFree. This
- * entry point has no counterpart in the reference. */
+/* GroupNorm(+SiLU) over NCHW tensors for callers that cannot allocate device
+ * memory where they run the op, such as a host framework's enqueue callback
+ * that owns all allocations or a serving loop that must not call the
+ * allocator. It always runs the shared-memory-resident fused NCHW kernel
+ * (osor_group_norm_silu may take the L2-resident one for the same shape), so
+ * its results match osor_group_norm_silu's to rounding (statistics to 1e-4
+ * relative, outputs to one unit in the last place of the 16-bit type). It
+ * takes no workspace: the scratch lives in one fixed device array of 397312
+ * bytes (32768 chunk partials plus 1024 group counters) that every GPU loading
+ * the library keeps until exit. Shapes that need more scratch, and shapes whose
+ * groups the fused kernel cannot hold in one wave of resident CTAs (which
+ * osor_group_norm_silu still accepts), return OSOR_ERR_INVALID_INPUT before
+ * any device work. The call runs on the device that owns x. The first call on
+ * a device looks up the array's address with that device current, so make
+ * that first call before any stream capture. All calls share the array (each
+ * call clears its counters first); calls that overlap on the GPU race and must
+ * not be issued. It calls no cudaMalloc / cudaFree. This entry point has no
+ * counterpart in the reference. */
 int osor_group_norm_silu_noalloc(const void* x, void* y, const float* gamma, const float* beta,
                                  int batch, int channels, int height, int width, int dtype,
                                  float eps, int silu, float* stats, void* stream);
+
+/* Test hook for the device-side bounded waits (no counterpart in the
+ * reference, whose own failure tests inject on the host, e.g. the
+ * cancel-after-N-checkpoints test of src/native/conv.rs:190-216). Launches
+ * the fused NCHW GroupNorm(+SiLU) kernel of osor_group_norm_silu with each
+ * group's arrival target one above its chunk count, so every CTA's cross-CTA
+ * group wait runs out after wait_ns (1 us .. 1 s) of %globaltimer. The kernel
+ * then records code 1 (wait timeout) in the device status word, lets its
+ * in-flight loads land and returns; y is left partly unwritten. Nothing
+ * faults or traps, and the context stays usable: read the code with
+ * osor_device_status(device, 1), then make normal calls. workspace: at least
+ * osor_group_norm_workspace_size(..., OSOR_LAYOUT_NCHW, dtype) bytes. */
+int osor_test_group_norm_wait_expiry(const void* x, void* y, const float* gamma,
+                                     const float* beta, int batch, int channels, int height,
+                                     int width, int dtype, unsigned long long wait_ns,
+                                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* The statistics half of StableGroupNorm::forward_reference
  * (src/native/vae_encoder.rs:55-75) on 16-bit NHWC x: stats (device f32

@@ -24,6 +24,7 @@
 //
 // Reference counterpart: Attention::forward_checked / attend_with
 // (src/native/vae_encoder.rs:237-340, src/native/attention.rs:27-84).
+#include <atomic>
 #include "attn_fa.h"
 #include "common.cuh"
 
@@ -421,7 +422,7 @@ EncodeTiledFnA encode_fn_a() {
 template <int D>
 cudaError_t fa_launch_typed(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                             const FaParams& p, cudaStream_t stream) {
-  static int sms[64] = {0};
+  static std::atomic<int> sms[64];  // zero-initialized; atomic for concurrent callers
   int device = 0;
   cudaGetDevice(&device);
   if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
@@ -433,7 +434,8 @@ cudaError_t fa_launch_typed(const CUtensorMap& tq, const CUtensorMap& tk, const 
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
     sms[device] = n > 0 ? n : 148;
   }
-  const int grid = p.tasks < sms[device] ? p.tasks : sms[device];
+  const int resident = sms[device].load();
+  const int grid = p.tasks < resident ? p.tasks : resident;
   attn_fa_kernel<D><<<grid, kFaThreads, kFaSmem, stream>>>(tq, tk, tv, p);
   return cudaGetLastError();
 }

@@ -5,6 +5,7 @@
 
 #include "common.cuh"
 #include "conv_tc.h"
+#include "device_guard.h"
 #include "groupnorm.h"
 #include "noise.h"
 #include "pipeline.h"
@@ -42,27 +43,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 bool is16(int dtype) { return dtype == OSOR_DTYPE_BF16 || dtype == OSOR_DTYPE_F16; }
 int internal_dtype(int dtype) { return dtype == OSOR_DTYPE_F16 ? osor::kF16 : osor::kBf16; }
 
-// Runs the call on the device that owns `ptr` (so callers need not set it).
-class DeviceOf {
- public:
-  explicit DeviceOf(const void* ptr) {
-    cudaGetDevice(&prev_);
-    cudaPointerAttributes attr;
-    if (ptr && cudaPointerGetAttributes(&attr, ptr) == cudaSuccess &&
-        attr.type == cudaMemoryTypeDevice && attr.device != prev_) {
-      cudaSetDevice(attr.device);
-      switched_ = true;
-    }
-    cudaGetLastError();
-  }
-  ~DeviceOf() {
-    if (switched_) cudaSetDevice(prev_);
-  }
-
- private:
-  int prev_ = 0;
-  bool switched_ = false;
-};
+using osor::DeviceOf;
 
 }  // namespace
 
@@ -326,6 +307,45 @@ int osor_group_norm_silu(const void* x, void* y, const float* gamma, const float
                                       stats, s);
   }
   return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "group norm");
+}
+
+int osor_test_group_norm_wait_expiry(const void* x, void* y, const float* gamma,
+                                     const float* beta, int batch, int channels, int height,
+                                     int width, int dtype, unsigned long long wait_ns,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+  if (!x || !y || !gamma || !beta) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (batch <= 0 || height <= 0 || width <= 0 || channels <= 0 || channels % 32 != 0)
+    return fail(OSOR_ERR_INVALID_INPUT, "VAE group normalization requires channels divisible by 32");
+  if (wait_ns < 1000ull || wait_ns > 1000000000ull)
+    return fail(OSOR_ERR_INVALID_INPUT, "wait limit must lie in [1 us, 1 s]");
+  if (dtype != OSOR_DTYPE_F32 && dtype != OSOR_DTYPE_BF16 && dtype != OSOR_DTYPE_F16)
+    return fail(OSOR_ERR_INVALID_INPUT, "dtype must be F32, BF16 or F16");
+  const long long spatial = (long long)height * width;
+  const osor::GnFusedPlan plan =
+      osor::gn_fused_plan(batch, channels, spatial, 32, dtype == OSOR_DTYPE_F32 ? 4 : 2);
+  if (!plan.feasible)
+    return fail(OSOR_ERR_INVALID_INPUT, "group is too large for the fused kernel's one wave");
+  if (!workspace || workspace_bytes < plan.workspace_bytes)
+    return fail(OSOR_ERR_INVALID_INPUT, "group-norm workspace is too small");
+  DeviceOf dev(x);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  osor::note_launches(1);
+  cudaError_t e;
+  // One arrival more than the group's chunks: nothing ever provides it.
+  if (dtype == OSOR_DTYPE_F32)
+    e = osor::gn_fused_launch<float>(static_cast<const float*>(x), static_cast<float*>(y), gamma,
+                                     beta, batch, channels, spatial, 32, 1e-6f, 1, workspace,
+                                     nullptr, s, 1, wait_ns);
+  else if (dtype == OSOR_DTYPE_BF16)
+    e = osor::gn_fused_launch<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x),
+                                             static_cast<__nv_bfloat16*>(y), gamma, beta, batch,
+                                             channels, spatial, 32, 1e-6f, 1, workspace, nullptr, s,
+                                             1, wait_ns);
+  else
+    e = osor::gn_fused_launch<__half>(static_cast<const __half*>(x), static_cast<__half*>(y), gamma,
+                                      beta, batch, channels, spatial, 32, 1e-6f, 1, workspace,
+                                      nullptr, s, 1, wait_ns);
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "group norm wait-expiry test");
 }
 
 int osor_group_norm_stats(const void* x, int batch, int channels, int height, int width,

@@ -22,6 +22,7 @@
 // (src/native/conv.rs:54-112) with its bias add (:116-145) and the residual
 // add of Resnet::forward_checked (src/native/vae_encoder.rs:150), and the
 // score / value matmuls of attend (src/native/attention.rs:23).
+#include <atomic>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -552,7 +553,7 @@ EncodeTiledFn encode_fn() {
 }
 
 int sm_count(int device) {
-  static int counts[64] = {0};
+  static std::atomic<int> counts[64];  // zero-initialized; atomic for concurrent callers
   if (device < 0 || device >= 64) return 148;
   if (counts[device] == 0) {
     int c = 0;
@@ -567,7 +568,7 @@ cudaError_t launch_typed(const CUtensorMap& ta, const CUtensorMap& tb, const CUt
                          const TcParams& p,
                          cudaStream_t stream) {
   using Cfg = TcConfig<BLOCK_N>;
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // zero-initialized; atomic for concurrent callers
   int device = 0;
   cudaGetDevice(&device);
   if (device >= 0 && device < 64 && !configured[device]) {

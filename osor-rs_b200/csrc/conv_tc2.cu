@@ -26,6 +26,7 @@
 //
 // Reference counterpart: the same convolution as conv_tc.cu
 // (BandedConv2d::forward_checked, src/native/conv.rs:54-145).
+#include <atomic>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -410,7 +411,7 @@ cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Param
   // once (not every SM need have a partner in its cluster-capable group, so
   // this can be below SMs / 2). The persistent grid never exceeds it: a pair
   // that had to wait for another to finish would double the kernel's time.
-  static int resident_pairs[64] = {0};
+  static std::atomic<int> resident_pairs[64];  // zero-initialized; atomic for concurrent callers
   int device = 0;
   cudaGetDevice(&device);
   if (device < 0 || device >= 64) return cudaErrorInvalidDevice;

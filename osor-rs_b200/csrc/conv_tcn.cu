@@ -27,6 +27,7 @@
 //
 // Reference counterpart: BandedConv2d::forward_checked
 // (src/native/conv.rs:54-145).
+#include <atomic>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -446,7 +447,7 @@ EncodeTiledFnN encode_fn_n() {
 template <int D, int CPG>
 cudaError_t launch_n(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& to,
                      const TcnParams& p, cudaStream_t stream) {
-  static int sms[64] = {0};
+  static std::atomic<int> sms[64];  // zero-initialized; atomic for concurrent callers
   int device = 0;
   cudaGetDevice(&device);
   if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
@@ -458,7 +459,8 @@ cudaError_t launch_n(const CUtensorMap& tx, const CUtensorMap& tw, const CUtenso
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
     sms[device] = n > 0 ? n : 148;
   }
-  const int grid = p.tiles < sms[device] ? p.tiles : sms[device];
+  const int resident = sms[device].load();
+  const int grid = p.tiles < resident ? p.tiles : resident;
   conv_tcn_kernel<D, CPG><<<grid, kThreadsN, kSmemN, stream>>>(tx, tw, to, p);
   return cudaGetLastError();
 }

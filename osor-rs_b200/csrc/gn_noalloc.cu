@@ -9,6 +9,10 @@
 // declares once. Every GPU that loads the library holds the array until the
 // process exits.
 //
+// The call runs on the device that owns x (made current for the call, then
+// restored), like osor_group_norm_silu, so the scratch it uses is that
+// device's copy of the array.
+//
 // The array has a fixed size (kNoAllocScratchBytes); shapes whose scratch
 // does not fit are rejected before any device work. The first call on a
 // device looks up the array's device address (cudaGetSymbolAddress) with that
@@ -24,6 +28,7 @@
 
 #include "../../include/osor_b200.h"
 #include "common.cuh"
+#include "device_guard.h"
 #include "groupnorm.h"
 
 namespace osor {
@@ -41,7 +46,6 @@ constexpr size_t kNoAllocScratchBytes = 32768 * 3 * sizeof(float) + 1024 * sizeo
 
 static __device__ __align__(256) unsigned char g_gn_noalloc_scratch[kNoAllocScratchBytes];
 
-constexpr int kMaxDevices = 64;
 void* g_scratch_ptr[kMaxDevices] = {nullptr};
 std::mutex g_scratch_mutex;
 
@@ -86,12 +90,19 @@ int osor_group_norm_silu_noalloc(const void* x, void* y, const float* gamma, con
   const int eb = dtype == OSOR_DTYPE_F32 ? 4 : 2;
   const GnFusedPlan plan = gn_fused_plan(batch, channels, spatial, 32, eb);
   if (!plan.feasible)
-    return fail(OSOR_ERR_INVALID_INPUT, "group is too large for one wave of resident CTAs");
+    return fail(OSOR_ERR_INVALID_INPUT,
+                "osor_group_norm_silu_noalloc runs only the shared-memory-resident kernel, and "
+                "a group of this shape needs more chunks than one wave of its resident CTAs; "
+                "osor_group_norm_silu (with a workspace) takes such shapes");
   if (plan.workspace_bytes > kNoAllocScratchBytes)
     return fail(OSOR_ERR_INVALID_INPUT,
                 "shape needs " + std::to_string(plan.workspace_bytes) +
                     " bytes of scratch; the fixed no-allocation scratch holds " +
                     std::to_string(kNoAllocScratchBytes));
+  // The scratch lookup and the launch both run on the device that owns x, as
+  // the workspace entry point does: a stream of x's device and x's own copy of
+  // the array, whichever device the calling thread had current.
+  DeviceOf dev(x);
   void* scratch = nullptr;
   cudaError_t e = scratch_address(&scratch);
   if (e != cudaSuccess) return fail(OSOR_ERR_CUDA, std::string("scratch lookup: ") + cudaGetErrorString(e));

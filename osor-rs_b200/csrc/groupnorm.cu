@@ -20,6 +20,7 @@
 //    so partials add across chunks; finalize turns them into per-(batch,
 //    channel) (mean, rstd * gamma, beta); apply streams x once with 16-byte
 //    vectors.
+#include <atomic>
 #include "common.cuh"
 #include "groupnorm.h"
 
@@ -111,6 +112,9 @@ struct FusedParams {
   float* partials;        // [groups_total, chunks_per_group, 3]
   int* arrive;            // [groups_total]
   float* stats_out;       // optional [groups_total, 2] (mean, var)
+  int arrive_target;      // arrivals a group waits for: chunks_per_group (more only in the
+                          // wait-expiry test, so that the wait runs out)
+  unsigned long long wait_ns;  // limit of the cross-CTA group wait
 };
 
 template <typename T>
@@ -219,8 +223,8 @@ __global__ void __launch_bounds__(kFusedThreads)
       const volatile int* arrived = p.arrive + group;
       const uint64_t t0 = global_timer_ns();
       bool ok = true;
-      while (*arrived < p.chunks_per_group) {
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
+      while (*arrived < p.arrive_target) {
+        if (global_timer_ns() - t0 > p.wait_ns) {
           record_device_error(kDevWaitTimeout);
           ok = false;
           break;
@@ -733,7 +737,7 @@ cudaError_t apply_launch(const void* x, void* y, const float* coef, int batch, i
   if (256 % (channels / 8) == 0 && image_bytes % kApplyChunk == 0 &&
       ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0) {
     const int smem = kApplyStages * kApplyChunk;
-    static bool configured[64] = {false};
+    static std::atomic<bool> configured[64];  // zero-initialized; atomic for concurrent callers
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
@@ -1100,10 +1104,14 @@ GnFusedPlan gn_fused_plan(int batch, int channels, long long spatial, int groups
 template <typename T>
 cudaError_t gn_fused_launch(const T* x, T* y, const float* gamma, const float* beta, int batch,
                             int channels, long long spatial, int groups, float eps, int silu,
-                            void* workspace, float* stats_out, cudaStream_t stream) {
+                            void* workspace, float* stats_out, cudaStream_t stream,
+                            int extra_arrivals, unsigned long long wait_ns) {
   const GnFusedPlan plan = gn_fused_plan(batch, channels, spatial, groups, (int)sizeof(T));
   if (!plan.feasible) return cudaErrorInvalidValue;
+  if (extra_arrivals < 0) return cudaErrorInvalidValue;
   FusedParams p;
+  p.arrive_target = plan.chunks_per_group + extra_arrivals;
+  p.wait_ns = wait_ns ? wait_ns : kWaitLimitNs;
   p.count = plan.count;
   p.chunk = plan.chunk;
   p.chunks_per_group = plan.chunks_per_group;
@@ -1124,7 +1132,7 @@ cudaError_t gn_fused_launch(const T* x, T* y, const float* gamma, const float* b
   p.stats_out = stats_out;
   cudaError_t e = cudaMemsetAsync(p.arrive, 0, (size_t)plan.groups_total * sizeof(int), stream);
   if (e != cudaSuccess) return e;
-  static bool configured[64] = {false};
+  static std::atomic<bool> configured[64];  // zero-initialized; atomic for concurrent callers
   int device = 0;
   cudaGetDevice(&device);
   if (device >= 0 && device < 64 && !configured[device]) {
@@ -1146,13 +1154,14 @@ cudaError_t gn_fused_launch(const T* x, T* y, const float* gamma, const float* b
 
 template cudaError_t gn_fused_launch<float>(const float*, float*, const float*, const float*, int,
                                             int, long long, int, float, int, void*, float*,
-                                            cudaStream_t);
+                                            cudaStream_t, int, unsigned long long);
 template cudaError_t gn_fused_launch<__nv_bfloat16>(const __nv_bfloat16*, __nv_bfloat16*,
                                                     const float*, const float*, int, int, long long,
-                                                    int, float, int, void*, float*, cudaStream_t);
+                                                    int, float, int, void*, float*, cudaStream_t,
+                                                    int, unsigned long long);
 template cudaError_t gn_fused_launch<__half>(const __half*, __half*, const float*, const float*,
                                              int, int, long long, int, float, int, void*, float*,
-                                             cudaStream_t);
+                                             cudaStream_t, int, unsigned long long);
 
 GnNhwcPlan gn_nhwc_plan(int batch, int channels, long long pixels, int groups) {
   GnNhwcPlan plan{};

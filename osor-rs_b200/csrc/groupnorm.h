@@ -42,10 +42,15 @@ GnFusedPlan gn_fused_plan(int batch, int channels, long long spatial, int groups
 
 // Standalone NCHW GroupNorm(+SiLU), T = float, __nv_bfloat16 or __half. stats_out
 // (nullable) receives [batch*groups][2] = (mean, biased variance).
+// extra_arrivals / wait_ns exist for the wait-expiry test only: a group then
+// waits for chunks_per_group + extra_arrivals arrivals (which never come) for
+// at most wait_ns (0: the library's limit) before the kernel records
+// kDevWaitTimeout and returns.
 template <typename T>
 cudaError_t gn_fused_launch(const T* x, T* y, const float* gamma, const float* beta, int batch,
                             int channels, long long spatial, int groups, float eps, int silu,
-                            void* workspace, float* stats_out, cudaStream_t stream);
+                            void* workspace, float* stats_out, cudaStream_t stream,
+                            int extra_arrivals = 0, unsigned long long wait_ns = 0);
 
 struct GnNhwcPlan {
   int threads;

@@ -108,6 +108,8 @@ SIGNATURES = {
                                   _sz, _vp]),
     "osor_group_norm_silu_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _i, _vp,
                                           _vp]),
+    "osor_test_group_norm_wait_expiry": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
+                                              ctypes.c_ulonglong, _vp, _sz, _vp]),
     "osor_group_norm_stats": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _sz, _vp]),
     "osor_group_norm_apply": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _i, _vp,
                                    _sz, _vp]),

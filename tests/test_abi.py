@@ -114,6 +114,28 @@ def test_band_pipeline_and_scheduler_entry_points_validate_on_the_host():
     assert lb.osor_scheduler_alphas(0, 0.1, 0.2, 0, None, out.ctypes.data) == bad
 
 
+def test_wait_expiry_hook_validates_on_the_host():
+    """The bounded-wait test hook refuses bad limits, shapes and workspaces
+    before any device work, so a mistaken call never launches."""
+    lb = _lib.lib()
+    d = ctypes.c_void_p(256)
+    bad = _lib.OSOR_ERR_INVALID_INPUT
+    f16 = _lib.DTYPE_F16
+    need = lb.osor_group_norm_workspace_size(1, 128, 64, 64, _lib.LAYOUT_NCHW, f16)
+    assert need > 0
+    for wait_ns in (0, 999, 1_000_000_001):  # outside [1 us, 1 s]
+        assert lb.osor_test_group_norm_wait_expiry(d, d, d, d, 1, 128, 64, 64, f16, wait_ns, d,
+                                                   need, None) == bad
+    assert lb.osor_test_group_norm_wait_expiry(d, d, d, d, 1, 48, 64, 64, f16, 10 ** 6, d, need,
+                                               None) == bad
+    assert lb.osor_test_group_norm_wait_expiry(None, d, d, d, 1, 128, 64, 64, f16, 10 ** 6, d,
+                                               need, None) == bad
+    assert lb.osor_test_group_norm_wait_expiry(d, d, d, d, 1, 128, 64, 64, f16, 10 ** 6, d, 16,
+                                               None) == bad
+    assert lb.osor_test_group_norm_wait_expiry(d, d, d, d, 1, 128, 64, 64, 9, 10 ** 6, d, need,
+                                               None) == bad
+
+
 def test_unet_handle_entry_points_validate_on_the_host():
     lb = _lib.lib()
     bad = _lib.OSOR_ERR_INVALID_INPUT

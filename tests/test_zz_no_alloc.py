@@ -5,8 +5,11 @@ allocator). Its scratch is a fixed device array inside the library, so the
 caller passes only inputs and outputs.
 
 Checked through the C ABI against the workspace-taking entry point
-(osor_group_norm_silu, NCHW) on two calls in a row, and a shape whose scratch
-would not fit is refused before any device work. This file is collected last.
+(osor_group_norm_silu, NCHW) on two calls in a row; warmed-up calls leave the
+device's free memory unchanged (nothing is allocated); a shape whose scratch
+would not fit is refused before any device work; and, where two GPUs are
+visible, a call on tensors of the second GPU made with the first one current
+runs on the tensors' device. This file is collected last.
 """
 import ctypes
 
@@ -72,9 +75,55 @@ def test_noalloc_matches_workspace_entry_point_twice(shape, dt, cuda_device):
 def test_noalloc_rejects_shapes_beyond_the_fixed_scratch(cuda_device):
     lb = _lib.lib()
     t = torch.zeros(64, device="cuda")
-    # 64 images x 32 groups x 86 chunks of [*, 128, 1024, 1024] 16-bit needs
-    # more scratch than the fixed array holds; refused before any device work.
+    # 64 images x 32 groups x 171 chunks of 48 KiB (a 16-bit [*, 128, 1024,
+    # 1024] group in the 96 KiB shared-memory-resident kernel) needs more
+    # scratch than the fixed array holds; refused before any device work.
     rc = lb.osor_group_norm_silu_noalloc(_p(t), _p(t), _p(t), _p(t), 64, 128, 1024, 1024,
                                          _lib.DTYPE_BF16, 1e-6, 1, None, _stream())
     assert rc == _lib.OSOR_ERR_INVALID_INPUT
     assert "fixed no-allocation scratch" in _lib.last_error()
+
+
+def _noalloc(xt, out, g, b, stream):
+    b_, c, h, w = xt.shape
+    return _lib.lib().osor_group_norm_silu_noalloc(_p(xt), _p(out), _p(g), _p(b), b_, c, h, w,
+                                                   _lib.dtype_code(xt.dtype), 1e-6, 1, None,
+                                                   stream)
+
+
+def test_noalloc_allocates_no_device_memory(cuda_device):
+    x, gamma, beta = workloads.groupnorm_inputs((2, 256, 64, 64), seed=3)
+    xt = torch.from_numpy(x).to(torch.bfloat16).cuda()
+    g = torch.from_numpy(gamma).cuda()
+    b = torch.from_numpy(beta).cuda()
+    out = torch.empty_like(xt)
+    _lib.check(_noalloc(xt, out, g, b, _stream()))  # first call: the scratch address lookup
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        _lib.check(_noalloc(xt, out, g, b, _stream()))
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    assert free_after == free_before
+    assert _lib.lib().osor_device_status(0, 1) == 0
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two visible GPUs")
+def test_noalloc_runs_on_the_device_of_its_tensors(cuda_device):
+    x, gamma, beta = workloads.groupnorm_inputs((1, 128, 64, 64), seed=3)
+    dev = torch.device("cuda", 1)
+    xt = torch.from_numpy(x).to(torch.float16).to(dev)
+    g = torch.from_numpy(gamma).to(dev)
+    b = torch.from_numpy(beta).to(dev)
+    out = torch.full_like(xt, float("nan"))
+    torch.cuda.set_device(0)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(_noalloc(xt, out, g, b, stream))
+    torch.cuda.synchronize(dev)
+    assert torch.cuda.current_device() == 0
+    ref = torch.empty((1, 128, 64, 64), dtype=torch.float16, device="cuda:0")
+    _lib.check(_noalloc(xt.to("cuda:0"), ref, g.to("cuda:0"), b.to("cuda:0"), _stream()))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), ref.cpu().numpy())
+    assert _lib.lib().osor_device_status(1, 1) == 0
