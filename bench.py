@@ -1,27 +1,31 @@
 #!/usr/bin/env python3
 """Benchmark: SDXL VAE decode megapixels/s on B200 (random-init weights).
 
-Workload per GPU and step: decode latents [4, 4, 128, 128] -> RGB
-[4, 3, 1024, 1024] (4.19 Mpx) through the library's decoder. With N GPUs
-(torchrun, one process per GPU) every rank decodes its own batch of 4 images;
-batch images are independent, so there is no collective on the data path
-(weak scaling) and the whole-job value is N * 4.19 Mpx / (max over ranks of
-the step time).
+Workload per step: decode latents [4, 4, 128, 128] -> RGB [4, 3, 1024, 1024]
+(4.19 Mpx, the global batch) through the library's decoder. With N GPUs
+(torchrun, one process per GPU) the same global batch is split (strong
+scaling): N = 2 and 4 give each rank 2 and 1 images (batch images are
+independent, no collective on the data path); N = 8 decodes every image on a
+pair of GPUs in two row bands (halo rows, GroupNorm statistics and the
+mid-block's q|k|v exchanged over NCCL), each rank's decode replayed as one
+CUDA graph. The value is 4.19 Mpx / (max over ranks of the step time).
 
 Timing: W untimed warm-up steps, then exactly K timed steps bracketed by a
 barrier and a device synchronize; each step is timed with CUDA events on the
 decode stream and an L2 flush (a 512 MiB write, more than the 126 MB L2) runs
-between timed steps outside the events. While the timed steps run, every op
-is bracketed by CUDA events on the same stream (osor_profile_begin), which
-gives the dominant kernel's live per-launch duration for the roofline.
+between timed steps outside the events. While the timed steps run (batch
+split), every op is bracketed by CUDA events on the same stream
+(osor_profile_begin), which gives the dominant kernel's live per-launch
+duration for the roofline.
 
 `e2e` repeats the measurement through the public API with host buffers:
-pinned host latents -> H2D copy -> NativeModel.decode -> D2H copy of the
-float32 RGB result, all inside the timed region.
+pinned host latents -> H2D copy -> NativeModel.decode (or the band decoder)
+-> D2H copy of the float32 RGB result, all inside the timed region.
 
 `--impl reference` times the reference's CPU implementation of the path,
 restated in C++ (the reference is a Rust crate that cannot be built here),
-with all host threads, on a bounded sample of the workload.
+with all host threads, on a bounded sample of the workload: one D1 decode
+([1,4,64,64] -> [1,3,512,512]) per step.
 """
 from __future__ import annotations
 
@@ -38,7 +42,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "osor-rs_b200"))
 sys.path.insert(0, ROOT)
 
-METRIC = "VAE decode Mpx/s (SDXL AutoencoderKL decoder, 4x[4,128,128] -> 4x[3,1024,1024] per GPU)"
+METRIC = "VAE decode Mpx/s (SDXL AutoencoderKL decoder, [4,4,128,128] -> [4,3,1024,1024] per step)"
 UNIT = "Mpx/s"
 BATCH, LATENT = 4, 128
 IMAGE = 8 * LATENT
@@ -110,30 +114,48 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def cpu_decode_sample(seconds_hint: float = 20.0):
-    """Times the C++ oracle (the reference's CPU F32 path restated) decoding a
-    bounded sample of the workload on all host threads: one image of
-    [1, 4, 32, 32] latents -> [1, 3, 256, 256]. Returns (Mpx/s, threads, sample)."""
+# The CPU sample: BASELINE's CPU-runnable config D1, one [1,4,64,64] latent ->
+# [1,3,512,512] (seed 42), the same layers as the headline at half the latent
+# side (the mid-block attention, quadratic in tokens, costs less per pixel).
+CPU_LATENT = 64
+CPU_SAMPLE = "D1: 1 x [4,64,64] latents -> [3,512,512] per step"
+
+
+def cpu_decode_sample(seconds_hint: float = 25.0):
+    """Times the C++ oracle (the reference's CPU F32 path restated) decoding
+    the D1 sample on all host threads. Returns (Mpx/s, threads, sample)."""
     import numpy as np
     import oracle
     from oracle import vae as ovae
     from osor_b200 import workloads
     from osor_b200.weights import random_vae_weights
     w = random_vae_weights(0, parts=("decoder", "encoder"))
-    lat = workloads.decoder_latents(1, 32, 32, seed=42)
-    ovae.decode(w, lat)  # first call pays allocation / page faults
+    lat = workloads.decoder_latents(1, CPU_LATENT, CPU_LATENT, seed=42)
     times = []
     t_end = time.perf_counter() + seconds_hint
     while True:
         t0 = time.perf_counter()
         out = ovae.decode(w, lat)
         times.append(time.perf_counter() - t0)
-        if time.perf_counter() > t_end or len(times) >= 5:
+        if time.perf_counter() > t_end or len(times) >= 3:
             break
     assert np.all(np.isfinite(out))
-    px = 256 * 256 / 1e6
+    px = (8 * CPU_LATENT) ** 2 / 1e6
     return px / statistics.median(times), oracle.threads(), \
-        "decode of 1 x [4,32,32] latents -> [3,256,256] per step (median of %d)" % len(times)
+        f"{CPU_SAMPLE} (median of {len(times)}), {_host_cpu()}"
+
+
+def _host_cpu() -> str:
+    name = "unknown CPU"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    name = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return f"{os.cpu_count()} logical cores, {name}"
 
 
 def run_reference(args, rank, world):
@@ -146,7 +168,7 @@ def run_reference(args, rank, world):
     from osor_b200 import workloads
     from osor_b200.weights import random_vae_weights
     w = random_vae_weights(0)
-    lat = workloads.decoder_latents(1, 32, 32, seed=42)
+    lat = workloads.decoder_latents(1, CPU_LATENT, CPU_LATENT, seed=42)
     for _ in range(max(args.warmup, 1)):
         ovae.decode(w, lat)
     times = []
@@ -155,24 +177,23 @@ def run_reference(args, rank, world):
         out = ovae.decode(w, lat)
         times.append(time.perf_counter() - t0)
     assert np.all(np.isfinite(out))
-    px = 256 * 256 / 1e6
+    px = (8 * CPU_LATENT) ** 2 / 1e6
     step_s = statistics.mean(times)
     value = px / step_s
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1)/0.13025 latents; random-init weights seed 0)",
-        "config": {"workload": "SDXL AutoencoderKL decoder [4,4,128,128] -> [4,3,1024,1024] per GPU",
-                   "sample_per_step": "1 x [4,32,32] -> [3,256,256]: a bounded sample of the "
-                                      "workload, the same layers at a quarter of the latent side "
-                                      "(the mid-block attention, quadratic in tokens, costs less "
-                                      "per pixel there)",
+        "config": {"workload": "SDXL AutoencoderKL decoder [4,4,128,128] -> [4,3,1024,1024]",
+                   "sample_per_step": CPU_SAMPLE + ": BASELINE's CPU-runnable configuration, "
+                                      "a bounded sample of the workload (the same layers at "
+                                      "half the latent side)",
                    "global_batch": 4, "latent": [LATENT, LATENT], "image": [IMAGE, IMAGE],
-                   "parallelism": f"host threads ({oracle.threads()})"},
+                   "parallelism": f"host threads ({oracle.threads()}; {_host_cpu()})"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": oracle.threads(), "kind": "port",
-                         "sample": "1 x [4,32,32] latents -> [3,256,256] per step; the reference "
-                                   "(Rust/Candle CPU) cannot be built here, this is its C++ restatement"},
+                         "sample": CPU_SAMPLE + "; the reference (Rust/Candle CPU) cannot be "
+                                   "built here, this is its C++ restatement"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -455,25 +476,25 @@ def run_bands(args, rank, world, local):
     if device_status(local) != 0 or not bool(torch.isfinite(out).all()):
         raise SystemExit("band decode failed (device status or non-finite output)")
 
-    # e2e: latents in from pinned host memory, the rank's band back out, per step.
+    # e2e: latents in from pinned host memory, the rank's band back out, per
+    # step (with a graph, the copy refills the graph's static latent buffer).
     h_lat = torch.from_numpy(lat_host).pin_memory()
     h_out = torch.empty(tuple(out.shape), dtype=torch.float32).pin_memory()
-    e2e_ms = None
-    if graph is None:
-        d_lat = lat
-        barrier()
-        torch.cuda.synchronize(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            d_lat.copy_(h_lat, non_blocking=True)
-            h_out.copy_(dec.decode(d_lat), non_blocking=True)
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
-        te = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e_ms = float(te.item())
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        lat.copy_(h_lat, non_blocking=True)
+        h_out.copy_(step(), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    te = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item())
+    if not bool(torch.isfinite(out).all()):
+        raise SystemExit("band decode failed (non-finite output in the e2e steps)")
     if rank == 0:
         line = {
             "metric": METRIC, "value": mpx / (ms_per_step / 1e3), "unit": UNIT,
@@ -481,15 +502,22 @@ def run_bands(args, rank, world, local):
             "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": args.dtype,
             "data": "synthetic: N(0,1)/0.13025 latents (seed 42 + group), random-init weights (seed 0)",
-            "config": {"workload": f"SDXL AutoencoderKL decoder [1,4,128,128] -> [1,3,1024,1024] "
-                                   f"per group of {k} GPUs",
-                       "global_batch": world // k, "parallelism": f"row bands x{k}, "
-                       f"{world // k} group(s)", "cuda_graph": bool(graph is not None),
-                       "l2": "512 MiB L2 flush between timed steps"},
-            "e2e": None if e2e_ms is None else {
-                "value": mpx / (e2e_ms / 1e3), "unit": UNIT,
-                "h2d_bytes_per_step": int(h_lat.numel() * 4),
-                "d2h_bytes_per_step": int(h_out.numel() * 4), "ms_per_step": e2e_ms},
+            "config": {"workload": f"SDXL AutoencoderKL decoder [{world // k},4,128,128] -> "
+                                   f"[{world // k},3,1024,1024], each image on a group of {k} "
+                                   f"GPUs",
+                       "global_batch": world // k, "latent": [LATENT, LATENT],
+                       "image": [IMAGE, IMAGE],
+                       "parallelism": f"row bands x{k} (halo rows, GroupNorm statistics and "
+                                      f"q|k|v over NCCL), {world // k} group(s)",
+                       "cuda_graph": bool(graph is not None),
+                       "l2": "512 MiB L2 flush between timed steps",
+                       "algorithmic_tflop_per_step": round(
+                           workloads.vae_decoder_flops(world // k, LATENT, LATENT) / 1e12, 2)},
+            "roofline": None,
+            "e2e": {"value": mpx / (e2e_ms / 1e3), "unit": UNIT,
+                    "h2d_bytes_per_step": int(h_lat.numel() * 4),
+                    "d2h_bytes_per_step": int(h_out.numel() * 4), "ms_per_step": e2e_ms,
+                    "per": "rank: its image's latents in, its band of the image out"},
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
         }
@@ -520,9 +548,9 @@ def main():
     ap.add_argument("--graph", action="store_true",
                     help="with --bands: replay each rank's decode, NCCL calls included, as one "
                          "CUDA graph")
-    ap.add_argument("--batch", type=int, default=BATCH,
-                    help="images per GPU for --op decode (the headline workload is 4; smaller "
-                         "batches are for profiler captures)")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="images per GPU for --op decode (default: the global batch of 4 split "
+                         "over the GPUs; other values are for profiler captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -536,9 +564,22 @@ def main():
     if args.op != "decode":
         run_ops(args)
         return
+    # The global batch of 4 over N GPUs: N = 1, 2, 4 split it by image; N = 8
+    # decodes each image on two GPUs in row bands, replayed as CUDA graphs.
+    if not args.bands and args.batch is None and world > BATCH:
+        if world % BATCH:
+            raise SystemExit(f"--gpus {world}: the global batch of {BATCH} splits over 1, 2, 4 "
+                             f"or a multiple of 4 GPUs")
+        args.bands = world // BATCH
+        args.graph = True
     if args.bands:
         run_bands(args, rank, world, local)
         return
+    if args.batch is None:
+        if BATCH % world:
+            raise SystemExit(f"--gpus {world}: the global batch of {BATCH} splits over 1, 2, 4 "
+                             f"or a multiple of 4 GPUs")
+        args.batch = BATCH // world
 
     import numpy as np
     import torch
@@ -618,7 +659,8 @@ def main():
                      "tflops": round(v["flops"] / (v["ms"] / 1e3) / 1e12, 1) if v["flops"] and v["ms"] > 0 else None,
                      "gbs": round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1) if v["ms"] > 0 else None}
                  for k, v in sorted(kinds.items(), key=lambda kv: -kv[1]["ms"])}
-    total_flops = sum(v["flops"] for v in kinds.values()) / args.steps
+    executed_flops = sum(v["flops"] for v in kinds.values()) / args.steps
+    algorithmic_flops = workloads.vae_decoder_flops(args.batch, LATENT, LATENT)
 
     # ------------------------------------------------------------ e2e (host buffers)
     # Every step copies its latents in from pinned host memory and its image
@@ -676,25 +718,36 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": args.dtype,
             "data": "synthetic: N(0,1)/0.13025 latents (seed 42 + rank), random-init weights (seed 0)",
-            "config": {"workload": f"SDXL AutoencoderKL decoder [{args.batch},4,128,128] -> [{args.batch},3,1024,1024] per GPU",
+            "config": {"workload": f"SDXL AutoencoderKL decoder [{args.batch * world},4,128,128] -> "
+                                   f"[{args.batch * world},3,1024,1024]",
                        "global_batch": args.batch * world, "latent": [LATENT, LATENT],
-                       "image": [IMAGE, IMAGE], "parallelism": f"batch split x{world} (no collective)",
+                       "image": [IMAGE, IMAGE],
+                       "parallelism": (f"batch split x{world}, {args.batch} image(s) per GPU "
+                                       f"(no collective)" if world > 1 else "one GPU"),
                        "l2": "512 MiB L2 flush between timed steps; activations 2.1 GB per buffer",
-                       "algorithmic_tflop_per_step": round(total_flops / 1e12, 2)},
+                       "algorithmic_tflop_per_step": round(algorithmic_flops * world / 1e12, 2),
+                       "executed_tflop_per_gpu_step": round(executed_flops / 1e12, 2)},
             "roofline": {"bound": "tensor", "kernel": "conv3x3_tc (tcgen05 implicit GEMM)",
                          "achieved": round(achieved, 1), "peak": tflops_sus, "unit": "TFLOP/s",
                          "frac": round(achieved / tflops_sus, 4),
                          "peak_source": f"{peak_src} bf16_tflops_sustained (dense cuBLAS bf16; f16 runs the same tensor-core rate)",
                          "traffic": round(CONV3X3_DRAM_BYTES_PER_IMAGE * args.batch),
                          "traffic_unit": "bytes per launch",
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the "
-                                           "decode's 28 3x3 conv launches, one image, times the "
-                                           "batch (profiles/decode_b1_dram_traffic.md)",
-                         "decode_tflops": round(total_flops / (ms_per_step / 1e3) / 1e12, 1)},
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum "
+                                           "over the 3x3 conv launches of a one-image decode, "
+                                           "per launch, times the batch",
+                         "decode_tflops": round(algorithmic_flops / (ms_per_step / 1e3) / 1e12, 1),
+                         "decode_tflops_note": "the decoder's algorithmic FLOPs (upsampler "
+                                               "convs at 9 taps, one Q K^T) per step time"},
             "op_breakdown": breakdown,
+            "op_breakdown_note": "device ms per step by op kind and its rate at the work "
+                                 "executed: upconv_tc = the upsamplers as four 2x2 phase "
+                                 "convolutions (4/9 of the 9-tap work); attn_scores and "
+                                 "attn_probs each run one Q K^T (softmax statistics, then 16-bit "
+                                 "probabilities)",
             "e2e": {"value": world * mpx / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": int(h_lat.numel() * 4),
                     "d2h_bytes_per_step": int(h_out.numel() * 4), "ms_per_step": e2e_ms},

@@ -395,9 +395,10 @@ Status upsample_conv(const Ctx& c, const ConvLayer& L, int xi, int batch, int h,
   }
   if (conv_tc_check(a) != nullptr) return Status::ok();
   const double px = 4.0 * batch * h * w;
-  // Algorithmic work of the reference's upsample + 3x3 conv; the phase
-  // kernels do 4/9 of it.
-  OpScope scope("upconv_tc", 2.0 * px * L.cout * 9 * L.cin,
+  // Executed work: each high-res output pixel takes a 2x2 phase kernel, 4/9
+  // of the reference's upsample + 3x3 conv (which the decoder's algorithmic
+  // total still counts at 9 taps).
+  OpScope scope("upconv_tc", 2.0 * px * L.cout * 4 * L.cin,
                 2.0 * batch * h * w * L.cin + 2.0 * px * L.cout, c.s, 1);
   const cudaError_t e = conv_tc_launch(a, c.s);
   if (e != cudaSuccess) return cuda_status(e, "upsample convolution");

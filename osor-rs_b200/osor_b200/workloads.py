@@ -73,6 +73,36 @@ def conv_inputs(batch: int, cin: int, cout: int, h: int, w: int, seed: int = 5):
     return x, wt, bias, res
 
 
+def vae_decoder_flops(batch: int, h: int, w: int, channels=(128, 256, 512, 512),
+                      layers: int = 2) -> float:
+    """Algorithmic FLOPs of VaeDecoder::forward (src/native/vae_decoder.rs:104-114)
+    on [batch, 4, h, w] latents: every convolution at its nominal 2 * pixels *
+    Cin * Cout * k^2 (the upsamplers' 3x3 convs at the upsampled resolution,
+    as the reference runs them), the mid-block's q / k / v / out projections
+    and one Q K^T and one P V per image."""
+    def conv(px, cin, cout, k):
+        return 2.0 * px * cin * cout * k * k
+
+    def resnet(px, cin, cout):
+        f = conv(px, cin, cout, 3) + conv(px, cout, cout, 3)
+        return f + (conv(px, cin, cout, 1) if cin != cout else 0.0)
+
+    n = h * w
+    c = channels[-1]
+    f = conv(batch * n, 4, 4, 1) + conv(batch * n, 4, c, 3)
+    f += 2 * resnet(batch * n, c, c) + batch * (8.0 * n * c * c + 4.0 * n * n * c)
+    rev = list(reversed(channels))
+    px, cin = batch * n, c
+    for i, cout in enumerate(rev):
+        for j in range(layers + 1):
+            f += resnet(px, cin if j == 0 else cout, cout)
+        cin = cout
+        if i + 1 < len(rev):
+            px *= 4
+            f += conv(px, cout, cout, 3)
+    return f + conv(px, channels[0], 3, 3)
+
+
 def psnr(got: np.ndarray, want: np.ndarray, peak_to_peak: float = 2.0) -> float:
     """PSNR in dB for raw RGB in [-1, 1] (peak-to-peak 2)."""
     mse = float(np.mean((np.asarray(got, np.float64) - np.asarray(want, np.float64)) ** 2))

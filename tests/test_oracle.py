@@ -13,6 +13,8 @@ so they can be restated exactly:
                        one score row is rejected (:185-195)
   vae_decoder.rs:167-218  decoder vs an independent implementation at F64
 """
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -20,6 +22,7 @@ import torch.nn.functional as F
 
 import oracle
 from oracle import vae as ovae
+from osor_b200 import workloads
 from osor_b200.weights import random_vae_weights
 
 EPS = 1e-6
@@ -309,3 +312,32 @@ def test_seeded_noise_prefix_and_moments():
     # Standard moments over 262,144 values (noise.rs:170-195).
     v = oracle.seeded_noise(42, 0, 4 * 4 * 128 * 128).astype(np.float64)
     assert abs(v.mean()) < 0.01 and abs(v.var() - 1.0) < 0.02
+
+
+def test_golden_fixtures_are_consistent():
+    """The committed golden fixtures (tests/golden/make_golden.py) hold what
+    the GPU tests assume: the strided sample visits all 64 (row mod 8,
+    column mod 8) phases of the three nearest-2x upsamplings; D1's f32 sample
+    rounds to its f16 whole image at the same positions; the seeded inputs
+    they were made from are the ones the tests regenerate."""
+    import importlib.util
+    golden = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    spec = importlib.util.spec_from_file_location("make_golden",
+                                                  os.path.join(golden, "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    rows, cols = mg.sample_index(1024)
+    phases = {(int(r) % 8, int(c) % 8) for i, r in enumerate(rows) for c in cols[i]}
+    assert len(phases) == 64
+    d1 = np.load(os.path.join(golden, "decoder_d1.npz"))
+    r, c = d1["f32_rows"], d1["f32_cols"]
+    f16_at = d1["image"][0][:, r[:, None], c]
+    np.testing.assert_array_equal(d1["f32_sample"].astype(np.float16), f16_at)
+    lat = workloads.decoder_latents(1, 64, 64, seed=42)
+    assert abs(float(lat.sum()) - float(d1["latents_sum"])) < 1e-3
+    d4 = np.load(os.path.join(golden, "decoder_d4.npz"))
+    assert d4["sample"].shape == (3, 128, 128) and d4["crop_centre"].shape == (3, 64, 64)
+    lat = workloads.decoder_latents(1, 128, 128, seed=42)
+    assert abs(float(lat.sum()) - float(d4["latents_sum"])) < 1e-2
+    e4 = np.load(os.path.join(golden, "encoder_e4.npz"))
+    assert e4["moments"].shape == (1, 8, 128, 128) and np.all(np.isfinite(e4["moments"]))
