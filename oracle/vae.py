@@ -26,6 +26,10 @@ SDXL_LAYERS = 2
 LATENT_SCALE = 0.13025
 
 
+def _keep(x):
+    return x
+
+
 def _conv(w, name, x, stride=1, padding=None):
     weight = w[name + ".weight"]
     k = weight.shape[-1]
@@ -38,14 +42,16 @@ def _gn(w, name, x, silu):
     return group_norm(x, w[name + ".weight"], w[name + ".bias"], silu=silu)
 
 
-def resnet(w, prefix, x):
+def resnet(w, prefix, x, q=_keep):
+    """q rounds each stored activation (identity for the F32 oracle; the
+    precision emulation passes a 16-bit rounding)."""
     if prefix + ".conv_shortcut.weight" in w:
-        shortcut = _conv(w, prefix + ".conv_shortcut", x)
+        shortcut = q(_conv(w, prefix + ".conv_shortcut", x))
     else:
         shortcut = x
-    h = _conv(w, prefix + ".conv1", _gn(w, prefix + ".norm1", x, True))
-    h = _conv(w, prefix + ".conv2", _gn(w, prefix + ".norm2", h, True))
-    return shortcut + h
+    h = q(_conv(w, prefix + ".conv1", q(_gn(w, prefix + ".norm1", x, True))))
+    h = _conv(w, prefix + ".conv2", q(_gn(w, prefix + ".norm2", h, True)))
+    return q(shortcut + h)
 
 
 def _linear_weight(w, name):
@@ -55,13 +61,13 @@ def _linear_weight(w, name):
     return weight, w[name + ".bias"]
 
 
-def attention(w, prefix, x):
+def attention(w, prefix, x, q=_keep):
     b, c, h, wd = x.shape
     names = ("to_q", "to_k", "to_v", "to_out.0")
     if prefix + ".to_q.weight" not in w:
         names = ("query", "key", "value", "proj_attn")
     n = h * wd
-    xs = _gn(w, prefix + ".group_norm", x, False).reshape(b, c, n).transpose(0, 2, 1)
+    xs = q(_gn(w, prefix + ".group_norm", x, False)).reshape(b, c, n).transpose(0, 2, 1)
     xs = np.ascontiguousarray(xs).reshape(b * n, c)
 
     def linear(name, inp):
@@ -69,34 +75,48 @@ def attention(w, prefix, x):
         return sgemm(inp, np.ascontiguousarray(weight.T)) + bias
 
     scale = np.float32(float(c) ** -0.25)
-    q = (linear(names[0], xs) * scale).reshape(b, n, c)
-    k = (linear(names[1], xs) * scale).reshape(b, n, c)
-    v = linear(names[2], xs).reshape(b, n, c)
-    kt = np.ascontiguousarray(k.transpose(0, 2, 1))
-    o = attend(q, kt, v).reshape(b * n, c)
+    qs = q(linear(names[0], xs) * scale).reshape(b, n, c)
+    ks = q(linear(names[1], xs) * scale).reshape(b, n, c)
+    vs = q(linear(names[2], xs)).reshape(b, n, c)
+    kt = np.ascontiguousarray(ks.transpose(0, 2, 1))
+    o = q(attend(qs, kt, vs)).reshape(b * n, c)
     o = linear(names[3], o).reshape(b, n, c).transpose(0, 2, 1).reshape(b, c, h, wd)
-    return o + x
+    return q(o + x)
 
 
-def mid_block(w, prefix, x):
-    x = resnet(w, prefix + ".resnets.0", x)
-    x = attention(w, prefix + ".attentions.0", x)
-    return resnet(w, prefix + ".resnets.1", x)
+def mid_block(w, prefix, x, q=_keep):
+    x = resnet(w, prefix + ".resnets.0", x, q)
+    x = attention(w, prefix + ".attentions.0", x, q)
+    return resnet(w, prefix + ".resnets.1", x, q)
 
 
-def decode(w, latents, channels=SDXL_CHANNELS, layers=SDXL_LAYERS):
-    """VaeDecoder::forward: unscaled latents [B,4,h,w] -> raw RGB [B,3,8h,8w]."""
+def decode(w, latents, channels=SDXL_CHANNELS, layers=SDXL_LAYERS, observer=None, q=_keep):
+    """VaeDecoder::forward: unscaled latents [B,4,h,w] -> raw RGB [B,3,8h,8w].
+
+    observer(name, x), when given, sees each block's output (NCHW f32) under
+    the reference's VAE trace names (src/native/precision_tests.rs:97-130):
+    post_quant_conv, decoder.conv_in, decoder.mid_block, decoder.up_blocks.{i}
+    (after its upsampler), decoder.conv_norm_out (after SiLU), decoder.conv_out.
+    q rounds each stored activation (identity here; see oracle.precision)."""
+    seen = observer or (lambda name, t: None)
     x = _conv(w, "post_quant_conv", np.asarray(latents, np.float32))
-    x = _conv(w, "decoder.conv_in", x)
-    x = mid_block(w, "decoder.mid_block", x)
+    seen("post_quant_conv", x)
+    x = q(_conv(w, "decoder.conv_in", q(x)))
+    seen("decoder.conv_in", x)
+    x = mid_block(w, "decoder.mid_block", x, q)
+    seen("decoder.mid_block", x)
     rev = list(reversed(channels))
     for i in range(len(rev)):
         for j in range(layers + 1):
-            x = resnet(w, f"decoder.up_blocks.{i}.resnets.{j}", x)
+            x = resnet(w, f"decoder.up_blocks.{i}.resnets.{j}", x, q)
         if i + 1 < len(rev):
-            x = _conv(w, f"decoder.up_blocks.{i}.upsamplers.0.conv", upsample_2x(x))
-    x = _gn(w, "decoder.conv_norm_out", x, True)
-    return _conv(w, "decoder.conv_out", x)
+            x = q(_conv(w, f"decoder.up_blocks.{i}.upsamplers.0.conv", upsample_2x(x)))
+        seen(f"decoder.up_blocks.{i}", x)
+    x = q(_gn(w, "decoder.conv_norm_out", x, True))
+    seen("decoder.conv_norm_out", x)
+    y = _conv(w, "decoder.conv_out", x)
+    seen("decoder.conv_out", y)
+    return y
 
 
 def encode_moments(w, image, channels=SDXL_CHANNELS, layers=SDXL_LAYERS):

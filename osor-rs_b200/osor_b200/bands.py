@@ -253,9 +253,21 @@ class BandDecoder(_BandModel):
         u = self.ops.upsample(self.halo(x))
         return self.ops.conv(name, u[:, 1:2 * r + 3])
 
-    def decode(self, latents: torch.Tensor) -> torch.Tensor:
+    def decode(self, latents: torch.Tensor, observer=None) -> torch.Tensor:
         """Unscaled latents [1, 4, h, w] (the whole image, on every rank) ->
-        this rank's rows of the raw RGB image, f32 NCHW [1, 3, 8 h / K, 8 w]."""
+        this rank's rows of the raw RGB image, f32 NCHW [1, 3, 8 h / K, 8 w].
+
+        observer(name, band), when given, sees each block's output: the band's
+        rows, NHWC 16-bit for the activations and NCHW f32 for
+        post_quant_conv and decoder.conv_out, under the reference's VAE trace
+        names (src/native/precision_tests.rs:97-130): post_quant_conv,
+        decoder.conv_in, decoder.mid_block, decoder.up_blocks.{i} (after its
+        upsampler), decoder.conv_norm_out (after SiLU), decoder.conv_out."""
+        def seen(name, x, nchw=False):
+            if observer is not None:
+                r = (x.shape[2] if nchw else x.shape[1]) - 2
+                observer(name, x[:, :, 1:r + 1] if nchw else x[:, 1:r + 1])
+
         lat = self._band_rows(latents, self.k, 4)
         r = lat.shape[2] - 2
         z = self.ops.conv("post_quant_conv", lat, out_nchw=True)
@@ -264,19 +276,25 @@ class BandDecoder(_BandModel):
             z[:, :, 0].zero_()
         if self.rank + 1 == self.k:
             z[:, :, r + 1].zero_()
+        seen("post_quant_conv", z, nchw=True)
         x = self.ops.conv("decoder.conv_in", z)
+        seen("decoder.conv_in", x)
         mid = "decoder.mid_block"
         x = self.resnet(mid + ".resnets.0", x)
         x = self.attention(mid + ".attentions.0", x)
         x = self.resnet(mid + ".resnets.1", x)
+        seen(mid, x)
         rev = list(reversed(self.channels))
         for i in range(len(rev)):
             for j in range(self.layers + 1):
                 x = self.resnet(f"decoder.up_blocks.{i}.resnets.{j}", x)
             if i + 1 < len(rev):
                 x = self.upsample(f"decoder.up_blocks.{i}.upsamplers.0.conv", x)
+            seen(f"decoder.up_blocks.{i}", x)
         x = self.group_norm("decoder.conv_norm_out", x, True)
+        seen("decoder.conv_norm_out", x)
         y = self.ops.conv("decoder.conv_out", x, out_nchw=True)
+        seen("decoder.conv_out", y, nchw=True)
         rows = y.shape[2] - 2
         return y[:, :, 1:rows + 1].contiguous()
 
