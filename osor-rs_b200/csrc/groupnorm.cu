@@ -1180,6 +1180,17 @@ GnNhwcPlan gn_nhwc_plan(int batch, int channels, long long pixels, int groups) {
   return plan;
 }
 
+cudaError_t gn_tiles_coef_launch(const float* tile_part, int batch, int channels,
+                                 long long pixels, int groups, const float* gamma,
+                                 const float* beta, float eps, float* coef, float* stats_out,
+                                 cudaStream_t stream) {
+  const int tiles = (int)(pixels / 128);
+  const float tile_count = 128.0f * (float)(channels / groups);
+  gn_tiles_finalize_kernel<<<dim3(groups, batch), 256, 0, stream>>>(
+      tile_part, tiles, tile_count, channels, groups, gamma, beta, eps, coef, stats_out);
+  return cudaGetLastError();
+}
+
 cudaError_t gn_nhwc_apply_tiles_launch(int dtype, const void* x, void* y, const float* gamma,
                                        const float* beta, int batch, int channels,
                                        long long pixels, int groups, float eps, int silu,

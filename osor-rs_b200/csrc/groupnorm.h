@@ -84,6 +84,13 @@ cudaError_t gn_nhwc_apply_stats_launch(int dtype, const void* x, void* y, const 
                                        const float* beta, const float* part_stats, int parts,
                                        int batch, int channels, long long pixels, int groups,
                                        float eps, int silu, float* coef, cudaStream_t stream);
+// Finalize only: per-channel apply coefficients coef[b][c][4] = (mean,
+// rstd * gamma, beta, 0) from the per-tile partials a convolution's epilogue
+// wrote (pixels % 128 == 0), for a consumer that applies them itself.
+cudaError_t gn_tiles_coef_launch(const float* tile_part, int batch, int channels,
+                                 long long pixels, int groups, const float* gamma,
+                                 const float* beta, float eps, float* coef, float* stats_out,
+                                 cudaStream_t stream);
 cudaError_t gn_nhwc_apply_tiles_launch(int dtype, const void* x, void* y, const float* gamma,
                                        const float* beta, int batch, int channels,
                                        long long pixels, int groups, float eps, int silu,

@@ -21,6 +21,7 @@
 
 #include "attn_fa.h"
 #include "common.cuh"
+#include "conv_out.h"
 #include "conv_tc.h"
 #include "groupnorm.h"
 #include "ops.h"
@@ -149,7 +150,19 @@ class Loader {
     // 128 zero-padded weight rows: the pixel-N kernel reads a full M = 128
     // weight tile (zeros from memory stream faster than the TMA's
     // out-of-bounds fill), the 16-wide one-CTA tile the first 16.
-    return conv_from(w->data, b->data, cin, cout, k, 1, pad, L, 128);
+    s = conv_from(w->data, b->data, cin, cout, k, 1, pad, L, 128);
+    if (!s.good() || k != 3 || 9 * cout > 32) return s;
+    // Tap matrix of the fused GroupNorm + conv_out kernel: one row per
+    // (ky, kx, co), so a pixel's product with it is its contribution to the
+    // nine neighbouring outputs.
+    std::vector<uint16_t> wz((size_t)32 * cin, to_bits(0.0f, model_->dtype));
+    for (int ky = 0; ky < 3; ++ky)
+      for (int kx = 0; kx < 3; ++kx)
+        for (int co = 0; co < cout; ++co)
+          for (int ci = 0; ci < cin; ++ci)
+            wz[((size_t)(ky * 3 + kx) * cout + co) * cin + ci] =
+                to_bits(w->data[(((size_t)co * cin + ci) * 3 + ky) * 3 + kx], model_->dtype);
+    return upload(wz, &L->w_z);
   }
   // A thin-input convolution as a 64-column 1x1 layer: column j < k*k*cin
   // holds tap j / cin, channel j % cin (thin_columns_launch's order).
@@ -478,6 +491,17 @@ bool fused_attention_enabled() {
   static const bool on = [] {
     const char* v = getenv("OSOR_FUSED_ATTENTION");
     return v && v[0] == '1';
+  }();
+  return on;
+}
+
+// The fused conv_norm_out + conv_out kernel is the default; OSOR_FUSED_CONV_OUT=0
+// in the environment (read once) keeps the separate GroupNorm apply and
+// pixels-on-N convolution, for comparing.
+bool gn_conv_out_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("OSOR_FUSED_CONV_OUT");
+    return !(v && v[0] == '0');
   }();
   return on;
 }
@@ -930,6 +954,33 @@ Status vae_decode(const Vae& m, const float* latents, float* image, int batch, i
     }
   }
   const int ti = (xi + 1) % 4;
+  // conv_norm_out + SiLU + conv_out in one pass when the last conv left its
+  // tile statistics: finalize them into per-channel coefficients, then the
+  // fused kernel reads the activation once and writes the image.
+  GnConvOutArgs fa;
+  fa.dtype = m.dtype;
+  fa.x = b.act[xi];
+  fa.batch = batch;
+  fa.height = h;
+  fa.width = w;
+  fa.cin = d.norm_out.c;
+  fa.coef = static_cast<float*>(b.gn);
+  fa.silu = 1;
+  fa.wz = d.conv_out.w_z;
+  fa.bias = d.conv_out.bias;
+  fa.cout = d.conv_out.cout;
+  fa.out = image;
+  if (has_stats[xi] && d.conv_out.w_z && gn_conv_out_enabled() &&
+      gn_conv_out_check(fa) == nullptr) {
+    const double px = (double)batch * h * w;
+    OpScope scope("gn_conv_out", 2.0 * px * fa.cout * 9 * fa.cin,
+                  2.0 * px * fa.cin + 4.0 * px * fa.cout, stream, 2);
+    cudaError_t e = gn_tiles_coef_launch(b.tstat[xi], batch, fa.cin, (long long)h * w, kGroups,
+                                         d.norm_out.gamma, d.norm_out.beta, kEps,
+                                         static_cast<float*>(b.gn), nullptr, stream);
+    if (e == cudaSuccess) e = gn_conv_out_launch(fa, stream);
+    return cuda_status(e, "group norm + conv_out");
+  }
   return gn_conv(c, d.norm_out, true, d.conv_out, xi, ti, batch, h, w, -1, image, kLayoutNchwF32,
                  nullptr);
 }

@@ -35,6 +35,10 @@ struct ConvLayer {
   // convolutions on the low-res input, [4 * cout][2][2][cin] (see
   // ConvTcArgs::upsample); nullptr otherwise.
   const uint16_t* w_up = nullptr;
+  // For a thin 3x3 output (Cout <= 3): the per-pixel tap matrix of the fused
+  // GroupNorm + conv kernel, 16-bit [32][cin], row (ky * 3 + kx) * cout + co
+  // = w[co][ky][kx][:], rows past 9 * cout zero; nullptr otherwise.
+  const uint16_t* w_z = nullptr;
 };
 
 // A convolution whose input has few channels (the image or the latent): run
