@@ -375,8 +375,115 @@ def run_ops(args):
                           "frac_of_sustained_peak": round(tf / tflops_sus, 4),
                           "gpu_launches": launches, "peak_source": src,
                           "breakdown": breakdown}), flush=True)
+    elif args.op == "e2e":
+        run_e2e(args, dev, flush)
     if device_status(0) != 0:
         raise SystemExit("device status reported a kernel wait timeout")
+
+
+def run_e2e(args, dev, flush):
+    """The end-to-end inpainting call at the benchmark's end-to-end
+    configuration: Osor::infer (src/runtime.rs:484 -> Pipeline::run,
+    src/pipeline.rs:655-860) on a batch of 4 1024^2 images with a seeded
+    10-25 % rectangle mask, the reference's seeded_noise(42, 4, 1024, 1024)
+    generated on the GPU, the VAE encoder and decoder (random-init, seed 0),
+    and one SDXL inpainting UNet call at t = 400 (random-init, bf16, CUDA-graph
+    replay). Each step copies the image and mask in from pinned host memory
+    and the image and alpha back out. A separate profiled call records CUDA
+    events at the pipeline's stage observations (Osor::infer_profiled's
+    per-stage times, src/runtime.rs:514-540)."""
+    import torch
+    from osor_b200 import _lib, workloads
+    from osor_b200.model import NativeModel
+    from osor_b200.noise import seeded_noise
+    from osor_b200.pipeline import Pipeline
+    from osor_b200.unet import Architecture, NativeUnet, random_unet_weights, unet_flops
+    from osor_b200.weights import random_vae_weights
+    b, hgt, wid = BATCH, IMAGE, IMAGE
+    arch = Architecture.sdxl()
+    g = torch.Generator(device=dev).manual_seed(11)
+    uw = random_unet_weights(arch, seed=0, device=dev)
+    context = torch.randn((1, 77, arch.context), generator=g, device=dev)
+    pooled = torch.randn((1, arch.pooled), generator=g, device=dev)
+    unet = NativeUnet(uw, context, pooled, arch=arch, device=0, dtype=torch.bfloat16, graphs=True)
+    del uw
+    model = NativeModel(random_vae_weights(0), device=0, dtype=args.dtype)
+    pipe = Pipeline(model, unet)
+    image, mask = workloads.inpaint_job(b, hgt, wid, seed=5)
+    h_img = torch.from_numpy(image).pin_memory()
+    h_mask = torch.from_numpy(mask).pin_memory()
+    d_img = torch.empty(h_img.shape, dtype=torch.float32, device=dev)
+    d_mask = torch.empty(h_mask.shape, dtype=torch.float32, device=dev)
+    h_out = torch.empty((b, 3, hgt, wid), dtype=torch.float32).pin_memory()
+    h_alpha = torch.empty((b, 1, hgt, wid), dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+
+    def step(observer=None):
+        d_img.copy_(h_img, non_blocking=True)
+        d_mask.copy_(h_mask, non_blocking=True)
+        noise = seeded_noise(42, b, hgt, wid, device=dev)
+        res = pipe.run(d_img, d_mask, noise.posterior, noise.diffusion, observer=observer)
+        h_out.copy_(res.image, non_blocking=True)
+        h_alpha.copy_(res.alpha, non_blocking=True)
+        return res
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    launches0 = _lib.launch_count()
+    times = []
+    with ClockSampler(0) as clocks:
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            step()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+    launches = (_lib.launch_count() - launches0) // args.steps
+    ms = statistics.mean(times)
+    # Per-stage device time: an event at every stage observation.
+    marks = []
+
+    def observe(stage, tensor):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        marks.append((stage.name, ev))
+
+    flush.fill_(1)
+    start = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    step(observe)
+    end = torch.cuda.Event(enable_timing=True)
+    end.record(stream)
+    end.synchronize()
+    stages, prev = {}, start
+    for name, ev in marks:
+        stages[name] = round(prev.elapsed_time(ev), 3)
+        prev = ev
+    stages["host_copy_out"] = round(prev.elapsed_time(end), 3)
+    img = h_out.numpy()
+    if not (img.min() >= 0.0 and img.max() <= 1.0):
+        raise SystemExit("end-to-end image outside [0, 1]")
+    mpx = b * hgt * wid / 1e6
+    vae_tflop = (workloads.vae_decoder_flops(b, hgt // 8, wid // 8) + 19.52e12) / 1e12
+    print(json.dumps({
+        "op": "end-to-end inpainting (Osor::infer equivalent: encode, stages, one UNet step, "
+              "decode, display mapping)",
+        "shape": [b, 3, hgt, wid], "vae_dtype": args.dtype, "unet_dtype": "bf16",
+        "ms": round(ms, 2), "mpx_per_s": round(mpx / (ms / 1e3), 2),
+        "e2e": {"value": round(mpx / (ms / 1e3), 2), "unit": UNIT,
+                "h2d_bytes_per_step": int((h_img.numel() + h_mask.numel()) * 4),
+                "d2h_bytes_per_step": int((h_out.numel() + h_alpha.numel()) * 4)},
+        "algorithmic_tflop": {"vae": round(vae_tflop, 2),
+                              "unet": round(unet_flops(arch, b, hgt // 8, wid // 8) / 1e12, 2)},
+        "stages_ms_profiled_call": stages,
+        "config": {"mask": "one seeded rectangle per image, 10-25 % of the area (seed 5)",
+                   "noise": "seeded_noise(42, 4, 1024, 1024) on the GPU inside the step",
+                   "timestep": 400, "unet": "SDXL inpainting, random-init seed 0, CUDA graph "
+                   "replay", "l2": "512 MiB L2 flush between timed steps"},
+        "gpu_launches_per_step": int(launches), "clocks": clocks.summary()}), flush=True)
 
 
 def run_bands(args, rank, world, local):
@@ -538,8 +645,9 @@ def main():
     ap.add_argument("--dtype", default="f16", choices=["f16", "bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op", default="decode",
-                    choices=["decode", "conv3x3", "groupnorm", "encode", "noise", "unet"],
-                    help="decode: the headline line; others: standalone op lines")
+                    choices=["decode", "conv3x3", "groupnorm", "encode", "noise", "unet", "e2e"],
+                    help="decode: the headline line; others: standalone op lines; e2e: the "
+                         "end-to-end inpainting call at B=4, 1024^2")
     ap.add_argument("--shape", default=None, help="comma-separated shape for --op conv3x3/groupnorm")
     ap.add_argument("--bands", type=int, default=0,
                     help="row-band split: each group of BANDS ranks decodes one 1024^2 image "

@@ -377,11 +377,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int ky = 0; ky < 3; ++ky)
 #pragma unroll
             for (int c = 0; c < kCout; ++c) {
-              // Pixel x takes kx = 1 from itself, kx = 2 from x - 1 and kx = 0
-              // from x + 1 (the lanes beside it; the warp's edge lanes get the
-              // other warp's value after the barrier below).
-              const float left = __shfl_up_sync(0xffffffffu, z[(ky * 3 + 2) * kCout + c], 1);
-              const float right = __shfl_down_sync(0xffffffffu, z[(ky * 3 + 0) * kCout + c], 1);
+              // Output x reads input x + kx - 1: kx = 1 from its own pixel,
+              // kx = 0 from x - 1 and kx = 2 from x + 1 (the lanes beside it;
+              // the warp's edge lanes get the other warp's value after the
+              // barrier below).
+              const float left = __shfl_up_sync(0xffffffffu, z[(ky * 3 + 0) * kCout + c], 1);
+              const float right = __shfl_down_sync(0xffffffffu, z[(ky * 3 + 2) * kCout + c], 1);
               float h = z[(ky * 3 + 1) * kCout + c];
               if (lane > 0) h += left;
               if (lane < 31) h += right;
@@ -389,19 +390,19 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (ky == 1) acc_b[i][c] += h;
               if (ky == 0) acc_c[i][c] = h;
             }
-          if (lane == 31) {  // for the pixel to the right: this pixel's kx = 2 terms
+          if (lane == 31) {  // for the pixel to the right: this pixel's kx = 0 terms
             float* e = edge_out + ((0 * kMaxTiles + t) * 4 + quad) * 9;
 #pragma unroll
             for (int ky = 0; ky < 3; ++ky)
 #pragma unroll
-              for (int c = 0; c < kCout; ++c) e[ky * 3 + c] = z[(ky * 3 + 2) * kCout + c];
+              for (int c = 0; c < kCout; ++c) e[ky * 3 + c] = z[(ky * 3 + 0) * kCout + c];
           }
-          if (lane == 0) {  // for the pixel to the left: this pixel's kx = 0 terms
+          if (lane == 0) {  // for the pixel to the left: this pixel's kx = 2 terms
             float* e = edge_out + ((1 * kMaxTiles + t) * 4 + quad) * 9;
 #pragma unroll
             for (int ky = 0; ky < 3; ++ky)
 #pragma unroll
-              for (int c = 0; c < kCout; ++c) e[ky * 3 + c] = z[(ky * 3 + 0) * kCout + c];
+              for (int c = 0; c < kCout; ++c) e[ky * 3 + c] = z[(ky * 3 + 2) * kCout + c];
           }
         }
         if (valid) {

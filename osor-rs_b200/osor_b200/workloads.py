@@ -14,6 +14,11 @@ the parity tests, the golden fixtures and the benchmark see the same values.
   groupnorm_inputs  x ~ N(0.5, 2.0), gamma ~ N(1, 0.1), beta ~ N(0, 0.1), seed 3.
   conv_inputs       x ~ N(0, 1), w ~ N(0, sqrt(2 / (9 Cin))), bias ~ U(+-1/sqrt(Cin)),
                     residual ~ N(0, 1), seed 5.
+  inpaint_job       the end-to-end inpainting job: image [B, 3, H, W] uniform [0, 1]
+                    with the 9x9 box blur (display range, as Osor::infer takes it),
+                    and a binary mask [B, 1, H, W] holding one axis-aligned rectangle
+                    per image that covers 10-25 % of its area at a seeded position
+                    (seed 5); the noise comes from the reference's seeded_noise.
 """
 from __future__ import annotations
 
@@ -51,6 +56,24 @@ def encoder_image(batch: int = 4, h: int = 1024, w: int = 1024, seed: int = 7):
     img = box_blur_9(img)
     noise = rng.standard_normal((batch, 4, h // 8, w // 8), dtype=np.float32)
     return (img * 2.0 - 1.0).astype(np.float32), noise
+
+
+def inpaint_job(batch: int = 4, h: int = 1024, w: int = 1024, seed: int = 5):
+    """Returns (image in [0, 1], mask in {0, 1}) for Osor::infer
+    (src/runtime.rs:484; InferenceInput, src/pipeline.rs:139-157)."""
+    rng = _rng(seed)
+    img = box_blur_9(rng.random((batch, 3, h, w), dtype=np.float32))
+    img = np.clip(img, 0.0, 1.0).astype(np.float32)
+    mask = np.zeros((batch, 1, h, w), np.float32)
+    for b in range(batch):
+        area = rng.uniform(0.10, 0.25)
+        aspect = rng.uniform(0.5, 2.0)
+        rh = int(min(h, max(8, round(np.sqrt(area * h * w * aspect)))))
+        rw = int(min(w, max(8, round(area * h * w / rh))))
+        y0 = int(rng.integers(0, h - rh + 1))
+        x0 = int(rng.integers(0, w - rw + 1))
+        mask[b, 0, y0:y0 + rh, x0:x0 + rw] = 1.0
+    return img, mask
 
 
 def groupnorm_inputs(shape, seed: int = 3):
