@@ -24,11 +24,13 @@
 //
 // Each CTA (one per SM) owns a band of whole rows of one image (two segments
 // when its band crosses an image boundary) and reads the band plus one halo
-// row above and below. Roles (448 threads): warp 0 TMA producer, warp 1 TMEM
-// allocator and MMA issuer, warps 2..5 the GroupNorm transform, warps 6..13
-// the epilogue (warp w reads TMEM lane quadrant w % 4; warps 6..9 own tiles
-// 0..3 of the row and warps 10..13 tiles 4..7, one pixel per thread and tile). Two TMEM row buffers of 8 tiles x 32
-// columns let the MMAs of row yi + 1 run under the epilogue of row yi.
+// row above and below. Roles (576 threads): warp 0 TMA producer, warp 1 TMEM
+// allocator and MMA issuer, warps 2..9 the GroupNorm transform (the
+// elementwise work dominates: eight warps keep the schedulers issuing), warps
+// 10..17 the epilogue (warp w reads TMEM lane quadrant w % 4; warps 10..13 own
+// tiles 0..3 of the row and warps 14..17 tiles 4..7, one pixel per thread and
+// tile). Two TMEM row buffers of 8 tiles x 32 columns let the MMAs of row
+// yi + 1 run under the epilogue of row yi.
 #include <atomic>
 
 #include "common.cuh"
@@ -49,8 +51,8 @@ constexpr int kMaxTiles = 8;                     // width <= 1024
 constexpr int kRowCols = kMaxTiles * kN;         // TMEM columns per row buffer
 constexpr int kWBoxBytes = kN * 128;             // 32 weight rows x 64 channels (4 KB)
 constexpr int kFirstTransformWarp = 2;
-constexpr int kTransformWarps = 4;
-constexpr int kFirstEpiWarp = 6;
+constexpr int kTransformWarps = 8;
+constexpr int kFirstEpiWarp = 10;
 constexpr int kEpiWarps = 8;                     // two per TMEM lane quadrant
 constexpr int kEpiTiles = kMaxTiles / 2;         // tiles per epilogue warp
 constexpr int kThreads = 32 * (kFirstEpiWarp + kEpiWarps);
@@ -260,7 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kFirstTransformWarp && warp < kFirstTransformWarp + kTransformWarps) {
     // ------------------------------------------------------ GroupNorm transform
-    // Thread k handles 16-byte chunk position q = k % 8 of rows k / 8 + 16 m of
+    // Thread k handles 16-byte chunk position q = k % 8 of rows k / 8 + 32 m of
     // both boxes; with the 128-byte swizzle (chunk j of row r at position
     // j ^ (r % 8)) that position always holds logical chunk j, i.e. channels
     // box * 64 + j * 8 .. + 7, so the thread keeps 16 coefficient pairs.
@@ -300,8 +302,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int b = 0; b < 2; ++b) {
 #pragma unroll 4
-            for (int m = 0; m < kTilePx / 16; ++m) {
-              const int row = row0 + 16 * m;
+            for (int m = 0; m < kTilePx / 32; ++m) {
+              const int row = row0 + 32 * m;
               uint4* ptr = reinterpret_cast<uint4*>(sbuf + b * kBoxBytes + row * 128 + q * 16);
               if (row < valid_px) {
                 float f[8];
@@ -326,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kFirstEpiWarp) {
     // ------------------------------------------------------ epilogue
-    const int quad = warp & 3;  // TMEM lanes quad * 32 ..: warps 6..9 take quadrants 2, 3, 0, 1
+    const int quad = warp & 3;  // TMEM lanes quad * 32 ..: warps 10..13 take quadrants 2, 3, 0, 1
     const int t0 = ((warp - kFirstEpiWarp) >> 2) * kEpiTiles;  // this warp's first tile
     const float bias0 = __ldg(p.bias), bias1 = __ldg(p.bias + 1), bias2 = __ldg(p.bias + 2);
     // Output rows yi - 1, yi, yi + 1 for this thread's pixel of each tile.
@@ -361,49 +363,61 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < kEpiTiles; ++i) {
           const int t = t0 + i;
           if (t >= p.tiles) break;
-          float z[kN];
-          if (valid) {
-            uint32_t rv[kN];
-            tmem_load_32x32b_x32(
-                tmem_base + ((uint32_t)(quad * 32) << 16) + rb * kRowCols + t * kN, rv);
-            tmem_wait_ld();
-#pragma unroll
-            for (int n = 0; n < kN; ++n) z[n] = __uint_as_float(rv[n]);
-          } else {
-#pragma unroll
-            for (int n = 0; n < kN; ++n) z[n] = 0.0f;
-          }
-#pragma unroll
-          for (int ky = 0; ky < 3; ++ky)
+          // One tap row (ky) of this pixel: z9[kx * 3 + co].
+          float* e_right = edge_out + ((0 * kMaxTiles + t) * 4 + quad) * 9;
+          float* e_left = edge_out + ((1 * kMaxTiles + t) * 4 + quad) * 9;
+          auto tap_row = [&](const float (&z9)[9], int ky) {
 #pragma unroll
             for (int c = 0; c < kCout; ++c) {
               // Output x reads input x + kx - 1: kx = 1 from its own pixel,
               // kx = 0 from x - 1 and kx = 2 from x + 1 (the lanes beside it;
               // the warp's edge lanes get the other warp's value after the
               // barrier below).
-              const float left = __shfl_up_sync(0xffffffffu, z[(ky * 3 + 0) * kCout + c], 1);
-              const float right = __shfl_down_sync(0xffffffffu, z[(ky * 3 + 2) * kCout + c], 1);
-              float h = z[(ky * 3 + 1) * kCout + c];
+              const float left = __shfl_up_sync(0xffffffffu, z9[0 * kCout + c], 1);
+              const float right = __shfl_down_sync(0xffffffffu, z9[2 * kCout + c], 1);
+              float h = z9[1 * kCout + c];
               if (lane > 0) h += left;
               if (lane < 31) h += right;
               if (ky == 2) acc_a[i][c] += h;
               if (ky == 1) acc_b[i][c] += h;
               if (ky == 0) acc_c[i][c] = h;
+              // For the pixel to the right (lane 31): this pixel's kx = 0
+              // term; for the pixel to the left (lane 0): its kx = 2 term.
+              if (lane == 31) e_right[ky * 3 + c] = z9[0 * kCout + c];
+              if (lane == 0) e_left[ky * 3 + c] = z9[2 * kCout + c];
             }
-          if (lane == 31) {  // for the pixel to the right: this pixel's kx = 0 terms
-            float* e = edge_out + ((0 * kMaxTiles + t) * 4 + quad) * 9;
+          };
+          // Columns 0..15 hold tap row 0 and most of row 1, columns 16..31
+          // the rest of row 1 and row 2: two 16-column loads keep fewer
+          // registers live than one of 32.
+          float z0[9], z1[9], z2[9];
+          uint32_t rv[16];
+          const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + rb * kRowCols + t * kN;
+          if (valid) {
+            tmem_load_32x32b_x16(taddr, rv);
+            tmem_wait_ld();
+          } else {
 #pragma unroll
-            for (int ky = 0; ky < 3; ++ky)
-#pragma unroll
-              for (int c = 0; c < kCout; ++c) e[ky * 3 + c] = z[(ky * 3 + 0) * kCout + c];
+            for (int n = 0; n < 16; ++n) rv[n] = 0u;
           }
-          if (lane == 0) {  // for the pixel to the left: this pixel's kx = 2 terms
-            float* e = edge_out + ((1 * kMaxTiles + t) * 4 + quad) * 9;
 #pragma unroll
-            for (int ky = 0; ky < 3; ++ky)
+          for (int n = 0; n < 9; ++n) z0[n] = __uint_as_float(rv[n]);
 #pragma unroll
-              for (int c = 0; c < kCout; ++c) e[ky * 3 + c] = z[(ky * 3 + 2) * kCout + c];
+          for (int n = 0; n < 7; ++n) z1[n] = __uint_as_float(rv[9 + n]);
+          tap_row(z0, 0);
+          if (valid) {
+            tmem_load_32x32b_x16(taddr + 16, rv);
+            tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int n = 0; n < 16; ++n) rv[n] = 0u;
           }
+          z1[7] = __uint_as_float(rv[0]);
+          z1[8] = __uint_as_float(rv[1]);
+#pragma unroll
+          for (int n = 0; n < 9; ++n) z2[n] = __uint_as_float(rv[2 + n]);
+          tap_row(z1, 1);
+          tap_row(z2, 2);
         }
         if (valid) {
           tc_fence_before();
