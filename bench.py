@@ -200,9 +200,10 @@ def run_reference(args, rank, world):
 
 
 # DRAM bytes (read + write) per 3x3 convolution launch of the decode for one
-# image, averaged over its 28 launches, from one ncu capture of the batch-1
-# decode; every layer is per image, so a launch over B images moves B times this.
-CONV3X3_DRAM_BYTES_PER_IMAGE = 253.13e6
+# image, averaged over its 28 launches, from one ncu capture of the conv
+# kernels of a batch-1 decode (7108 MB over 28 launches); every layer is per
+# image, so a launch over B images moves B times this.
+CONV3X3_DRAM_BYTES_PER_IMAGE = 253.9e6
 
 CONV_SHAPES = [(4, 512, 512, 128, 128), (4, 512, 512, 256, 256), (4, 256, 256, 512, 512),
                (4, 128, 128, 1024, 1024), (1, 128, 3, 1024, 1024)]
