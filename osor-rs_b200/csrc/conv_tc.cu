@@ -672,8 +672,9 @@ int conv_tc_softmax_block(int cout) {
 
 cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
   // 3x3 layers with Cout <= 128 on rows of 256 pixels run with the pixels on
-  // the MMA's N side (conv_tcn.cu); other Cout = 128 layers on CTA pairs
-  // (conv_tc2.cu).
+  // the MMA's N side (conv_tcn.cu); other layers with Cout 128 or a multiple
+  // of 256 on CTA pairs (conv_tc2.cu); the rest (upsample phases, softmax
+  // passes, odd tile counts) here.
   if (tcn_enabled() && conv_tcn_check(a) == nullptr) return conv_tcn_launch(a, stream);
   if (pair_enabled() && conv_tc2_check(a) == nullptr) return conv_tc2_launch(a, stream);
   EncodeTiledFn encode = encode_fn();

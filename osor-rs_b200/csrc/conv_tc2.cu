@@ -1,12 +1,15 @@
-// Implicit-GEMM convolution for Cout = 128 on CTA pairs (2-SM tcgen05 MMA).
+// Implicit-GEMM convolution on CTA pairs (2-SM tcgen05 MMA), N = BN output
+// channels per pair tile: BN = 128 for Cout = 128, BN = 256 for Cout a
+// multiple of 256 (Cout / 256 channel tiles).
 //
-// With Cout = 128 the one-CTA kernel (conv_tc.cu) re-fetches the whole weight
-// matrix for every 128-pixel tile and its 128x128 MMAs read both operands
-// from one SM's shared memory; on the 1024^2 VAE layers that leaves the
-// tensor pipe under half busy. Here two CTAs of a cluster cooperate on 256
-// pixels: `tcgen05.mma.cta_group::2` with M = 256, N = 128 takes A rows
-// 0..127 from the even CTA and 128..255 from the odd one, and B rows
-// (output channels) 0..63 / 64..127 likewise, so each SM holds only half of
+// The one-CTA kernel (conv_tc.cu) re-fetches the whole weight matrix for
+// every 128-pixel tile and reads both MMA operands from one SM's shared
+// memory: per 128 x 256 x 16 instruction that is 12 KB of operand reads plus
+// the stage's TMA writes, more than shared memory delivers at the tensor
+// core's rate. Here two CTAs of a cluster cooperate on 256 pixels:
+// `tcgen05.mma.cta_group::2` with M = 256, N = BN takes A rows 0..127 from
+// the even CTA and 128..255 from the odd one, and B rows (output channels)
+// 0..BN/2-1 / BN/2..BN-1 likewise, so each SM reads and stores only half of
 // the weights. When that half fits (K <= 1152) it is loaded once per CTA and
 // stays resident in shared memory for every tile the pair computes, and the
 // pipeline stages carry only the A (input) tiles; otherwise each stage also
@@ -17,9 +20,9 @@
 // the three horizontal taps read it as views starting one pixel (one 128-byte
 // swizzle row) apart, so a tile loads 3 * Cin / 64 stages instead of 9 *.
 //
-// Roles per CTA (320 threads): warp 0 TMA producer, warp 1 TMEM allocator
-// (both CTAs) and MMA issuer (even CTA only), warps 2..9 epilogue (two per
-// TMEM lane quadrant, 64 columns each). The even CTA's barriers gate the
+// Roles per CTA (576 threads): warp 0 TMA producer, warp 1 TMEM allocator
+// (both CTAs) and MMA issuer (even CTA only), warps 2..17 epilogue (four per
+// TMEM lane quadrant, BN / 4 columns each, in 32-column chunks). The even CTA's barriers gate the
 // MMAs: both CTAs' TMA loads complete on them, the MMA commits arrive on both
 // CTAs' barriers (multicast commit), and both CTAs' epilogues release the
 // accumulators on the even CTA's barrier. No TMA load uses cluster multicast.
@@ -37,14 +40,12 @@ namespace osor {
 namespace {
 
 constexpr int kM = 128;           // pixels per CTA
-constexpr int kN = 128;           // output channels of the pair
 constexpr int kBK = 64;           // K block (one 128-byte swizzle row)
 constexpr int kEpiWarps = 16;     // four per TMEM lane quadrant, 32 columns each
 constexpr int kThreads2 = 64 + 32 * kEpiWarps;
 constexpr int kAB = kM * kBK * 2;            // A tile bytes (16 KB)
 constexpr int kShiftRows = kM + 2;           // row-shift stage: 130 pixels
 constexpr int kShiftAB = 17 * 1024;          // row-shift A bytes in a stage (>= 130 x 128 B)
-constexpr int kBB = (kN / 2) * kBK * 2;      // B bytes per K block per CTA (8 KB)
 constexpr int kMaxStages = 12;
 constexpr int kMaxResidentKBlocks = 18;      // resident weights: K <= 1152
 constexpr int kStat2 = 2 * 4 * 64 * 2 * 4;  // per accumulator: [quad][group](mean, M2)
@@ -52,8 +53,15 @@ constexpr int kTail2 = 256;                  // barriers, TMEM address, abort fl
 constexpr int kSmem2 = 225 * 1024;
 constexpr int kSmemBudget = kSmem2 - 1024 - kTail2 - kStat2;  // stages + resident weights
 
+// B bytes per K block per CTA: BN / 2 weight rows of 64 channels.
+template <int BN>
+__host__ __device__ constexpr int b_block_bytes() {
+  return (BN / 2) * kBK * 2;
+}
+
 struct Tc2Params {
   int num_m_tiles;         // even
+  int n_tiles;             // Cout / BN
   int k_blocks, c_blocks;
   int ksize, stride, pad;
   int tiles_x, tiles_y, tile_w, tile_h;
@@ -94,10 +102,11 @@ __device__ __forceinline__ bool chunk_all(int bar, bool ok) {
   return r != 0;
 }
 
-template <int D, int CPG>
+template <int BN, int D, int CPG>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
     conv_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, const Tc2Params p) {
+  constexpr int kBB = b_block_bytes<BN>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -134,7 +143,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
     fence_mbarrier_init();
   }
   if (warp == 1) {
-    tmem_alloc_pair(tmem_holder, 2 * kN);
+    tmem_alloc_pair(tmem_holder, 2 * BN);
     tmem_relinquish_pair();
   }
   tc_fence_before();
@@ -142,7 +151,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
-  const int pairs = p.num_m_tiles / 2;
+  // Pair tiles: (256-pixel pair of m tiles, channel tile), channel tile inner
+  // so that clusters running together share input rows in L2.
+  const int pairs = p.num_m_tiles / 2 * p.n_tiles;
   const int cluster_id = blockIdx.x >> 1;
   const int clusters = gridDim.x >> 1;
   const int tiles_per_image = p.tiles_x * p.tiles_y;
@@ -155,13 +166,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
         if (leader) mbar_arrive_expect_tx(bfull, 2u * p.k_blocks * kBB);
         for (int kb = 0; kb < p.k_blocks; ++kb)
           tma_load_2d_pair(smem_b + kb * kBB, &tmap_b, map_to_rank(smem_u32(bfull), 0), kb * kBK,
-                           (int)rank * (kN / 2));
+                           (int)rank * (BN / 2));
       }
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       for (int pt = cluster_id; pt < pairs && ok; pt += clusters) {
-        const int m_tile = 2 * pt + (int)rank;
+        const int n_tile = pt % p.n_tiles;
+        const int m_tile = 2 * (pt / p.n_tiles) + (int)rank;
+        const int b_row = n_tile * BN + (int)rank * (BN / 2);
         const int img = m_tile / tiles_per_image;
         const int rem = m_tile - img * tiles_per_image;
         const int ty = rem / p.tiles_x;
@@ -194,8 +207,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
             const int taps = p.row_shift ? 3 : 1;
             for (int t = 0; t < taps; ++t) {
               const int kb = p.row_shift ? (ky * 3 + t) * p.c_blocks + cb : u;
-              tma_load_2d_pair(st + p.a_bytes + t * kBB, &tmap_b, bar, kb * kBK,
-                               (int)rank * (kN / 2));
+              tma_load_2d_pair(st + p.a_bytes + t * kBB, &tmap_b, bar, kb * kBK, b_row);
             }
           }
           if (++stage == p.stages) {
@@ -208,7 +220,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // ------------------------------------------------------------ MMA issuer
-      constexpr uint32_t idesc = umma_idesc_f32acc(2 * kM, kN, Elem<D>::kUmmaFormat);
+      constexpr uint32_t idesc = umma_idesc_f32acc(2 * kM, BN, Elem<D>::kUmmaFormat);
       bool ok = !p.b_resident || mbar_wait(bfull, 0, abort_flag);
       bool issued = false;
       int stage = 0;
@@ -221,7 +233,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * kN;
+        const uint32_t d_tmem = tmem_base + acc * BN;
         for (int u = 0; u < p.units; ++u) {
           if (!mbar_wait(&full[stage], phase, abort_flag)) {
             ok = false;
@@ -277,97 +289,116 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Warp (quad, slot) owns 32-column chunks slot, slot + 4, ... of the BN
+    // accumulator columns (BN / 128 chunks).
+    constexpr int kChunks = BN / 128;
     const int quad = warp & 3;           // TMEM lanes quad*32 .. quad*32+31
-    const int chunk = (warp - 2) >> 2;   // columns chunk*32 .. +31
-    const int cbar = 2 + chunk;
+    const int slot = (warp - 2) >> 2;    // 0..3
+    const int cbar = 2 + slot;
     const int row = quad * 32 + lane;
     const uint32_t tempty_leader[2] = {map_to_rank(smem_u32(&tempty[0]), 0),
                                        map_to_rank(smem_u32(&tempty[1]), 0)};
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int pt = cluster_id; pt < pairs; pt += clusters) {
-      const int m_tile = 2 * pt + (int)rank;
+      const int n_tile = pt % p.n_tiles;
+      const int m_tile = 2 * (pt / p.n_tiles) + (int)rank;
       const long long m = (long long)m_tile * kM + row;
-      // The residual does not depend on the accumulator: start its loads
-      // before waiting for the MMAs.
+      // The residual does not depend on the accumulator: start the first
+      // chunk's loads before waiting for the MMAs.
       uint4 res[4];
       if (p.residual) {
         const uint4* r4 = reinterpret_cast<const uint4*>(
-            static_cast<const uint16_t*>(p.residual) + m * p.ld_res + chunk * 32);
+            static_cast<const uint16_t*>(p.residual) + m * p.ld_res + n_tile * BN + slot * 32);
 #pragma unroll
         for (int j = 0; j < 4; ++j) res[j] = __ldg(r4 + j);
       }
       if (!chunk_all(cbar, mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;
       tc_fence_after();
       const float scale = p.row_scale ? __ldg(p.row_scale + m) : 1.0f;
-      uint32_t r[32];
-      tmem_load_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * kN + chunk * 32, r);
-      tmem_wait_ld();
-      // This warp's part of the accumulator is in registers: release it on
-      // the even CTA so the next tile's MMAs can start.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
-      const int n0 = chunk * 32;
-      float v[32];
-      if (p.bias) {
-        const float4* b4 = reinterpret_cast<const float4*>(p.bias + n0);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float4 b = __ldg(b4 + j);
-          v[4 * j + 0] = fmaf(__uint_as_float(r[4 * j + 0]), scale, b.x);
-          v[4 * j + 1] = fmaf(__uint_as_float(r[4 * j + 1]), scale, b.y);
-          v[4 * j + 2] = fmaf(__uint_as_float(r[4 * j + 2]), scale, b.z);
-          v[4 * j + 3] = fmaf(__uint_as_float(r[4 * j + 3]), scale, b.w);
+#pragma unroll 1
+      for (int ci = 0; ci < kChunks; ++ci) {
+        const int chunk = slot + 4 * ci;
+        uint32_t r[32];
+        tmem_load_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + chunk * 32,
+                             r);
+        tmem_wait_ld();
+        if (ci == kChunks - 1) {
+          // This warp's part of the accumulator is in registers: release it
+          // on the even CTA so the next tile's MMAs can start.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
         }
-      } else {
+        const int n0 = n_tile * BN + chunk * 32;
+        float v[32];
+        if (p.bias) {
+          const float4* b4 = reinterpret_cast<const float4*>(p.bias + n0);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * scale;
-      }
-      if (p.residual) {
+          for (int j = 0; j < 8; ++j) {
+            const float4 b = __ldg(b4 + j);
+            v[4 * j + 0] = fmaf(__uint_as_float(r[4 * j + 0]), scale, b.x);
+            v[4 * j + 1] = fmaf(__uint_as_float(r[4 * j + 1]), scale, b.y);
+            v[4 * j + 2] = fmaf(__uint_as_float(r[4 * j + 2]), scale, b.z);
+            v[4 * j + 3] = fmaf(__uint_as_float(r[4 * j + 3]), scale, b.w);
+          }
+        } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float f[8];
-          unpack8<D>(res[j], f);
-#pragma unroll
-          for (int t = 0; t < 8; ++t) v[8 * j + t] += f[t];
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * scale;
         }
-      }
-      uint4* o4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + m * p.ld_out + n0);
-      uint32_t pk[16];
+        if (p.residual) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) pk[j] = Elem<D>::pack(v[2 * j], v[2 * j + 1]);
+          for (int j = 0; j < 4; ++j) {
+            float f[8];
+            unpack8<D>(res[j], f);
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        o4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-      if constexpr (CPG > 0) {
-        // Statistics of the stored (rounded) values.
+            for (int t = 0; t < 8; ++t) v[8 * j + t] += f[t];
+          }
+          if (ci + 1 < kChunks) {
+            const uint4* r4 = reinterpret_cast<const uint4*>(
+                static_cast<const uint16_t*>(p.residual) + m * p.ld_res + n0 + 4 * 32);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float2 f = Elem<D>::unpack(pk[j]);
-          v[2 * j] = f.x;
-          v[2 * j + 1] = f.y;
+            for (int j = 0; j < 4; ++j) res[j] = __ldg(r4 + j);
+          }
         }
-        // Per-quadrant statistics into this accumulator's half of stat_smem;
-        // the chunk's first warp merges the four quadrants. The halves
-        // alternate with the accumulators, and a warp reaches tile i + 2's
-        // writes only after the merging warp has passed tile i + 1's
-        // barrier, i.e. finished reading tile i's half.
-        constexpr int G = 32 / CPG;
-        float* st = stat_smem + acc * (4 * 64 * 2);
-        gn_chunk_stats<CPG>(v, lane, st + (quad * 64 + chunk * G) * 2);
-        chunk_sync(cbar);
-        if (((warp - 2) & 3) == 0 && lane < G) {
-          const int g = chunk * G + lane;
-          const float n = 32.0f * CPG;
-          float ma = st[(0 * 64 + g) * 2], qa = st[(0 * 64 + g) * 2 + 1];
-          float mb = st[(2 * 64 + g) * 2], qb = st[(2 * 64 + g) * 2 + 1];
-          merge_equal_counts(ma, qa, st[(1 * 64 + g) * 2], st[(1 * 64 + g) * 2 + 1], n);
-          merge_equal_counts(mb, qb, st[(3 * 64 + g) * 2], st[(3 * 64 + g) * 2 + 1], n);
-          merge_equal_counts(ma, qa, mb, qb, 2.0f * n);
-          float* dst = p.gn_part + ((long long)m_tile * p.gn_groups + g) * 2;
-          dst[0] = ma;
-          dst[1] = qa;
+        uint4* o4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + m * p.ld_out + n0);
+        uint32_t pk[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) pk[j] = Elem<D>::pack(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          o4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+        if constexpr (CPG > 0) {
+          // Statistics of the stored (rounded) values.
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float2 f = Elem<D>::unpack(pk[j]);
+            v[2 * j] = f.x;
+            v[2 * j + 1] = f.y;
+          }
+          // Per-quadrant statistics into this accumulator's half of
+          // stat_smem; the slot's first warp merges the four quadrants. The
+          // halves alternate with the accumulators, and a warp reaches tile
+          // i + 2's writes only after the merging warp has passed tile i + 1's
+          // barriers, i.e. finished reading tile i's half. Within a tile the
+          // chunks of one slot use disjoint groups.
+          constexpr int G = 32 / CPG;
+          float* st = stat_smem + acc * (4 * 64 * 2);
+          gn_chunk_stats<CPG>(v, lane, st + (quad * 64 + chunk * G) * 2);
+          chunk_sync(cbar);
+          if (quad == 0 && lane < G) {
+            const int g = chunk * G + lane;
+            const float n = 32.0f * CPG;
+            float ma = st[(0 * 64 + g) * 2], qa = st[(0 * 64 + g) * 2 + 1];
+            float mb = st[(2 * 64 + g) * 2], qb = st[(2 * 64 + g) * 2 + 1];
+            merge_equal_counts(ma, qa, st[(1 * 64 + g) * 2], st[(1 * 64 + g) * 2 + 1], n);
+            merge_equal_counts(mb, qb, st[(3 * 64 + g) * 2], st[(3 * 64 + g) * 2 + 1], n);
+            merge_equal_counts(ma, qa, mb, qb, 2.0f * n);
+            float* dst =
+                p.gn_part + ((long long)m_tile * p.gn_groups + n_tile * (BN / CPG) + g) * 2;
+            dst[0] = ma;
+            dst[1] = qa;
+          }
         }
       }
       if (++acc == 2) {
@@ -382,7 +413,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
   cluster_sync();  // neither CTA leaves while the pair's MMAs or arrivals are pending
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc_pair(tmem_base, 2 * kN);
+    tmem_dealloc_pair(tmem_base, 2 * BN);
   }
 }
 
@@ -404,7 +435,7 @@ EncodeTiledFn2 encode_fn2() {
   return fn;
 }
 
-template <int D, int CPG>
+template <int BN, int D, int CPG>
 cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Params& p,
                     cudaStream_t stream) {
   // Per device: the shared-memory opt-in and how many pairs fit on the GPU at
@@ -416,7 +447,7 @@ cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Param
   cudaGetDevice(&device);
   if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
   if (resident_pairs[device] == 0) {
-    cudaError_t e = cudaFuncSetAttribute(conv_tc2_kernel<D, CPG>,
+    cudaError_t e = cudaFuncSetAttribute(conv_tc2_kernel<BN, D, CPG>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2);
     if (e != cudaSuccess) return e;
     int sms = 148;
@@ -427,15 +458,15 @@ cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Param
     cfg.dynamicSmemBytes = kSmem2;
     cfg.stream = stream;
     int n = 0;
-    e = cudaOccupancyMaxActiveClusters(&n, conv_tc2_kernel<D, CPG>, &cfg);
+    e = cudaOccupancyMaxActiveClusters(&n, conv_tc2_kernel<BN, D, CPG>, &cfg);
     if (e != cudaSuccess) return e;
     if (n <= 0) return cudaErrorNotSupported;
     resident_pairs[device] = n < sms / 2 ? n : sms / 2;
   }
-  const int pairs = p.num_m_tiles / 2;
+  const int pairs = p.num_m_tiles / 2 * p.n_tiles;
   int clusters = resident_pairs[device];
   if (clusters > pairs) clusters = pairs;
-  conv_tc2_kernel<D, CPG><<<2 * clusters, kThreads2, kSmem2, stream>>>(ta, tb, p);
+  conv_tc2_kernel<BN, D, CPG><<<2 * clusters, kThreads2, kSmem2, stream>>>(ta, tb, p);
   return cudaGetLastError();
 }
 
@@ -444,7 +475,8 @@ cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Param
 const char* conv_tc2_check(const ConvTcArgs& a) {
   if (a.upsample || a.out_nchw || a.out_f32 || a.softmax_stats || a.softmax_max)
     return "pair kernel: plain 16-bit output only";
-  if (a.cout != kN) return "pair kernel: Cout must be 128";
+  if (a.cout != 128 && (a.cout <= 0 || a.cout % 256 != 0))
+    return "pair kernel: Cout 128 or a multiple of 256";
   if (a.ksize != 1 && a.ksize != 3) return "pair kernel: 1x1 or 3x3";
   if (a.stride != 1 && a.stride != 2) return "pair kernel: stride 1 or 2";
   if (a.cin <= 0 || a.cin % kBK != 0) return "pair kernel: Cin % 64";
@@ -469,7 +501,11 @@ const char* conv_tc2_check(const ConvTcArgs& a) {
   return nullptr;
 }
 
-cudaError_t conv_tc2_launch(const ConvTcArgs& a, cudaStream_t stream) {
+namespace {
+
+template <int BN>
+cudaError_t conv_tc2_launch_bn(const ConvTcArgs& a, cudaStream_t stream) {
+  constexpr int kBB = b_block_bytes<BN>();
   EncodeTiledFn2 encode = encode_fn2();
   if (!encode) return cudaErrorNotSupported;
   const int tile_w = a.out_w >= kM ? kM : a.out_w;
@@ -498,9 +534,9 @@ cudaError_t conv_tc2_launch(const ConvTcArgs& a, cudaStream_t stream) {
   }
   {
     const int k_total = a.ksize * a.ksize * a.cin;
-    cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)kN};
+    cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)a.cout};
     cuuint64_t strides[1] = {(cuuint64_t)a.ldw * 2};
-    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)(kN / 2)};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)(BN / 2)};
     cuuint32_t estr[2] = {1, 1};
     if (encode(&tb, tdt, 2, const_cast<void*>(a.w), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -513,6 +549,7 @@ cudaError_t conv_tc2_launch(const ConvTcArgs& a, cudaStream_t stream) {
   p.tiles_x = a.out_w / tile_w;
   p.tiles_y = a.out_h / tile_h;
   p.num_m_tiles = a.batch * p.tiles_x * p.tiles_y;
+  p.n_tiles = a.cout / BN;
   p.c_blocks = a.cin / kBK;
   p.k_blocks = a.ksize * a.ksize * p.c_blocks;
   p.ksize = a.ksize;
@@ -520,7 +557,9 @@ cudaError_t conv_tc2_launch(const ConvTcArgs& a, cudaStream_t stream) {
   p.pad = a.pad;
   p.row_shift = row_shift ? 1 : 0;
   p.units = row_shift ? 3 * p.c_blocks : p.k_blocks;
-  p.b_resident = p.k_blocks <= kMaxResidentKBlocks ? 1 : 0;
+  // The weight half stays resident when one channel tile's K blocks fit
+  // (Cout 128, K <= 1152); otherwise each stage carries its weight slices.
+  p.b_resident = (p.n_tiles == 1 && p.k_blocks * kBB <= kMaxResidentKBlocks * 8 * 1024) ? 1 : 0;
   p.a_bytes = row_shift ? kShiftAB : kAB;
   p.a_tx = row_shift ? kShiftRows * kBK * 2 : kAB;
   p.b_tx = p.b_resident ? 0 : (row_shift ? 3 : 1) * kBB;
@@ -537,21 +576,28 @@ cudaError_t conv_tc2_launch(const ConvTcArgs& a, cudaStream_t stream) {
   p.row_scale = a.row_scale;
   const int cpg = a.gn_part ? a.gn_cpg : 0;
   p.gn_part = a.gn_part;
-  p.gn_groups = cpg ? kN / cpg : 0;
+  p.gn_groups = cpg ? a.cout / cpg : 0;
   if (a.dtype == kF16) {
     switch (cpg) {
-      case 4: return launch2<kF16, 4>(ta, tb, p, stream);
-      case 8: return launch2<kF16, 8>(ta, tb, p, stream);
-      case 16: return launch2<kF16, 16>(ta, tb, p, stream);
-      default: return launch2<kF16, 0>(ta, tb, p, stream);
+      case 4: return launch2<BN, kF16, 4>(ta, tb, p, stream);
+      case 8: return launch2<BN, kF16, 8>(ta, tb, p, stream);
+      case 16: return launch2<BN, kF16, 16>(ta, tb, p, stream);
+      default: return launch2<BN, kF16, 0>(ta, tb, p, stream);
     }
   }
   switch (cpg) {
-    case 4: return launch2<kBf16, 4>(ta, tb, p, stream);
-    case 8: return launch2<kBf16, 8>(ta, tb, p, stream);
-    case 16: return launch2<kBf16, 16>(ta, tb, p, stream);
-    default: return launch2<kBf16, 0>(ta, tb, p, stream);
+    case 4: return launch2<BN, kBf16, 4>(ta, tb, p, stream);
+    case 8: return launch2<BN, kBf16, 8>(ta, tb, p, stream);
+    case 16: return launch2<BN, kBf16, 16>(ta, tb, p, stream);
+    default: return launch2<BN, kBf16, 0>(ta, tb, p, stream);
   }
+}
+
+}  // namespace
+
+cudaError_t conv_tc2_launch(const ConvTcArgs& a, cudaStream_t stream) {
+  if (a.cout == 128) return conv_tc2_launch_bn<128>(a, stream);
+  return conv_tc2_launch_bn<256>(a, stream);
 }
 
 }  // namespace osor
