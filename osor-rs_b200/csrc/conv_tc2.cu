@@ -15,10 +15,16 @@
 // pipeline stages carry only the A (input) tiles; otherwise each stage also
 // carries the weight slices it needs.
 //
-// Row-shift mode (3x3, stride 1, tiles of one 128-pixel output row): a stage
-// holds 130 consecutive input pixels of one input row and channel block, and
-// the three horizontal taps read it as views starting one pixel (one 128-byte
-// swizzle row) apart, so a tile loads 3 * Cin / 64 stages instead of 9 *.
+// Row-shift mode (3x3, or the 2x2 upsample phases, stride 1, tiles of one
+// 128-pixel output row): a stage holds 130 consecutive input pixels of one
+// input row and channel block, and the ksize horizontal taps read it as views
+// starting one pixel (one 128-byte swizzle row) apart, so a tile loads
+// ksize * Cin / 64 stages instead of ksize^2 * Cin / 64.
+//
+// Fused nearest-2x upsample + 3x3 conv: as in conv_tc.cu, four 2x2 phase
+// convolutions of the low-res input (4/9 of the FLOPs); each pair tile is one
+// (m pair, phase, channel tile), and the epilogue stores low-res pixel
+// (i, j)'s result at high-res pixel (2i + a, 2j + b) of phase (a, b).
 //
 // Roles per CTA (576 threads): warp 0 TMA producer, warp 1 TMEM allocator
 // (both CTAs) and MMA issuer (even CTA only), warps 2..17 epilogue (four per
@@ -66,6 +72,14 @@ struct Tc2Params {
   int ksize, stride, pad;
   int tiles_x, tiles_y, tile_w, tile_h;
   int row_shift;           // 1: row-shift stages (see above)
+  // Fused nearest-2x upsample (phases == 4, ksize 2): the tile grid runs over
+  // the low_h x low_w input and every tile is computed for the four output
+  // phases (a, b) with weight rows [phase * cout_total, ...): pair tiles are
+  // (m pair, phase, channel tile), and each low-res pixel's result lands on
+  // high-res pixel (2i + a, 2j + b). phases == 1: plain convolution.
+  int phases;
+  int low_h, low_w;
+  int cout_total;
   int units;               // stages per tile: k_blocks, or 3 * c_blocks in row-shift mode
   int b_resident;          // 1: weight half loaded once; 0: streamed with each stage
   int stages;              // pipeline depth (<= kMaxStages)
@@ -153,7 +167,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
 
   // Pair tiles: (256-pixel pair of m tiles, channel tile), channel tile inner
   // so that clusters running together share input rows in L2.
-  const int pairs = p.num_m_tiles / 2 * p.n_tiles;
+  const int pairs = p.num_m_tiles / 2 * p.phases * p.n_tiles;
   const int cluster_id = blockIdx.x >> 1;
   const int clusters = gridDim.x >> 1;
   const int tiles_per_image = p.tiles_x * p.tiles_y;
@@ -173,14 +187,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
       bool ok = true;
       for (int pt = cluster_id; pt < pairs && ok; pt += clusters) {
         const int n_tile = pt % p.n_tiles;
-        const int m_tile = 2 * (pt / p.n_tiles) + (int)rank;
-        const int b_row = n_tile * BN + (int)rank * (BN / 2);
+        const int rest = pt / p.n_tiles;
+        const int ph = rest % p.phases;
+        const int m_tile = 2 * (rest / p.phases) + (int)rank;
+        const int b_row = ph * p.cout_total + n_tile * BN + (int)rank * (BN / 2);
         const int img = m_tile / tiles_per_image;
         const int rem = m_tile - img * tiles_per_image;
         const int ty = rem / p.tiles_x;
         const int tx = rem - ty * p.tiles_x;
-        const int ox = tx * p.tile_w * p.stride - p.pad;
-        const int oy = ty * p.tile_h * p.stride - p.pad;
+        // Upsample phase (a, b) = (ph >> 1, ph & 1): a 2x2 conv on the
+        // low-res input starting one row / column up-left for a / b = 0.
+        const int pad_y = p.phases == 4 ? 1 - (ph >> 1) : p.pad;
+        const int pad_x = p.phases == 4 ? 1 - (ph & 1) : p.pad;
+        const int ox = tx * p.tile_w * p.stride - pad_x;
+        const int oy = ty * p.tile_h * p.stride - pad_y;
         for (int u = 0; u < p.units; ++u) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
             ok = false;
@@ -202,11 +222,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
           if (leader) mbar_arrive_expect_tx(&full[stage], 2u * (p.a_tx + p.b_tx));
           tma_load_4d_pair(st, &tmap_a, bar, cb * kBK, ox + kx, oy + ky, img);
           if (!p.b_resident) {
-            // The weight slices of this stage's taps: one, or the three kx
+            // The weight slices of this stage's taps: one, or the ksize kx
             // taps of row ky in row-shift mode.
-            const int taps = p.row_shift ? 3 : 1;
+            const int taps = p.row_shift ? p.ksize : 1;
             for (int t = 0; t < taps; ++t) {
-              const int kb = p.row_shift ? (ky * 3 + t) * p.c_blocks + cb : u;
+              const int kb = p.row_shift ? (ky * p.ksize + t) * p.c_blocks + cb : u;
               tma_load_2d_pair(st + p.a_bytes + t * kBB, &tmap_b, bar, kb * kBK, b_row);
             }
           }
@@ -247,10 +267,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
             // on any row of a swizzle atom).
             const int ky = u / p.c_blocks;
             const int cb = u - ky * p.c_blocks;
-#pragma unroll
-            for (int kx = 0; kx < 3; ++kx) {
+#pragma unroll 1
+            for (int kx = 0; kx < p.ksize; ++kx) {
               const uint32_t b_addr =
-                  p.b_resident ? smem_u32(smem_b + ((ky * 3 + kx) * p.c_blocks + cb) * kBB)
+                  p.b_resident ? smem_u32(smem_b + ((ky * p.ksize + kx) * p.c_blocks + cb) * kBB)
                                : a_addr + p.a_bytes + kx * kBB;
 #pragma unroll
               for (int k = 0; k < kBK / 16; ++k)
@@ -302,8 +322,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
     uint32_t acc_phase = 0;
     for (int pt = cluster_id; pt < pairs; pt += clusters) {
       const int n_tile = pt % p.n_tiles;
-      const int m_tile = 2 * (pt / p.n_tiles) + (int)rank;
+      const int rest = pt / p.n_tiles;
+      const int ph = rest % p.phases;
+      const int m_tile = 2 * (rest / p.phases) + (int)rank;
       const long long m = (long long)m_tile * kM + row;
+      // Output row of pixel m: itself, or for an upsample phase (a, b) the
+      // high-res pixel (img, 2i + a, 2j + b) of low-res pixel (img, i, j);
+      // GroupNorm tile slot: the image's tiles stay contiguous, phase-major.
+      long long orow = m;
+      int stat_tile = m_tile;
+      if (p.phases == 4) {
+        const long long low_hw = (long long)p.low_h * p.low_w;
+        const long long im = m / low_hw;
+        const long long rem = m - im * low_hw;
+        const long long i = rem / p.low_w, j = rem - (rem / p.low_w) * p.low_w;
+        orow = (im * 2 * p.low_h + 2 * i + (ph >> 1)) * (2LL * p.low_w) + 2 * j + (ph & 1);
+        const int mt_img = m_tile / tiles_per_image;
+        stat_tile = (mt_img * 4 + ph) * tiles_per_image + (m_tile - mt_img * tiles_per_image);
+      }
       // The residual does not depend on the accumulator: start the first
       // chunk's loads before waiting for the MMAs.
       uint4 res[4];
@@ -361,7 +397,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
             for (int j = 0; j < 4; ++j) res[j] = __ldg(r4 + j);
           }
         }
-        uint4* o4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + m * p.ld_out + n0);
+        uint4* o4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + orow * p.ld_out + n0);
         uint32_t pk[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) pk[j] = Elem<D>::pack(v[2 * j], v[2 * j + 1]);
@@ -395,7 +431,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
             merge_equal_counts(mb, qb, st[(3 * 64 + g) * 2], st[(3 * 64 + g) * 2 + 1], n);
             merge_equal_counts(ma, qa, mb, qb, 2.0f * n);
             float* dst =
-                p.gn_part + ((long long)m_tile * p.gn_groups + n_tile * (BN / CPG) + g) * 2;
+                p.gn_part + ((long long)stat_tile * p.gn_groups + n_tile * (BN / CPG) + g) * 2;
             dst[0] = ma;
             dst[1] = qa;
           }
@@ -463,7 +499,7 @@ cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Param
     if (n <= 0) return cudaErrorNotSupported;
     resident_pairs[device] = n < sms / 2 ? n : sms / 2;
   }
-  const int pairs = p.num_m_tiles / 2 * p.n_tiles;
+  const int pairs = p.num_m_tiles / 2 * p.phases * p.n_tiles;
   int clusters = resident_pairs[device];
   if (clusters > pairs) clusters = pairs;
   conv_tc2_kernel<BN, D, CPG><<<2 * clusters, kThreads2, kSmem2, stream>>>(ta, tb, p);
@@ -473,11 +509,15 @@ cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Param
 }  // namespace
 
 const char* conv_tc2_check(const ConvTcArgs& a) {
-  if (a.upsample || a.out_nchw || a.out_f32 || a.softmax_stats || a.softmax_max)
+  if (a.out_nchw || a.out_f32 || a.softmax_stats || a.softmax_max)
     return "pair kernel: plain 16-bit output only";
+  if (a.upsample && (a.ksize != 2 || a.stride != 1 || a.pad != 0 || a.residual ||
+                     a.out_h != a.in_h || a.out_w != a.in_w))
+    return "pair kernel: upsample takes 2x2 phase weights on the low-res grid";
+  if (!a.upsample && a.ksize == 2) return "pair kernel: 2x2 kernels only as upsample phases";
   if (a.cout != 128 && (a.cout <= 0 || a.cout % 256 != 0))
     return "pair kernel: Cout 128 or a multiple of 256";
-  if (a.ksize != 1 && a.ksize != 3) return "pair kernel: 1x1 or 3x3";
+  if (a.ksize != 1 && a.ksize != 2 && a.ksize != 3) return "pair kernel: 1x1, 2x2 or 3x3";
   if (a.stride != 1 && a.stride != 2) return "pair kernel: stride 1 or 2";
   if (a.cin <= 0 || a.cin % kBK != 0) return "pair kernel: Cin % 64";
   if (a.out_w <= 0 || a.out_h <= 0 || a.batch <= 0) return "empty convolution";
@@ -514,7 +554,8 @@ cudaError_t conv_tc2_launch_bn(const ConvTcArgs& a, cudaStream_t stream) {
     const char* v = getenv("OSOR_ROW_SHIFT");
     return !(v && v[0] == '0');
   }();
-  const bool row_shift = row_shift_enabled && a.ksize == 3 && a.stride == 1 && tile_h == 1;
+  const bool row_shift =
+      row_shift_enabled && (a.ksize == 3 || a.ksize == 2) && a.stride == 1 && tile_h == 1;
   const CUtensorMapDataType tdt =
       a.dtype == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap ta, tb;
@@ -534,7 +575,7 @@ cudaError_t conv_tc2_launch_bn(const ConvTcArgs& a, cudaStream_t stream) {
   }
   {
     const int k_total = a.ksize * a.ksize * a.cin;
-    cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)a.cout};
+    cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)(a.upsample ? 4 * a.cout : a.cout)};
     cuuint64_t strides[1] = {(cuuint64_t)a.ldw * 2};
     cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)(BN / 2)};
     cuuint32_t estr[2] = {1, 1};
@@ -550,19 +591,24 @@ cudaError_t conv_tc2_launch_bn(const ConvTcArgs& a, cudaStream_t stream) {
   p.tiles_y = a.out_h / tile_h;
   p.num_m_tiles = a.batch * p.tiles_x * p.tiles_y;
   p.n_tiles = a.cout / BN;
+  p.phases = a.upsample ? 4 : 1;
+  p.low_h = a.in_h;
+  p.low_w = a.in_w;
+  p.cout_total = a.upsample ? a.cout : 0;
   p.c_blocks = a.cin / kBK;
   p.k_blocks = a.ksize * a.ksize * p.c_blocks;
   p.ksize = a.ksize;
   p.stride = a.stride;
   p.pad = a.pad;
   p.row_shift = row_shift ? 1 : 0;
-  p.units = row_shift ? 3 * p.c_blocks : p.k_blocks;
+  p.units = row_shift ? a.ksize * p.c_blocks : p.k_blocks;
   // The weight half stays resident when one channel tile's K blocks fit
   // (Cout 128, K <= 1152); otherwise each stage carries its weight slices.
-  p.b_resident = (p.n_tiles == 1 && p.k_blocks * kBB <= kMaxResidentKBlocks * 8 * 1024) ? 1 : 0;
+  p.b_resident =
+      (p.n_tiles == 1 && p.phases == 1 && p.k_blocks * kBB <= kMaxResidentKBlocks * 8 * 1024) ? 1 : 0;
   p.a_bytes = row_shift ? kShiftAB : kAB;
   p.a_tx = row_shift ? kShiftRows * kBK * 2 : kAB;
-  p.b_tx = p.b_resident ? 0 : (row_shift ? 3 : 1) * kBB;
+  p.b_tx = p.b_resident ? 0 : (row_shift ? a.ksize : 1) * kBB;
   p.stage_bytes = p.a_bytes + (int)p.b_tx;
   const int resident = p.b_resident ? p.k_blocks * kBB : 0;
   p.stages = (kSmemBudget - resident) / p.stage_bytes;

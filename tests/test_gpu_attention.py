@@ -20,9 +20,11 @@ pytestmark = pytest.mark.gpu
 
 
 CASES = [
-    (1, 256, 512),    # fused kernel, one 256-key tile, VAE width
-    (2, 1024, 512),   # fused kernel, four key tiles, two channel halves
-    (1, 512, 256),    # fused kernel, one channel half
+    (1, 256, 512),    # pair kernel, one 256-key tile, VAE width
+    (2, 1024, 512),   # pair kernel, four key tiles, two images
+    (3, 512, 512),    # pair kernel, three images
+    (3, 4096, 512),   # pair kernel: 96 tasks, more than the resident clusters take at once
+    (1, 512, 256),    # three-kernel path (the pair kernel takes width 512 only)
     (2, 384, 128),    # three-kernel tensor-core path
     (2, 35, 32),      # reference batch test shapes, CUDA-core path
     (4, 143, 32),
@@ -55,8 +57,8 @@ def test_attend_matches_oracle(case, dt, cuda_device):
 def test_fused_attention_rescales_growing_maxima(dt, cuda_device):
     """Logits that grow along the keys (up to ~40 in natural units) for every
     other query row and shrink for the rest, so within each warp some rows'
-    running maximum jumps by more than 2^8 across key tiles (the fused kernel
-    rescales their output accumulator) while the others keep theirs."""
+    running maximum jumps by more than 2^8 across key tiles (the fused
+    kernels rescale their output accumulator) while the others keep theirs."""
     b, n, d = 1, 1024, 512
     rng = np.random.default_rng(3)
 
@@ -78,12 +80,25 @@ def test_fused_attention_rescales_growing_maxima(dt, cuda_device):
     assert err.max() <= 2e-2, err.max()
 
 
-def test_fused_kernel_runs_the_same_cases(cuda_device):
-    """The fused attention kernel is opt-in (OSOR_FUSED_ATTENTION=1, read once
-    per process): run this file's oracle cases again in a child process with
-    it selected. Shapes with tokens % 256 == 0 and D of 256 or 512 take it."""
-    env = dict(os.environ, OSOR_FUSED_ATTENTION="1")
+def _rerun_in_child(env_overrides):
+    env = dict(os.environ, **env_overrides)
     r = subprocess.run([sys.executable, "-m", "pytest", __file__, "-q", "-p", "no:cacheprovider",
                         "-k", "attend_matches_oracle or rescales_growing_maxima"],
                        env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+def test_single_cta_fused_kernel_runs_the_same_cases(cuda_device):
+    """By default width-512 attention with tokens % 256 == 0 runs on the CTA
+    pair kernel (attn_pair.cu). The single-CTA fused kernel is opt-in
+    (OSOR_PAIR_ATTENTION=0 and OSOR_FUSED_ATTENTION=1, read once per process):
+    run this file's oracle cases again in a child process with it selected
+    (tokens % 256 == 0 and D of 256 or 512 take it)."""
+    _rerun_in_child({"OSOR_PAIR_ATTENTION": "0", "OSOR_FUSED_ATTENTION": "1"})
+
+
+def test_three_kernel_path_runs_the_same_cases(cuda_device):
+    """The three-kernel path (scores with softmax statistics, probabilities,
+    P V) that the pair kernel replaced, in a child process with
+    OSOR_PAIR_ATTENTION=0."""
+    _rerun_in_child({"OSOR_PAIR_ATTENTION": "0", "OSOR_FUSED_ATTENTION": "0"})
