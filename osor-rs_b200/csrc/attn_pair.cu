@@ -52,7 +52,9 @@ constexpr int kPBlock = kRows * 64 * 2;             // P: 128 rows x 64 keys (16
 constexpr int kAStages = 2;
 constexpr int kVStages = 2;
 constexpr int kThreads = 192;
-constexpr int kExBytes = (2 * kRows + kRows) * 4;   // row maxima [2][128], row sums [128]
+// Exchange area: the peer's row maxima [2][128], the peer's row sums [128],
+// and this CTA's row maxima staged for the copy to the peer [2][128].
+constexpr int kExBytes = (2 * kRows + kRows + 2 * kRows) * 4;
 constexpr int kSmem = kAStages * kAStage + kVStages * kVStage + 4 * kPBlock + kExBytes + 256 +
                       1024;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -95,7 +97,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint8_t* pbuf = ring_v + kVStages * kVStage;
   float* mx = reinterpret_cast<float*>(pbuf + 4 * kPBlock);  // [2][128], written by the peer
   float* lx = mx + 2 * kRows;                                 // [128], written by the peer
-  uint64_t* a_full = reinterpret_cast<uint64_t*>(lx + kRows);
+  float* mstage = lx + kRows;                                 // [2][128], copied to the peer
+  uint64_t* a_full = reinterpret_cast<uint64_t*>(mstage + 2 * kRows);
   uint64_t* a_empty = a_full + kAStages;
   uint64_t* v_full = a_empty + kAStages;
   uint64_t* v_empty = v_full + kVStages;
@@ -126,9 +129,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&s_free[b], 4);    // the four softmax warps
-      mbar_init(&mx_ready[b], 4);  // the peer's four softmax warps
+      // Four local arrivals (one per softmax warp, each expecting the 128
+      // bytes of row maxima that the peer's warp of the same rows copies in).
+      mbar_init(&mx_ready[b], 4);
     }
-    mbar_init(p_ready, 8);  // four local and four peer softmax warps
+    // Four local arrivals (each softmax warp after writing its P rows, each
+    // expecting the 8 KB of P rows that the peer's warp copies in).
+    mbar_init(p_ready, 4);
     mbar_init(p_free, 2);   // this CTA's and the peer's PV commit
     mbar_init(o_free, 4);
     mbar_init(l_ready, 4);
@@ -308,7 +315,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t peer_pbuf = map_to_rank(smem_u32(pbuf), peer);
     const uint32_t peer_mx_ready[2] = {map_to_rank(smem_u32(&mx_ready[0]), peer),
                                        map_to_rank(smem_u32(&mx_ready[1]), peer)};
-    const uint32_t own_p_ready = map_to_rank(smem_u32(p_ready), rank);
     const uint32_t peer_p_ready = map_to_rank(smem_u32(p_ready), peer);
     const uint32_t peer_l_ready = map_to_rank(smem_u32(l_ready), peer);
     long long u = 0;
@@ -329,22 +335,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
+        // This row's 128 scores stay in registers for both passes.
         const uint32_t s_tmem = tmem_base + buf * kOwnKeys + lane_off;
-        // Row maximum of this CTA's 128 scores (log2 units), shared with the peer.
-        float mloc = -3.0e38f;
-#pragma unroll 1
-        for (int c = 0; c < kOwnKeys / 32; ++c) {
-          uint32_t r[32];
-          tmem_load_32x32b_x32(s_tmem + c * 32, r);
+        float sv[kOwnKeys];
+        {
+          uint32_t r[kOwnKeys];
+#pragma unroll
+          for (int c = 0; c < kOwnKeys / 32; ++c)
+            tmem_load_32x32b_x32(s_tmem + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
           tmem_wait_ld();
 #pragma unroll
-          for (int k = 0; k < 32; ++k) mloc = fmaxf(mloc, __uint_as_float(r[k]));
+          for (int k = 0; k < kOwnKeys; ++k) sv[k] = __uint_as_float(r[k]);
         }
-        mloc *= kLog2e;
-        st_cluster_f32(peer_mx + (uint32_t)((buf * kRows + row) * 4), mloc);
+        // The scores have been read: the buffer takes tile u + 2.
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster_release(peer_mx_ready[buf]);
-        if (!__all_sync(0xffffffffu, mbar_wait_cluster(&mx_ready[buf], par, abort_flag))) {
+        if (lane == 0) mbar_arrive(&s_free[buf]);
+        float mloc = -3.0e38f;
+#pragma unroll
+        for (int k = 0; k < kOwnKeys; ++k) mloc = fmaxf(mloc, sv[k]);
+        mloc *= kLog2e;
+        // Row maxima to the peer: staged, then one bulk copy per warp that
+        // completes its 128 bytes on the peer's mx_ready.
+        mstage[buf * kRows + row] = mloc;
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&mx_ready[buf], 128);
+          bulk_copy_to_cluster(peer_mx + (uint32_t)((buf * kRows + quad * 32) * 4),
+                               mstage + buf * kRows + quad * 32, 128, peer_mx_ready[buf]);
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait(&mx_ready[buf], par, abort_flag))) {
           ok = false;
           break;
         }
@@ -383,43 +404,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
         }
         // P = 2^(S log2 e - m) for this CTA's keys: 16-bit K-major tiles of 64
-        // keys (blocks 2r, 2r + 1 of the tile's four), here and in the peer.
+        // keys (blocks 2r, 2r + 1 of the tile's four).
         float lsum = 0.0f;
-#pragma unroll 1
+#pragma unroll
         for (int c = 0; c < kOwnKeys / 32; ++c) {
-          uint32_t r[32];
-          tmem_load_32x32b_x32(s_tmem + c * 32, r);
-          tmem_wait_ld();
           uint32_t pk[16];
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
-            const float p0 = ex2_approx(fmaf(__uint_as_float(r[2 * k]), kLog2e, -m));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(r[2 * k + 1]), kLog2e, -m));
+            const float p0 = ex2_approx(fmaf(sv[c * 32 + 2 * k], kLog2e, -m));
+            const float p1 = ex2_approx(fmaf(sv[c * 32 + 2 * k + 1], kLog2e, -m));
             lsum += p0 + p1;
             pk[k] = Elem<D>::pack(p0, p1);
           }
           const int blk = 2 * (int)rank + (c >> 1);
-          const uint32_t off = (uint32_t)(blk * kPBlock + row * 128);
+          uint8_t* rowp = pbuf + blk * kPBlock + row * 128;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int chunk = (c & 1) * 4 + q;
-            const uint32_t o = off + (uint32_t)((chunk ^ (row & 7)) << 4);
-            const uint4 v = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-            *reinterpret_cast<uint4*>(pbuf + o) = v;
-            st_cluster_v4(peer_pbuf + o, v);
+            *reinterpret_cast<uint4*>(rowp + ((chunk ^ (row & 7)) << 4)) =
+                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
           }
         }
         l += lsum;
-        // The scores have been read: the buffer takes tile u + 2.
+        // The warp's 32 rows of both blocks to the peer (two 4 KB bulk copies
+        // completing on the peer's p_ready), then ready here: P (and a
+        // rescaled O) visible to this CTA's tensor core.
         tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[buf]);
-        // P visible to both CTAs' tensor cores, then ready on both.
-        fence_proxy_async_cluster();
+        fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive_cluster_release(own_p_ready);
-          mbar_arrive_cluster_release(peer_p_ready);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t off = (uint32_t)((2 * (int)rank + h) * kPBlock + quad * 32 * 128);
+            bulk_copy_to_cluster(peer_pbuf + off, pbuf + off, 32 * 128, peer_p_ready);
+          }
+          mbar_arrive_expect_tx(p_ready, 2 * 32 * 128);
         }
       }
       if (!ok) break;

@@ -328,6 +328,24 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, const uint4
 __device__ __forceinline__ void st_cluster_f32(uint32_t cluster_addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
 }
+// Bulk copy from this CTA's shared memory into another CTA's (shared::cluster
+// destination and mbarrier; 16-byte aligned, size % 16 == 0); the bytes
+// complete on that mbarrier.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, const void* src,
+                                                     uint32_t bytes, uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+      "[%3];" ::"r"(dst_cluster),
+      "r"(smem_u32(src)), "r"(bytes), "r"(bar_cluster)
+      : "memory");
+}
+// Raise the expected transaction bytes of the mbarrier's current phase
+// without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
 // Make this thread's generic-proxy shared-memory writes, local and remote,
 // visible to the async proxy (the tensor core of the CTA that owns them).
 __device__ __forceinline__ void fence_proxy_async_cluster() {
