@@ -6,6 +6,7 @@
 // GroupNorm and linear projections over pixels run on the tensor-core and
 // GroupNorm kernels shared with the VAE.
 #include <math.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "unet.h"
@@ -552,6 +553,17 @@ __global__ void __launch_bounds__(kMmaWarps * 32)
   }
 }
 
+// Head width 64 takes the tcgen05 kernel (attn_heads.cu) where its shapes
+// allow; OSOR_HEADS_TC=0 in the environment (read once) keeps the mma.sync
+// kernel for every shape, for comparing.
+bool heads_tc_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("OSOR_HEADS_TC");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 template <int D>
 cudaError_t attention_heads_typed(const void* q, long long ld_q, long long q_bs, const void* k,
                                   const void* v, long long ld_kv, long long kv_bs, void* out,
@@ -569,6 +581,10 @@ cudaError_t attention_heads_typed(const void* q, long long ld_q, long long q_bs,
           qb, ld_q, q_bs, kb, vb, ld_kv, kv_bs, ob, ld_out, out_bs, n_q, n_kv);
       break;
     case 64:
+      if (heads_tc_enabled() &&
+          attn_heads64_tc_ok(q, ld_q, q_bs, k, v, ld_kv, kv_bs, out, ld_out, out_bs, n_q, n_kv))
+        return attn_heads64_tc_launch(D, q, ld_q, q_bs, k, v, ld_kv, kv_bs, out, ld_out, out_bs,
+                                      batch, heads, n_q, n_kv, s);
       attention_heads64_mma_kernel<D><<<grid(kMmaRows), dim3(kMmaWarps * 32), 0, s>>>(
           qb, ld_q, q_bs, kb, vb, ld_kv, kv_bs, ob, ld_out, out_bs, n_q, n_kv);
       break;

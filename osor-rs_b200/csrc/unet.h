@@ -55,4 +55,16 @@ cudaError_t attention_heads_launch(int dtype, const void* q, long long ld_q, lon
                                    void* out, long long ld_out, long long out_bs, int batch,
                                    int heads, int n_q, int n_kv, int head_dim, cudaStream_t s);
 
+// The tcgen05 kernel for head width 64 (attn_heads.cu): true when it takes
+// the shapes (n_q a multiple of 256, strides multiples of 8 elements, 16-byte
+// aligned operands, batch strides that do not overlap).
+bool attn_heads64_tc_ok(const void* q, long long ld_q, long long q_bs, const void* k,
+                        const void* v, long long ld_kv, long long kv_bs, const void* out,
+                        long long ld_out, long long out_bs, int n_q, int n_kv);
+// Same contract as attention_heads_launch with head_dim 64.
+cudaError_t attn_heads64_tc_launch(int dtype, const void* q, long long ld_q, long long q_bs,
+                                   const void* k, const void* v, long long ld_kv, long long kv_bs,
+                                   void* out, long long ld_out, long long out_bs, int batch,
+                                   int heads, int n_q, int n_kv, cudaStream_t s);
+
 }  // namespace osor

@@ -157,8 +157,17 @@ def _attention_f64(q, k, v, heads, hd):
     return (p @ vh).transpose(0, 2, 1, 3).reshape(b, n, heads * hd)
 
 
-@pytest.mark.parametrize("hd,heads,n_q,n_kv,shared", [(64, 5, 70, 77, True), (64, 10, 256, 256, False),
-                                                      (32, 2, 33, 300, False), (128, 3, 19, 40, True)])
+# Head width 64 with n_q a multiple of 256 runs on the tcgen05 kernel
+# (attn_heads.cu): one 128-key tile, ragged last tiles, shared cross-attention
+# keys, and more tasks (batch x heads x 256-row tiles) than SMs so that CTAs
+# take several in turn. The other shapes run on the mma.sync / CUDA-core
+# kernels.
+HEAD_CASES = [(64, 5, 70, 77, True), (64, 10, 256, 256, False), (64, 10, 512, 77, True),
+              (64, 4, 1024, 1000, False), (64, 20, 2048, 300, False), (32, 2, 33, 300, False),
+              (128, 3, 19, 40, True)]
+
+
+@pytest.mark.parametrize("hd,heads,n_q,n_kv,shared", HEAD_CASES)
 def test_attention_heads_match_f64(hd, heads, n_q, n_kv, shared, cuda_device):
     lb = _lib.lib()
     rng = np.random.default_rng(hd + n_q)
@@ -178,6 +187,44 @@ def test_attention_heads_match_f64(hd, heads, n_q, n_kv, shared, cuda_device):
     want = _attention_f64(qa[..., :c], k, v, heads, hd)
     # f16 output rounding (2^-11 relative) plus f32 softmax arithmetic.
     assert np.all(np.abs(host(out) - want) <= 1e-3 + 1e-3 * np.abs(want))
+
+
+def test_attention_heads_rescales_growing_maxima(cuda_device):
+    """Logits that grow along the keys (to about 40 over 1000 keys) move the
+    running row maximum past the 2^8 rescale threshold several times; the
+    tcgen05 kernel rescales its O accumulator in TMEM each time."""
+    lb = _lib.lib()
+    rng = np.random.default_rng(9)
+    b, heads, hd, n_q, n_kv = 1, 2, 64, 256, 1000
+    c = heads * hd
+    u = rng.standard_normal(hd)
+    u /= np.linalg.norm(u)
+    q = np.tile(u, (b, n_q, heads)) + 0.05 * rng.standard_normal((b, n_q, c))
+    ramp = np.linspace(0.0, 40.0, n_kv)[None, :, None]
+    k = np.tile(u, (b, n_kv, heads)) * ramp + 0.2 * rng.standard_normal((b, n_kv, c))
+    v = rng.standard_normal((b, n_kv, c))
+    qd, kd, vd = dev16(q, torch.float16), dev16(k, torch.float16), dev16(v, torch.float16)
+    out = torch.zeros((b, n_q, c), device="cuda", dtype=torch.float16)
+    check(lb.osor_attention_heads(P(qd), c, n_q * c, P(kd), P(vd), c, n_kv * c, P(out), c,
+                                  n_q * c, b, heads, n_q, n_kv, hd, dtype_code(torch.float16),
+                                  S()))
+    want = _attention_f64(host(qd).astype(np.float64), host(kd).astype(np.float64),
+                          host(vd).astype(np.float64), heads, hd)
+    assert np.all(np.abs(host(out) - want) <= 1e-3 + 1e-3 * np.abs(want))
+
+
+def test_attention_heads_mma_sync_kernel_runs_the_same_cases(cuda_device):
+    """OSOR_HEADS_TC=0 (read once per process) keeps head width 64 on the
+    mma.sync kernel for every shape: run the cases above again in a child
+    process with it set."""
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ, OSOR_HEADS_TC="0")
+    r = subprocess.run([sys.executable, "-m", "pytest", __file__, "-q", "-p", "no:cacheprovider",
+                        "-k", "attention_heads_match_f64 or rescales_growing_maxima"],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
 
 
 @pytest.mark.parametrize("channels", [1920, 2560])
