@@ -376,6 +376,50 @@ def run_ops(args):
                           "frac_of_sustained_peak": round(tf / tflops_sus, 4),
                           "gpu_launches": launches, "peak_source": src,
                           "breakdown": breakdown}), flush=True)
+    elif args.op == "attn_heads":
+        # The SDXL UNet's multi-head attention for the 4 x 1024^2 job (batch 4,
+        # head width 64, f16 or bf16): self-attention on the fused q|k|v
+        # product (row stride 3C) and cross-attention over the 77 cached
+        # prompt tokens, at the 64^2 and 32^2 latent levels.
+        import ctypes
+        lb = _lib.lib()
+        dt = torch.float16 if args.dtype == "f16" else torch.bfloat16
+        g = torch.Generator(device=dev).manual_seed(3)
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+        def ptr(t, off=0):
+            return ctypes.c_void_p(t.data_ptr() + off * t.element_size())
+
+        for b, heads, n, n_kv in [(4, 10, 4096, 4096), (4, 20, 1024, 1024), (4, 10, 4096, 77),
+                                  (4, 20, 1024, 77)]:
+            c = heads * 64
+            out = torch.empty((b, n, c), device=dev, dtype=dt)
+            if n_kv == n:
+                qkv = (torch.randn((b, n, 3 * c), generator=g, device=dev) * 0.4).to(dt)
+                q, k, v, ld_q, ld_kv = ptr(qkv), ptr(qkv, c), ptr(qkv, 2 * c), 3 * c, 3 * c
+                kv_bs, kind = n * 3 * c, "self"
+            else:
+                qt = (torch.randn((b, n, c), generator=g, device=dev) * 0.4).to(dt)
+                kv = torch.randn((b, n_kv, 2 * c), generator=g, device=dev).to(dt)
+                q, k, v, ld_q, ld_kv = ptr(qt), ptr(kv), ptr(kv, c), c, 2 * c
+                kv_bs, kind = n_kv * 2 * c, "cross"
+
+            def call():
+                _lib.check(lb.osor_attention_heads(q, ld_q, n * ld_q, k, v, ld_kv, kv_bs, ptr(out),
+                                                   c, n * c, b, heads, n, n_kv, 64,
+                                                   _lib.dtype_code(dt), stream))
+
+            ms = _timed(call, args.steps, args.warmup, flush)
+            tf = 4.0 * b * n * n_kv * c / (ms / 1e3) / 1e12
+            path = ("tcgen05 (attn_heads64_tc_kernel)" if n % 256 == 0 and
+                    os.environ.get("OSOR_HEADS_TC", "1") != "0" else "mma.sync")
+            print(json.dumps({"op": "multi-head attention (%s)" % kind,
+                              "shape": {"batch": b, "heads": heads, "head_dim": 64, "n_q": n,
+                                        "n_kv": n_kv},
+                              "dtype": args.dtype, "path": path, "ms": round(ms, 4),
+                              "tflops": round(tf, 1),
+                              "frac_of_sustained_peak": round(tf / tflops_sus, 4),
+                              "peak_source": src}), flush=True)
     elif args.op == "e2e":
         run_e2e(args, dev, flush)
     if device_status(0) != 0:
@@ -646,7 +690,8 @@ def main():
     ap.add_argument("--dtype", default="f16", choices=["f16", "bf16"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op", default="decode",
-                    choices=["decode", "conv3x3", "groupnorm", "encode", "noise", "unet", "e2e"],
+                    choices=["decode", "conv3x3", "groupnorm", "encode", "noise", "unet", "e2e",
+                             "attn_heads"],
                     help="decode: the headline line; others: standalone op lines; e2e: the "
                          "end-to-end inpainting call at B=4, 1024^2")
     ap.add_argument("--shape", default=None, help="comma-separated shape for --op conv3x3/groupnorm")
