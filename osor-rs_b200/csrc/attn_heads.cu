@@ -8,8 +8,10 @@
 //   O_g += P_g V       M = 128, N = 64, K = 128 keys    -> TMEM (per group)
 // Two softmax warp groups (four warps each, one query row per thread) work on
 // A and B in turn, so one group's exponentials overlap the other group's
-// MMAs: the MMA issuer runs S_A(0), S_B(0), then per tile PV_A(j), S_A(j+1),
-// PV_B(j), S_B(j+1). The running maximum moves, and O is rescaled, only when
+// MMAs: the MMA issuer runs S_A(0), S_B(0), then per tile S_A(j+1), PV_A(j),
+// S_B(j+1), PV_B(j): a group's softmax takes its scores into registers and
+// frees the TMEM buffer at once, so the next tile's scores are computed while
+// it evaluates the exponentials. The running maximum moves, and O is rescaled, only when
 // it grows by more than 2^8 (so P <= 256); keys past the last valid one of a
 // ragged tile are masked.
 //
@@ -86,60 +88,6 @@ __device__ void heads_drain(uint64_t* bars, int n, int stage, uint32_t phase) {
     while (!mbar_try_wait(addr, ph) && global_timer_ns() - t0 < kWaitLimitNs) {
     }
   }
-}
-
-// Row maximum of one 128-key score tile (TMEM, f32, this thread's row),
-// skipping keys >= valid when kMasked. Read 64 columns at a time.
-template <bool kMasked>
-__device__ __forceinline__ float heads_row_max(uint32_t s_tmem, int valid) {
-  float mt = -3.0e38f;
-#pragma unroll 1
-  for (int h2 = 0; h2 < 2; ++h2) {
-    uint32_t r[64];
-    tmem_load_32x32b_x32(s_tmem + h2 * 64, *reinterpret_cast<uint32_t(*)[32]>(r));
-    tmem_load_32x32b_x32(s_tmem + h2 * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
-    tmem_wait_ld();
-#pragma unroll
-    for (int k = 0; k < 64; ++k)
-      if (!kMasked || h2 * 64 + k < valid) mt = fmaxf(mt, __uint_as_float(r[k]));
-  }
-  return mt;
-}
-
-// P = 2^(s log2e - m) of one score tile into the group's two 64-key P blocks
-// (rows of 128 bytes in the 128-byte swizzled K-major layout; prow = row
-// 0 of this thread's row in block 0), zero for keys >= valid when kMasked.
-// Returns the row sum of the f32 probabilities.
-template <int D, bool kMasked>
-__device__ __forceinline__ float heads_probs(uint32_t s_tmem, float m, int valid, uint8_t* prow,
-                                             int row) {
-  float lsum = 0.0f;
-#pragma unroll 1
-  for (int h2 = 0; h2 < 2; ++h2) {
-    uint32_t r[64];
-    tmem_load_32x32b_x32(s_tmem + h2 * 64, *reinterpret_cast<uint32_t(*)[32]>(r));
-    tmem_load_32x32b_x32(s_tmem + h2 * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
-    tmem_wait_ld();
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      uint32_t pk[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int k = q * 8 + 2 * e;
-        float p0 = ex2_approx(fmaf(__uint_as_float(r[k]), kLog2eH, -m));
-        float p1 = ex2_approx(fmaf(__uint_as_float(r[k + 1]), kLog2eH, -m));
-        if (kMasked) {
-          if (h2 * 64 + k >= valid) p0 = 0.0f;
-          if (h2 * 64 + k + 1 >= valid) p1 = 0.0f;
-        }
-        lsum += p0 + p1;
-        pk[e] = Elem<D>::pack(p0, p1);
-      }
-      *reinterpret_cast<uint4*>(prow + h2 * kPBlockH + ((q ^ (row & 7)) << 4)) =
-          make_uint4(pk[0], pk[1], pk[2], pk[3]);
-    }
-  }
-  return lsum;
 }
 
 template <int D>
@@ -335,12 +283,10 @@ __global__ void __launch_bounds__(kThreadsH, 1)
           kph ^= 1;
         }
         for (int j = 0; j < p.tiles && ok; ++j, ++tile_u) {
+          // Per group: the next tile's scores as soon as the softmax has
+          // taken this tile's into registers (they run while it computes
+          // P), then this tile's P V once P is in shared memory.
           const int vb = (int)(tile_u & 1);
-          if (!mbar_wait(&vt_ready[vb], (uint32_t)((tile_u >> 1) & 1), abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
           const bool more = j + 1 < p.tiles;
           if (more) {
             if (!mbar_wait(&k_full[ks], kph, abort_flag)) {
@@ -350,6 +296,17 @@ __global__ void __launch_bounds__(kThreadsH, 1)
             tc_fence_after();
           }
           for (int g = 0; g < 2 && ok; ++g) {
+            if (more) {
+              if (!(ok = s_product(g, j + 2 == p.tiles))) break;
+              if (g == 1) umma_commit(&k_empty[ks]);
+            }
+            if (g == 0) {
+              if (!mbar_wait(&vt_ready[vb], (uint32_t)((tile_u >> 1) & 1), abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
             if (j == 0 && task_idx > 0) {
               // The previous task's epilogue of this group has read O_g.
               if (!mbar_wait(&o_free[g], (uint32_t)((task_idx - 1) & 1), abort_flag)) {
@@ -359,13 +316,11 @@ __global__ void __launch_bounds__(kThreadsH, 1)
               tc_fence_after();
             }
             if (!(ok = pv_product(g, j == 0))) break;
-            if (more && !(ok = s_product(g, j + 2 == p.tiles))) break;
           }
           if (!ok) break;
           umma_commit(&vt_free[vb]);
           if (more) {
             ++s_use;
-            umma_commit(&k_empty[ks]);
             if (++ks == kKStages) {
               ks = 0;
               kph ^= 1;
@@ -454,11 +409,65 @@ __global__ void __launch_bounds__(kThreadsH, 1)
           break;
         }
         tc_fence_after();
-        // Keys past the last one of a ragged tile do not take part.
+        // The row's 128 scores into registers; the buffer then takes the
+        // next tile's scores while P is computed.
+        float sv[kKeys];
+        {
+          uint32_t r[kKeys];
+#pragma unroll
+          for (int c = 0; c < kKeys / 32; ++c)
+            tmem_load_32x32b_x32(s_tmem + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
+          tmem_wait_ld();
+#pragma unroll
+          for (int k = 0; k < kKeys; ++k) sv[k] = __uint_as_float(r[k]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[g]);
+        // Keys past the last one of a ragged tile do not take part (their
+        // probability underflows to zero).
         const int valid = p.n_kv - j * kKeys;
-        const float mt =
-            (valid < kKeys ? heads_row_max<true>(s_tmem, valid) : heads_row_max<false>(s_tmem, 0)) *
-            kLog2eH;
+        if (valid < kKeys) {
+#pragma unroll
+          for (int k = 0; k < kKeys; ++k)
+            if (k >= valid) sv[k] = -3.0e38f;
+        }
+        // Row maximum as a tree of eight chains (one chain of 128 dependent
+        // max operations would sit on every tile's critical path).
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = sv[i];
+#pragma unroll
+        for (int k = 8; k < kKeys; ++k) acc[k & 7] = fmaxf(acc[k & 7], sv[k]);
+#pragma unroll
+        for (int w = 4; w > 0; w >>= 1)
+#pragma unroll
+          for (int i = 0; i < w; ++i) acc[i] = fmaxf(acc[i], acc[i + w]);
+        const float mt = acc[0] * kLog2eH;
+        float f = 1.0f;
+        bool rescale = false;
+        if (j == 0) {
+          m = mt;
+          l = 0.0f;
+        } else {
+          const bool grow = mt > m + kRescaleLog2H;
+          rescale = __any_sync(0xffffffffu, grow);  // tcgen05.ld / st below are warp-wide
+          if (grow) {
+            f = ex2_approx(m - mt);
+            m = mt;
+          }
+          l *= f;
+        }
+        float lsum = 0.0f;
+        uint32_t pk[kKeys / 2];
+#pragma unroll
+        for (int k = 0; k < kKeys / 2; ++k) {
+          const float p0 = ex2_approx(fmaf(sv[2 * k], kLog2eH, -m));
+          const float p1 = ex2_approx(fmaf(sv[2 * k + 1], kLog2eH, -m));
+          lsum += p0 + p1;
+          pk[k] = Elem<D>::pack(p0, p1);
+        }
+        l += lsum;
         // P and O may be written once this group's previous PV completed.
         if (j > 0 || task_idx > 0) {
           if (!__all_sync(0xffffffffu,
@@ -468,38 +477,28 @@ __global__ void __launch_bounds__(kThreadsH, 1)
           }
           tc_fence_after();
         }
-        if (j == 0) {
-          m = mt;
-          l = 0.0f;
-        } else {
-          const bool grow = mt > m + kRescaleLog2H;
-          if (__any_sync(0xffffffffu, grow)) {
-            const float f = grow ? ex2_approx(m - mt) : 1.0f;
-            l *= f;
-            if (grow) m = mt;
+        if (rescale) {
 #pragma unroll 1
-            for (int c = 0; c < kHd / 32; ++c) {
-              uint32_t r[32];
-              tmem_load_32x32b_x32(o_tmem + c * 32, r);
-              tmem_wait_ld();
+          for (int c = 0; c < kHd / 32; ++c) {
+            uint32_t r[32];
+            tmem_load_32x32b_x32(o_tmem + c * 32, r);
+            tmem_wait_ld();
 #pragma unroll
-              for (int k = 0; k < 32; ++k) r[k] = __float_as_uint(__uint_as_float(r[k]) * f);
-              tmem_store_32x32b_x32(o_tmem + c * 32, r);
-            }
-            tmem_wait_st();
+            for (int k = 0; k < 32; ++k) r[k] = __float_as_uint(__uint_as_float(r[k]) * f);
+            tmem_store_32x32b_x32(o_tmem + c * 32, r);
           }
+          tmem_wait_st();
         }
+        // P into the group's two 64-key blocks (128-byte rows, 128-byte swizzle).
         uint8_t* prow = pbuf + g * 2 * kPBlockH + row * 128;
-        l += valid < kKeys ? heads_probs<D, true>(s_tmem, m, valid, prow, row)
-                           : heads_probs<D, false>(s_tmem, m, 0, prow, row);
-        // S has been read and P written: the group's next S and this PV may go.
+#pragma unroll
+        for (int q = 0; q < 16; ++q)
+          *reinterpret_cast<uint4*>(prow + (q >> 3) * kPBlockH + (((q & 7) ^ (row & 7)) << 4)) =
+              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         tc_fence_before();
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&s_free[g]);
-          mbar_arrive(&p_ready[g]);
-        }
+        if (lane == 0) mbar_arrive(&p_ready[g]);
       }
       if (!ok) break;
       // O_g is final after this group's last PV.

@@ -20,9 +20,12 @@
 // The score buffers are double buffered, so S of tile j + 1 is computed while
 // the softmax warps work on tile j, and PV of tile j runs after.
 //
-// Roles (192 threads per CTA): warp 0 TMA producer (Q and K chunks, V^T
-// chunks of this CTA's output half), warp 1 TMEM allocator and MMA issuer,
-// warps 2..5 softmax and output epilogue. All waits are bounded; a CTA that
+// Roles (224 threads per CTA): warp 0 TMA producer of the Q and K chunks,
+// warp 6 TMA producer of the V^T chunks of this CTA's output half (two
+// producers, so that neither stream waits behind the other's ring), warp 1
+// TMEM allocator and MMA issuer, which issues each score chunk and each P V
+// chunk as soon as its operands have arrived, warps 2..5 softmax and output
+// epilogue. All waits are bounded; a CTA that
 // gives up sets its abort flag, and the cluster barrier at the end keeps
 // either CTA from leaving while the other may still write into it.
 //
@@ -51,7 +54,7 @@ constexpr int kVStage = kDHalf * 64 * 2;            // V^T chunk: 256 rows x 64 
 constexpr int kPBlock = kRows * 64 * 2;             // P: 128 rows x 64 keys (16 KB)
 constexpr int kAStages = 2;
 constexpr int kVStages = 2;
-constexpr int kThreads = 192;
+constexpr int kThreads = 224;
 // Exchange area: the peer's row maxima [2][128], the peer's row sums [128],
 // and this CTA's row maxima staged for the copy to the peer [2][128].
 constexpr int kExBytes = (2 * kRows + kRows + 2 * kRows) * 4;
@@ -161,22 +164,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------- producer
-      int as = 0, vs = 0;
-      uint32_t aph = 0, vph = 0;
+      int as = 0;
+      uint32_t aph = 0;
       bool ok = true;
-      auto load_v = [&](int b, int tile) -> bool {
-        for (int c = 0; c < kTileKeys / 64; ++c) {
-          if (!mbar_wait(&v_empty[vs], vph ^ 1, abort_flag)) return false;
-          mbar_arrive_expect_tx(&v_full[vs], kVStage);
-          tma_load_3d(ring_v + vs * kVStage, &tmap_vt, &v_full[vs], tile * kTileKeys + c * 64,
-                      (int)rank * kDHalf, b);
-          if (++vs == kVStages) {
-            vs = 0;
-            vph ^= 1;
-          }
-        }
-        return true;
-      };
       for (int t = cluster_id; t < p.tasks && ok; t += clusters) {
         const int qt = t % qtiles;
         const int b = t / qtiles;
@@ -197,14 +187,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               aph ^= 1;
             }
           }
-          if (ok && j > 0) ok = load_v(b, j - 1);
         }
-        if (ok) ok = load_v(b, p.tiles - 1);
       }
-      if (!ok) {
-        pair_drain(a_full, kAStages, as, aph);
-        pair_drain(v_full, kVStages, vs, vph);
+      if (!ok) pair_drain(a_full, kAStages, as, aph);
+    }
+  } else if (warp == 6) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- V^T producer
+      int vs = 0;
+      uint32_t vph = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < p.tasks && ok; t += clusters) {
+        const int b = t / qtiles;
+        for (int j = 0; j < p.tiles && ok; ++j) {
+          for (int c = 0; c < kTileKeys / 64; ++c) {
+            if (!mbar_wait(&v_empty[vs], vph ^ 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&v_full[vs], kVStage);
+            tma_load_3d(ring_v + vs * kVStage, &tmap_vt, &v_full[vs], j * kTileKeys + c * 64,
+                        (int)rank * kDHalf, b);
+            if (++vs == kVStages) {
+              vs = 0;
+              vph ^= 1;
+            }
+          }
+        }
       }
+      if (!ok) pair_drain(v_full, kVStages, vs, vph);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -218,83 +229,98 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       long long pv = 0;  // global PV counter
       int task_idx = 0;
       bool ok = true, issued = false;
-      // O += P V for the tile whose P is (or will be) in shared memory.
-      auto pv_tile = [&](bool first) -> bool {
-        if (!mbar_wait_cluster(p_ready, (uint32_t)(pv & 1), abort_flag)) return false;
-        tc_fence_after();
-        for (int c = 0; c < kTileKeys / 64; ++c) {
-          if (!mbar_wait(&v_full[vs], vph, abort_flag)) return false;
-          tc_fence_after();
-          const uint32_t a_addr = smem_u32(pbuf + c * kPBlock);
-          const uint32_t b_addr = smem_u32(ring_v + vs * kVStage);
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_bf16(tmem_o, sw128_kmajor_desc(a_addr + k * 32),
-                      sw128_kmajor_desc(b_addr + k * 32), idesc_o, !(first && c == 0 && k == 0));
-          issued = true;
-          umma_commit(&v_empty[vs]);
-          if (++vs == kVStages) {
-            vs = 0;
-            vph ^= 1;
-          }
-        }
-        // P and O are free once these MMAs complete, here and in the peer.
-        umma_commit_multicast(p_free, 0x3);
-        ++pv;
-        return true;
-      };
+      // Iteration j of a task issues the scores of tile j (kDChunks chunks
+      // of Q and K) and O += P V of tile j - 1 (four V^T chunks), each chunk
+      // as soon as its operands have arrived, P V first when both can go:
+      // the loads of the two rings overlap instead of one waiting behind
+      // the other. The barriers are polled with test_wait (which never
+      // suspends the thread); a poll that finds nothing ready for
+      // kWaitLimitNs gives up like the other waits.
+      uint64_t t_idle = 0;
       for (int t = cluster_id; t < p.tasks && ok; t += clusters, ++task_idx) {
-        for (int j = 0; j < p.tiles && ok; ++j, ++u) {
+        for (int j = 0; j <= p.tiles && ok; ++j) {
+          int sc = j < p.tiles ? 0 : kDChunks;  // score chunks issued
+          int pc = j > 0 ? 0 : 4;               // P V chunks issued
+          bool s_gate = false, p_gate = false;
           const int buf = (int)(u & 1);
-          // The softmax warps have read this buffer's previous scores.
-          if (!mbar_wait(&s_free[buf], (uint32_t)(((u >> 1) & 1) ^ 1), abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
           const uint32_t d_tmem = tmem_base + buf * kOwnKeys;
-          for (int dc = 0; dc < kDChunks; ++dc) {
-            if (!mbar_wait(&a_full[as], aph, abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t q_addr = smem_u32(ring_a + as * kAStage);
-            const uint32_t k_addr = q_addr + kQBytes;
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              umma_bf16(d_tmem, sw128_kmajor_desc(q_addr + k * 32),
-                        sw128_kmajor_desc(k_addr + k * 32), idesc_s, (dc | k) != 0);
-            issued = true;
-            umma_commit(&a_empty[as]);
-            if (++as == kAStages) {
-              as = 0;
-              aph ^= 1;
-            }
-          }
-          if (!ok) break;
-          umma_commit(&s_full[buf]);
-          if (j > 0) {
-            if (j == 1 && task_idx > 0) {
-              // The previous task's epilogue has read O.
-              if (!mbar_wait(o_free, (uint32_t)((task_idx - 1) & 1), abort_flag)) {
-                ok = false;
-                break;
+          while (sc < kDChunks || pc < 4) {
+            bool progress = false;
+            if (pc < 4) {
+              if (!p_gate) {
+                // The first P V of a task overwrites O: the previous task's
+                // epilogue must have read it. P of the tile must be complete
+                // in this CTA (its rows and the peer's).
+                const bool o_ok = !(j == 1 && task_idx > 0) ||
+                                  mbar_test_wait(smem_u32(o_free), (uint32_t)((task_idx - 1) & 1));
+                if (o_ok && mbar_test_wait_cluster(smem_u32(p_ready), (uint32_t)(pv & 1))) {
+                  p_gate = true;
+                  tc_fence_after();
+                }
               }
-              tc_fence_after();
+              if (p_gate && mbar_test_wait(smem_u32(&v_full[vs]), vph)) {
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(pbuf + pc * kPBlock);
+                const uint32_t b_addr = smem_u32(ring_v + vs * kVStage);
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                  umma_bf16(tmem_o, sw128_kmajor_desc(a_addr + k * 32),
+                            sw128_kmajor_desc(b_addr + k * 32), idesc_o,
+                            !(j == 1 && pc == 0 && k == 0));
+                issued = true;
+                umma_commit(&v_empty[vs]);
+                if (++vs == kVStages) {
+                  vs = 0;
+                  vph ^= 1;
+                }
+                if (++pc == 4) {
+                  // P and O are free once these MMAs complete, here and in the peer.
+                  umma_commit_multicast(p_free, 0x3);
+                  ++pv;
+                }
+                progress = true;
+              }
             }
-            if (!(ok = pv_tile(j == 1))) break;
+            if (sc < kDChunks) {
+              // The softmax warps have read this buffer's previous scores.
+              if (!s_gate &&
+                  mbar_test_wait(smem_u32(&s_free[buf]), (uint32_t)(((u >> 1) & 1) ^ 1))) {
+                s_gate = true;
+                tc_fence_after();
+              }
+              if (s_gate && mbar_test_wait(smem_u32(&a_full[as]), aph)) {
+                tc_fence_after();
+                const uint32_t q_addr = smem_u32(ring_a + as * kAStage);
+                const uint32_t k_addr = q_addr + kQBytes;
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                  umma_bf16(d_tmem, sw128_kmajor_desc(q_addr + k * 32),
+                            sw128_kmajor_desc(k_addr + k * 32), idesc_s, (sc | k) != 0);
+                issued = true;
+                umma_commit(&a_empty[as]);
+                if (++as == kAStages) {
+                  as = 0;
+                  aph ^= 1;
+                }
+                if (++sc == kDChunks) umma_commit(&s_full[buf]);
+                progress = true;
+              }
+            }
+            if (progress) {
+              t_idle = 0;
+            } else if (*abort_flag) {
+              ok = false;
+            } else if (t_idle == 0) {
+              t_idle = global_timer_ns();
+            } else if (global_timer_ns() - t_idle > kWaitLimitNs) {
+              record_device_error(kDevWaitTimeout);
+              *abort_flag = 1;
+              ok = false;
+            }
+            if (!ok) break;
           }
+          if (j < p.tiles) ++u;
         }
-        if (!ok) break;
-        if (p.tiles == 1 && task_idx > 0) {
-          if (!mbar_wait(o_free, (uint32_t)((task_idx - 1) & 1), abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-        }
-        if (!(ok = pv_tile(p.tiles == 1))) break;
       }
       if (!ok && issued) {
         umma_commit(drain);
@@ -351,10 +377,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[buf]);
-        float mloc = -3.0e38f;
+        // Row maximum as a tree of eight chains (one chain of 128 dependent
+        // max operations would put its latency on every tile's critical path).
+        float acc[8];
 #pragma unroll
-        for (int k = 0; k < kOwnKeys; ++k) mloc = fmaxf(mloc, sv[k]);
-        mloc *= kLog2e;
+        for (int i = 0; i < 8; ++i) acc[i] = sv[i];
+#pragma unroll
+        for (int k = 8; k < kOwnKeys; ++k) acc[k & 7] = fmaxf(acc[k & 7], sv[k]);
+#pragma unroll
+        for (int w = 4; w > 0; w >>= 1)
+#pragma unroll
+          for (int i = 0; i < w; ++i) acc[i] = fmaxf(acc[i], acc[i + w]);
+        const float mloc = acc[0] * kLog2e;
         // Row maxima to the peer: staged, then one bulk copy per warp that
         // completes its 128 bytes on the peer's mx_ready.
         mstage[buf * kRows + row] = mloc;
@@ -370,6 +404,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           break;
         }
         const float mt = fmaxf(mloc, mx[buf * kRows + row]);
+        // The running-maximum decision and this tile's probabilities need
+        // only the scores: they are computed while the previous tile's PV
+        // still runs, and only the stores into P (and a rescale of O) wait
+        // for it.
+        float f = 1.0f;
+        bool rescale = false;
+        if (j == 0) {
+          m = mt;
+          l = 0.0f;
+        } else {
+          const bool grow = mt > m + kRescaleLog2;
+          // tcgen05.ld / st are warp-collective (.sync.aligned): the warp
+          // rescales together when any of its rows needs it, each row with
+          // its own factor (1 for rows whose maximum stays).
+          rescale = __any_sync(0xffffffffu, grow);
+          if (grow) {
+            f = ex2_approx(m - mt);
+            m = mt;
+          }
+          l *= f;
+        }
+        // P = 2^(S log2 e - m) for this CTA's keys, packed 16-bit.
+        float lsum = 0.0f;
+        uint32_t pk[kOwnKeys / 2];
+#pragma unroll
+        for (int k = 0; k < kOwnKeys / 2; ++k) {
+          const float p0 = ex2_approx(fmaf(sv[2 * k], kLog2e, -m));
+          const float p1 = ex2_approx(fmaf(sv[2 * k + 1], kLog2e, -m));
+          lsum += p0 + p1;
+          pk[k] = Elem<D>::pack(p0, p1);
+        }
+        l += lsum;
         // P (and, for a rescale, O) may be written once both CTAs' PV of the
         // previous tile have completed.
         if (u > 0 &&
@@ -379,53 +445,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        if (j == 0) {
-          m = mt;
-          l = 0.0f;
-        } else {
-          // tcgen05.ld / st are warp-collective (.sync.aligned): the warp
-          // rescales together when any of its rows needs it, each row with
-          // its own factor (1 for rows whose maximum stays).
-          const bool grow = mt > m + kRescaleLog2;
-          if (__any_sync(0xffffffffu, grow)) {
-            const float f = grow ? ex2_approx(m - mt) : 1.0f;
-            l *= f;
-            if (grow) m = mt;
+        if (rescale) {
 #pragma unroll 1
-            for (int c = 0; c < kDHalf / 32; ++c) {
-              uint32_t r[32];
-              tmem_load_32x32b_x32(tmem_o + lane_off + c * 32, r);
-              tmem_wait_ld();
+          for (int c = 0; c < kDHalf / 32; ++c) {
+            uint32_t r[32];
+            tmem_load_32x32b_x32(tmem_o + lane_off + c * 32, r);
+            tmem_wait_ld();
 #pragma unroll
-              for (int k = 0; k < 32; ++k) r[k] = __float_as_uint(__uint_as_float(r[k]) * f);
-              tmem_store_32x32b_x32(tmem_o + lane_off + c * 32, r);
-            }
-            tmem_wait_st();
+            for (int k = 0; k < 32; ++k) r[k] = __float_as_uint(__uint_as_float(r[k]) * f);
+            tmem_store_32x32b_x32(tmem_o + lane_off + c * 32, r);
           }
+          tmem_wait_st();
         }
-        // P = 2^(S log2 e - m) for this CTA's keys: 16-bit K-major tiles of 64
-        // keys (blocks 2r, 2r + 1 of the tile's four).
-        float lsum = 0.0f;
+        // P as 16-bit K-major tiles of 64 keys (blocks 2r, 2r + 1 of the
+        // tile's four).
 #pragma unroll
         for (int c = 0; c < kOwnKeys / 32; ++c) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            const float p0 = ex2_approx(fmaf(sv[c * 32 + 2 * k], kLog2e, -m));
-            const float p1 = ex2_approx(fmaf(sv[c * 32 + 2 * k + 1], kLog2e, -m));
-            lsum += p0 + p1;
-            pk[k] = Elem<D>::pack(p0, p1);
-          }
           const int blk = 2 * (int)rank + (c >> 1);
           uint8_t* rowp = pbuf + blk * kPBlock + row * 128;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int chunk = (c & 1) * 4 + q;
+            const int k0 = c * 16 + 4 * q;
             *reinterpret_cast<uint4*>(rowp + ((chunk ^ (row & 7)) << 4)) =
-                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+                make_uint4(pk[k0], pk[k0 + 1], pk[k0 + 2], pk[k0 + 3]);
           }
         }
-        l += lsum;
         // The warp's 32 rows of both blocks to the peer (two 4 KB bulk copies
         // completing on the peer's p_ready), then ready here: P (and a
         // rescaled O) visible to this CTA's tensor core.

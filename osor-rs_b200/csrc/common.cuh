@@ -301,6 +301,30 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t addr, uint32_t pa
       : "memory");
   return ok != 0;
 }
+// Non-blocking tests of a phase (mbarrier.test_wait never suspends the
+// thread), for a thread that polls several barriers in turn.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_test_wait_cluster(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait of mbar_wait's contract with cluster-scope acquire.
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort) {
