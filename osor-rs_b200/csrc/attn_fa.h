@@ -18,7 +18,7 @@ cudaError_t attn_fused_launch(int dtype, const void* q, const void* k, long long
                               int dim, cudaStream_t stream);
 
 // The CTA-pair attention (attn_pair.cu) at width 512: true when
-// attn_pair_launch takes the shapes (tokens % 256 == 0, dim 512, 16-byte
+// attn_pair_launch takes the shapes (tokens % 512 == 0, dim 512, 16-byte
 // aligned operands and row strides).
 bool attn_pair_ok(int tokens, int dim, long long ld, long long ld_out, const void* q,
                   const void* k, const void* vt, const void* out);

@@ -17,8 +17,12 @@
 //     whole 128 x 256 P from local shared memory;
 //   * each CTA keeps the fp32 row sum of its own P half; the halves are added
 //     once per task before the output is normalised and stored.
-// The score buffers are double buffered, so S of tile j + 1 is computed while
-// the softmax warps work on tile j, and PV of tile j runs after.
+// The two score buffers are filled together: each shared-memory stage carries
+// one 64-wide chunk of Q and the matching K chunks of two tiles, so Q crosses
+// from L2 once per two tiles (the stages' load latency, not the tensor core,
+// bounds this kernel). The scores of tiles j + 2 and j + 3 are computed while
+// the softmax warps work on tiles j and j + 1, and P V of each tile follows
+// its softmax.
 //
 // Roles (224 threads per CTA): warp 0 TMA producer of the Q and K chunks,
 // warp 6 TMA producer of the V^T chunks of this CTA's output half (two
@@ -49,7 +53,7 @@ constexpr int kDChunk = 64;
 constexpr int kDChunks = kDim / kDChunk;    // 8
 constexpr int kQBytes = kRows * kDChunk * 2;        // 16 KB
 constexpr int kKBytes = kOwnKeys * kDChunk * 2;     // 16 KB
-constexpr int kAStage = kQBytes + kKBytes;          // 32 KB
+constexpr int kAStage = kQBytes + 2 * kKBytes;      // 48 KB: a Q chunk and the K chunks of two tiles
 constexpr int kVStage = kDHalf * 64 * 2;            // V^T chunk: 256 rows x 64 keys (32 KB)
 constexpr int kPBlock = kRows * 64 * 2;             // P: 128 rows x 64 keys (16 KB)
 constexpr int kAStages = 2;
@@ -58,15 +62,17 @@ constexpr int kThreads = 224;
 // Exchange area: the peer's row maxima [2][128], the peer's row sums [128],
 // and this CTA's row maxima staged for the copy to the peer [2][128].
 constexpr int kExBytes = (2 * kRows + kRows + 2 * kRows) * 4;
-constexpr int kSmem = kAStages * kAStage + kVStages * kVStage + 4 * kPBlock + kExBytes + 256 +
-                      1024;
+// No alignment slack: the dynamic window of a kernel without static shared
+// memory starts 1024-byte aligned (checked in the kernel).
+constexpr int kSmem = kAStages * kAStage + kVStages * kVStage + 4 * kPBlock + kExBytes + 256;
+static_assert(kSmem <= 227 * 1024, "shared memory");
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.0f;
 constexpr uint32_t kTmemO = 256;                    // O half at columns 256..511
 
 struct PairParams {
   int tokens, batch;
-  int tiles;  // tokens / 256
+  int tiles;  // tokens / 256 (even)
   int tasks;  // batch * tokens / 128
   void* out;
   long long ld_out;
@@ -92,10 +98,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     attn_pair_kernel(const __grid_constant__ CUtensorMap tmap_q,
                      const __grid_constant__ CUtensorMap tmap_k,
                      const __grid_constant__ CUtensorMap tmap_vt, const PairParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  uint8_t* ring_a = smem;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // The 128-byte swizzled tiles need 1024-byte aligned addresses.
+  if ((smem_u32(smem_raw) & 1023u) != 0) {
+    if (threadIdx.x == 0) record_device_error(kDevBadShape);
+    return;
+  }
+  uint8_t* ring_a = smem_raw;
   uint8_t* ring_v = ring_a + kAStages * kAStage;
   uint8_t* pbuf = ring_v + kVStages * kVStage;
   float* mx = reinterpret_cast<float*>(pbuf + 4 * kPBlock);  // [2][128], written by the peer
@@ -171,7 +180,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int qt = t % qtiles;
         const int b = t / qtiles;
         const int qrow = b * p.tokens + qt * kRows;
-        for (int j = 0; j < p.tiles && ok; ++j) {
+        for (int j = 0; j < p.tiles && ok; j += 2) {
+          // One Q chunk serves the scores of two tiles, j and j + 1.
           const int krow = b * p.tokens + j * kTileKeys + (int)rank * kOwnKeys;
           for (int dc = 0; dc < kDChunks; ++dc) {
             if (!mbar_wait(&a_empty[as], aph ^ 1, abort_flag)) {
@@ -182,6 +192,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint8_t* st = ring_a + as * kAStage;
             tma_load_2d(st, &tmap_q, &a_full[as], dc * kDChunk, qrow);
             tma_load_2d(st + kQBytes, &tmap_k, &a_full[as], dc * kDChunk, krow);
+            tma_load_2d(st + kQBytes + kKBytes, &tmap_k, &a_full[as], dc * kDChunk,
+                        krow + kTileKeys);
             if (++as == kAStages) {
               as = 0;
               aph ^= 1;
@@ -229,29 +241,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       long long pv = 0;  // global PV counter
       int task_idx = 0;
       bool ok = true, issued = false;
-      // Iteration j of a task issues the scores of tile j (kDChunks chunks
-      // of Q and K) and O += P V of tile j - 1 (four V^T chunks), each chunk
-      // as soon as its operands have arrived, P V first when both can go:
-      // the loads of the two rings overlap instead of one waiting behind
-      // the other. The barriers are polled with test_wait (which never
-      // suspends the thread); a poll that finds nothing ready for
-      // kWaitLimitNs gives up like the other waits.
+      // Iteration i of a task issues the scores of tiles 2i and 2i + 1 into
+      // the two score buffers (kDChunks A stages, each a Q chunk with both
+      // tiles' K chunks) and O += P V of tiles 2i - 2 and 2i - 1 (four V^T
+      // chunks each), each chunk as soon as its operands have arrived, P V
+      // first when both can go: the two rings' loads overlap instead of one
+      // waiting behind the other. The barriers are polled with test_wait
+      // (which never suspends the thread); a poll that finds nothing ready
+      // for kWaitLimitNs gives up like the other waits.
       uint64_t t_idle = 0;
+      const int pairs = p.tiles / 2;
       for (int t = cluster_id; t < p.tasks && ok; t += clusters, ++task_idx) {
-        for (int j = 0; j <= p.tiles && ok; ++j) {
-          int sc = j < p.tiles ? 0 : kDChunks;  // score chunks issued
-          int pc = j > 0 ? 0 : 4;               // P V chunks issued
+        for (int i = 0; i <= pairs && ok; ++i) {
+          int sc = i < pairs ? 0 : kDChunks;  // A stages issued
+          int pc = i > 0 ? 0 : 8;             // P V chunks issued (two tiles)
           bool s_gate = false, p_gate = false;
-          const int buf = (int)(u & 1);
-          const uint32_t d_tmem = tmem_base + buf * kOwnKeys;
-          while (sc < kDChunks || pc < 4) {
+          const uint32_t s_par = (uint32_t)(((u >> 1) & 1) ^ 1);
+          while (sc < kDChunks || pc < 8) {
             bool progress = false;
-            if (pc < 4) {
+            if (pc < 8) {
               if (!p_gate) {
                 // The first P V of a task overwrites O: the previous task's
                 // epilogue must have read it. P of the tile must be complete
                 // in this CTA (its rows and the peer's).
-                const bool o_ok = !(j == 1 && task_idx > 0) ||
+                const bool o_ok = !(i == 1 && pc == 0 && task_idx > 0) ||
                                   mbar_test_wait(smem_u32(o_free), (uint32_t)((task_idx - 1) & 1));
                 if (o_ok && mbar_test_wait_cluster(smem_u32(p_ready), (uint32_t)(pv & 1))) {
                   p_gate = true;
@@ -260,49 +273,55 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               }
               if (p_gate && mbar_test_wait(smem_u32(&v_full[vs]), vph)) {
                 tc_fence_after();
-                const uint32_t a_addr = smem_u32(pbuf + pc * kPBlock);
+                const int c = pc & 3;
+                const uint32_t a_addr = smem_u32(pbuf + c * kPBlock);
                 const uint32_t b_addr = smem_u32(ring_v + vs * kVStage);
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
                   umma_bf16(tmem_o, sw128_kmajor_desc(a_addr + k * 32),
                             sw128_kmajor_desc(b_addr + k * 32), idesc_o,
-                            !(j == 1 && pc == 0 && k == 0));
+                            !(i == 1 && pc == 0 && k == 0));
                 issued = true;
                 umma_commit(&v_empty[vs]);
                 if (++vs == kVStages) {
                   vs = 0;
                   vph ^= 1;
                 }
-                if (++pc == 4) {
+                if ((++pc & 3) == 0) {
                   // P and O are free once these MMAs complete, here and in the peer.
                   umma_commit_multicast(p_free, 0x3);
                   ++pv;
+                  p_gate = false;
                 }
                 progress = true;
               }
             }
             if (sc < kDChunks) {
-              // The softmax warps have read this buffer's previous scores.
-              if (!s_gate &&
-                  mbar_test_wait(smem_u32(&s_free[buf]), (uint32_t)(((u >> 1) & 1) ^ 1))) {
+              // The softmax warps have read both buffers' previous scores.
+              if (!s_gate && mbar_test_wait(smem_u32(&s_free[0]), s_par) &&
+                  mbar_test_wait(smem_u32(&s_free[1]), s_par)) {
                 s_gate = true;
                 tc_fence_after();
               }
               if (s_gate && mbar_test_wait(smem_u32(&a_full[as]), aph)) {
                 tc_fence_after();
                 const uint32_t q_addr = smem_u32(ring_a + as * kAStage);
-                const uint32_t k_addr = q_addr + kQBytes;
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                  umma_bf16(d_tmem, sw128_kmajor_desc(q_addr + k * 32),
-                            sw128_kmajor_desc(k_addr + k * 32), idesc_s, (sc | k) != 0);
+                for (int tb = 0; tb < 2; ++tb) {
+                  const uint32_t k_addr = q_addr + kQBytes + tb * kKBytes;
+#pragma unroll
+                  for (int k = 0; k < 4; ++k)
+                    umma_bf16(tmem_base + tb * kOwnKeys, sw128_kmajor_desc(q_addr + k * 32),
+                              sw128_kmajor_desc(k_addr + k * 32), idesc_s, (sc | k) != 0);
+                  if (sc == kDChunks - 1) umma_commit(&s_full[tb]);
+                }
                 issued = true;
                 umma_commit(&a_empty[as]);
                 if (++as == kAStages) {
                   as = 0;
                   aph ^= 1;
                 }
-                if (++sc == kDChunks) umma_commit(&s_full[buf]);
+                ++sc;
                 progress = true;
               }
             }
@@ -319,7 +338,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             if (!ok) break;
           }
-          if (j < p.tiles) ++u;
+          if (i < pairs) u += 2;
         }
       }
       if (!ok && issued) {
@@ -586,7 +605,7 @@ cudaError_t pair_launch_typed(const CUtensorMap& tq, const CUtensorMap& tk, cons
 
 bool attn_pair_ok(int tokens, int dim, long long ld, long long ld_out, const void* q,
                   const void* k, const void* vt, const void* out) {
-  if (tokens <= 0 || tokens % kTileKeys != 0 || dim != kDim) return false;
+  if (tokens <= 0 || tokens % (2 * kTileKeys) != 0 || dim != kDim) return false;
   if (ld % 8 != 0 || ld_out % 8 != 0) return false;
   return ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
            reinterpret_cast<uintptr_t>(vt) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
