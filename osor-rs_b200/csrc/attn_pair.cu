@@ -71,9 +71,9 @@ constexpr float kRescaleLog2 = 8.0f;
 constexpr uint32_t kTmemO = 256;                    // O half at columns 256..511
 
 struct PairParams {
-  int tokens, batch;
-  int tiles;  // tokens / 256 (even)
-  int tasks;  // batch * tokens / 128
+  int n_q, n_kv, batch;
+  int tiles;  // n_kv / 256 (even)
+  int tasks;  // batch * n_q / 128
   void* out;
   long long ld_out;
 };
@@ -166,7 +166,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync();  // both CTAs' barriers initialised before any remote arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-  const int qtiles = p.tokens / kRows;
+  const int qtiles = p.n_q / kRows;
   const int cluster_id = blockIdx.x >> 1;
   const int clusters = gridDim.x >> 1;
 
@@ -179,10 +179,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int t = cluster_id; t < p.tasks && ok; t += clusters) {
         const int qt = t % qtiles;
         const int b = t / qtiles;
-        const int qrow = b * p.tokens + qt * kRows;
+        const int qrow = b * p.n_q + qt * kRows;
         for (int j = 0; j < p.tiles && ok; j += 2) {
           // One Q chunk serves the scores of two tiles, j and j + 1.
-          const int krow = b * p.tokens + j * kTileKeys + (int)rank * kOwnKeys;
+          const int krow = b * p.n_kv + j * kTileKeys + (int)rank * kOwnKeys;
           for (int dc = 0; dc < kDChunks; ++dc) {
             if (!mbar_wait(&a_empty[as], aph ^ 1, abort_flag)) {
               ok = false;
@@ -518,7 +518,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const float inv = 1.0f / (l + lx[row]);
       uint4* dst = reinterpret_cast<uint4*>(
           static_cast<uint16_t*>(p.out) +
-          ((long long)b * p.tokens + qt * kRows + row) * p.ld_out + (int)rank * kDHalf);
+          ((long long)b * p.n_q + qt * kRows + row) * p.ld_out + (int)rank * kDHalf);
 #pragma unroll 1
       for (int c = 0; c < kDHalf / 32; ++c) {
         uint32_t r[32];
@@ -603,17 +603,19 @@ cudaError_t pair_launch_typed(const CUtensorMap& tq, const CUtensorMap& tk, cons
 
 }  // namespace
 
-bool attn_pair_ok(int tokens, int dim, long long ld, long long ld_out, const void* q,
-                  const void* k, const void* vt, const void* out) {
-  if (tokens <= 0 || tokens % (2 * kTileKeys) != 0 || dim != kDim) return false;
-  if (ld % 8 != 0 || ld_out % 8 != 0) return false;
+bool attn_pair_ok(int n_q, int n_kv, int dim, long long ld_q, long long ld_kv, long long ld_out,
+                  const void* q, const void* k, const void* vt, const void* out) {
+  if (n_q <= 0 || n_q % kRows != 0 || n_kv <= 0 || n_kv % (2 * kTileKeys) != 0 || dim != kDim)
+    return false;
+  if (ld_q % 8 != 0 || ld_kv % 8 != 0 || ld_out % 8 != 0) return false;
   return ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
            reinterpret_cast<uintptr_t>(vt) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
 }
 
-cudaError_t attn_pair_launch(int dtype, const void* q, const void* k, long long ld, const void* vt,
-                             void* out, long long ld_out, int batch, int tokens, cudaStream_t stream) {
-  if (!attn_pair_ok(tokens, kDim, ld, ld_out, q, k, vt, out) || batch <= 0)
+cudaError_t attn_pair_launch(int dtype, const void* q, long long ld_q, const void* k,
+                             long long ld_kv, const void* vt, void* out, long long ld_out,
+                             int batch, int n_q, int n_kv, cudaStream_t stream) {
+  if (!attn_pair_ok(n_q, n_kv, kDim, ld_q, ld_kv, ld_out, q, k, vt, out) || batch <= 0)
     return cudaErrorInvalidValue;
   EncodeTiledFnP encode = encode_fn_p();
   if (!encode) return cudaErrorNotSupported;
@@ -622,13 +624,15 @@ cudaError_t attn_pair_launch(int dtype, const void* q, const void* k, long long 
   CUtensorMap tq, tk, tv;
   cuuint32_t estr[3] = {1, 1, 1};
   {
-    cuuint64_t dims[2] = {(cuuint64_t)kDim, (cuuint64_t)batch * tokens};
-    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint64_t dims[2] = {(cuuint64_t)kDim, (cuuint64_t)batch * n_q};
+    cuuint64_t strides[1] = {(cuuint64_t)ld_q * 2};
     cuuint32_t box[2] = {(cuuint32_t)kDChunk, (cuuint32_t)kRows};
     if (encode(&tq, tdt, 2, const_cast<void*>(q), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
+    dims[1] = (cuuint64_t)batch * n_kv;
+    strides[0] = (cuuint64_t)ld_kv * 2;
     box[1] = kOwnKeys;
     if (encode(&tk, tdt, 2, const_cast<void*>(k), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -636,9 +640,9 @@ cudaError_t attn_pair_launch(int dtype, const void* q, const void* k, long long 
       return cudaErrorInvalidValue;
   }
   {
-    // V^T per image: [dim][tokens], images contiguous.
-    cuuint64_t dims[3] = {(cuuint64_t)tokens, (cuuint64_t)kDim, (cuuint64_t)batch};
-    cuuint64_t strides[2] = {(cuuint64_t)tokens * 2, (cuuint64_t)tokens * kDim * 2};
+    // V^T per image: [dim][n_kv], images contiguous.
+    cuuint64_t dims[3] = {(cuuint64_t)n_kv, (cuuint64_t)kDim, (cuuint64_t)batch};
+    cuuint64_t strides[2] = {(cuuint64_t)n_kv * 2, (cuuint64_t)n_kv * kDim * 2};
     cuuint32_t box[3] = {64, (cuuint32_t)kDHalf, 1};
     if (encode(&tv, tdt, 3, const_cast<void*>(vt), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -646,10 +650,11 @@ cudaError_t attn_pair_launch(int dtype, const void* q, const void* k, long long 
       return cudaErrorInvalidValue;
   }
   PairParams p;
-  p.tokens = tokens;
+  p.n_q = n_q;
+  p.n_kv = n_kv;
   p.batch = batch;
-  p.tiles = tokens / kTileKeys;
-  p.tasks = batch * (tokens / kRows);
+  p.tiles = n_kv / kTileKeys;
+  p.tasks = batch * (n_q / kRows);
   p.out = out;
   p.ld_out = ld_out;
   return dtype == kF16 ? pair_launch_typed<kF16>(tq, tk, tv, p, stream)

@@ -541,22 +541,22 @@ Status attention_core(int dtype, const void* q, long long ld_q, const void* k, c
     }
     return Status::ok();
   }
-  if (n_q == n_kv && ld_q == ld_kv && pair_attention_enabled() &&
-      attn_pair_ok(n_q, dim, ld_q, ld_out, q, k, vt, out)) {
+  if (pair_attention_enabled() &&
+      attn_pair_ok(n_q, n_kv, dim, ld_q, ld_kv, ld_out, q, k, vt, out)) {
     // V^T of every image, then one launch over all images on CTA pairs: the
     // scores stay in TMEM / shared memory and Q K^T is computed once.
-    const int tokens = n_q;
     cudaError_t e;
     for (int bi = 0; bi < batch; ++bi) {
-      const long long off = (long long)bi * tokens;
-      OpScope scope("attn_transpose", 0.0, 4.0 * tokens * dim, s, 1);
+      const long long off = (long long)bi * n_kv;
+      OpScope scope("attn_transpose", 0.0, 4.0 * n_kv * dim, s, 1);
       e = transpose16_launch(vb + off * ld_kv, ld_kv, static_cast<uint16_t*>(vt) + off * dim,
-                             tokens, tokens, dim, s);
+                             n_kv, n_kv, dim, s);
       if (e != cudaSuccess) return cuda_status(e, "attention transpose");
     }
-    const double nn = (double)tokens * tokens;
-    OpScope scope("attn_pair", 4.0 * batch * nn * dim, 8.0 * batch * tokens * dim, s, 1);
-    return cuda_status(attn_pair_launch(dtype, q, k, ld_q, vt, out, ld_out, batch, tokens, s),
+    OpScope scope("attn_pair", 4.0 * batch * (double)n_q * n_kv * dim,
+                  4.0 * batch * ((double)n_q + n_kv) * dim, s, 1);
+    return cuda_status(attn_pair_launch(dtype, q, ld_q, k, ld_kv, vt, out, ld_out, batch, n_q,
+                                        n_kv, s),
                        "pair attention");
   }
   if (n_q == n_kv && ld_q == ld_kv && fused_attention_enabled() &&

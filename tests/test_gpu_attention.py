@@ -20,8 +20,8 @@ pytestmark = pytest.mark.gpu
 
 
 CASES = [
-    (1, 256, 512),    # pair kernel, one 256-key tile, VAE width
-    (2, 1024, 512),   # pair kernel, four key tiles, two images
+    (1, 256, 512),    # three-kernel path (the pair kernel takes n_kv % 512 == 0)
+    (2, 1024, 512),   # pair kernel, two pairs of key tiles, two images
     (3, 512, 512),    # pair kernel, three images
     (3, 4096, 512),   # pair kernel: 96 tasks, more than the resident clusters take at once
     (1, 512, 256),    # three-kernel path (the pair kernel takes width 512 only)
@@ -49,6 +49,33 @@ def test_attend_matches_oracle(case, dt, cuda_device):
     want = oracle.attend(qf, np.ascontiguousarray(kf.transpose(0, 2, 1)), vf)
     err = np.abs(got - want)
     # bf16 probabilities (relative 2^-9) and bf16 output rounding.
+    assert err.max() <= 2e-2, err.max()
+    assert np.sqrt((err ** 2).mean()) <= 3e-3
+
+
+# (batch, n_q, n_kv, D): queries against a different number of keys, as a row
+# band's queries attend to the whole image (the band split): pair kernel for
+# n_q % 128 == 0 and n_kv % 512 == 0, the three-kernel path otherwise.
+KV_CASES = [(1, 256, 1024, 512), (2, 384, 512, 512), (1, 128, 2048, 512), (1, 256, 768, 512)]
+
+
+@pytest.mark.parametrize("case", KV_CASES, ids=lambda c: "x".join(map(str, c)))
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+def test_attend_kv_matches_oracle(case, dt, cuda_device):
+    b, nq, nkv, d = case
+    rng = np.random.default_rng(nq + nkv)
+
+    def half(a):
+        return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dt)
+
+    q = half(rng.standard_normal((b, nq, d)) * d ** -0.25 * 1.4)
+    k = half(rng.standard_normal((b, nkv, d)) * d ** -0.25 * 1.4)
+    v = half(rng.standard_normal((b, nkv, d)))
+    got = ops.attend_kv(q.cuda(), k.cuda(), v.cuda()).float().cpu().numpy()
+    qf, kf, vf = q.float().numpy(), k.float().numpy(), v.float().numpy()
+    want = oracle.attend(qf, np.ascontiguousarray(kf.transpose(0, 2, 1)), vf)
+    err = np.abs(got - want)
+    assert got.shape == (b, nq, d)
     assert err.max() <= 2e-2, err.max()
     assert np.sqrt((err ** 2).mean()) <= 3e-3
 
@@ -83,7 +110,7 @@ def test_fused_attention_rescales_growing_maxima(dt, cuda_device):
 def _rerun_in_child(env_overrides):
     env = dict(os.environ, **env_overrides)
     r = subprocess.run([sys.executable, "-m", "pytest", __file__, "-q", "-p", "no:cacheprovider",
-                        "-k", "attend_matches_oracle or rescales_growing_maxima"],
+                        "-k", "attend_matches_oracle or attend_kv_matches or rescales_growing_maxima"],
                        env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
 
