@@ -659,8 +659,11 @@ def run_bands(args, rank, world, local):
                                    f"GPUs",
                        "global_batch": world // k, "latent": [LATENT, LATENT],
                        "image": [IMAGE, IMAGE],
-                       "parallelism": f"row bands x{k} (halo rows, GroupNorm statistics and "
-                                      f"q|k|v over NCCL), {world // k} group(s)",
+                       "parallelism": (f"row bands x{k} (halo rows and GroupNorm statistics "
+                                       f"by peer stores over NVLink, q|k|v over NCCL), "
+                                       f"{world // k} group(s)" if dec.peer is not None else
+                                       f"row bands x{k} (halo rows, GroupNorm statistics and "
+                                       f"q|k|v over NCCL), {world // k} group(s)"),
                        "cuda_graph": bool(graph is not None),
                        "l2": "512 MiB L2 flush between timed steps",
                        "algorithmic_tflop_per_step": round(
@@ -678,6 +681,7 @@ def run_bands(args, rank, world, local):
     graph = None  # a graph holding NCCL calls must go before the process group
     if world > 1:
         dist.barrier()
+        dec.close()  # the peer arenas, after every rank's last exchange
         dist.destroy_process_group()
 
 

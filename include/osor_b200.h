@@ -431,6 +431,41 @@ int osor_unet_denoise(const osor_unet* unet, const float* input, int timestep,
                       const float* time_ids, float* output, int batch, int height, int width,
                       void* stream, const volatile int* cancel);
 
+/* ---- Row-band exchanges over peer memory (NVLink) ------------------------
+ * A group of `ranks` processes, one GPU each, decoding one image in row bands
+ * exchanges halo rows before each 3x3 convolution and GroupNorm statistics
+ * before each normalisation. These entry points do it with peer stores into
+ * the neighbours' device memory instead of NCCL calls: each rank creates an
+ * arena, the ranks exchange the handles (OSOR_PEER_HANDLE_BYTES each, by any
+ * host channel) and open every other rank's; the exchange kernels then take
+ * the same arguments every call (their epochs live on the device), so a
+ * decode that uses them can be captured in a CUDA graph. Every rank of the
+ * group must issue the same exchanges in the same order. The exchange
+ * itself has no counterpart in the reference, which runs its row bands one
+ * after another on one device (band geometry: src/native/conv.rs:96-108). */
+#define OSOR_PEER_HANDLE_BYTES 64
+typedef struct osor_peer_group osor_peer_group;
+
+/* Allocates this rank's arena on `device` (halo slots of halo_row_bytes,
+ * all-gather slots of gather_bytes) and writes its IPC handle to handle_out. */
+int osor_peer_group_create(int device, int ranks, int rank, size_t halo_row_bytes,
+                           size_t gather_bytes, osor_peer_group** out, void* handle_out);
+/* Maps rank `peer`'s arena (its handle from osor_peer_group_create). */
+int osor_peer_group_open(osor_peer_group* group, int peer, const void* handle);
+/* Waits for the device, unmaps the peers' arenas and frees this rank's (call
+ * after every rank has finished its exchanges). */
+void osor_peer_group_destroy(osor_peer_group* group);
+
+/* Fills the halo rows of an extended band x [rows + 2][row_bytes] (rows
+ * 1..rows are this rank's): row 0 from the rank above's last band row, row
+ * rows + 1 from the rank below's first, zeros at the image's top and bottom;
+ * this rank's rows 1 and `rows` go to its neighbours. */
+int osor_band_halo(osor_peer_group* group, void* x, long long row_bytes, int rows, void* stream);
+
+/* dst[r * bytes ..] = rank r's src for every rank of the group. */
+int osor_band_gather(osor_peer_group* group, const void* src, size_t bytes, void* dst,
+                     void* stream);
+
 /* One profiled op: kind ("conv_tc", "conv_direct", "groupnorm", ...),
  * algorithmic FLOPs and bytes, device time between the CUDA events recorded
  * on its stream, and the number of kernels it launched. */

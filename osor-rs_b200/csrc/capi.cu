@@ -10,6 +10,7 @@
 #include "noise.h"
 #include "pipeline.h"
 #include "ops.h"
+#include "peer.h"
 #include "profile.h"
 #include "unet.h"
 #include "unet_model.h"
@@ -21,6 +22,10 @@ struct osor_vae {
 
 struct osor_unet {
   osor::Unet* impl;
+};
+
+struct osor_peer_group {
+  osor::PeerGroup* impl;
 };
 
 namespace {
@@ -784,6 +789,59 @@ int osor_unet_denoise(const osor_unet* unet, const float* input, int timestep,
   if (!unet || !unet->impl) return fail(OSOR_ERR_INVALID_INPUT, "null UNet handle");
   return report(osor::unet_denoise(*unet->impl, input, timestep, time_ids, output, batch, height,
                                    width, static_cast<cudaStream_t>(stream), cancel));
+}
+
+int osor_peer_group_create(int device, int ranks, int rank, size_t halo_row_bytes,
+                           size_t gather_bytes, osor_peer_group** out, void* handle_out) {
+  if (!out || !handle_out) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  *out = nullptr;
+  if (osor_device_check(device) != OSOR_OK) return OSOR_ERR_UNAVAILABLE;
+  static_assert(OSOR_PEER_HANDLE_BYTES == osor::kPeerHandleBytes, "handle size");
+  osor::PeerGroup* g = nullptr;
+  if (const char* err = osor::peer_group_create(device, ranks, rank, halo_row_bytes, gather_bytes,
+                                                &g, handle_out))
+    return fail(OSOR_ERR_INVALID_INPUT, err);
+  *out = new osor_peer_group{g};
+  return OSOR_OK;
+}
+
+int osor_peer_group_open(osor_peer_group* group, int peer, const void* handle) {
+  if (!group || !group->impl || !handle) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (const char* err = osor::peer_group_open(group->impl, peer, handle))
+    return fail(OSOR_ERR_CUDA, err);
+  return OSOR_OK;
+}
+
+void osor_peer_group_destroy(osor_peer_group* group) {
+  if (!group) return;
+  osor::peer_group_destroy(group->impl);
+  delete group;
+}
+
+int osor_band_halo(osor_peer_group* group, void* x, long long row_bytes, int rows, void* stream) {
+  if (!group || !group->impl || !x) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (!aligned16(x)) return fail(OSOR_ERR_INVALID_INPUT, "band halo: x must be 16-byte aligned");
+  if (const char* err = osor::band_halo_check(group->impl, row_bytes, rows))
+    return fail(OSOR_ERR_INVALID_INPUT, err);
+  DeviceOf dev(x);
+  osor::OpScope scope("band_halo", 0.0, 4.0 * row_bytes, static_cast<cudaStream_t>(stream), 1);
+  const cudaError_t e =
+      osor::band_halo_launch(group->impl, x, row_bytes, rows, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "band halo");
+}
+
+int osor_band_gather(osor_peer_group* group, const void* src, size_t bytes, void* dst,
+                     void* stream) {
+  if (!group || !group->impl || !src || !dst) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (!aligned16(src) || !aligned16(dst))
+    return fail(OSOR_ERR_INVALID_INPUT, "band gather: 16-byte aligned buffers");
+  if (const char* err = osor::band_gather_check(group->impl, bytes))
+    return fail(OSOR_ERR_INVALID_INPUT, err);
+  DeviceOf dev(src);
+  osor::OpScope scope("band_gather", 0.0, 2.0 * bytes, static_cast<cudaStream_t>(stream), 1);
+  const cudaError_t e =
+      osor::band_gather_launch(group->impl, src, bytes, dst, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "band gather");
 }
 
 }  // extern "C"

@@ -13,13 +13,15 @@ Activations are held as *extended* NHWC tensors ``[1, R + 2, W, C]``: rows
 result equal to the one-GPU decode:
 
 * halo: before every 3x3 convolution each rank sends its first band row to the
-  rank above and its last band row to the rank below (torch.distributed
-  point-to-point, NCCL over NVLink on GPUs) into their halo rows; the image's
+  rank above and its last band row to the rank below into their halo rows (on
+  GPUs by peer stores into the neighbours' memory over NVLink,
+  ``osor_band_halo``; torch.distributed point-to-point otherwise); the image's
   top and bottom halo rows are zeros, the convolution's zero padding. The
   convolution runs over all R + 2 rows with padding 1, and rows 1..R of its
   output are exact (rows 0 and R + 1 are overwritten by the next exchange).
 * GroupNorm: each rank computes its band's per-group (mean, variance) over
-  rows 1..R (``osor_group_norm_stats``), the ranks all-gather them, and the
+  rows 1..R (``osor_group_norm_stats``), the ranks all-gather them (peer
+  stores, ``osor_band_gather``, on GPUs), and the
   apply kernel merges the K equal-count sets before normalizing the band
   (``osor_group_norm_apply``).
 * attention: the ranks all-gather the band's q|k|v projection, and each
@@ -36,17 +38,80 @@ band logic in the multi-process tests.
 """
 from __future__ import annotations
 
+import ctypes
+import os
 from typing import Dict, Optional
 
 import numpy as np
 import torch
 import torch.distributed as dist
 
-from . import ops
-from ._lib import InvalidInput, LAYOUT_NCHW
+from . import _lib, ops
+from ._lib import InvalidInput, LAYOUT_NCHW, check
 from .weights import SDXL_CHANNELS, SDXL_LAYERS
 
 GROUPS = 32
+GATHER_BYTES = 4096  # GroupNorm statistics: 32 groups x (mean, variance) per rank
+
+
+class PeerExchange:
+    """The band group's halo rows and small all-gathers over peer memory
+    (``osor_peer_group_*``, ``osor_band_halo``, ``osor_band_gather``): each
+    rank's arena is mapped into its neighbours' processes through CUDA IPC
+    handles that the ranks exchange once through the process group. The
+    exchanges then need no host synchronisation and no NCCL call, and a
+    decode built on them can be captured in a CUDA graph."""
+
+    def __init__(self, group: Optional[dist.ProcessGroup], device: torch.device,
+                 halo_row_bytes: int, gather_bytes: int = GATHER_BYTES):
+        self.lib = _lib.lib()
+        self.group = group
+        self.device = device
+        self.k = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.halo_row_bytes = int(halo_row_bytes)
+        self.gather_bytes = int(gather_bytes)
+        handle = (ctypes.c_uint8 * 64)()
+        g = ctypes.c_void_p()
+        index = device.index if device.index is not None else torch.cuda.current_device()
+        check(self.lib.osor_peer_group_create(index, self.k, self.rank,
+                                              self.halo_row_bytes, self.gather_bytes,
+                                              ctypes.byref(g), handle))
+        self.handle = g
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=device)
+        every = torch.empty((self.k, 64), dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        every = every.cpu().numpy()
+        for r in range(self.k):
+            if r != self.rank:
+                buf = (ctypes.c_uint8 * 64).from_buffer_copy(every[r].tobytes())
+                check(self.lib.osor_peer_group_open(g, r, buf))
+        dist.barrier(group=group)  # every arena mapped before the first exchange
+
+    def _stream(self):
+        return ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+
+    def halo(self, x: torch.Tensor) -> torch.Tensor:
+        r = x.shape[1] - 2
+        row_bytes = x.shape[2] * x.shape[3] * x.element_size()
+        check(self.lib.osor_band_halo(self.handle, ctypes.c_void_p(x.data_ptr()), row_bytes, r,
+                                      self._stream()))
+        return x
+
+    def gather(self, t: torch.Tensor) -> torch.Tensor:
+        t = t.contiguous()
+        out = torch.empty((self.k,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        check(self.lib.osor_band_gather(self.handle, ctypes.c_void_p(t.data_ptr()),
+                                        t.numel() * t.element_size(),
+                                        ctypes.c_void_p(out.data_ptr()), self._stream()))
+        return out
+
+    def close(self) -> None:
+        if self.handle is not None:
+            dist.barrier(group=self.group)  # no rank still writes into an arena
+            torch.cuda.synchronize(self.device)
+            self.lib.osor_peer_group_destroy(self.handle)
+            self.handle = None
 
 
 class CudaBandOps:
@@ -154,6 +219,25 @@ class _BandModel:
         self.k = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self._nccl = dist.is_initialized() and dist.get_backend(group) == "nccl"
+        # Peer-memory exchanges on GPUs (OSOR_BAND_P2P=0 keeps NCCL for them).
+        self._p2p = self._nccl and self.k > 1 and os.environ.get("OSOR_BAND_P2P", "1") != "0"
+        self.peer: Optional[PeerExchange] = None
+
+    def _ensure_peer(self, halo_row_bytes: int, device: torch.device) -> None:
+        """Creates (or, for wider rows, recreates) the peer arena; every rank
+        of the group reaches this at the same point of its decode."""
+        if not self._p2p:
+            return
+        if self.peer is not None and self.peer.halo_row_bytes >= halo_row_bytes:
+            return
+        if self.peer is not None:
+            self.peer.close()
+        self.peer = PeerExchange(self.group, device, halo_row_bytes)
+
+    def close(self) -> None:
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def _peer(self, local: int) -> int:
         return dist.get_global_rank(self.group, local) if self.group is not None else local
@@ -162,6 +246,8 @@ class _BandModel:
     def halo(self, x: torch.Tensor) -> torch.Tensor:
         """Fill the halo rows of extended x [1, R + 2, W, C] from the neighbours
         (zeros at the image's top and bottom)."""
+        if self.peer is not None and x.is_contiguous():
+            return self.peer.halo(x)
         r = x.shape[1] - 2
         p2p = []
         if self.rank > 0:
@@ -185,6 +271,9 @@ class _BandModel:
         """[K, *t.shape]: every rank's t in rank order."""
         if self.k == 1:
             return t.unsqueeze(0)
+        nbytes = t.numel() * t.element_size()
+        if self.peer is not None and nbytes <= self.peer.gather_bytes and nbytes % 16 == 0:
+            return self.peer.gather(t)
         out = torch.empty((self.k,) + tuple(t.shape), dtype=t.dtype, device=t.device)
         if self._nccl:
             dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
@@ -268,6 +357,11 @@ class BandDecoder(_BandModel):
                 r = (x.shape[2] if nchw else x.shape[1]) - 2
                 observer(name, x[:, :, 1:r + 1] if nchw else x[:, 1:r + 1])
 
+        # Widest halo row over the resolutions: w 2^i pixels of up block i,
+        # whose first resnet still takes block i - 1's channels (16-bit).
+        rev = list(reversed(self.channels))
+        self._ensure_peer(max(latents.shape[3] * 2 ** i * max(c, rev[max(i - 1, 0)]) * 2
+                              for i, c in enumerate(rev)), latents.device)
         lat = self._band_rows(latents, self.k, 4)
         r = lat.shape[2] - 2
         z = self.ops.conv("post_quant_conv", lat, out_nchw=True)
@@ -322,6 +416,11 @@ class BandEncoder(_BandModel):
         rank's rows of the posterior moments, f32 NCHW [1, 8, H / 8 / K, W / 8]."""
         if image.ndim == 4 and image.shape[2] % (8 * self.k):
             raise InvalidInput("image height must divide into 8 x the band group")
+        # Widest halo row over the resolutions: W / 2^i pixels of down block
+        # i, whose first resnet still takes block i - 1's channels (16-bit).
+        ch = list(self.channels)
+        self._ensure_peer(max(image.shape[3] // 2 ** i * max(c, ch[max(i - 1, 0)]) * 2
+                              for i, c in enumerate(ch)), image.device)
         x = self.ops.conv("encoder.conv_in", self._band_rows(image, self.k, 3))
         for i in range(len(self.channels)):
             for j in range(self.layers):

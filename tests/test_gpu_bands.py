@@ -137,18 +137,102 @@ def _rank_main(out_path: str) -> None:
         if dist.get_rank() == 0:
             np.save(out_path, torch.cat(list(every), dim=2).cpu().numpy())
             np.save(out_path + ".moments.npy", torch.cat(list(mevery), dim=2).cpu().numpy())
+        dec.close()
+        enc.close()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_band_decoder_two_gpus_matches_oracle(tmp_path):
-    out = str(tmp_path / "bands.npy")
+def _exchange_main() -> None:
+    """One rank of the peer-exchange check: osor_band_halo and osor_band_gather
+    against the rows and statistics the neighbours hold, eagerly (three calls,
+    both slot parities) and replayed from a CUDA graph (the epochs advance on
+    the device)."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    from osor_b200.bands import PeerExchange
+    local = int(os.environ["LOCAL_RANK"])
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        k, rank = dist.get_world_size(), dist.get_rank()
+        r, w, c = 6, 40, 96
+        ex = PeerExchange(None, dev, w * c * 2)
+
+        def band(seed):
+            t = torch.arange((r + 2) * w * c, device=dev, dtype=torch.float32).reshape(1, r + 2, w, c)
+            return ((t + 1000 * rank + 7 * seed) % 2039).to(torch.float16)
+
+        def expect(seed, x):
+            ref_up = ((torch.arange((r + 2) * w * c, device=dev, dtype=torch.float32)
+                       .reshape(1, r + 2, w, c) + 1000 * (rank - 1) + 7 * seed) % 2039).half()
+            ref_dn = ((torch.arange((r + 2) * w * c, device=dev, dtype=torch.float32)
+                       .reshape(1, r + 2, w, c) + 1000 * (rank + 1) + 7 * seed) % 2039).half()
+            top = ref_up[:, r] if rank > 0 else torch.zeros_like(x[:, 0])
+            bottom = ref_dn[:, 1] if rank + 1 < k else torch.zeros_like(x[:, 0])
+            assert torch.equal(x[:, 0], top), (rank, seed, "top")
+            assert torch.equal(x[:, r + 1], bottom), (rank, seed, "bottom")
+            assert torch.equal(x[:, 1:r + 1], band(seed)[:, 1:r + 1])
+
+        for seed in range(3):
+            x = band(seed)
+            ex.halo(x)
+            expect(seed, x)
+            st = torch.full((32, 2), float(rank * 10 + seed), device=dev)
+            got = ex.gather(st)
+            for q in range(k):
+                assert torch.all(got[q] == q * 10 + seed), (rank, seed, q)
+        # Captured once, replayed twice.
+        xs = band(5)
+        st = torch.full((32, 2), float(rank * 10 + 5), device=dev)
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                ex.halo(xs)
+                gathered = ex.gather(st)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        for _ in range(2):
+            xs.copy_(band(5))
+            xs[:, 0].fill_(-1.0)
+            xs[:, r + 1].fill_(-1.0)
+            g.replay()
+            torch.cuda.synchronize(dev)
+            expect(5, xs)
+            for q in range(k):
+                assert torch.all(gathered[q] == q * 10 + 5)
+        del g
+        from osor_b200.model import device_status
+        assert device_status(local) == 0
+        ex.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def _two_gpu_run(script_args, port, extra_env=None):
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1",
-           "--master-port=29531", __file__, out]
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=os.path.dirname(HERE))
+           f"--master-port={port}", __file__] + script_args
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", **(extra_env or {}))
+    return subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=os.path.dirname(HERE))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_exchange_two_gpus():
+    r = _two_gpu_run(["--exchange"], 29533)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("p2p", ["1", "0"], ids=["peer", "nccl"])
+def test_band_decoder_two_gpus_matches_oracle(tmp_path, p2p):
+    """The band decoder and encoder on two GPUs, with the halo rows and
+    statistics exchanged by peer stores (default) or by NCCL
+    (OSOR_BAND_P2P=0)."""
+    out = str(tmp_path / "bands.npy")
+    r = _two_gpu_run([out], 29531 if p2p == "1" else 29532, {"OSOR_BAND_P2P": p2p})
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     got = np.load(out)
     lat = workloads.decoder_latents(1, 16, 16, seed=42)
@@ -164,4 +248,7 @@ def test_band_decoder_two_gpus_matches_oracle(tmp_path):
 
 
 if __name__ == "__main__":
-    _rank_main(sys.argv[1])
+    if sys.argv[1] == "--exchange":
+        _exchange_main()
+    else:
+        _rank_main(sys.argv[1])
