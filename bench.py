@@ -539,8 +539,8 @@ def run_bands(args, rank, world, local):
     from datetime import timedelta
 
     from osor_b200 import _lib, workloads
-    from osor_b200.bands import BandDecoder, CudaBandOps
-    from osor_b200.model import device_status
+    from osor_b200.bands import BandDecoder, CudaBandOps, NativeBandDecoder
+    from osor_b200.model import NativeModel, device_status
     from osor_b200.weights import random_vae_weights
 
     k = args.bands
@@ -559,7 +559,14 @@ def run_bands(args, rank, world, local):
                     group = pg
     dtype = torch.float16 if args.dtype == "f16" else torch.bfloat16
     weights = random_vae_weights(0, parts=("decoder",))
-    dec = BandDecoder(CudaBandOps(weights, device=dev, dtype=dtype), group=group)
+    # The band decoder in C++ behind the C ABI (osor_vae_decode_band); with
+    # OSOR_NATIVE_BANDS=0 the Python one that calls the library per layer.
+    native = os.environ.get("OSOR_NATIVE_BANDS", "1") != "0"
+    if native:
+        model = NativeModel(weights, device=local, parts=("decoder",), dtype=args.dtype)
+        dec = NativeBandDecoder(model, group=group)
+    else:
+        dec = BandDecoder(CudaBandOps(weights, device=dev, dtype=dtype), group=group)
     lat_host = workloads.decoder_latents(1, LATENT, LATENT, seed=42 + rank // k)
     lat = torch.from_numpy(lat_host).to(dev)
     flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
@@ -659,7 +666,11 @@ def run_bands(args, rank, world, local):
                                    f"GPUs",
                        "global_batch": world // k, "latent": [LATENT, LATENT],
                        "image": [IMAGE, IMAGE],
-                       "parallelism": (f"row bands x{k} (halo rows and GroupNorm statistics "
+                       "parallelism": (f"row bands x{k}, one osor_vae_decode_band call per "
+                                       f"rank (halo rows, GroupNorm statistics and q|k|v by "
+                                       f"peer stores over NVLink), {world // k} group(s)"
+                                       if native else
+                                       f"row bands x{k} (halo rows and GroupNorm statistics "
                                        f"by peer stores over NVLink, q|k|v over NCCL), "
                                        f"{world // k} group(s)" if dec.peer is not None else
                                        f"row bands x{k} (halo rows, GroupNorm statistics and "

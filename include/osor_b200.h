@@ -447,9 +447,12 @@ int osor_unet_denoise(const osor_unet* unet, const float* input, int timestep,
 typedef struct osor_peer_group osor_peer_group;
 
 /* Allocates this rank's arena on `device` (halo slots of halo_row_bytes,
- * all-gather slots of gather_bytes) and writes its IPC handle to handle_out. */
+ * all-gather slots of gather_bytes, one bulk slot of bulk_bytes per rank for
+ * osor_vae_decode_band's attention keys and values, 0 for none) and writes
+ * its IPC handle to handle_out. */
 int osor_peer_group_create(int device, int ranks, int rank, size_t halo_row_bytes,
-                           size_t gather_bytes, osor_peer_group** out, void* handle_out);
+                           size_t gather_bytes, size_t bulk_bytes, osor_peer_group** out,
+                           void* handle_out);
 /* Maps rank `peer`'s arena (its handle from osor_peer_group_create). */
 int osor_peer_group_open(osor_peer_group* group, int peer, const void* handle);
 /* Waits for the device, unmaps the peers' arenas and frees this rank's (call
@@ -465,6 +468,27 @@ int osor_band_halo(osor_peer_group* group, void* x, long long row_bytes, int row
 /* dst[r * bytes ..] = rank r's src for every rank of the group. */
 int osor_band_gather(osor_peer_group* group, const void* src, size_t bytes, void* dst,
                      void* stream);
+
+/* Row-band decode of one image on one rank of a peer group: sizes of the
+ * per-call workspace, of the group's halo slots (halo_row_bytes) and of its
+ * bulk slots (bulk_bytes) for `ranks` ranks and [1, 4, latent_h, latent_w]
+ * latents (latent_h a multiple of ranks, bands of at least two rows). */
+int osor_vae_decode_band_sizes(const osor_vae* vae, int ranks, int latent_h, int latent_w,
+                               size_t* workspace_bytes, size_t* halo_row_bytes,
+                               size_t* bulk_bytes);
+
+/* The decoder over this rank's latent rows [r R, (r + 1) R), R = latent_h /
+ * ranks, with halo rows, GroupNorm statistics and the mid-block attention's
+ * keys and values exchanged with the group's other ranks over peer memory.
+ * latents: the whole image's f32 NCHW [1, 4, latent_h, latent_w] on this
+ * rank's device; image_band: this rank's rows of the raw decoded image, f32
+ * NCHW [1, 3, 8 R, 8 latent_w]. Every rank of the group calls it together.
+ * Replaces VaeDecoder::forward (src/native/vae_decoder.rs:104-114) for one
+ * image spread over GPUs in the row-band geometry of src/native/conv.rs
+ * :96-108. */
+int osor_vae_decode_band(const osor_vae* vae, osor_peer_group* group, const float* latents,
+                         float* image_band, int latent_h, int latent_w, void* workspace,
+                         size_t workspace_bytes, void* stream);
 
 /* One profiled op: kind ("conv_tc", "conv_direct", "groupnorm", ...),
  * algorithmic FLOPs and bytes, device time between the CUDA events recorded

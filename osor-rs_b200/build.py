@@ -21,7 +21,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-rdc=true",
          "-I" + INCLUDE, "-I" + CSRC]
-SOURCES = ["conv_tc.cu", "conv_tc2.cu", "conv_tcn.cu", "attn_fa.cu", "groupnorm.cu", "ops.cu", "vae.cu", "capi.cu", "profile.cu", "gn_noalloc.cu", "noise.cu", "pipeline.cu", "unet.cu", "unet_model.cu", "conv_out.cu", "attn_pair.cu", "attn_heads.cu", "peer.cu"]
+SOURCES = ["conv_tc.cu", "conv_tc2.cu", "conv_tcn.cu", "attn_fa.cu", "groupnorm.cu", "ops.cu", "vae.cu", "capi.cu", "profile.cu", "gn_noalloc.cu", "noise.cu", "pipeline.cu", "unet.cu", "unet_model.cu", "conv_out.cu", "attn_pair.cu", "attn_heads.cu", "peer.cu", "vae_band.cu"]
 
 
 def _compile(src: str) -> str:

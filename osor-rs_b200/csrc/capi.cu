@@ -149,6 +149,41 @@ int osor_vae_decode(const osor_vae* vae, const float* latents, float* image, int
   return report(s);
 }
 
+int osor_vae_decode_band_sizes(const osor_vae* vae, int ranks, int latent_h, int latent_w,
+                               size_t* workspace_bytes, size_t* halo_row_bytes,
+                               size_t* bulk_bytes) {
+  if (!vae || !workspace_bytes || !halo_row_bytes || !bulk_bytes)
+    return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (!decode_shape_ok(1, latent_h, latent_w))
+    return fail(OSOR_ERR_INVALID_INPUT, "band decode needs latent axes 4..=128");
+  osor::BandSizes sz;
+  osor::Status s = osor::vae_decode_band_sizes(*vae->impl, ranks, latent_h, latent_w, &sz);
+  if (!s.good()) return report(s);
+  *workspace_bytes = sz.workspace;
+  *halo_row_bytes = sz.halo_row_bytes;
+  *bulk_bytes = sz.bulk_bytes;
+  return OSOR_OK;
+}
+
+int osor_vae_decode_band(const osor_vae* vae, osor_peer_group* group, const float* latents,
+                         float* image_band, int latent_h, int latent_w, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  if (!vae || !group || !group->impl || !latents || !image_band || !workspace)
+    return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (!decode_shape_ok(1, latent_h, latent_w))
+    return fail(OSOR_ERR_INVALID_INPUT, "band decode needs latent axes 4..=128");
+  if (group->impl->device != vae->impl->device)
+    return fail(OSOR_ERR_INVALID_INPUT, "the peer group and the model are on different devices");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(vae->impl->device);
+  osor::Status s = osor::vae_decode_band(*vae->impl, group->impl, latents, image_band, latent_h,
+                                         latent_w, workspace, workspace_bytes,
+                                         static_cast<cudaStream_t>(stream));
+  cudaSetDevice(prev);
+  return report(s);
+}
+
 int osor_vae_encode_moments(const osor_vae* vae, const float* image, float* moments, int batch,
                             int height, int width, void* workspace, size_t workspace_bytes,
                             void* stream, const volatile int* cancel) {
@@ -792,14 +827,15 @@ int osor_unet_denoise(const osor_unet* unet, const float* input, int timestep,
 }
 
 int osor_peer_group_create(int device, int ranks, int rank, size_t halo_row_bytes,
-                           size_t gather_bytes, osor_peer_group** out, void* handle_out) {
+                           size_t gather_bytes, size_t bulk_bytes, osor_peer_group** out,
+                           void* handle_out) {
   if (!out || !handle_out) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
   *out = nullptr;
   if (osor_device_check(device) != OSOR_OK) return OSOR_ERR_UNAVAILABLE;
   static_assert(OSOR_PEER_HANDLE_BYTES == osor::kPeerHandleBytes, "handle size");
   osor::PeerGroup* g = nullptr;
   if (const char* err = osor::peer_group_create(device, ranks, rank, halo_row_bytes, gather_bytes,
-                                                &g, handle_out))
+                                                bulk_bytes, &g, handle_out))
     return fail(OSOR_ERR_INVALID_INPUT, err);
   *out = new osor_peer_group{g};
   return OSOR_OK;

@@ -1235,6 +1235,15 @@ cudaError_t gn_nhwc_apply_stats_launch(int dtype, const void* x, void* y, const 
   return apply_launch<kBf16>(x, y, coef, batch, channels, pixels, silu, stream);
 }
 
+cudaError_t gn_coef_from_stats_launch(const float* part_stats, int parts, int batch, int channels,
+                                      int groups, const float* gamma, const float* beta,
+                                      float eps, float* coef, cudaStream_t stream) {
+  const int total = batch * channels;
+  gn_coef_from_stats_kernel<<<(total + 255) / 256, 256, 0, stream>>>(
+      part_stats, parts, batch, channels, groups, gamma, beta, eps, coef);
+  return cudaGetLastError();
+}
+
 cudaError_t gn_nhwc_launch(int dtype, const void* x, void* y, const float* gamma, const float* beta,
                            int batch, int channels, long long pixels, int groups, float eps,
                            int silu, void* workspace, float* stats_out, cudaStream_t stream) {

@@ -91,6 +91,11 @@ cudaError_t gn_tiles_coef_launch(const float* tile_part, int batch, int channels
                                  long long pixels, int groups, const float* gamma,
                                  const float* beta, float eps, float* coef, float* stats_out,
                                  cudaStream_t stream);
+// Coefficients only: coef[b][c] = (mean, rstd * gamma, beta, 0) from `parts`
+// equal-count (mean, var) sets part_stats[p][b][g][2] (as the apply above).
+cudaError_t gn_coef_from_stats_launch(const float* part_stats, int parts, int batch, int channels,
+                                      int groups, const float* gamma, const float* beta,
+                                      float eps, float* coef, cudaStream_t stream);
 cudaError_t gn_nhwc_apply_tiles_launch(int dtype, const void* x, void* y, const float* gamma,
                                        const float* beta, int batch, int channels,
                                        long long pixels, int groups, float eps, int silu,

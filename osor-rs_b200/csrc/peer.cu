@@ -37,25 +37,28 @@ constexpr int kHaloCtas = 16;  // per direction
 constexpr int kHaloThreads = 256;
 constexpr uint64_t kPeerWaitNs = 2000000000ull;
 
-struct ArenaLayout {
-  size_t halo_bytes, gather_bytes;
-  size_t from_up, from_down, gather, flags_halo, flags_gather, counters, total;
-};
+}  // namespace
 
-ArenaLayout layout_of(size_t halo_bytes, size_t gather_bytes) {
+ArenaLayout layout_of(size_t halo_bytes, size_t gather_bytes, size_t bulk_bytes, int ranks) {
   ArenaLayout l;
   l.halo_bytes = (halo_bytes + 255) / 256 * 256;
   l.gather_bytes = (gather_bytes + 255) / 256 * 256;
+  l.bulk_bytes = (bulk_bytes + 255) / 256 * 256;
   l.from_up = 0;
   l.from_down = l.from_up + 2 * l.halo_bytes;
   l.gather = l.from_down + 2 * l.halo_bytes;
-  l.flags_halo = l.gather + 2 * (size_t)kMaxPeerRanks * l.gather_bytes;
+  l.bulk = l.gather + 2 * (size_t)kMaxPeerRanks * l.gather_bytes;
+  l.flags_halo = l.bulk + (size_t)ranks * l.bulk_bytes;
   l.flags_gather = l.flags_halo + kMaxPeerRanks * sizeof(unsigned int);
-  l.counters = l.flags_gather + kMaxPeerRanks * sizeof(unsigned int);
-  // counters: halo epoch, gather epoch, halo phase-1 count, halo phase-3 count
-  l.total = l.counters + 4 * sizeof(unsigned long long);
+  l.flags_bulk = l.flags_gather + kMaxPeerRanks * sizeof(unsigned int);
+  l.counters = l.flags_bulk + kMaxPeerRanks * sizeof(unsigned int);
+  // counters: halo epoch, gather epoch, halo phase-1 count, halo phase-3
+  // count, bulk epoch, bulk phase-1 count, bulk phase-3 count
+  l.total = l.counters + 8 * sizeof(unsigned long long);
   return l;
 }
+
+namespace {
 
 __device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
   unsigned int v;
@@ -223,29 +226,73 @@ __global__ void __launch_bounds__(256) band_gather_kernel(const GatherArgs a) {
   }
 }
 
-}  // namespace
+constexpr int kBulkCtas = 64;
 
-struct PeerGroup {
-  int device = 0, ranks = 0, rank = 0;
-  ArenaLayout l{};
-  uint8_t* arena = nullptr;
-  uint8_t* peers[kMaxPeerRanks] = {};
-  bool opened[kMaxPeerRanks] = {};
+struct BulkArgs {
+  const uint8_t* src;
+  long long bytes;
+  uint8_t* local;
+  uint8_t* peers[kMaxPeerRanks];
+  int rank, ranks;
+  ArenaLayout l;
 };
 
+// Grid: kBulkCtas CTAs. Every CTA stores its share of src into slot [rank] of
+// every rank's arena (this rank's included); the last CTA to finish
+// publishes the epoch in every peer's flag; every CTA then waits for all
+// peers' flags; the last CTA to finish advances the epoch.
+__global__ void __launch_bounds__(256) band_bulk_kernel(const BulkArgs a) {
+  unsigned long long* counters = reinterpret_cast<unsigned long long*>(a.local + a.l.counters);
+  unsigned int* flags = reinterpret_cast<unsigned int*>(a.local + a.l.flags_bulk);
+  const unsigned int epoch = (unsigned int)(*reinterpret_cast<volatile unsigned long long*>(&counters[4])) + 1u;
+  const long long n16 = a.bytes / 16;
+  const long long first = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long step = (long long)gridDim.x * blockDim.x;
+  for (int r = 0; r < a.ranks; ++r)
+    copy16(reinterpret_cast<uint4*>(a.peers[r] + a.l.bulk + (size_t)a.rank * a.l.bulk_bytes),
+           reinterpret_cast<const uint4*>(a.src), n16, first, step);
+  __threadfence_system();
+  __syncthreads();
+  __shared__ bool last;
+  if (threadIdx.x == 0) {
+    const unsigned long long target = (unsigned long long)epoch * gridDim.x;
+    last = atomicAdd(&counters[5], 1ull) + 1ull == target;
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    __threadfence_system();
+    for (int r = 0; r < a.ranks; ++r)
+      if (r != a.rank)
+        st_release_sys(reinterpret_cast<unsigned int*>(a.peers[r] + a.l.flags_bulk) + a.rank,
+                       epoch);
+  }
+  if (threadIdx.x == 0) {
+    for (int r = 0; r < a.ranks; ++r)
+      if (r != a.rank && !wait_flag(flags + r, epoch)) break;
+    const unsigned long long target = (unsigned long long)epoch * gridDim.x;
+    if (atomicAdd(&counters[6], 1ull) + 1ull == target) {
+      __threadfence();
+      atomicAdd(&counters[4], 1ull);
+    }
+  }
+}
+
+}  // namespace
+
 const char* peer_group_create(int device, int ranks, int rank, size_t halo_bytes,
-                              size_t gather_bytes, PeerGroup** out, void* handle) {
+                              size_t gather_bytes, size_t bulk_bytes, PeerGroup** out,
+                              void* handle) {
   *out = nullptr;
   if (ranks < 1 || ranks > kMaxPeerRanks || rank < 0 || rank >= ranks)
     return "peer group: 1..64 ranks and a rank inside the group";
   if (halo_bytes == 0 || gather_bytes == 0 || halo_bytes > (1ull << 30) ||
-      gather_bytes > (1ull << 20))
-    return "peer group: halo slots up to 1 GiB and gather slots up to 1 MiB";
+      gather_bytes > (1ull << 20) || bulk_bytes > (1ull << 34))
+    return "peer group: halo slots up to 1 GiB, gather slots up to 1 MiB, bulk parts up to 16 GiB";
   PeerGroup* g = new PeerGroup;
   g->device = device;
   g->ranks = ranks;
   g->rank = rank;
-  g->l = layout_of(halo_bytes, gather_bytes);
+  g->l = layout_of(halo_bytes, gather_bytes, bulk_bytes, ranks);
   int prev = 0;
   cudaGetDevice(&prev);
   const char* err = nullptr;
@@ -343,6 +390,27 @@ const char* band_gather_check(const PeerGroup* g, size_t bytes) {
   for (int r = 0; r < g->ranks; ++r)
     if (!g->peers[r]) return "band gather: a rank's arena is not mapped";
   return nullptr;
+}
+
+const char* band_bulk_check(const PeerGroup* g, size_t bytes) {
+  if (bytes == 0 || bytes % 16 != 0) return "band bulk gather: a multiple of 16 bytes";
+  if (bytes > g->l.bulk_bytes) return "band bulk gather: larger than the bulk slots";
+  for (int r = 0; r < g->ranks; ++r)
+    if (!g->peers[r]) return "band bulk gather: a rank's arena is not mapped";
+  return nullptr;
+}
+
+cudaError_t band_bulk_launch(PeerGroup* g, const void* src, size_t bytes, cudaStream_t s) {
+  BulkArgs a;
+  a.src = static_cast<const uint8_t*>(src);
+  a.bytes = (long long)bytes;
+  a.local = g->arena;
+  for (int r = 0; r < kMaxPeerRanks; ++r) a.peers[r] = r < g->ranks ? g->peers[r] : nullptr;
+  a.rank = g->rank;
+  a.ranks = g->ranks;
+  a.l = g->l;
+  band_bulk_kernel<<<kBulkCtas, 256, 0, s>>>(a);
+  return cudaGetLastError();
 }
 
 cudaError_t band_gather_launch(PeerGroup* g, const void* src, size_t bytes, void* dst,

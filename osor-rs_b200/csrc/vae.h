@@ -132,6 +132,23 @@ Status vae_encode(const Vae& m, const float* image, float* moments, int batch, i
                   int width, void* workspace, size_t workspace_bytes, cudaStream_t stream,
                   const volatile int* cancel);
 
+// Row-band decode of one image on one rank of a peer group (peer.h): the
+// rank's rows [r R, (r + 1) R) of the latent (R = h / ranks) through the
+// whole decoder, halo rows and GroupNorm statistics exchanged with the other
+// ranks between layers and the mid-block attention's keys and values
+// gathered from all of them. latents: the whole image [1, 4, h, w] f32 NCHW on
+// every rank; image_band: this rank's rows of the f32 NCHW image,
+// [1, 3, 8 R, 8 w].
+struct PeerGroup;
+struct BandSizes {
+  size_t workspace = 0;       // bytes of device workspace per call
+  size_t halo_row_bytes = 0;  // the peer group's halo slot size
+  size_t bulk_bytes = 0;      // the peer group's bulk slot size (attention q|k|v part)
+};
+Status vae_decode_band_sizes(const Vae& m, int ranks, int h, int w, BandSizes* out);
+Status vae_decode_band(const Vae& m, PeerGroup* g, const float* latents, float* image_band, int h,
+                       int w, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 // Single-op entry points shared with the C ABI. in_mode / out_mode are
 // kLayoutNhwc16 (16-bit of `dtype`) or kLayoutNchwF32.
 // With gn_part set and a tensor-core shape whose Cout has 4, 8 or 16

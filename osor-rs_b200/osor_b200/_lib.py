@@ -140,11 +140,13 @@ SIGNATURES = {
     "osor_unet_create": (_i, [ctypes.POINTER(OsorTensor), _sz, ctypes.POINTER(OsorUnetConfig),
                               _vp, _i, _vp, _i, ctypes.POINTER(_vp)]),
     "osor_unet_destroy": (None, [_vp]),
-    "osor_peer_group_create": (_i, [_i, _i, _i, _sz, _sz, _vp, _vp]),
+    "osor_peer_group_create": (_i, [_i, _i, _i, _sz, _sz, _sz, _vp, _vp]),
     "osor_peer_group_open": (_i, [_vp, _i, _vp]),
     "osor_peer_group_destroy": (None, [_vp]),
     "osor_band_halo": (_i, [_vp, _vp, _ll, _i, _vp]),
     "osor_band_gather": (_i, [_vp, _vp, _sz, _vp, _vp]),
+    "osor_vae_decode_band_sizes": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp]),
+    "osor_vae_decode_band": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp, _sz, _vp]),
     "osor_unet_denoise": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "osor_profile_begin": (None, []),
     "osor_profile_end": (_i, [_vp, _i, ctypes.POINTER(_i)]),

@@ -63,30 +63,33 @@ class PeerExchange:
     decode built on them can be captured in a CUDA graph."""
 
     def __init__(self, group: Optional[dist.ProcessGroup], device: torch.device,
-                 halo_row_bytes: int, gather_bytes: int = GATHER_BYTES):
+                 halo_row_bytes: int, gather_bytes: int = GATHER_BYTES, bulk_bytes: int = 0):
         self.lib = _lib.lib()
         self.group = group
         self.device = device
-        self.k = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        distributed = dist.is_available() and dist.is_initialized()
+        self.k = dist.get_world_size(group) if distributed else 1
+        self.rank = dist.get_rank(group) if distributed else 0
         self.halo_row_bytes = int(halo_row_bytes)
         self.gather_bytes = int(gather_bytes)
         handle = (ctypes.c_uint8 * 64)()
         g = ctypes.c_void_p()
         index = device.index if device.index is not None else torch.cuda.current_device()
+        self.bulk_bytes = int(bulk_bytes)
         check(self.lib.osor_peer_group_create(index, self.k, self.rank,
                                               self.halo_row_bytes, self.gather_bytes,
-                                              ctypes.byref(g), handle))
+                                              self.bulk_bytes, ctypes.byref(g), handle))
         self.handle = g
-        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=device)
-        every = torch.empty((self.k, 64), dtype=torch.uint8, device=device)
-        dist.all_gather_into_tensor(every, mine, group=group)
-        every = every.cpu().numpy()
-        for r in range(self.k):
-            if r != self.rank:
-                buf = (ctypes.c_uint8 * 64).from_buffer_copy(every[r].tobytes())
-                check(self.lib.osor_peer_group_open(g, r, buf))
-        dist.barrier(group=group)  # every arena mapped before the first exchange
+        if self.k > 1:
+            mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=device)
+            every = torch.empty((self.k, 64), dtype=torch.uint8, device=device)
+            dist.all_gather_into_tensor(every, mine, group=group)
+            every = every.cpu().numpy()
+            for r in range(self.k):
+                if r != self.rank:
+                    buf = (ctypes.c_uint8 * 64).from_buffer_copy(every[r].tobytes())
+                    check(self.lib.osor_peer_group_open(g, r, buf))
+            dist.barrier(group=group)  # every arena mapped before the first exchange
 
     def _stream(self):
         return ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
@@ -108,7 +111,8 @@ class PeerExchange:
 
     def close(self) -> None:
         if self.handle is not None:
-            dist.barrier(group=self.group)  # no rank still writes into an arena
+            if self.k > 1:
+                dist.barrier(group=self.group)  # no rank still writes into an arena
             torch.cuda.synchronize(self.device)
             self.lib.osor_peer_group_destroy(self.handle)
             self.handle = None
@@ -436,3 +440,66 @@ class BandEncoder(_BandModel):
         m = self.ops.conv("quant_conv", y, out_nchw=True)
         rows = m.shape[2] - 2
         return m[:, :, 1:rows + 1].contiguous()
+
+
+class NativeBandDecoder:
+    """The whole decoder on this rank's row band in one C ABI call
+    (``osor_vae_decode_band``): the library runs the band with the
+    whole-image decoder's kernels (GroupNorm statistics from the convolutions'
+    epilogues, fused upsample phases, CTA-pair attention, fused conv_norm_out
+    + conv_out) and the peer-memory exchanges between layers, with no Python
+    per layer. ``model`` is a NativeModel with the decoder on this rank's GPU;
+    ``group`` the band group (default: the whole world, or one rank without a
+    process group)."""
+
+    def __init__(self, model, group: Optional[dist.ProcessGroup] = None):
+        self.model = model
+        self.group = group
+        distributed = dist.is_available() and dist.is_initialized()
+        self.k = dist.get_world_size(group) if distributed else 1
+        self.rank = dist.get_rank(group) if distributed else 0
+        self.peer: Optional[PeerExchange] = None
+        self._ws: Optional[torch.Tensor] = None
+        self._sizes = None
+
+    def _prepare(self, h: int, w: int, device: torch.device) -> None:
+        lb = _lib.lib()
+        ws, halo, bulk = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t()
+        check(lb.osor_vae_decode_band_sizes(self.model._handle, self.k, h, w, ctypes.byref(ws),
+                                            ctypes.byref(halo), ctypes.byref(bulk)))
+        sizes = (ws.value, halo.value, bulk.value)
+        if self._sizes == sizes:
+            return
+        if self.peer is not None:
+            self.peer.close()
+        self.peer = PeerExchange(self.group, device, halo.value, GATHER_BYTES, bulk.value)
+        self._ws = torch.empty(max(ws.value, 1), dtype=torch.uint8, device=device)
+        self._sizes = sizes
+
+    def decode(self, latents: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Unscaled latents [1, 4, h, w] f32 (the whole image, on every rank)
+        -> this rank's rows of the raw RGB image, f32 NCHW [1, 3, 8 h / K, 8 w]."""
+        if latents.ndim != 4 or latents.shape[0] != 1 or latents.shape[1] != 4:
+            raise InvalidInput("band decode takes one latent image [1, 4, h, w]")
+        if latents.dtype != torch.float32 or not latents.is_cuda:
+            raise InvalidInput("band decode takes f32 CUDA latents")
+        latents = latents.contiguous()
+        _, _, h, w = latents.shape
+        if h % self.k:
+            raise InvalidInput("the latent height must divide evenly into the band group")
+        self._prepare(h, w, latents.device)
+        if out is None:
+            out = torch.empty((1, 3, 8 * h // self.k, 8 * w), dtype=torch.float32,
+                              device=latents.device)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(latents.device).cuda_stream)
+        check(_lib.lib().osor_vae_decode_band(self.model._handle, self.peer.handle,
+                                              ctypes.c_void_p(latents.data_ptr()),
+                                              ctypes.c_void_p(out.data_ptr()), h, w,
+                                              ctypes.c_void_p(self._ws.data_ptr()),
+                                              self._ws.numel(), stream))
+        return out
+
+    def close(self) -> None:
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None

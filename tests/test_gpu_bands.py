@@ -113,6 +113,69 @@ def test_band_encoder_one_rank_matches_oracle(cuda_device):
     assert workloads.rel_l2(got.cpu().numpy(), want) <= 1e-2
 
 
+def test_native_band_decoder_one_rank_matches_oracle(cuda_device):
+    """osor_vae_decode_band on a group of one rank (the band is the whole
+    image): the tiny shape against the oracle, the headline's 128 x 128
+    latents against the whole-image decode."""
+    from osor_b200.bands import NativeBandDecoder
+    from osor_b200.model import NativeModel
+    weights = _weights()
+    m = NativeModel(weights, device=0, parts=("decoder",), dtype="f16")
+    dec = NativeBandDecoder(m)
+    lat = workloads.decoder_latents(1, 16, 16, seed=42)
+    got = dec.decode(torch.from_numpy(lat).cuda()).cpu().numpy()
+    assert device_status(0) == 0
+    want = ovae.decode(weights, lat)
+    assert got.shape == want.shape
+    assert np.abs(got - want).max() <= MAX_ABS[torch.float16]
+    assert workloads.psnr(got, want) >= 40.0
+    big = torch.from_numpy(workloads.decoder_latents(1, 128, 128, seed=42)).cuda()
+    band = dec.decode(big)
+    whole = m.decode(big)
+    torch.cuda.synchronize()
+    assert device_status(0) == 0
+    diff = (band - whole).abs().max().item()
+    assert diff <= 2e-2, diff
+    assert workloads.psnr(band.cpu().numpy(), whole.cpu().numpy()) >= 45.0
+    dec.close()
+    m.close()
+
+
+def _native_main(out_path: str) -> None:
+    """One rank of the two-GPU native band check: the tiny decode and the
+    128 x 128 decode through osor_vae_decode_band, gathered on rank 0, with
+    rank 0's whole-image decode of the latter for comparison."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    from osor_b200.bands import NativeBandDecoder
+    from osor_b200.model import NativeModel
+    local = int(os.environ["LOCAL_RANK"])
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        m = NativeModel(_weights(), device=local, parts=("decoder",), dtype="f16")
+        dec = NativeBandDecoder(m)
+        outs = []
+        for size in (16, 128):
+            lat = torch.from_numpy(workloads.decoder_latents(1, size, size, seed=42)).to(dev)
+            band = dec.decode(lat)
+            every = torch.empty((dist.get_world_size(),) + tuple(band.shape), device=dev)
+            dist.all_gather_into_tensor(every, band.contiguous())
+            outs.append(torch.cat(list(every), dim=2).cpu().numpy())
+            if size == 128 and dist.get_rank() == 0:
+                outs.append(m.decode(lat).cpu().numpy())
+        assert device_status(local) == 0
+        if dist.get_rank() == 0:
+            np.save(out_path, outs[0])
+            np.save(out_path + ".big.npy", outs[1])
+            np.save(out_path + ".whole.npy", outs[2])
+        dec.close()
+        m.close()
+    finally:
+        dist.destroy_process_group()
+
+
 def _rank_main(out_path: str) -> None:
     """One rank of the two-GPU check (run under torch.distributed.run)."""
     import torch.distributed as dist
@@ -247,8 +310,30 @@ def test_band_decoder_two_gpus_matches_oracle(tmp_path, p2p):
     assert workloads.rel_l2(moments, want_m) <= 1e-2
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_native_band_decoder_two_gpus_matches_oracle(tmp_path):
+    """osor_vae_decode_band on two GPUs: the gathered bands of the tiny decode
+    against the oracle, those of the 128 x 128 decode against the whole-image
+    decode."""
+    out = str(tmp_path / "native.npy")
+    r = _two_gpu_run(["--native", out], 29534)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    got = np.load(out)
+    lat = workloads.decoder_latents(1, 16, 16, seed=42)
+    want = ovae.decode(_weights(), lat)
+    assert got.shape == want.shape
+    assert np.abs(got - want).max() <= MAX_ABS[torch.float16]
+    assert workloads.psnr(got, want) >= 40.0
+    big, whole = np.load(out + ".big.npy"), np.load(out + ".whole.npy")
+    assert big.shape == whole.shape == (1, 3, 1024, 1024)
+    assert np.abs(big - whole).max() <= 2e-2
+    assert workloads.psnr(big, whole) >= 45.0
+
+
 if __name__ == "__main__":
     if sys.argv[1] == "--exchange":
         _exchange_main()
+    elif sys.argv[1] == "--native":
+        _native_main(sys.argv[2])
     else:
         _rank_main(sys.argv[1])
