@@ -125,10 +125,12 @@ __global__ void __launch_bounds__(kHaloThreads) band_halo_kernel(const HaloArgs 
            reinterpret_cast<const uint4*>(a.x + (long long)a.rows * a.row_bytes), n16, first,
            step);
   }
-  __threadfence_system();
+  // One system-scope fence per CTA after the barrier: it is cumulative over
+  // the stores the barrier ordered before it.
   __syncthreads();
   __shared__ bool last;
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const unsigned long long target = (unsigned long long)epoch * gridDim.x;
     last = atomicAdd(&counters[2], 1ull) + 1ull == target;
   }
@@ -195,9 +197,9 @@ __global__ void __launch_bounds__(256) band_gather_kernel(const GatherArgs a) {
   }
   copy16(reinterpret_cast<uint4*>(a.dst + (size_t)a.rank * a.bytes),
          reinterpret_cast<const uint4*>(a.src), n16, threadIdx.x, blockDim.x);
-  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     for (int r = 0; r < a.ranks; ++r)
       if (r != a.rank)
         st_release_sys(reinterpret_cast<unsigned int*>(a.peers[r] + a.l.flags_gather) + a.rank,
@@ -251,10 +253,12 @@ __global__ void __launch_bounds__(256) band_bulk_kernel(const BulkArgs a) {
   for (int r = 0; r < a.ranks; ++r)
     copy16(reinterpret_cast<uint4*>(a.peers[r] + a.l.bulk + (size_t)a.rank * a.l.bulk_bytes),
            reinterpret_cast<const uint4*>(a.src), n16, first, step);
-  __threadfence_system();
+  // One system-scope fence per CTA after the barrier: it is cumulative over
+  // the stores the barrier ordered before it.
   __syncthreads();
   __shared__ bool last;
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const unsigned long long target = (unsigned long long)epoch * gridDim.x;
     last = atomicAdd(&counters[5], 1ull) + 1ull == target;
   }

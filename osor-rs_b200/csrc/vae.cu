@@ -481,12 +481,12 @@ Status mid_block(const Ctx& c, const MidLayer& L, int xi, int batch, int h, int 
   return st;
 }
 
-// The fused kernel (attn_fa.cu) runs when OSOR_FUSED_ATTENTION=1 is set in
-// the environment. By default attention takes the three-kernel path (scores
-// GEMM with TMA stores, softmax, P V), which measured faster at the VAE's
-// D = 512: TMEM holds one 256-key score tile and one half of the 128 x 512
-// output, so the fused kernel computes Q K^T once per output half and its
-// S tile cannot be double buffered.
+// The one-CTA fused kernel (attn_fa.cu) runs for the shapes the pair kernel
+// does not take when OSOR_FUSED_ATTENTION=1 is set in the environment;
+// otherwise those shapes take the three-kernel path (scores GEMM with TMA
+// stores, softmax, P V). At the VAE's D = 512 TMEM holds one 256-key score
+// tile and one half of the 128 x 512 output, so the one-CTA kernel computes
+// Q K^T once per output half and its S tile cannot be double buffered.
 bool fused_attention_enabled() {
   static const bool on = [] {
     const char* v = getenv("OSOR_FUSED_ATTENTION");

@@ -61,8 +61,8 @@ struct BandBufs {
   uint8_t* act[4] = {};
   float* tstat[4] = {};
   float* coef = nullptr;    // [C][4]
-  float* st_local = nullptr;  // [32][2]
-  float* st_all = nullptr;    // [ranks][32][2]
+  float* st_local = nullptr;  // [sets <= 4][32][2]
+  float* st_all = nullptr;    // [ranks][sets][32][2]
   void* gn_ws = nullptr;
   size_t gn_bytes = 0;
   float* lat = nullptr;     // the band's latent rows, [4][rows][w] f32
@@ -110,9 +110,9 @@ BandBufs band_layout(const Vae& m, int ranks, int h, int w) {
   const size_t coef_off = off;
   off += a256(512 * 4 * sizeof(float) * 2);
   const size_t st_off = off;
-  off += a256(kBandGroups * 2 * sizeof(float));
+  off += a256(4 * kBandGroups * 2 * sizeof(float));
   const size_t sta_off = off;
-  off += a256((size_t)ranks * kBandGroups * 2 * sizeof(float));
+  off += a256((size_t)ranks * 4 * kBandGroups * 2 * sizeof(float));
   const size_t gn_off = off;
   off += b.gn_bytes;
   const size_t lat_off = off;
@@ -173,6 +173,11 @@ struct BT {
   int c = 0;
   bool stats = false;
   long long tile0 = 0;
+  // A fused upsample's partials are phase-major: four ranges of tiles, one
+  // per output phase, `set_stride` tiles apart, each an equal share of the
+  // band's pixels. Their statistics go out as four sets.
+  int sets = 1;
+  long long set_stride = 0;
 };
 
 struct Band {
@@ -181,21 +186,31 @@ struct Band {
   PeerGroup* g;
   cudaStream_t s;
   BandGeom geo;  // current level
+  mutable int sets = 1;  // statistics sets per rank of the last band_stats
   uint8_t* ext(int buf) const { return b.act[buf] + b.spare; }
   long long row_bytes(int c) const { return (long long)geo.W * c * 2; }
   uint8_t* band_rows(const BT& t) const { return ext(t.buf) + row_bytes(t.c); }
   long long band_px() const { return (long long)geo.R * geo.W; }
 };
 
-// Band (mean, var) per group of t's rows 1..R into st_local.
+// Band (mean, var) per group of t's rows 1..R into st_local (B.sets equal-
+// count sets).
 Status band_stats(const Band& B, const BT& t, const NormLayer& N) {
-  if (t.stats && B.geo.W % 128 == 0) {
-    OpScope scope("groupnorm", 0.0, 0.0, B.s, 1);
-    return cuda_err(
-        gn_tiles_coef_launch(B.b.tstat[t.buf] + t.tile0 * kBandGroups * 2, 1, t.c, B.band_px(),
-                             kBandGroups, N.gamma, N.beta, kBandEps, B.b.coef, B.b.st_local, B.s),
-        "band group-norm statistics");
+  const int low_w = t.sets == 4 ? B.geo.W / 2 : B.geo.W;
+  if (t.stats && low_w % 128 == 0) {
+    B.sets = t.sets;
+    const long long px = B.band_px() / t.sets;
+    OpScope scope("groupnorm", 0.0, 0.0, B.s, t.sets);
+    for (int k = 0; k < t.sets; ++k) {
+      const cudaError_t e = gn_tiles_coef_launch(
+          B.b.tstat[t.buf] + (t.tile0 + k * t.set_stride) * kBandGroups * 2, 1, t.c, px,
+          kBandGroups, N.gamma, N.beta, kBandEps, B.b.coef, B.b.st_local + k * kBandGroups * 2,
+          B.s);
+      if (e != cudaSuccess) return cuda_err(e, "band group-norm statistics");
+    }
+    return Status::ok();
   }
+  B.sets = 1;
   const GnNhwcPlan plan = gn_nhwc_plan(1, t.c, B.band_px(), kBandGroups);
   if (plan.workspace_bytes > B.b.gn_bytes)
     return Status::err(OSOR_ERR_INVALID_INPUT, "band group-norm workspace too small");
@@ -206,9 +221,9 @@ Status band_stats(const Band& B, const BT& t, const NormLayer& N) {
 }
 
 Status band_gather_stats(const Band& B) {
-  OpScope scope("band_gather", 0.0, 2.0 * kBandGroups * 2 * 4 * B.geo.ranks, B.s, 1);
-  return cuda_err(band_gather_launch(B.g, B.b.st_local, kBandGroups * 2 * sizeof(float),
-                                     B.b.st_all, B.s),
+  const size_t bytes = (size_t)B.sets * kBandGroups * 2 * sizeof(float);
+  OpScope scope("band_gather", 0.0, 2.0 * bytes * B.geo.ranks, B.s, 1);
+  return cuda_err(band_gather_launch(B.g, B.b.st_local, bytes, B.b.st_all, B.s),
                   "band statistics gather");
 }
 
@@ -227,7 +242,7 @@ Status band_gn(const Band& B, const BT& t, const NormLayer& N, bool silu, int yi
   {
     OpScope scope("groupnorm", 0.0, 4.0 * B.band_px() * t.c, B.s, 2);
     st = cuda_err(gn_nhwc_apply_stats_launch(B.dtype, B.band_rows(t), B.ext(yi) + B.row_bytes(t.c),
-                                             N.gamma, N.beta, B.b.st_all, B.geo.ranks, 1, t.c,
+                                             N.gamma, N.beta, B.b.st_all, B.sets * B.geo.ranks, 1, t.c,
                                              B.band_px(), kBandGroups, kBandEps, silu ? 1 : 0,
                                              B.b.coef, B.s),
                   "band group-norm apply");
@@ -391,7 +406,7 @@ Status vae_decode_band(const Vae& m, PeerGroup* g, const float* latents, float* 
     const ConvLayer& L = up.resample_conv;
     const int oi = (x.buf + 1) % 4;
     const long long hi_row = (long long)(2 * B.geo.W) * L.cout * 2;
-    bool fused = false;
+    bool fused = false, phase_stats = false;
     if (L.w_up) {
       ConvTcArgs a;
       a.dtype = m.dtype;
@@ -414,6 +429,12 @@ Status vae_decode_band(const Vae& m, PeerGroup* g, const float* latents, float* 
       a.out = B.ext(oi) - hi_row;
       a.ld_out = L.cout;
       a.upsample = 1;
+      const int cpg = L.cout % kBandGroups == 0 ? L.cout / kBandGroups : 0;
+      if (B.geo.W % 128 == 0 && (cpg == 4 || cpg == 8 || cpg == 16)) {
+        a.gn_part = b.tstat[oi];
+        a.gn_cpg = cpg;
+        phase_stats = true;
+      }
       if (conv_tc_check(a) == nullptr) {
         const double px = 4.0 * a.in_h * a.in_w;
         OpScope scope("upconv_tc", 2.0 * px * L.cout * 4 * L.cin,
@@ -423,11 +444,16 @@ Status vae_decode_band(const Vae& m, PeerGroup* g, const float* latents, float* 
       }
     }
     if (fused) {
+      // Low-res rows 1..R of each phase's tiles are high-res band rows 1..2R.
+      const long long low_tiles_per_row = B.geo.W / 128;
+      x.stats = phase_stats;
+      x.sets = 4;
+      x.set_stride = (long long)(B.geo.R + 2) * low_tiles_per_row;
+      x.tile0 = low_tiles_per_row;
       B.geo.R *= 2;
       B.geo.W *= 2;
       x.buf = oi;
       x.c = L.cout;
-      x.stats = false;
     } else {
       // Nearest 2x of all R + 2 rows, then the 3x3 convolution over the
       // upsampled extended band (rows 1 .. 2R + 2 of the upsampled rows).
@@ -441,7 +467,7 @@ Status vae_decode_band(const Vae& m, PeerGroup* g, const float* latents, float* 
       if (!st.good()) return st;
       B.geo.R *= 2;
       B.geo.W *= 2;
-      BT u{ui, x.c, false, 0};
+      BT u{ui, x.c, false, 0, 1, 0};
       BT y;
       if (!(st = band_conv(B, L, u, x.buf, nullptr, &y)).good()) return st;
       x = y;
@@ -475,7 +501,7 @@ Status vae_decode_band(const Vae& m, PeerGroup* g, const float* latents, float* 
     const double px = (double)height * Wf;
     OpScope scope("gn_conv_out", 2.0 * px * fa.cout * 9 * fa.cin,
                   2.0 * px * fa.cin + 4.0 * px * fa.cout, s, 2);
-    cudaError_t e = gn_coef_from_stats_launch(b.st_all, ranks, 1, fa.cin, kBandGroups,
+    cudaError_t e = gn_coef_from_stats_launch(b.st_all, B.sets * ranks, 1, fa.cin, kBandGroups,
                                               d.norm_out.gamma, d.norm_out.beta, kBandEps, b.coef,
                                               s);
     if (e == cudaSuccess) e = gn_conv_out_launch(fa, s);
@@ -488,7 +514,7 @@ Status vae_decode_band(const Vae& m, PeerGroup* g, const float* latents, float* 
       OpScope scope("groupnorm", 0.0, 4.0 * B.band_px() * x.c, s, 2);
       st = cuda_err(gn_nhwc_apply_stats_launch(m.dtype, B.band_rows(x),
                                                B.ext(ti) + B.row_bytes(x.c), d.norm_out.gamma,
-                                               d.norm_out.beta, b.st_all, ranks, 1, x.c,
+                                               d.norm_out.beta, b.st_all, B.sets * ranks, 1, x.c,
                                                B.band_px(), kBandGroups, kBandEps, 1, b.coef, s),
                     "band group-norm apply");
     }
