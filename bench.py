@@ -256,6 +256,21 @@ def run_ops(args):
                 ms = _timed(lambda: conv.forward_checked(xt, residual=rt), args.steps, args.warmup,
                             flush)
             flop = 2.0 * b * h * w * cout * 9 * cin
+            # Vendor comparator (informational): cuDNN through torch on the same
+            # bf16 tensors, channels_last, with the residual add.
+            xv = torch.from_numpy(x).to(dev, torch.bfloat16).contiguous(
+                memory_format=torch.channels_last)
+            wv = torch.from_numpy(wt).to(dev, torch.bfloat16).contiguous(
+                memory_format=torch.channels_last)
+            bv = torch.from_numpy(bias).to(dev, torch.bfloat16)
+            if cout <= 16:
+                vendor = lambda: torch.nn.functional.conv2d(xv, wv, bv, padding=1).float()
+            else:
+                rv = torch.from_numpy(res).to(dev, torch.bfloat16).contiguous(
+                    memory_format=torch.channels_last)
+                vendor = lambda: torch.nn.functional.conv2d(xv, wv, bv, padding=1).add_(rv)
+            vendor_ms = _timed(vendor, args.steps, args.warmup, flush)
+            del xv, wv, bv
             if cout <= 16:
                 nbytes = 2.0 * b * h * w * cin + 4.0 * b * h * w * cout + 2.0 * cout * 9 * cin
             else:
@@ -276,6 +291,9 @@ def run_ops(args):
                               "tflops": round(tf, 1), "frac_of_sustained_peak": round(tf / tflops_sus, 4),
                               "gbs_min_bytes": round(nbytes / (ms / 1e3) / 1e9, 1),
                               "frac_of_hbm": round(nbytes / (ms / 1e3) / 1e9 / hbm, 4),
+                              "vendor_cudnn": {"ms": round(vendor_ms, 4),
+                                               "tflops": round(flop / (vendor_ms / 1e3) / 1e12, 1),
+                                               "what": "torch conv2d bf16 channels_last (+ residual)"},
                               "peak_source": src}), flush=True)
     elif args.op == "groupnorm":
         shapes = [tuple(int(v) for v in args.shape.split(","))] if args.shape else GN_SHAPES
@@ -286,9 +304,19 @@ def run_ops(args):
             ms = _timed(lambda: norm.forward_silu(xt), args.steps, args.warmup, flush)
             nbytes = 4.0 * xt.numel()
             gbs = nbytes / (ms / 1e3) / 1e9
+            # Vendor comparator (informational): torch group_norm + silu on the same tensor.
+            gt = torch.from_numpy(gamma).to(dev, torch.bfloat16)
+            bt = torch.from_numpy(beta).to(dev, torch.bfloat16)
+            vendor_ms = _timed(lambda: torch.nn.functional.silu(
+                torch.nn.functional.group_norm(xt, 32, gt, bt, eps=1e-6)), args.steps,
+                args.warmup, flush)
             print(json.dumps({"op": "groupnorm32+silu (NCHW, fused)", "shape": list(shape),
                               "dtype": "bf16", "ms": round(ms, 4), "gbs": round(gbs, 1),
-                              "frac_of_hbm": round(gbs / hbm, 4), "peak_source": src}), flush=True)
+                              "frac_of_hbm": round(gbs / hbm, 4),
+                              "vendor_torch": {"ms": round(vendor_ms, 4),
+                                               "gbs": round(nbytes / (vendor_ms / 1e3) / 1e9, 1),
+                                               "what": "torch group_norm + silu, bf16"},
+                              "peak_source": src}), flush=True)
     elif args.op == "encode":
         from osor_b200.model import NativeModel
         from osor_b200.weights import random_vae_weights
