@@ -276,7 +276,11 @@ def run_ops(args):
             else:
                 nbytes = 2.0 * b * h * w * (cin + 2 * cout) + 2.0 * cout * 9 * cin
             tf = flop / (ms / 1e3) / 1e12
-            if (cin % 64 == 0 and (cout in (64, 128) or cout <= 16) and w % 256 == 0
+            if (cin == 128 and cout == 3 and w <= 1024
+                    and os.environ.get("OSOR_FUSED_THIN_CONV", "1") != "0"):
+                path = ("tcgen05 per-pixel tap product (M=128 pixels, N=32 (tap, channel) "
+                        "columns, taps summed in the epilogue)")
+            elif (cin % 64 == 0 and (cout in (64, 128) or cout <= 16) and w % 256 == 0
                     and os.environ.get("OSOR_PIXEL_N_CONV", "1") != "0"):
                 path = "tcgen05 implicit GEMM, pixels on N (M=Cout 128, N=256 pixels)"
             elif cin % 64 == 0 and cout == 128 and os.environ.get("OSOR_PAIR_CONV", "1") != "0":

@@ -64,6 +64,9 @@ struct OutParams {
   int batch, height, width, tiles;
   const float* coef;  // [batch][kCin][4]: (mean, rstd * gamma, beta, -)
   int silu;
+  int normalize;      // 0: S = x (a plain 3x3 convolution; coef unused)
+  int w_conv;         // 1: weights in the convolution layout [cout][3][3][cin] at wconv
+  const uint16_t* wconv;
   const float* bias;  // [kCout]
   float* out;         // [batch][kCout][height][width]
 };
@@ -157,6 +160,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(tmem_holder, 2 * kRowCols);
     tmem_relinquish();
   }
+  if (p.w_conv && threadIdx.x < 2 * kN * 8) {
+    // Convolution-layout weights [co][ky][kx][ci] into the operand's
+    // tap-major rows (ky * 3 + kx) * 3 + co, 16 bytes per thread, in the
+    // 128-byte swizzled layout (chunk j of row r at j ^ (r % 8)); rows 27..31
+    // of the N = 32 operand are zero.
+    const int box = threadIdx.x / (kN * 8), rem = threadIdx.x % (kN * 8);
+    const int r = rem >> 3, j = rem & 7;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (r < 9 * kCout) {
+      const int tap = r / kCout, co = r % kCout;
+      v = __ldg(reinterpret_cast<const uint4*>(p.wconv + ((long long)co * 9 + tap) * kCin +
+                                               box * 64 + j * 8));
+    }
+    *reinterpret_cast<uint4*>(wz + box * kWBoxBytes + r * 128 + ((j ^ (r & 7)) << 4)) = v;
+    fence_proxy_async_smem();
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -166,9 +185,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------ TMA producer
-      mbar_arrive_expect_tx(wfull, 2 * kWBoxBytes);
-      tma_load_2d(wz, &tmap_w, wfull, 0, 0);
-      tma_load_2d(wz + kWBoxBytes, &tmap_w, wfull, 64, 0);
+      if (p.w_conv) {
+        mbar_arrive(wfull);  // the weights were stored before the setup barrier
+      } else {
+        mbar_arrive_expect_tx(wfull, 2 * kWBoxBytes);
+        tma_load_2d(wz, &tmap_w, wfull, 0, 0);
+        tma_load_2d(wz + kWBoxBytes, &tmap_w, wfull, 64, 0);
+      }
       int st = 0;
       uint32_t ph = 0;
       bool ok = true;
@@ -280,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int y0 = (int)(r - (long long)img * p.height);
       const int y1 = (int)min((long long)p.height, y0 + (rows.end - r));
       r += y1 - y0;
-      if (img != cur_img) {
+      if (img != cur_img && p.normalize) {
 #pragma unroll
         for (int b = 0; b < 2; ++b)
 #pragma unroll
@@ -299,8 +322,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sbuf = stages + st * kStageBytes;
           const int valid_px = min(kTilePx, p.width - t * kTilePx);
+          // Without the normalisation the stage is the convolution's input
+          // as loaded (the TMA zero fill covers the pixels past the edge).
 #pragma unroll
-          for (int b = 0; b < 2; ++b) {
+          for (int b = 0; b < (p.normalize ? 2 : 0); ++b) {
 #pragma unroll 4
             for (int m = 0; m < kTilePx / 32; ++m) {
               const int row = row0 + 32 * m;
@@ -519,7 +544,7 @@ const char* gn_conv_out_check(const GnConvOutArgs& a) {
   if (a.cout != kCout) return "fused conv_out: 3 output channels";
   if (a.batch <= 0 || a.height <= 0 || a.width <= 0) return "empty convolution";
   if (a.width > kMaxTiles * kTilePx) return "fused conv_out: width <= 1024";
-  if (!a.x || !a.wz || !a.coef || !a.bias || !a.out) return "null argument";
+  if (!a.x || !a.wz || (a.normalize && !a.coef) || !a.bias || !a.out) return "null argument";
   if ((reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.wz) |
        reinterpret_cast<uintptr_t>(a.coef)) & 15)
     return "alignment";
@@ -545,7 +570,11 @@ cudaError_t gn_conv_out_launch(const GnConvOutArgs& a, cudaStream_t stream) {
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
-  {
+  if (a.w_conv) {
+    // The kernel stores the convolution-layout weights itself; the weight
+    // map is unused (a copy of the input's keeps the parameter valid).
+    tw = tx;
+  } else {
     cuuint64_t dims[2] = {(cuuint64_t)kCin, (cuuint64_t)kN};
     cuuint64_t strides[1] = {(cuuint64_t)kCin * 2};
     cuuint32_t box[2] = {64, (cuuint32_t)kN};
@@ -562,6 +591,9 @@ cudaError_t gn_conv_out_launch(const GnConvOutArgs& a, cudaStream_t stream) {
   p.tiles = (a.width + kTilePx - 1) / kTilePx;
   p.coef = a.coef;
   p.silu = a.silu;
+  p.normalize = a.normalize;
+  p.w_conv = a.w_conv;
+  p.wconv = static_cast<const uint16_t*>(a.wz);
   p.bias = a.bias;
   p.out = a.out;
   const int di = a.dtype == kF16 ? 1 : 0;

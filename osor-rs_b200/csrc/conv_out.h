@@ -23,6 +23,11 @@ struct GnConvOutArgs {
   const float* bias = nullptr;
   int cout = 0;
   float* out = nullptr;
+  // normalize = 0: S = x, a plain 3x3 convolution (coef unused, may be null).
+  int normalize = 1;
+  // w_conv = 1: wz holds the convolution's own weights [cout][3][3][128]
+  // (16-bit, rows of 9 * 128) instead of the tap matrix.
+  int w_conv = 0;
 };
 
 // nullptr when the fused kernel takes the shape (Cin 128, Cout 3, width <=

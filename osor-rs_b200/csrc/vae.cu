@@ -506,6 +506,17 @@ bool gn_conv_out_enabled() {
   return on;
 }
 
+// The fused conv_out kernel also runs plain 128 -> 3 3x3 convolutions into
+// NCHW f32; OSOR_FUSED_THIN_CONV=0 in the environment (read once) keeps them on
+// the padded pixels-on-N kernel, for comparing.
+bool thin_conv_fused_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("OSOR_FUSED_THIN_CONV");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 // The CTA-pair attention (attn_pair.cu) is the default at width 512;
 // OSOR_PAIR_ATTENTION=0 in the environment (read once) keeps the other paths.
 bool pair_attention_enabled() {
@@ -725,6 +736,35 @@ Status run_conv(int dtype, const ConvLayer& L, const void* x, int in_mode, int b
   const double out_bytes = out_px * L.cout * (out_mode == kLayoutNchwF32 ? 4 : 2);
   const double bytes = in_bytes + out_bytes + (residual ? out_px * L.cout * 2 : 0.0) +
                        2.0 * L.cout * L.k * L.k * L.cin;
+  // A 3x3, 128 -> 3 convolution into an NCHW f32 image (the decoder's
+  // conv_out when its GroupNorm is applied separately, and the standalone
+  // op): the fused conv_out kernel without its normalisation, one MMA of
+  // N = 32 (tap, channel) columns per pixel instead of 3 channels padded to
+  // a 128-row tile.
+  if (in_mode == kLayoutNhwc16 && out_mode == kLayoutNchwF32 && !residual && L.k == 3 &&
+      L.stride == 1 && L.pad == 1 && L.pad_end == 1 && in_pixel_stride == L.cin &&
+      out_h == in_h && out_w == in_w && thin_conv_fused_enabled()) {
+    GnConvOutArgs f;
+    f.dtype = dtype;
+    f.x = x;
+    f.batch = batch;
+    f.height = in_h;
+    f.width = in_w;
+    f.cin = L.cin;
+    f.coef = nullptr;
+    f.silu = 0;
+    f.normalize = 0;
+    f.w_conv = 1;
+    f.wz = L.w;
+    f.bias = L.bias;
+    f.cout = L.cout;
+    f.out = static_cast<float*>(out);
+    if (L.bias && gn_conv_out_check(f) == nullptr) {
+      OpScope scope("conv_thin_tc", flops, bytes, s, 1);
+      const cudaError_t e = gn_conv_out_launch(f, s);
+      if (e != cudaErrorInvalidValue) return cuda_status(e, "thin convolution");
+    }
+  }
   ConvTcArgs a;
   if (tc_args(&a, dtype, L, x, in_mode, batch, in_h, in_w, in_pixel_stride, out_h, out_w, out,
               out_mode, out_pixel_stride, residual, ld_res)) {

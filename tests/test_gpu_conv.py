@@ -150,7 +150,11 @@ def test_upsample_matches_oracle(cuda_device):
 
 
 def test_pixel_n_thin_nchw_output_exact(cuda_device):
-    """conv_out shape class: 16-bit NHWC in, Cout 3 NCHW f32 out, pixels on N."""
+    """conv_out shape class: 16-bit NHWC in, Cout 3 NCHW f32 out. By default
+    the fused conv_out kernel runs it without its normalisation (one N = 32
+    product of (tap, channel) columns per pixel, taps summed in the
+    epilogue); test_padded_thin_path_runs_the_same_case runs the pixels-on-N
+    kernel it replaced."""
     b, cin, h, w, cout = 1, 128, 3, 256, 3
     x = dyadic((b, cin, h, w), 13, 41, 20, 1 / 16).reshape(b, cin, h, w)
     wt = dyadic((cout, cin, 3, 3), 7, 11, 5, 1 / 32).reshape(cout, cin, 3, 3) / np.float32(8)
@@ -160,3 +164,17 @@ def test_pixel_n_thin_nchw_output_exact(cuda_device):
     got = conv.forward_checked(xt, out_layout=LAYOUT_NCHW)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(got.cpu().numpy(), oracle.conv2d(x, wt, bias, stride=1, padding=1))
+
+
+def test_padded_thin_path_runs_the_same_case(cuda_device):
+    """OSOR_FUSED_THIN_CONV=0 (read once per process) keeps 128 -> 3
+    convolutions on the pixels-on-N kernel with the weights padded to a
+    128-row tile: the exact case above again, in a child process."""
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ, OSOR_FUSED_THIN_CONV="0")
+    r = subprocess.run([sys.executable, "-m", "pytest", __file__, "-q", "-p", "no:cacheprovider",
+                        "-k", "pixel_n_thin_nchw_output_exact"],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
