@@ -106,14 +106,14 @@ struct HaloArgs {
 // neighbours and copies its share of the received rows into rows 0 and
 // rows + 1 (zeros at the image's top and bottom). The last CTA to finish
 // advances the epoch.
-__global__ void __launch_bounds__(kHaloThreads) band_halo_kernel(const HaloArgs a) {
+__device__ __forceinline__ void halo_body(const HaloArgs& a, int nctas, int cta) {
   unsigned long long* counters = reinterpret_cast<unsigned long long*>(a.local + a.l.counters);
   unsigned int* flags = reinterpret_cast<unsigned int*>(a.local + a.l.flags_halo);
   const unsigned int epoch = (unsigned int)(*reinterpret_cast<volatile unsigned long long*>(&counters[0])) + 1u;
   const int parity = (int)(epoch & 1u);
   const long long n16 = a.row_bytes / 16;
-  const bool to_up = blockIdx.x < kHaloCtas;
-  const int part = to_up ? blockIdx.x : blockIdx.x - kHaloCtas;
+  const bool to_up = cta < kHaloCtas;
+  const int part = to_up ? cta : cta - kHaloCtas;
   const long long first = (long long)part * blockDim.x + threadIdx.x;
   const long long step = (long long)kHaloCtas * blockDim.x;
   // Phase 1.
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(kHaloThreads) band_halo_kernel(const HaloArgs 
   __shared__ bool last;
   if (threadIdx.x == 0) {
     __threadfence_system();
-    const unsigned long long target = (unsigned long long)epoch * gridDim.x;
+    const unsigned long long target = (unsigned long long)epoch * nctas;
     last = atomicAdd(&counters[2], 1ull) + 1ull == target;
   }
   __syncthreads();
@@ -163,12 +163,16 @@ __global__ void __launch_bounds__(kHaloThreads) band_halo_kernel(const HaloArgs 
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned long long target = (unsigned long long)epoch * gridDim.x;
+    const unsigned long long target = (unsigned long long)epoch * nctas;
     if (atomicAdd(&counters[3], 1ull) + 1ull == target) {
       __threadfence();
       atomicAdd(&counters[0], 1ull);
     }
   }
+}
+
+__global__ void __launch_bounds__(kHaloThreads) band_halo_kernel(const HaloArgs a) {
+  halo_body(a, gridDim.x, blockIdx.x);
 }
 
 struct GatherArgs {
@@ -183,7 +187,7 @@ struct GatherArgs {
 
 // One CTA: write src into every peer's gather slot [parity][rank], publish
 // the epoch, wait for every peer's, copy the slots into dst in rank order.
-__global__ void __launch_bounds__(256) band_gather_kernel(const GatherArgs a) {
+__device__ __forceinline__ void gather_body(const GatherArgs& a) {
   unsigned long long* counters = reinterpret_cast<unsigned long long*>(a.local + a.l.counters);
   unsigned int* flags = reinterpret_cast<unsigned int*>(a.local + a.l.flags_gather);
   const unsigned int epoch = (unsigned int)(*reinterpret_cast<volatile unsigned long long*>(&counters[1])) + 1u;
@@ -226,6 +230,18 @@ __global__ void __launch_bounds__(256) band_gather_kernel(const GatherArgs a) {
     __threadfence();
     atomicAdd(&counters[1], 1ull);
   }
+}
+
+__global__ void __launch_bounds__(256) band_gather_kernel(const GatherArgs a) { gather_body(a); }
+
+// The halo exchange (CTAs [0, 2 kHaloCtas)) and the all-gather (the last CTA)
+// of one layer in one launch, so the ranks meet once.
+__global__ void __launch_bounds__(kHaloThreads) band_halo_gather_kernel(const HaloArgs h,
+                                                                        const GatherArgs g) {
+  if (blockIdx.x < 2 * kHaloCtas)
+    halo_body(h, 2 * kHaloCtas, blockIdx.x);
+  else
+    gather_body(g);
 }
 
 constexpr int kBulkCtas = 64;
@@ -371,8 +387,8 @@ const char* band_halo_check(const PeerGroup* g, long long row_bytes, int rows) {
   return nullptr;
 }
 
-cudaError_t band_halo_launch(PeerGroup* g, void* x, long long row_bytes, int rows,
-                             cudaStream_t s) {
+namespace {
+HaloArgs halo_args(PeerGroup* g, void* x, long long row_bytes, int rows) {
   HaloArgs a;
   a.x = static_cast<uint8_t*>(x);
   a.row_bytes = row_bytes;
@@ -384,7 +400,32 @@ cudaError_t band_halo_launch(PeerGroup* g, void* x, long long row_bytes, int row
   a.up_arena = a.up >= 0 ? g->peers[a.up] : nullptr;
   a.down_arena = a.down >= 0 ? g->peers[a.down] : nullptr;
   a.l = g->l;
-  band_halo_kernel<<<2 * kHaloCtas, kHaloThreads, 0, s>>>(a);
+  return a;
+}
+GatherArgs gather_args(PeerGroup* g, const void* src, size_t bytes, void* dst) {
+  GatherArgs a;
+  a.src = static_cast<const uint8_t*>(src);
+  a.bytes = (long long)bytes;
+  a.dst = static_cast<uint8_t*>(dst);
+  a.local = g->arena;
+  for (int r = 0; r < kMaxPeerRanks; ++r) a.peers[r] = r < g->ranks ? g->peers[r] : nullptr;
+  a.rank = g->rank;
+  a.ranks = g->ranks;
+  a.l = g->l;
+  return a;
+}
+}  // namespace
+
+cudaError_t band_halo_launch(PeerGroup* g, void* x, long long row_bytes, int rows,
+                             cudaStream_t s) {
+  band_halo_kernel<<<2 * kHaloCtas, kHaloThreads, 0, s>>>(halo_args(g, x, row_bytes, rows));
+  return cudaGetLastError();
+}
+
+cudaError_t band_halo_gather_launch(PeerGroup* g, void* x, long long row_bytes, int rows,
+                                    const void* src, size_t bytes, void* dst, cudaStream_t s) {
+  band_halo_gather_kernel<<<2 * kHaloCtas + 1, kHaloThreads, 0, s>>>(
+      halo_args(g, x, row_bytes, rows), gather_args(g, src, bytes, dst));
   return cudaGetLastError();
 }
 
@@ -419,16 +460,7 @@ cudaError_t band_bulk_launch(PeerGroup* g, const void* src, size_t bytes, cudaSt
 
 cudaError_t band_gather_launch(PeerGroup* g, const void* src, size_t bytes, void* dst,
                                cudaStream_t s) {
-  GatherArgs a;
-  a.src = static_cast<const uint8_t*>(src);
-  a.bytes = (long long)bytes;
-  a.dst = static_cast<uint8_t*>(dst);
-  a.local = g->arena;
-  for (int r = 0; r < kMaxPeerRanks; ++r) a.peers[r] = r < g->ranks ? g->peers[r] : nullptr;
-  a.rank = g->rank;
-  a.ranks = g->ranks;
-  a.l = g->l;
-  band_gather_kernel<<<1, 256, 0, s>>>(a);
+  band_gather_kernel<<<1, 256, 0, s>>>(gather_args(g, src, bytes, dst));
   return cudaGetLastError();
 }
 

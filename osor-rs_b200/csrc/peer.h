@@ -46,6 +46,11 @@ const char* band_halo_check(const PeerGroup* g, long long row_bytes, int rows);
 cudaError_t band_halo_launch(PeerGroup* g, void* x, long long row_bytes, int rows,
                              cudaStream_t s);
 
+// band_halo and band_gather of one layer in one launch (one rendezvous of the
+// ranks instead of two); the checks of both apply.
+cudaError_t band_halo_gather_launch(PeerGroup* g, void* x, long long row_bytes, int rows,
+                                    const void* src, size_t bytes, void* dst, cudaStream_t s);
+
 // dst[r] = rank r's src (bytes each), for every rank of the group.
 const char* band_gather_check(const PeerGroup* g, size_t bytes);
 cudaError_t band_gather_launch(PeerGroup* g, const void* src, size_t bytes, void* dst,

@@ -232,27 +232,53 @@ Status band_halo(const Band& B, int buf, int c) {
   return cuda_err(band_halo_launch(B.g, B.ext(buf), B.row_bytes(c), B.geo.R, B.s), "band halo");
 }
 
-// GroupNorm(+SiLU) of t's band rows into buffer yi's band rows (statistics
-// merged over the ranks), then, with halo, the exchange of y's halo rows.
+// The band's statistics (band_stats) to every rank and, with halo, t's raw
+// edge rows to the neighbours (filling t's halo rows; zeros at the image's
+// top and bottom) in one launch, so the ranks meet once per GroupNorm.
+Status band_exchange(const Band& B, const BT& t, bool halo) {
+  if (!halo) return band_gather_stats(B);
+  const size_t bytes = (size_t)B.sets * kBandGroups * 2 * sizeof(float);
+  OpScope scope("band_exchange", 0.0, 4.0 * B.row_bytes(t.c) + 2.0 * bytes * B.geo.ranks, B.s, 1);
+  return cuda_err(band_halo_gather_launch(B.g, B.ext(t.buf), B.row_bytes(t.c), B.geo.R,
+                                          B.b.st_local, bytes, B.b.st_all, B.s),
+                  "band halo and statistics exchange");
+}
+
+// GroupNorm(+SiLU) of t into buffer yi (statistics merged over the ranks).
+// With halo, t's raw halo rows come from the neighbours in the same exchange
+// as the statistics and are normalised with the band (a row of the image is
+// normalised alike on every rank), so y's halo rows are ready for the next
+// convolution; the image's own top / bottom halo rows are zeroed in y (the
+// convolution's zero padding). Without halo only rows 1..R are written.
 Status band_gn(const Band& B, const BT& t, const NormLayer& N, bool silu, int yi, bool halo,
                BT* y) {
   Status st = band_stats(B, t, N);
-  if (st.good()) st = band_gather_stats(B);
+  if (st.good()) st = band_exchange(B, t, halo);
   if (!st.good()) return st;
+  const bool top = B.geo.rank == 0, bottom = B.geo.rank + 1 == B.geo.ranks;
+  const int lo = halo && !top ? 0 : 1;
+  const int hi = halo && !bottom ? B.geo.R + 2 : B.geo.R + 1;
+  const long long rb = B.row_bytes(t.c);
+  const long long px = (long long)(hi - lo) * B.geo.W;
   {
-    OpScope scope("groupnorm", 0.0, 4.0 * B.band_px() * t.c, B.s, 2);
-    st = cuda_err(gn_nhwc_apply_stats_launch(B.dtype, B.band_rows(t), B.ext(yi) + B.row_bytes(t.c),
-                                             N.gamma, N.beta, B.b.st_all, B.sets * B.geo.ranks, 1, t.c,
-                                             B.band_px(), kBandGroups, kBandEps, silu ? 1 : 0,
+    OpScope scope("groupnorm", 0.0, 4.0 * px * t.c, B.s, 2);
+    st = cuda_err(gn_nhwc_apply_stats_launch(B.dtype, B.ext(t.buf) + lo * rb, B.ext(yi) + lo * rb,
+                                             N.gamma, N.beta, B.b.st_all, B.sets * B.geo.ranks,
+                                             1, t.c, px, kBandGroups, kBandEps, silu ? 1 : 0,
                                              B.b.coef, B.s),
                   "band group-norm apply");
   }
   if (!st.good()) return st;
+  if (halo && top)
+    st = cuda_err(cudaMemsetAsync(B.ext(yi), 0, rb, B.s), "band top padding row");
+  if (st.good() && halo && bottom)
+    st = cuda_err(cudaMemsetAsync(B.ext(yi) + (long long)(B.geo.R + 1) * rb, 0, rb, B.s),
+                  "band bottom padding row");
   y->buf = yi;
   y->c = t.c;
   y->stats = false;
-  if (halo) return band_halo(B, yi, t.c);
-  return Status::ok();
+  y->sets = 1;
+  return st;
 }
 
 // Convolution of the extended tensor x (all R + 2 rows) into buffer oi's
@@ -350,6 +376,11 @@ Status vae_decode_band(const Vae& m, PeerGroup* g, const float* latents, float* 
     return Status::err(OSOR_ERR_INVALID_INPUT, "band decode workspace is too small");
   if (g->l.halo_bytes < sizes.halo_row_bytes)
     return Status::err(OSOR_ERR_INVALID_INPUT, "the peer group's halo slots are too small");
+  if (g->l.gather_bytes < 4 * kBandGroups * 2 * sizeof(float))
+    return Status::err(OSOR_ERR_INVALID_INPUT, "the peer group's gather slots are too small");
+  for (int r = 0; r < g->ranks; ++r)
+    if (!g->peers[r])
+      return Status::err(OSOR_ERR_INVALID_INPUT, "a rank's arena is not mapped in the peer group");
   const int ranks = g->ranks, rank = g->rank;
   const int R = h / ranks, r0 = rank * R;
   const bool scratch = !pair_takes(R * w, ranks * R * w, m.channels[3]);
@@ -478,7 +509,9 @@ Status vae_decode_band(const Vae& m, PeerGroup* g, const float* latents, float* 
   // neighbours' rows as its halo (exchanged first) and writes the image rows.
   const int Rf = B.geo.R, Wf = B.geo.W;
   if (!(st = band_stats(B, x, d.norm_out)).good()) return st;
-  if (!(st = band_gather_stats(B)).good()) return st;
+  // Statistics and x's raw halo rows in one exchange (the fused kernel
+  // normalises the halo rows itself).
+  if (!(st = band_exchange(B, x, true)).good()) return st;
   const bool top = rank == 0, bottom = rank + 1 == ranks;
   const int first = top ? 1 : 0;
   const int height = Rf + 2 - (top ? 1 : 0) - (bottom ? 1 : 0);
@@ -496,7 +529,6 @@ Status vae_decode_band(const Vae& m, PeerGroup* g, const float* latents, float* 
   fa.bias = d.conv_out.bias;
   fa.cout = d.conv_out.cout;
   fa.out = tmp;
-  if (!(st = band_halo(B, x.buf, x.c)).good()) return st;
   if (d.conv_out.w_z && gn_conv_out_check(fa) == nullptr) {
     const double px = (double)height * Wf;
     OpScope scope("gn_conv_out", 2.0 * px * fa.cout * 9 * fa.cin,
