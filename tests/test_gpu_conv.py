@@ -73,6 +73,12 @@ TC_CASES = [
     (2, 256, 4, 128, 128, 3, 1, 1),    # streamed, row shift
     (2, 256, 8, 128, 128, 1, 1, 0),    # 1x1, resident, deep pipeline
     (3, 64, 8, 16, 128, 3, 1, 1),      # odd number of tiles: one-CTA kernel
+    # The UNet's widths: Cout 384 / 640 (multiples of 128 only: one-CTA
+    # kernel, several 128-wide channel tiles) and Cout 1280 over few pixels
+    # (pairs, five 256-wide channel tiles)
+    (1, 128, 4, 128, 384, 3, 1, 1),
+    (2, 128, 16, 64, 640, 1, 1, 0),
+    (1, 256, 8, 128, 1280, 1, 1, 0),
     # Pixels on the MMA's N side (3x3, Cout <= 128, width % 256 == 0)
     (1, 128, 4, 256, 128, 3, 1, 1),    # two channel blocks
     (2, 64, 3, 512, 64, 3, 1, 1),      # Cout 64: weight rows past Cout read as zeros
