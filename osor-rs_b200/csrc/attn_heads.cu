@@ -5,7 +5,9 @@
 // One CTA (one per SM) takes a task of one batch entry, one head and 256
 // query rows as two 128-row groups A and B that share every key / value tile:
 //   S_g = Q_g K^T      M = 128, N = 128 keys, K = 64    -> TMEM (one buffer per group)
-//   O_g += P_g V       M = 128, N = 64, K = 128 keys    -> TMEM (per group)
+//   O_g += P_g V       M = 128, N = 64, K = 128 keys    -> TMEM (per group), with P_g
+//                      itself in TMEM (written by the softmax threads with
+//                      tcgen05.st, read as the MMA's A operand)
 // Two softmax warp groups (four warps each, one query row per thread) work on
 // A and B in turn, so one group's exponentials overlap the other group's
 // MMAs: the MMA issuer runs S_A(0), S_B(0), then per tile S_A(j+1), PV_A(j),
@@ -15,15 +17,16 @@
 // it grows by more than 2^8 (so P <= 256); keys past the last valid one of a
 // ragged tile are masked.
 //
-// The P V product needs V with the keys contiguous per output column (the
-// K-major B operand). V arrives in its natural layout (rows = keys, 64 head
-// columns per row) and a transposer warp turns each 128 x 64 tile around in
-// shared memory with ldmatrix.trans / stmatrix, so the library takes q, k and
-// v straight from the fused q|k|v product.
+// Both products keep their shared-memory traffic small: P never goes through
+// shared memory (the softmax threads store it into TMEM with tcgen05.st and
+// the P V MMA reads its A operand from TMEM), and V is read as loaded (rows =
+// keys of 64 head columns) as the MMA's MN-major B operand, so q, k and v come
+// straight from the fused q|k|v product with no transpose.
 //
 // Roles (352 threads): warp 0 TMA producer, warp 1 TMEM allocator and MMA
-// issuer, warp 2 V transposer, warps 3..6 softmax group A, warps 7..10 group
-// B (warp w reads TMEM lanes 32 (w % 4) ..). All waits are bounded.
+// issuer, warp 2 idle, warps 3..6 softmax group A, warps 7..10 group B (warp
+// w reads TMEM lanes 32 (w % 4) ..). TMEM: S_A 0..127, S_B 128..255, O_A
+// 256..319, O_B 320..383, P_A 384..447, P_B 448..511. All waits are bounded.
 //
 // Reference counterpart: SelfAttention / FixedCrossAttention's attend
 // (src/native/spatial.rs:29-46, 83-158).
@@ -40,16 +43,14 @@ constexpr int kHd = 64;                       // head width
 constexpr int kGRows = 128;                   // query rows per group
 constexpr int kKeys = 128;                    // keys per tile
 constexpr int kTileBytes = kKeys * kHd * 2;   // 16 KB: Q group, K tile, V tile, V^T tile
-constexpr int kPBlockH = kGRows * 64 * 2;     // P: 128 rows x 64 keys (16 KB)
 constexpr int kKStages = 2;
 constexpr int kVStages = 2;
 constexpr int kThreadsH = 352;
 constexpr int kSmemH = 2 * kTileBytes            // Q groups
                        + kKStages * kTileBytes   // K ring
-                       + kVStages * kTileBytes   // V staging ring
-                       + 2 * kTileBytes          // V^T, two buffers
-                       + 2 * 2 * kPBlockH        // P, per group two 64-key blocks
+                       + kVStages * kTileBytes   // V ring
                        + 256 + 1024;
+constexpr uint32_t kTmemP = 384;  // P_g (16-bit, two keys per column) at 384 + 64 g
 constexpr float kLog2eH = 1.4426950408889634f;
 constexpr float kRescaleLog2H = 8.0f;
 
@@ -101,17 +102,13 @@ __global__ void __launch_bounds__(kThreadsH, 1)
   uint8_t* qbuf = smem;                                  // [2 groups][16 KB]
   uint8_t* kring = qbuf + 2 * kTileBytes;
   uint8_t* vring = kring + kKStages * kTileBytes;
-  uint8_t* vtbuf = vring + kVStages * kTileBytes;        // [2][16 KB]: two 64-key atoms each
-  uint8_t* pbuf = vtbuf + 2 * kTileBytes;                // [group][2 blocks][16 KB]
-  uint64_t* q_full = reinterpret_cast<uint64_t*>(pbuf + 2 * 2 * kPBlockH);
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(vring + kVStages * kTileBytes);
   uint64_t* q_free = q_full + 1;
   uint64_t* k_full = q_free + 1;
   uint64_t* k_empty = k_full + kKStages;
   uint64_t* v_full = k_empty + kKStages;
   uint64_t* v_empty = v_full + kVStages;
-  uint64_t* vt_ready = v_empty + kVStages;  // [2]
-  uint64_t* vt_free = vt_ready + 2;         // [2]
-  uint64_t* s_full = vt_free + 2;           // [group]
+  uint64_t* s_full = v_empty + kVStages;    // [group]
   uint64_t* s_free = s_full + 2;            // [group]
   uint64_t* p_ready = s_free + 2;           // [group]
   uint64_t* p_free = p_ready + 2;           // [group]
@@ -134,8 +131,6 @@ __global__ void __launch_bounds__(kThreadsH, 1)
       mbar_init(&v_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&vt_ready[b], 1);
-      mbar_init(&vt_free[b], 1);
       mbar_init(&s_full[b], 1);
       mbar_init(&s_free[b], 4);
       mbar_init(&p_ready[b], 4);
@@ -221,10 +216,12 @@ __global__ void __launch_bounds__(kThreadsH, 1)
     if (lane == 0) {
       // ---------------------------------------------------------- MMA issuer
       constexpr uint32_t idesc_s = umma_idesc_f32acc(kGRows, kKeys, Elem<D>::kUmmaFormat);
-      constexpr uint32_t idesc_o = umma_idesc_f32acc(kGRows, kHd, Elem<D>::kUmmaFormat);
-      int ks = 0;
-      uint32_t kph = 0;
-      long long tile_u = 0;   // global tile counter: V^T buffers and phases
+      // B (V) is MN-major: bit 16 of the instruction descriptor transposes it.
+      constexpr uint32_t idesc_o =
+          umma_idesc_f32acc(kGRows, kHd, Elem<D>::kUmmaFormat) | (1u << 16);
+      int ks = 0, vs = 0;
+      uint32_t kph = 0, vph = 0;
+      long long tile_u = 0;   // global tile counter
       long long s_use = 0;    // S products issued per group (same for both)
       int task_idx = 0;
       bool ok = true, issued = false;
@@ -247,17 +244,16 @@ __global__ void __launch_bounds__(kThreadsH, 1)
       auto pv_product = [&](int g, bool first) -> bool {
         if (!mbar_wait(&p_ready[g], (uint32_t)(tile_u & 1), abort_flag)) return false;
         tc_fence_after();
-        const int vb = (int)(tile_u & 1);
         const uint32_t o_tmem = tmem_base + 256 + g * kHd;
+        // A = P_g from TMEM (keys 16 kb .. + 15 in columns 8 kb .. + 7); B =
+        // the V tile as loaded, rows = keys of 64 head columns (128 bytes):
+        // the MN-major operand, 16 keys = two 8-row swizzle atoms per step.
+        const uint32_t p_tmem = tmem_base + kTmemP + g * 64;
+        const uint32_t v_addr = smem_u32(vring + vs * kTileBytes);
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const uint32_t a_addr = smem_u32(pbuf + (g * 2 + c) * kPBlockH);
-          const uint32_t b_addr = smem_u32(vtbuf + vb * kTileBytes + c * (kTileBytes / 2));
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_bf16(o_tmem, sw128_kmajor_desc(a_addr + k * 32),
-                      sw128_kmajor_desc(b_addr + k * 32), idesc_o, !(first && c == 0 && k == 0));
-        }
+        for (int kb = 0; kb < kKeys / 16; ++kb)
+          umma_bf16_tmem_a(o_tmem, p_tmem + kb * 8, sw128_kmajor_desc(v_addr + kb * 2048), idesc_o,
+                           !(first && kb == 0));
         issued = true;
         umma_commit(&p_free[g]);
         return true;
@@ -286,7 +282,6 @@ __global__ void __launch_bounds__(kThreadsH, 1)
           // Per group: the next tile's scores as soon as the softmax has
           // taken this tile's into registers (they run while it computes
           // P), then this tile's P V once P is in shared memory.
-          const int vb = (int)(tile_u & 1);
           const bool more = j + 1 < p.tiles;
           if (more) {
             if (!mbar_wait(&k_full[ks], kph, abort_flag)) {
@@ -301,7 +296,7 @@ __global__ void __launch_bounds__(kThreadsH, 1)
               if (g == 1) umma_commit(&k_empty[ks]);
             }
             if (g == 0) {
-              if (!mbar_wait(&vt_ready[vb], (uint32_t)((tile_u >> 1) & 1), abort_flag)) {
+              if (!mbar_wait(&v_full[vs], vph, abort_flag)) {
                 ok = false;
                 break;
               }
@@ -318,7 +313,11 @@ __global__ void __launch_bounds__(kThreadsH, 1)
             if (!(ok = pv_product(g, j == 0))) break;
           }
           if (!ok) break;
-          umma_commit(&vt_free[vb]);
+          umma_commit(&v_empty[vs]);
+          if (++vs == kVStages) {
+            vs = 0;
+            vph ^= 1;
+          }
           if (more) {
             ++s_use;
             if (++ks == kKStages) {
@@ -336,56 +335,7 @@ __global__ void __launch_bounds__(kThreadsH, 1)
         }
       }
     }
-  } else if (warp == 2) {
-    // ---------------------------------------------------------- V transposer
-    // V tile: rows = 128 keys of 128 bytes (64 head columns), 128-byte
-    // swizzle (16-byte chunk c of row r at chunk c ^ (r & 7)). V^T tile: two
-    // 64-key atoms of 64 rows (head columns) x 128 bytes, same swizzle. Each
-    // ldmatrix.trans reads four 8 x 8 blocks (keys 8kb.., columns 8jj..) and
-    // stmatrix writes them transposed at (rows 8jj.., keys 8kb..).
-    int vs = 0;
-    uint32_t vph = 0;
-    long long tile_u = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < p.tasks && ok; t += gridDim.x) {
-      for (int j = 0; j < p.tiles; ++j, ++tile_u) {
-        const int vb = (int)(tile_u & 1);
-        if (!__all_sync(0xffffffffu, mbar_wait(&v_full[vs], vph, abort_flag)) ||
-            !__all_sync(0xffffffffu, mbar_wait(&vt_free[vb], (uint32_t)(((tile_u >> 1) & 1) ^ 1),
-                                               abort_flag))) {
-          ok = false;
-          break;
-        }
-        const uint32_t src = smem_u32(vring + vs * kTileBytes);
-        const uint32_t dst = smem_u32(vtbuf + vb * kTileBytes);
-        const int mi = lane >> 3;  // which of the four 8 x 8 blocks this lane addresses
-        const int ri = lane & 7;   // row within the block
-#pragma unroll 4
-        for (int it = 0; it < (kKeys / 8) * (kHd / 8) / 4; ++it) {
-          // Blocks (kb, jj) with jj = 4 * (it & 1) + mi, kb = it >> 1.
-          const int kb = it >> 1;
-          const int jj = 4 * (it & 1) + mi;
-          const int key = kb * 8 + ri;
-          uint32_t r[4];
-          ldmatrix_x4_trans(src + key * 128 + ((jj ^ (key & 7)) << 4), r);
-          const int col = jj * 8 + ri;   // destination row (head column)
-          const int atom = kb >> 3;      // keys 0..63 / 64..127
-          const int c = kb & 7;          // 16-byte chunk (8 keys) within the atom row
-          stmatrix_x4(dst + atom * (kTileBytes / 2) + col * 128 + ((c ^ (col & 7)) << 4), r);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&vt_ready[vb]);
-          mbar_arrive(&v_empty[vs]);
-        }
-        if (++vs == kVStages) {
-          vs = 0;
-          vph ^= 1;
-        }
-      }
-    }
-  } else {
+  } else if (warp >= 3) {
     // ---------------------------------------------------------- softmax + epilogue
     const int g = (warp - 3) >> 2;     // group
     const int quad = warp & 3;         // TMEM lane quadrant
@@ -489,14 +439,13 @@ __global__ void __launch_bounds__(kThreadsH, 1)
           }
           tmem_wait_st();
         }
-        // P into the group's two 64-key blocks (128-byte rows, 128-byte swizzle).
-        uint8_t* prow = pbuf + g * 2 * kPBlockH + row * 128;
-#pragma unroll
-        for (int q = 0; q < 16; ++q)
-          *reinterpret_cast<uint4*>(prow + (q >> 3) * kPBlockH + (((q & 7) ^ (row & 7)) << 4)) =
-              make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        // P into TMEM (this row's lane, two keys per column), the A operand
+        // of the group's P V product: no shared-memory round trip.
+        const uint32_t p_tmem = tmem_base + kTmemP + g * 64 + lane_off;
+        tmem_store_32x32b_x32(p_tmem, *reinterpret_cast<const uint32_t(*)[32]>(pk));
+        tmem_store_32x32b_x32(p_tmem + 32, *reinterpret_cast<const uint32_t(*)[32]>(pk + 32));
+        tmem_wait_st();
         tc_fence_before();
-        fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_ready[g]);
       }
