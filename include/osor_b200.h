@@ -345,7 +345,8 @@ int osor_rows_linear(const float* x, int rows, int in_features, const void* weig
                      int dtype, float* y, void* stream);
 
 /* LayerNorm over the last axis of [rows][channels] (channels % 8 == 0, at most
- * 2048) with f32 statistics and f32 gamma / beta. Replaces the transformer
+ * 2048) with f32 statistics and f32 gamma / beta (all four pointers 16-byte
+ * aligned). Replaces the transformer
  * blocks' nn::LayerNorm (src/native/spatial.rs:171-173). */
 int osor_layer_norm(const void* x, void* y, const float* gamma, const float* beta, long long rows,
                     int channels, float eps, int dtype, void* stream);

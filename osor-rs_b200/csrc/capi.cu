@@ -684,7 +684,7 @@ int osor_layer_norm(const void* x, void* y, const float* gamma, const float* bet
   if (rows < 1 || channels < 8 || channels % 8 != 0 || channels > 2048 || !(eps >= 0.0f))
     return fail(OSOR_ERR_INVALID_INPUT, "layer norm needs rows of 8..2048 channels (multiple of 8)");
   if (!is16(dtype)) return fail(OSOR_ERR_INVALID_INPUT, "layer norm dtype must be BF16 or F16");
-  if (!aligned16(x) || !aligned16(y))
+  if (!aligned16(x) || !aligned16(y) || !aligned16(gamma) || !aligned16(beta))
     return fail(OSOR_ERR_INVALID_INPUT, "layer norm tensors must be 16-byte aligned");
   DeviceOf dev(x);
   osor::OpScope scope("layernorm", 0.0, 4.0 * rows * channels, static_cast<cudaStream_t>(stream),

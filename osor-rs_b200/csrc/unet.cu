@@ -164,16 +164,20 @@ __global__ void __launch_bounds__(256)
   }
   const float rstd = 1.0f / sqrtf(warp_sum(q) / (float)channels + eps);
   uint4* dst = y + row * vc;
+  // gamma / beta as 16-byte vectors (eight channels in four loads).
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  const float4* b4 = reinterpret_cast<const float4*>(beta);
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
     const int c8 = lane + 32 * j;
     if (c8 < vc) {
+      const float4 ga = __ldg(g4 + 2 * c8), gb = __ldg(g4 + 2 * c8 + 1);
+      const float4 ba = __ldg(b4 + 2 * c8), bb = __ldg(b4 + 2 * c8 + 1);
+      const float gm[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+      const float bt[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
       float o[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int c = c8 * 8 + u;
-        o[u] = (v[j][u] - mean) * rstd * __ldg(gamma + c) + __ldg(beta + c);
-      }
+      for (int u = 0; u < 8; ++u) o[u] = (v[j][u] - mean) * rstd * gm[u] + bt[u];
       dst[c8] = pack8<D>(o);
     }
   }
@@ -627,6 +631,8 @@ cudaError_t layer_norm_launch(int dtype, const void* x, void* y, const float* ga
                               const float* beta, long long rows, int channels, float eps,
                               cudaStream_t s) {
   if (channels % 8 != 0 || channels / 8 > 32 * kLnMaxVec) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 15)
+    return cudaErrorInvalidValue;  // read as 16-byte vectors
   const unsigned grid = (unsigned)((rows + 7) / 8);
   const uint4* xv = static_cast<const uint4*>(x);
   uint4* yv = static_cast<uint4*>(y);
