@@ -616,6 +616,11 @@ bool pair_enabled() {
 
 const char* conv_tc_check(const ConvTcArgs& a) {
   if (tcn_enabled() && conv_tcn_check(a) == nullptr) return nullptr;
+  if (a.in_coef) {
+    // The normalising transform lives in the row-shift kernels.
+    if (pair_enabled() && conv_tc2_check(a) == nullptr) return nullptr;
+    return "fused input GroupNorm needs a 3x3 stride-1 layer on the pixel-N or CTA-pair kernel";
+  }
   if (a.upsample) {
     if (a.ksize != 2 || a.stride != 1 || a.out_nchw || a.out_f32)
       return "the fused upsample convolution takes 2x2 phase weights and a 16-bit output";
@@ -677,6 +682,7 @@ cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
   // passes, odd tile counts) here.
   if (tcn_enabled() && conv_tcn_check(a) == nullptr) return conv_tcn_launch(a, stream);
   if (pair_enabled() && conv_tc2_check(a) == nullptr) return conv_tc2_launch(a, stream);
+  if (a.in_coef) return cudaErrorInvalidValue;
   EncodeTiledFn encode = encode_fn();
   if (!encode) return cudaErrorNotSupported;
   const int tile_w = a.out_w >= kBlockM ? kBlockM : a.out_w;

@@ -54,6 +54,16 @@ struct ConvTcArgs {
   float* softmax_stats = nullptr;
   int softmax_stats_ld = 0;
   const float* softmax_max = nullptr;
+  // Fused input GroupNorm(+SiLU): x is the raw activation and the kernel
+  // normalises every loaded input tile with in_coef[b][c][4] = (mean,
+  // rstd * gamma, beta, 0) (c < cin; the GroupNorm finalize's layout) before
+  // the MMAs read it. Input rows outside [in_y0, in_y1) (in_y1 < 0: in_h)
+  // are zero padding, as rows outside the tensor are; an extended band
+  // tensor marks its image-edge halo rows this way. 3x3, stride 1, pad 1 on
+  // the row-shift kernels only (conv_tc_check says which shapes).
+  const float* in_coef = nullptr;
+  int in_silu = 1;
+  int in_y0 = 0, in_y1 = -1;
 };
 
 // Columns per (max, sum) partial of the softmax statistics pass.

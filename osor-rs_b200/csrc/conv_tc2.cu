@@ -33,6 +33,13 @@
 // CTAs' barriers (multicast commit), and both CTAs' epilogues release the
 // accumulators on the even CTA's barrier. No TMA load uses cluster multicast.
 //
+// Fused input GroupNorm (FUSE = 1, row-shift 3x3 only): the input is the raw
+// activation and per-channel GroupNorm coefficients come with it. Each CTA's
+// loads complete on its own barrier, four transform warps normalise (+SiLU)
+// the CTA's stage in place (gn_stage.cuh) and arrive on the even CTA's
+// `ready` barrier, which gates the MMAs instead. 448 threads: warps 2..9
+// epilogue (two per TMEM lane quadrant), warps 10..13 transform.
+//
 // Reference counterpart: the same convolution as conv_tc.cu
 // (BandedConv2d::forward_checked, src/native/conv.rs:54-145).
 #include <atomic>
@@ -41,23 +48,44 @@
 #include "common.cuh"
 #include "conv_epilogue.cuh"
 #include "conv_tc.h"
+#include "gn_stage.cuh"
 
 namespace osor {
 namespace {
 
 constexpr int kM = 128;           // pixels per CTA
 constexpr int kBK = 64;           // K block (one 128-byte swizzle row)
-constexpr int kEpiWarps = 16;     // four per TMEM lane quadrant, 32 columns each
-constexpr int kThreads2 = 64 + 32 * kEpiWarps;
 constexpr int kAB = kM * kBK * 2;            // A tile bytes (16 KB)
 constexpr int kShiftRows = kM + 2;           // row-shift stage: 130 pixels
 constexpr int kShiftAB = 17 * 1024;          // row-shift A bytes in a stage (>= 130 x 128 B)
 constexpr int kMaxStages = 12;
 constexpr int kMaxResidentKBlocks = 18;      // resident weights: K <= 1152
 constexpr int kStat2 = 2 * 4 * 64 * 2 * 4;  // per accumulator: [quad][group](mean, M2)
-constexpr int kTail2 = 256;                  // barriers, TMEM address, abort flag
 constexpr int kSmem2 = 225 * 1024;
-constexpr int kSmemBudget = kSmem2 - 1024 - kTail2 - kStat2;  // stages + resident weights
+
+// Warp roles and shared-memory tail per variant: FUSE = 1 trades half of the
+// epilogue warps for the four transform warps (the epilogue of a tile takes
+// a small part of its MMA time) and a weight producer warp, and adds the
+// `ready` and weight-ring barriers.
+template <int FUSE>
+struct Tc2Shape {
+  static constexpr int kEpi = FUSE ? 8 : 16;  // epilogue warps, kEpi / 4 per lane quadrant
+  static constexpr int kFirstXf = 2 + kEpi;   // first transform warp
+  static constexpr int kBWarp = kFirstXf + kXfThreads / 32;  // FUSE: weight producer
+  static constexpr int kThreads = 64 + 32 * kEpi + (FUSE ? kXfThreads + 32 : 0);
+  static constexpr int kTail = FUSE ? 1024 : 256;  // barriers, TMEM address, abort flag
+  static constexpr int kBudget = kSmem2 - 1024 - kTail - kStat2;  // stages + resident weights
+};
+
+// OSOR_ROW_SHIFT=0 in the environment keeps 3x3 / phase layers on one
+// stage per tap (for comparison).
+bool row_shift_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("OSOR_ROW_SHIFT");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 // B bytes per K block per CTA: BN / 2 weight rows of 64 channels.
 template <int BN>
@@ -83,6 +111,7 @@ struct Tc2Params {
   int units;               // stages per tile: k_blocks, or 3 * c_blocks in row-shift mode
   int b_resident;          // 1: weight half loaded once; 0: streamed with each stage
   int stages;              // pipeline depth (<= kMaxStages)
+  int w_stages;            // FUSE with streamed weights: depth of the separate weight ring
   int stage_bytes;         // A bytes + streamed B bytes, 1 KB multiple
   int a_bytes;             // A bytes reserved at the start of a stage
   uint32_t a_tx;           // A bytes one CTA's load writes
@@ -95,6 +124,10 @@ struct Tc2Params {
   const float* row_scale;
   float* gn_part;
   int gn_groups;
+  // FUSE = 1: GroupNorm(+SiLU) of the input from coef[img][c][4]; input rows
+  // outside [in_y0, in_y1) are zero padding; in_w = input width.
+  const float* in_coef;
+  int in_c, in_silu, in_y0, in_y1, in_w;
 };
 
 // The four epilogue warps of one 32-column chunk (one per TMEM lane quadrant)
@@ -116,26 +149,32 @@ __device__ __forceinline__ bool chunk_all(int bar, bool ok) {
   return r != 0;
 }
 
-template <int BN, int D, int CPG>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
+template <int BN, int D, int CPG, int FUSE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Tc2Shape<FUSE>::kThreads, 1)
     conv_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, const Tc2Params p) {
+  using Sh = Tc2Shape<FUSE>;
+  constexpr int kEpiWarps = Sh::kEpi;
   constexpr int kBB = b_block_bytes<BN>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* stages = smem;
-  uint8_t* smem_b = smem + p.stages * p.stage_bytes;  // resident weight half
-  uint8_t* tail = smem_b + (p.b_resident ? p.k_blocks * kBB : 0);
+  // Resident weight half, or (FUSE, streamed) the weight ring of one tap per stage.
+  uint8_t* smem_b = smem + p.stages * p.stage_bytes;
+  uint8_t* tail = smem_b + (p.b_resident ? p.k_blocks * kBB : (FUSE ? p.w_stages * kBB : 0));
   uint64_t* full = reinterpret_cast<uint64_t*>(tail);
   uint64_t* empty = full + kMaxStages;
   uint64_t* tfull = empty + kMaxStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* bfull = tempty + 2;
   uint64_t* drain = bfull + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* ready = drain + 1;  // FUSE: stage normalised in both CTAs (even CTA's count)
+  uint64_t* wfull = ready + kMaxStages;  // FUSE: weight ring (both CTAs' bytes, even CTA's)
+  uint64_t* wempty = wfull + kMaxStages;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(ready + (FUSE ? 3 * kMaxStages : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  float* stat_smem = reinterpret_cast<float*>(tail + kTail2);
+  float* stat_smem = reinterpret_cast<float*>(tail + Sh::kTail);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -146,7 +185,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      if (FUSE) mbar_init(&ready[s], 2 * kXfThreads / 32);  // transform warps of both CTAs
     }
+    if (FUSE)
+      for (int s = 0; s < p.w_stages; ++s) {
+        mbar_init(&wfull[s], 1);
+        mbar_init(&wempty[s], 1);
+      }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 2 * kEpiWarps);  // every epilogue warp of both CTAs
@@ -218,6 +263,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
             kx = tap - ky * p.ksize;
           }
           uint8_t* st = stages + stage * p.stage_bytes;
+          if (FUSE) {
+            // This CTA's transform warps wait for its own stage; the weights
+            // come through their own ring (warp kBWarp).
+            mbar_arrive_expect_tx(&full[stage], p.a_tx);
+            tma_load_4d(st, &tmap_a, &full[stage], cb * kBK, ox + kx, oy + ky, img);
+            if (++stage == p.stages) {
+              stage = 0;
+              phase ^= 1;
+            }
+            continue;
+          }
           const uint32_t bar = map_to_rank(smem_u32(&full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2u * (p.a_tx + p.b_tx));
           tma_load_4d_pair(st, &tmap_a, bar, cb * kBK, ox + kx, oy + ky, img);
@@ -245,6 +301,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
       bool issued = false;
       int stage = 0;
       uint32_t phase = 0;
+      int ws = 0;  // FUSE: weight ring
+      uint32_t wph = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int pt = cluster_id; pt < pairs && ok; pt += clusters) {
@@ -255,7 +313,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int u = 0; u < p.units; ++u) {
-          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+          if (!(FUSE ? mbar_wait_cluster(&ready[stage], phase, abort_flag)
+                     : mbar_wait(&full[stage], phase, abort_flag))) {
             ok = false;
             break;
           }
@@ -269,14 +328,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
             const int cb = u - ky * p.c_blocks;
 #pragma unroll 1
             for (int kx = 0; kx < p.ksize; ++kx) {
-              const uint32_t b_addr =
-                  p.b_resident ? smem_u32(smem_b + ((ky * p.ksize + kx) * p.c_blocks + cb) * kBB)
-                               : a_addr + p.a_bytes + kx * kBB;
+              uint32_t b_addr;
+              if (p.b_resident) {
+                b_addr = smem_u32(smem_b + ((ky * p.ksize + kx) * p.c_blocks + cb) * kBB);
+              } else if (FUSE) {
+                if (!mbar_wait(&wfull[ws], wph, abort_flag)) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+                b_addr = smem_u32(smem_b + ws * kBB);
+              } else {
+                b_addr = a_addr + p.a_bytes + kx * kBB;
+              }
 #pragma unroll
               for (int k = 0; k < kBK / 16; ++k)
                 umma_bf16_pair(d_tmem, sw128_kmajor_desc(a_addr + kx * 128 + k * 32),
                                sw128_kmajor_desc(b_addr + k * 32), idesc, (u | kx | k) != 0);
+              issued = true;
+              if (FUSE && !p.b_resident) {
+                umma_commit_pair(&wempty[ws], 0x3);
+                if (++ws == p.w_stages) {
+                  ws = 0;
+                  wph ^= 1;
+                }
+              }
             }
+            if (!ok) break;
           } else {
             const uint32_t b_addr =
                 p.b_resident ? smem_u32(smem_b + u * kBB) : a_addr + p.a_bytes;
@@ -307,13 +385,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
         }
       }
     }
-  } else {
+  } else if (warp < Sh::kFirstXf) {
     // ------------------------------------------------------------ epilogue
-    // Warp (quad, slot) owns 32-column chunks slot, slot + 4, ... of the BN
-    // accumulator columns (BN / 128 chunks).
-    constexpr int kChunks = BN / 128;
+    // Warp (quad, slot) owns 32-column chunks slot, slot + kSlots, ... of the
+    // BN accumulator columns.
+    constexpr int kSlots = kEpiWarps / 4;
+    constexpr int kChunks = BN / 32 / kSlots;
     const int quad = warp & 3;           // TMEM lanes quad*32 .. quad*32+31
-    const int slot = (warp - 2) >> 2;    // 0..3
+    const int slot = (warp - 2) >> 2;    // 0 .. kSlots - 1
     const int cbar = 2 + slot;
     const int row = quad * 32 + lane;
     const uint32_t tempty_leader[2] = {map_to_rank(smem_u32(&tempty[0]), 0),
@@ -354,7 +433,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
       const float scale = p.row_scale ? __ldg(p.row_scale + m) : 1.0f;
 #pragma unroll 1
       for (int ci = 0; ci < kChunks; ++ci) {
-        const int chunk = slot + 4 * ci;
+        const int chunk = slot + kSlots * ci;
         uint32_t r[32];
         tmem_load_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN + chunk * 32,
                              r);
@@ -392,7 +471,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
           }
           if (ci + 1 < kChunks) {
             const uint4* r4 = reinterpret_cast<const uint4*>(
-                static_cast<const uint16_t*>(p.residual) + m * p.ld_res + n0 + 4 * 32);
+                static_cast<const uint16_t*>(p.residual) + m * p.ld_res + n0 + kSlots * 32);
 #pragma unroll
             for (int j = 0; j < 4; ++j) res[j] = __ldg(r4 + j);
           }
@@ -442,6 +521,81 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
         acc_phase ^= 1;
       }
     }
+  } else if (FUSE && warp < Sh::kBWarp) {
+    // ------------------------------------------------------------ transform
+    // Same tile / unit order as the producer (plain 3x3, stride 1, one
+    // 128-pixel row per tile): wait for this CTA's stage, normalise it,
+    // publish it to the even CTA's MMA issuer.
+    const int tid = threadIdx.x - 32 * Sh::kFirstXf;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    // Image of pair tile pt in this CTA; coefficients fetched one unit ahead.
+    auto tile_img = [&](int pt) { return (2 * (pt / p.n_tiles) + (int)rank) / tiles_per_image; };
+    float4 raw[8];
+    if (cluster_id < pairs) gn_stage_coef_fetch(p.in_coef, tile_img(cluster_id), p.in_c, 0, tid, raw);
+    for (int pt = cluster_id; pt < pairs && ok; pt += clusters) {
+      const int m_tile = 2 * (pt / p.n_tiles) + (int)rank;
+      const int img = m_tile / tiles_per_image;
+      const int rem = m_tile - img * tiles_per_image;
+      const int ty = rem / p.tiles_x;
+      const int tx = rem - ty * p.tiles_x;
+      const int ox = tx * p.tile_w - p.pad;
+      const int oy = ty - p.pad;
+      for (int u = 0; u < p.units; ++u) {
+        const int ky = u / p.c_blocks;
+        const int cb = u - ky * p.c_blocks;
+        const int y = oy + ky;
+        StageCoef<D> k;
+        gn_stage_coef_prepare<D>(raw, p.in_silu != 0, k);
+        {
+          const int npt = u + 1 < p.units ? pt : pt + clusters;
+          gn_stage_coef_fetch(p.in_coef, npt < pairs ? tile_img(npt) : img, p.in_c,
+                              u + 1 < p.units ? (cb + 1) % p.c_blocks : 0, tid, raw);
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort_flag))) {
+          ok = false;
+          break;
+        }
+        gn_stage_apply<D>(stages + stage * p.stage_bytes, kShiftRows, ox, p.in_w,
+                          y >= p.in_y0 && y < p.in_y1, k, p.in_silu != 0, tid);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster_release(map_to_rank(smem_u32(&ready[stage]), 0));
+        if (++stage == p.stages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (FUSE && lane == 0 && !p.b_resident) {
+    // ------------------------------------------------------------ weight producer
+    // FUSE: one 64-channel slice of this CTA's weight half per tap, in the
+    // MMA's (tile, unit, kx) order; both CTAs' loads complete on the even
+    // CTA's barrier.
+    int ws = 0;
+    uint32_t wph = 0;
+    bool ok = true;
+    for (int pt = cluster_id; pt < pairs && ok; pt += clusters) {
+      const int b_row = (pt % p.n_tiles) * BN + (int)rank * (BN / 2);
+      for (int u = 0; u < p.units && ok; ++u) {
+        const int ky = u / p.c_blocks;
+        const int cb = u - ky * p.c_blocks;
+        for (int kx = 0; kx < p.ksize; ++kx) {
+          if (!mbar_wait(&wempty[ws], wph ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&wfull[ws], 2u * kBB);
+          tma_load_2d_pair(smem_b + ws * kBB, &tmap_b, map_to_rank(smem_u32(&wfull[ws]), 0),
+                           ((ky * p.ksize + kx) * p.c_blocks + cb) * kBK, b_row);
+          if (++ws == p.w_stages) {
+            ws = 0;
+            wph ^= 1;
+          }
+        }
+      }
+    }
   }
 
   tc_fence_before();
@@ -471,9 +625,10 @@ EncodeTiledFn2 encode_fn2() {
   return fn;
 }
 
-template <int BN, int D, int CPG>
+template <int BN, int D, int CPG, int FUSE>
 cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Params& p,
                     cudaStream_t stream) {
+  constexpr int kThreads2 = Tc2Shape<FUSE>::kThreads;
   // Per device: the shared-memory opt-in and how many pairs fit on the GPU at
   // once (not every SM need have a partner in its cluster-capable group, so
   // this can be below SMs / 2). The persistent grid never exceeds it: a pair
@@ -483,7 +638,7 @@ cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Param
   cudaGetDevice(&device);
   if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
   if (resident_pairs[device] == 0) {
-    cudaError_t e = cudaFuncSetAttribute(conv_tc2_kernel<BN, D, CPG>,
+    cudaError_t e = cudaFuncSetAttribute(conv_tc2_kernel<BN, D, CPG, FUSE>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2);
     if (e != cudaSuccess) return e;
     int sms = 148;
@@ -494,7 +649,7 @@ cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Param
     cfg.dynamicSmemBytes = kSmem2;
     cfg.stream = stream;
     int n = 0;
-    e = cudaOccupancyMaxActiveClusters(&n, conv_tc2_kernel<BN, D, CPG>, &cfg);
+    e = cudaOccupancyMaxActiveClusters(&n, conv_tc2_kernel<BN, D, CPG, FUSE>, &cfg);
     if (e != cudaSuccess) return e;
     if (n <= 0) return cudaErrorNotSupported;
     resident_pairs[device] = n < sms / 2 ? n : sms / 2;
@@ -502,7 +657,7 @@ cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Param
   const int pairs = p.num_m_tiles / 2 * p.phases * p.n_tiles;
   int clusters = resident_pairs[device];
   if (clusters > pairs) clusters = pairs;
-  conv_tc2_kernel<BN, D, CPG><<<2 * clusters, kThreads2, kSmem2, stream>>>(ta, tb, p);
+  conv_tc2_kernel<BN, D, CPG, FUSE><<<2 * clusters, kThreads2, kSmem2, stream>>>(ta, tb, p);
   return cudaGetLastError();
 }
 
@@ -538,10 +693,37 @@ const char* conv_tc2_check(const ConvTcArgs& a) {
   if (a.gn_part && a.gn_cpg != 4 && a.gn_cpg != 8 && a.gn_cpg != 16) return "statistics";
   if (a.dtype != kBf16 && a.dtype != kF16) return "dtype";
   if (m_tiles * kM > 0x7fffffffLL) return "problem too large";
+  if (a.in_coef) {
+    if (a.upsample || a.ksize != 3 || a.stride != 1 || a.pad != 1 || tile_h != 1 ||
+        !row_shift_enabled())
+      return "pair kernel: fused input GroupNorm on row-shift 3x3 stride-1 tiles only";
+    if (reinterpret_cast<uintptr_t>(a.in_coef) & 15) return "pair kernel: coefficient alignment";
+    if (a.in_y0 < 0 || (a.in_y1 >= 0 && (a.in_y1 < a.in_y0 || a.in_y1 > a.in_h)))
+      return "pair kernel: input row range";
+  }
   return nullptr;
 }
 
 namespace {
+
+template <int BN, int FUSE>
+cudaError_t launch_cpg(int dtype, int cpg, const CUtensorMap& ta, const CUtensorMap& tb,
+                       const Tc2Params& p, cudaStream_t stream) {
+  if (dtype == kF16) {
+    switch (cpg) {
+      case 4: return launch2<BN, kF16, 4, FUSE>(ta, tb, p, stream);
+      case 8: return launch2<BN, kF16, 8, FUSE>(ta, tb, p, stream);
+      case 16: return launch2<BN, kF16, 16, FUSE>(ta, tb, p, stream);
+      default: return launch2<BN, kF16, 0, FUSE>(ta, tb, p, stream);
+    }
+  }
+  switch (cpg) {
+    case 4: return launch2<BN, kBf16, 4, FUSE>(ta, tb, p, stream);
+    case 8: return launch2<BN, kBf16, 8, FUSE>(ta, tb, p, stream);
+    case 16: return launch2<BN, kBf16, 16, FUSE>(ta, tb, p, stream);
+    default: return launch2<BN, kBf16, 0, FUSE>(ta, tb, p, stream);
+  }
+}
 
 template <int BN>
 cudaError_t conv_tc2_launch_bn(const ConvTcArgs& a, cudaStream_t stream) {
@@ -550,12 +732,8 @@ cudaError_t conv_tc2_launch_bn(const ConvTcArgs& a, cudaStream_t stream) {
   if (!encode) return cudaErrorNotSupported;
   const int tile_w = a.out_w >= kM ? kM : a.out_w;
   const int tile_h = kM / tile_w;
-  static const bool row_shift_enabled = [] {
-    const char* v = getenv("OSOR_ROW_SHIFT");
-    return !(v && v[0] == '0');
-  }();
   const bool row_shift =
-      row_shift_enabled && (a.ksize == 3 || a.ksize == 2) && a.stride == 1 && tile_h == 1;
+      row_shift_enabled() && (a.ksize == 3 || a.ksize == 2) && a.stride == 1 && tile_h == 1;
   const CUtensorMapDataType tdt =
       a.dtype == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap ta, tb;
@@ -610,8 +788,27 @@ cudaError_t conv_tc2_launch_bn(const ConvTcArgs& a, cudaStream_t stream) {
   p.a_tx = row_shift ? kShiftRows * kBK * 2 : kAB;
   p.b_tx = p.b_resident ? 0 : (row_shift ? a.ksize : 1) * kBB;
   p.stage_bytes = p.a_bytes + (int)p.b_tx;
+  const int fuse = a.in_coef ? 1 : 0;
   const int resident = p.b_resident ? p.k_blocks * kBB : 0;
-  p.stages = (kSmemBudget - resident) / p.stage_bytes;
+  p.w_stages = 0;
+  if (fuse) {
+    // Pixel stages alone (the transform adds latency between a stage's load
+    // and its MMAs, which a deeper pixel ring hides), streamed weights in a
+    // ring of their own, one tap per stage.
+    p.b_tx = 0;
+    p.stage_bytes = p.a_bytes;
+    const int budget = Tc2Shape<1>::kBudget - resident;
+    if (p.b_resident) {
+      p.stages = budget / p.stage_bytes;
+    } else {
+      p.stages = 6;
+      p.w_stages = (budget - p.stages * p.stage_bytes) / kBB;
+      if (p.w_stages > kMaxStages) p.w_stages = kMaxStages;
+      if (p.w_stages < 2) return cudaErrorInvalidValue;
+    }
+  } else {
+    p.stages = (Tc2Shape<0>::kBudget - resident) / p.stage_bytes;
+  }
   if (p.stages > kMaxStages) p.stages = kMaxStages;
   if (p.stages < 2) return cudaErrorInvalidValue;
   p.bias = a.bias;
@@ -623,20 +820,14 @@ cudaError_t conv_tc2_launch_bn(const ConvTcArgs& a, cudaStream_t stream) {
   const int cpg = a.gn_part ? a.gn_cpg : 0;
   p.gn_part = a.gn_part;
   p.gn_groups = cpg ? a.cout / cpg : 0;
-  if (a.dtype == kF16) {
-    switch (cpg) {
-      case 4: return launch2<BN, kF16, 4>(ta, tb, p, stream);
-      case 8: return launch2<BN, kF16, 8>(ta, tb, p, stream);
-      case 16: return launch2<BN, kF16, 16>(ta, tb, p, stream);
-      default: return launch2<BN, kF16, 0>(ta, tb, p, stream);
-    }
-  }
-  switch (cpg) {
-    case 4: return launch2<BN, kBf16, 4>(ta, tb, p, stream);
-    case 8: return launch2<BN, kBf16, 8>(ta, tb, p, stream);
-    case 16: return launch2<BN, kBf16, 16>(ta, tb, p, stream);
-    default: return launch2<BN, kBf16, 0>(ta, tb, p, stream);
-  }
+  p.in_coef = a.in_coef;
+  p.in_c = a.cin;
+  p.in_silu = a.in_silu;
+  p.in_y0 = a.in_y0;
+  p.in_y1 = a.in_y1 < 0 ? a.in_h : a.in_y1;
+  p.in_w = a.in_w;
+  if (fuse) return launch_cpg<BN, 1>(a.dtype, cpg, ta, tb, p, stream);
+  return launch_cpg<BN, 0>(a.dtype, cpg, ta, tb, p, stream);
 }
 
 }  // namespace

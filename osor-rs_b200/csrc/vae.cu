@@ -362,10 +362,33 @@ Status conv16(const Ctx& c, const ConvLayer& L, int xi, int batch, int h, int w,
 
 // GroupNorm(+SiLU) of buffer xi into buffer ti, then convolution L of ti into
 // buffer oi (16-bit NHWC, with tile statistics) or, with oi < 0, into
-// ext_out in out_mode.
+// ext_out in out_mode. When xi carries tile statistics and the convolution
+// can normalise its own input, the GroupNorm is only its finalize (per-channel
+// coefficients) and the convolution reads xi directly; ti is not written.
 Status gn_conv(const Ctx& c, const NormLayer& N, bool silu, const ConvLayer& L, int xi, int ti,
                int batch, int h, int w, int oi, void* ext_out, int out_mode,
                const void* residual) {
+  if (oi >= 0 && c.has_stats[xi] && fused_input_norm_enabled()) {
+    InputNorm norm;
+    norm.coef = static_cast<float*>(c.b.gn);
+    norm.silu = silu ? 1 : 0;
+    if (conv_takes_input_norm(c.dtype, L, c.b.act[xi], batch, h, w, L.cin, c.b.act[oi], L.cout,
+                              residual, L.cout, norm)) {
+      {
+        OpScope scope("groupnorm", 0.0, 0.0, c.s, 1);
+        const cudaError_t e =
+            gn_tiles_coef_launch(c.b.tstat[xi], batch, N.c, (long long)h * w, kGroups, N.gamma,
+                                 N.beta, kEps, static_cast<float*>(c.b.gn), nullptr, c.s);
+        if (e != cudaSuccess) return cuda_status(e, "group-norm coefficients");
+      }
+      bool produced = false;
+      Status st = run_conv(c.dtype, L, c.b.act[xi], kLayoutNhwc16, batch, h, w, L.cin,
+                           c.b.act[oi], kLayoutNhwc16, L.cout, residual, L.cout, c.s,
+                           c.b.tstat[oi], &produced, &norm);
+      c.has_stats[oi] = produced;
+      return st;
+    }
+  }
   Status st = gn(c, N, xi, ti, batch, (long long)h * w, silu);
   if (!st.good()) return st;
   if (oi >= 0) return conv16(c, L, ti, batch, h, w, oi, residual, true);
@@ -532,6 +555,14 @@ bool attention_tc_ok(int tokens, int dim) {
 }
 
 }  // namespace
+
+bool fused_input_norm_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("OSOR_FUSED_INPUT_NORM");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
 
 Status attention_core(int dtype, const void* q, long long ld_q, const void* k, const void* v,
                       long long ld_kv, void* out, long long ld_out, int batch, int n_q, int n_kv,
@@ -716,12 +747,43 @@ bool tc_args(ConvTcArgs* a, int dtype, const ConvLayer& L, const void* x, int in
   return true;
 }
 
+// Tensor-core arguments of a 16-bit NHWC -> NHWC convolution that applies
+// `norm` to its input; false when no kernel takes that shape.
+bool input_norm_args(ConvTcArgs* a, int dtype, const ConvLayer& L, const void* x, int batch,
+                     int in_h, int in_w, long long in_pixel_stride, void* out,
+                     long long out_pixel_stride, const void* residual, long long ld_res,
+                     float* gn_part, const InputNorm& norm) {
+  if (!norm.coef || L.k != 3 || L.stride != 1 || L.pad != 1 || L.pad_end != 1) return false;
+  if (!tc_args(a, dtype, L, x, kLayoutNhwc16, batch, in_h, in_w, in_pixel_stride, in_h, in_w, out,
+               kLayoutNhwc16, out_pixel_stride, residual, ld_res))
+    return false;
+  const int cpg = L.cout % kGroups == 0 ? L.cout / kGroups : 0;
+  if (gn_part && (cpg == 4 || cpg == 8 || cpg == 16)) {
+    a->gn_part = gn_part;
+    a->gn_cpg = cpg;
+  }
+  a->in_coef = norm.coef;
+  a->in_silu = norm.silu;
+  a->in_y0 = norm.y0;
+  a->in_y1 = norm.y1;
+  return conv_tc_check(*a) == nullptr;
+}
+
 }  // namespace
+
+bool conv_takes_input_norm(int dtype, const ConvLayer& L, const void* x, int batch, int in_h,
+                           int in_w, long long in_pixel_stride, void* out,
+                           long long out_pixel_stride, const void* residual, long long ld_res,
+                           const InputNorm& norm) {
+  ConvTcArgs a;
+  return input_norm_args(&a, dtype, L, x, batch, in_h, in_w, in_pixel_stride, out,
+                         out_pixel_stride, residual, ld_res, nullptr, norm);
+}
 
 Status run_conv(int dtype, const ConvLayer& L, const void* x, int in_mode, int batch, int in_h,
                 int in_w, long long in_pixel_stride, void* out, int out_mode,
                 long long out_pixel_stride, const void* residual, long long ld_res,
-                cudaStream_t s, float* gn_part, bool* gn_done) {
+                cudaStream_t s, float* gn_part, bool* gn_done, const InputNorm* norm) {
   if (gn_done) *gn_done = false;
   const int ph = in_h + L.pad + L.pad_end, pw = in_w + L.pad + L.pad_end;
   if (ph < L.k || pw < L.k)
@@ -736,6 +798,18 @@ Status run_conv(int dtype, const ConvLayer& L, const void* x, int in_mode, int b
   const double out_bytes = out_px * L.cout * (out_mode == kLayoutNchwF32 ? 4 : 2);
   const double bytes = in_bytes + out_bytes + (residual ? out_px * L.cout * 2 : 0.0) +
                        2.0 * L.cout * L.k * L.k * L.cin;
+  if (norm) {
+    ConvTcArgs a;
+    if (in_mode != kLayoutNhwc16 || out_mode != kLayoutNhwc16 ||
+        !input_norm_args(&a, dtype, L, x, batch, in_h, in_w, in_pixel_stride, out,
+                         out_pixel_stride, residual, ld_res, gn_part, *norm))
+      return Status::err(OSOR_ERR_INVALID_INPUT,
+                         "this convolution cannot apply its input's group norm");
+    OpScope scope("conv3x3_tc", flops, bytes, s, 1);
+    const cudaError_t e = conv_tc_launch(a, s);
+    if (gn_done) *gn_done = e == cudaSuccess && a.gn_part != nullptr;
+    return cuda_status(e, "tensor-core conv with input group norm");
+  }
   // A 3x3, 128 -> 3 convolution into an NCHW f32 image (the decoder's
   // conv_out when its GroupNorm is applied separately, and the standalone
   // op): the fused conv_out kernel without its normalisation, one MMA of

@@ -154,10 +154,33 @@ Status vae_decode_band(const Vae& m, PeerGroup* g, const float* latents, float* 
 // With gn_part set and a tensor-core shape whose Cout has 4, 8 or 16
 // channels per group of 32, the epilogue also writes per-tile GroupNorm
 // statistics of the output to gn_part and sets *gn_done.
+//
+// With norm set, x is the raw activation and the convolution applies
+// GroupNorm(+SiLU) to its input itself (norm->coef[b][c][4] from the
+// GroupNorm finalize; input rows outside [norm->y0, norm->y1), y1 < 0 for
+// all rows, are zero padding): 16-bit NHWC in and out, and only the shapes
+// conv_takes_input_norm accepts (others are refused with
+// OSOR_ERR_INVALID_INPUT; the caller normalises separately instead).
+struct InputNorm {
+  const float* coef = nullptr;
+  int silu = 1;
+  int y0 = 0, y1 = -1;
+};
 Status run_conv(int dtype, const ConvLayer& L, const void* x, int in_mode, int batch, int in_h,
                 int in_w, long long in_pixel_stride, void* out, int out_mode,
                 long long out_pixel_stride, const void* residual, long long ld_res,
-                cudaStream_t s, float* gn_part = nullptr, bool* gn_done = nullptr);
+                cudaStream_t s, float* gn_part = nullptr, bool* gn_done = nullptr,
+                const InputNorm* norm = nullptr);
+bool conv_takes_input_norm(int dtype, const ConvLayer& L, const void* x, int batch, int in_h,
+                           int in_w, long long in_pixel_stride, void* out,
+                           long long out_pixel_stride, const void* residual, long long ld_res,
+                           const InputNorm& norm);
+// OSOR_FUSED_INPUT_NORM=1 in the environment (read once per process) lets
+// the decoder's and band decoder's resnet convolutions apply their input
+// GroupNorm themselves. Off by default: on B200 the fused 3x3 convolutions
+// measured 1.7-2x slower than the separate apply pass plus the plain
+// convolution (the transform warps' arithmetic does not overlap the MMAs).
+bool fused_input_norm_enabled();
 
 // softmax(q k^T) v for `batch` images: n_q query rows (stride ld_q) against
 // n_kv key / value rows (stride ld_kv) per image. scores (softmax partials:

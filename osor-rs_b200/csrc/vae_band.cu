@@ -297,20 +297,63 @@ Status band_conv(const Band& B, const ConvLayer& L, const BT& x, int oi, const u
   return st;
 }
 
+// GroupNorm(+SiLU) of x followed by convolution L into buffer oi. When the
+// convolution can normalise its own input, the ranks exchange the band
+// statistics and x's raw halo rows (one rendezvous, as band_gn), the merged
+// statistics become per-channel coefficients, and L reads x directly: rows
+// of the extended tensor outside the image are its zero padding. Otherwise
+// band_gn into buffer ti, then band_conv.
+Status band_gn_conv(const Band& B, const BT& x, const NormLayer& N, bool silu, int ti,
+                    const ConvLayer& L, int oi, const uint8_t* residual, BT* y) {
+  const bool top = B.geo.rank == 0, bottom = B.geo.rank + 1 == B.geo.ranks;
+  const int rows = B.geo.R + 2;
+  InputNorm norm;
+  norm.coef = B.b.coef;
+  norm.silu = silu ? 1 : 0;
+  norm.y0 = top ? 1 : 0;
+  norm.y1 = bottom ? B.geo.R + 1 : rows;
+  if (fused_input_norm_enabled() &&
+      conv_takes_input_norm(B.dtype, L, B.ext(x.buf), 1, rows, B.geo.W, L.cin, B.ext(oi), L.cout,
+                            residual, L.cout, norm)) {
+    Status st = band_stats(B, x, N);
+    if (st.good()) st = band_exchange(B, x, true);
+    if (!st.good()) return st;
+    {
+      OpScope scope("groupnorm", 0.0, 0.0, B.s, 1);
+      st = cuda_err(gn_coef_from_stats_launch(B.b.st_all, B.sets * B.geo.ranks, 1, x.c,
+                                              kBandGroups, N.gamma, N.beta, kBandEps, B.b.coef,
+                                              B.s),
+                    "band group-norm coefficients");
+    }
+    if (!st.good()) return st;
+    bool produced = false;
+    st = run_conv(B.dtype, L, B.ext(x.buf), kLayoutNhwc16, 1, rows, B.geo.W, L.cin, B.ext(oi),
+                  kLayoutNhwc16, L.cout, residual, L.cout, B.s, B.b.tstat[oi], &produced, &norm);
+    y->buf = oi;
+    y->c = L.cout;
+    y->stats = produced;
+    y->sets = 1;
+    y->tile0 = B.geo.W / 128;
+    return st;
+  }
+  BT t;
+  Status st = band_gn(B, x, N, silu, ti, true, &t);
+  if (st.good()) st = band_conv(B, L, t, oi, residual, y);
+  return st;
+}
+
 Status band_resnet(const Band& B, const ResnetLayer& L, BT* x) {
   const int xi = x->buf;
   const int ti = (xi + 1) % 4, hi = (xi + 2) % 4, si = (xi + 3) % 4;
   const uint8_t* residual = B.ext(xi);
   Status st;
-  BT sc, t, h, t2, out;
+  BT sc, h, out;
   if (L.has_shortcut) {
     if (!(st = band_conv(B, L.shortcut, *x, si, nullptr, &sc)).good()) return st;
     residual = B.ext(si);
   }
-  if (!(st = band_gn(B, *x, L.n1, true, ti, true, &t)).good()) return st;
-  if (!(st = band_conv(B, L.c1, t, hi, nullptr, &h)).good()) return st;
-  if (!(st = band_gn(B, h, L.n2, true, ti, true, &t2)).good()) return st;
-  if (!(st = band_conv(B, L.c2, t2, xi, residual, &out)).good()) return st;
+  if (!(st = band_gn_conv(B, *x, L.n1, true, ti, L.c1, hi, nullptr, &h)).good()) return st;
+  if (!(st = band_gn_conv(B, h, L.n2, true, ti, L.c2, xi, residual, &out)).good()) return st;
   *x = out;
   return Status::ok();
 }
