@@ -946,9 +946,9 @@ def main():
             "op_breakdown": breakdown,
             "op_breakdown_note": "device ms per step by op kind and its rate at the work "
                                  "executed: upconv_tc = the upsamplers as four 2x2 phase "
-                                 "convolutions (4/9 of the 9-tap work); attn_scores and "
-                                 "attn_probs each run one Q K^T (softmax statistics, then 16-bit "
-                                 "probabilities)",
+                                 "convolutions (4/9 of the 9-tap work); attn_pair = the fused "
+                                 "mid-block attention on CTA pairs (one Q K^T and one P V per "
+                                 "key tile); attn_transpose = its V transposes",
             "e2e": {"value": world * mpx / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": int(h_lat.numel() * 4),
                     "d2h_bytes_per_step": int(h_out.numel() * 4), "ms_per_step": e2e_ms},

@@ -138,9 +138,10 @@ int osor_pack_conv_weight(const float* w_oihw, uint16_t* out, int cout, int cin,
  * of the packed weight, the residual and any NHWC operand; in/out layout:
  * OSOR_LAYOUT_NHWC (16-bit) or OSOR_LAYOUT_NCHW (f32). bias f32 [Cout]
  * (nullable); residual NHWC [B][Ho][Wo][Cout] (nullable, NHWC output only) is
- * added after the bias. Tensor cores are used when both layouts are NHWC,
- * Cin % 64 == 0, Cout % 128 == 0 and the output tiles into 128-pixel blocks;
- * other shapes run a CUDA-core direct convolution. Replaces
+ * added after the bias. Tensor cores are used when the input is NHWC,
+ * Cin % 64 == 0, the output tiles into 128-pixel blocks and either the output
+ * is NHWC with Cout % 128 == 0 or NCHW f32 with Cout <= 16; other shapes run
+ * a CUDA-core direct convolution. Replaces
  * BandedConv2d::forward_checked + add_bias (src/native/conv.rs:54-145) and the
  * residual add of Resnet::forward_checked (src/native/vae_encoder.rs:150). */
 int osor_conv2d(const void* x, void* y, const void* weight_packed, const float* bias,

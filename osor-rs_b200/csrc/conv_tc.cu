@@ -633,7 +633,6 @@ const char* conv_tc_check(const ConvTcArgs& a) {
   if (a.out_nchw) {
     if (a.cout <= 0 || a.cout > 16 || !a.out_f32 || a.residual || a.gn_part || a.row_scale)
       return "thin NCHW output needs 1..16 f32 channels without residual or statistics";
-    if (a.w_rows < 16) return "the 16-wide thin tile reads 16 weight rows";
   } else if (a.cout <= 0 || a.cout % 128 != 0) {
     return "output channels must be a multiple of 128";
   }
@@ -708,10 +707,12 @@ cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
   }
   {
     const int k_total = a.ksize * a.ksize * a.cin;
-    // Thin outputs read 16 weight rows (the caller pads them with zeros).
-    // Weight rows: 16 for a thin output (zero-padded by the caller), four
-    // phase blocks of cout for the fused upsample, else cout.
-    const int rows = a.out_nchw ? 16 : (a.upsample ? 4 * a.cout : a.cout);
+    // Weight rows: for a thin output the 16 rows of its tile, zero-padded by
+    // the caller when it allocated 16, else cout (the box reads the rows past
+    // the tensor as zeros); four phase blocks of cout for the fused upsample;
+    // else cout.
+    const int rows = a.out_nchw ? (a.w_rows >= 16 ? 16 : a.cout)
+                                : (a.upsample ? 4 * a.cout : a.cout);
     cuuint64_t dims[2] = {(cuuint64_t)k_total, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)a.ldw * 2};
     cuuint32_t box[2] = {(cuuint32_t)kBlockK, (cuuint32_t)block_n};

@@ -22,7 +22,7 @@ struct ConvTcArgs {
   int out_h = 0, out_w = 0, cout = 0;
   const void* w = nullptr;
   long long ldw = 0;
-  int w_rows = 0;  // weight rows allocated (>= cout; the thin one-CTA tile reads 16)
+  int w_rows = 0;  // weight rows allocated (>= cout; a thin tile reads 16, zeros past cout)
   const float* bias = nullptr;
   const void* residual = nullptr;
   long long ld_res = 0;

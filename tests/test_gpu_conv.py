@@ -172,6 +172,28 @@ def test_pixel_n_thin_nchw_output_exact(cuda_device):
     np.testing.assert_array_equal(got.cpu().numpy(), oracle.conv2d(x, wt, bias, stride=1, padding=1))
 
 
+def test_unet_conv_out_thin_nchw_on_tensor_cores_exact(cuda_device):
+    """The UNet's conv_out shape class (unet_model.cu, osor_conv2d): Cin 320
+    16-bit NHWC in, Cout 5 NCHW f32 out, weights packed with exactly 5 rows.
+    The tensor-core thin tile reads its 16 weight rows with the rows past
+    Cout zero-filled, so the shape runs as `conv_thin_tc`, not on the direct
+    kernel; dyadic operands keep the sum exact."""
+    from osor_b200 import _lib
+    b, cin, h, w, cout = 2, 320, 3, 128, 5
+    x = dyadic((b, cin, h, w), 13, 41, 20, 1 / 16).reshape(b, cin, h, w)
+    wt = dyadic((cout, cin, 3, 3), 7, 11, 5, 1 / 32).reshape(cout, cin, 3, 3) / np.float32(8)
+    bias = np.array([-0.125, 0.0625, 0.25, 0.0, 0.5], np.float32)
+    conv = ops.BandedConv2d(wt, bias, stride=1, padding=1, dtype=DT)
+    xt = ops.nchw_to_nhwc(torch.from_numpy(x).cuda(), DT)
+    torch.cuda.synchronize()
+    _lib.profile_begin()
+    got = conv.forward_checked(xt, out_layout=LAYOUT_NCHW)
+    kinds = [e[0] for e in _lib.profile_end()]
+    torch.cuda.synchronize()
+    assert kinds == ["conv_thin_tc"], kinds
+    np.testing.assert_array_equal(got.cpu().numpy(), oracle.conv2d(x, wt, bias, stride=1, padding=1))
+
+
 def test_padded_thin_path_runs_the_same_case(cuda_device):
     """OSOR_FUSED_THIN_CONV=0 (read once per process) keeps 128 -> 3
     convolutions on the pixels-on-N kernel with the weights padded to a
