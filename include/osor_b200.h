@@ -357,6 +357,24 @@ int osor_layer_norm(const void* x, void* y, const float* gamma, const float* bet
  * (src/native/transformer.rs:17-23). */
 int osor_geglu(const void* x, void* y, long long rows, int features, int dtype, void* stream);
 
+/* FeedForward's input projection and GEGLU gate in one call: y[p][f] =
+ * value * gelu_erf(gate) with (value, gate) = the 1x1 product x W^T + bias,
+ * x NHWC [B][H][W][cin] 16-bit, y [B][H][W][features] 16-bit (features %
+ * 128 == 0). weight_packed holds the projection's 2 * features rows
+ * (osor_pack_conv_weight's layout) reordered per 128 features: rows t * 256 ..
+ * t * 256 + 127 are value rows t * 128 .. t * 128 + 127 and the next 128 rows
+ * the matching gate rows features + t * 128 ..; bias f32 [2 * features]
+ * (nullable) in the same order. Shapes the CTA-pair kernel takes apply the
+ * gate in the product's epilogue and need no workspace; others need
+ * osor_linear_geglu_workspace_size bytes (the product is stored there and
+ * gated in a second pass). Replaces FeedForward::forward's gate linear,
+ * narrow and gelu_erf product (src/native/transformer.rs:18-24). */
+size_t osor_linear_geglu_workspace_size(int batch, int height, int width, int cin, int features,
+                                        int dtype);
+int osor_linear_geglu(const void* x, void* y, const void* weight_packed, const float* bias,
+                      int batch, int height, int width, int cin, int features, int dtype,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
 /* y[p] = (a[p], b[p]) for NHWC a [P][ca], b [P][cb] (ca, cb % 8 == 0).
  * Replaces Tensor::cat(&[xs, skip], 1) of the up blocks
  * (src/native/unet_blocks.rs:214-219, src/native/cross_blocks.rs:206). */

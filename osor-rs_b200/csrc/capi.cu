@@ -708,6 +708,32 @@ int osor_geglu(const void* x, void* y, long long rows, int features, int dtype, 
   return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "GEGLU");
 }
 
+size_t osor_linear_geglu_workspace_size(int batch, int height, int width, int cin, int features,
+                                        int dtype) {
+  if (batch <= 0 || height <= 0 || width <= 0 || cin <= 0 || cin % 8 != 0 || features <= 0 ||
+      features % 128 != 0 || !is16(dtype))
+    return 0;
+  return osor::geglu_product_workspace(internal_dtype(dtype), batch, height, width, cin, features);
+}
+
+int osor_linear_geglu(const void* x, void* y, const void* weight_packed, const float* bias,
+                      int batch, int height, int width, int cin, int features, int dtype,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  if (!x || !y || !weight_packed) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (batch <= 0 || height <= 0 || width <= 0 || cin <= 0 || cin % 8 != 0)
+    return fail(OSOR_ERR_INVALID_INPUT, "invalid GEGLU product shape");
+  if (features <= 0 || features % 128 != 0)
+    return fail(OSOR_ERR_INVALID_INPUT, "GEGLU product needs a positive multiple of 128 features");
+  if (!is16(dtype)) return fail(OSOR_ERR_INVALID_INPUT, "GEGLU product dtype must be BF16 or F16");
+  if (!aligned16(x) || !aligned16(y) || !aligned16(weight_packed) || (bias && !aligned16(bias)))
+    return fail(OSOR_ERR_INVALID_INPUT, "GEGLU product operands must be 16-byte aligned");
+  DeviceOf dev(x);
+  return report(osor::run_geglu_product(internal_dtype(dtype),
+                                        static_cast<const uint16_t*>(weight_packed), bias, x,
+                                        batch, height, width, cin, features, y, workspace,
+                                        workspace_bytes, static_cast<cudaStream_t>(stream)));
+}
+
 int osor_concat_channels(const void* a, int ca, const void* b, int cb, void* y, long long pixels,
                          int dtype, void* stream) {
   if (!a || !b || !y) return fail(OSOR_ERR_INVALID_INPUT, "null argument");

@@ -615,6 +615,7 @@ bool pair_enabled() {
 }  // namespace
 
 const char* conv_tc_check(const ConvTcArgs& a) {
+  if (a.geglu) return pair_enabled() ? conv_tc2_check(a) : "GEGLU products run on CTA pairs";
   if (tcn_enabled() && conv_tcn_check(a) == nullptr) return nullptr;
   if (a.in_coef) {
     // The normalising transform lives in the row-shift kernels.
@@ -679,6 +680,7 @@ cudaError_t conv_tc_launch(const ConvTcArgs& a, cudaStream_t stream) {
   // the MMA's N side (conv_tcn.cu); other layers with Cout 128 or a multiple
   // of 256 on CTA pairs (conv_tc2.cu); the rest (upsample phases, softmax
   // passes, odd tile counts) here.
+  if (a.geglu) return conv_tc_check(a) == nullptr ? conv_tc2_launch(a, stream) : cudaErrorInvalidValue;
   if (tcn_enabled() && conv_tcn_check(a) == nullptr) return conv_tcn_launch(a, stream);
   if (pair_enabled() && conv_tc2_check(a) == nullptr) return conv_tc2_launch(a, stream);
   if (a.in_coef) return cudaErrorInvalidValue;

@@ -45,6 +45,12 @@ struct ConvTcArgs {
   // (a, b) = rows [(2a + b) * cout, ...)); out_h / out_w equal in_h / in_w.
   // GroupNorm partials (gn_part) are written per phase tile, image-major.
   int upsample = 0;
+  // GEGLU product (1x1, Cout a multiple of 256, on CTA pairs): the weight
+  // rows of each 256-row channel tile t hold the value rows t * 128 .. t * 128
+  // + 127 of the projection and then the matching gate rows (bias alike); the
+  // epilogue writes y[pixel][t * 128 + j] = value * gelu_erf(gate), cout / 2
+  // channels (ld_out). No residual, statistics or row scale.
+  int geglu = 0;
   // Softmax over each output row in two passes of the same product (the
   // attention scores, 1x1, no bias / residual / statistics, Cout a multiple
   // of 128). softmax_stats: no output is stored; for every row and every

@@ -128,6 +128,7 @@ struct Tc2Params {
   // outside [in_y0, in_y1) are zero padding; in_w = input width.
   const float* in_coef;
   int in_c, in_silu, in_y0, in_y1, in_w;
+  int geglu;               // GEGLU epilogue (ConvTcArgs::geglu); BN 256 without FUSE
 };
 
 // The four epilogue warps of one 32-column chunk (one per TMEM lane quadrant)
@@ -149,7 +150,7 @@ __device__ __forceinline__ bool chunk_all(int bar, bool ok) {
   return r != 0;
 }
 
-template <int BN, int D, int CPG, int FUSE>
+template <int BN, int D, int CPG, int FUSE, int GG = 0>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Tc2Shape<FUSE>::kThreads, 1)
     conv_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, const Tc2Params p) {
@@ -431,6 +432,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Tc2Shape<FUSE>::kThr
       if (!chunk_all(cbar, mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;
       tc_fence_after();
       const float scale = p.row_scale ? __ldg(p.row_scale + m) : 1.0f;
+      // GEGLU (GG): with BN 256 and four slots this warp's chunks are `slot`
+      // (values) and `slot + 4` (their gates); the values wait here.
+      static_assert(!GG || (BN == 256 && kChunks == 2 && CPG == 0 && FUSE == 0),
+                    "GEGLU epilogue: BN 256, four slots, no statistics");
+      float gv[GG ? 32 : 1];
 #pragma unroll 1
       for (int ci = 0; ci < kChunks; ++ci) {
         const int chunk = slot + kSlots * ci;
@@ -476,7 +482,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Tc2Shape<FUSE>::kThr
             for (int j = 0; j < 4; ++j) res[j] = __ldg(r4 + j);
           }
         }
-        uint4* o4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + orow * p.ld_out + n0);
+        long long oc = n0;
+        if constexpr (GG != 0) {
+          if (ci == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) gv[j] = v[j];
+            continue;
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            v[j] = gv[j] * (0.5f * v[j] * (1.0f + erff(v[j] * 0.70710678118654752f)));
+          oc = (long long)n_tile * (BN / 2) + slot * 32;
+        }
+        uint4* o4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + orow * p.ld_out + oc);
         uint32_t pk[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) pk[j] = Elem<D>::pack(v[2 * j], v[2 * j + 1]);
@@ -625,7 +643,7 @@ EncodeTiledFn2 encode_fn2() {
   return fn;
 }
 
-template <int BN, int D, int CPG, int FUSE>
+template <int BN, int D, int CPG, int FUSE, int GG = 0>
 cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Params& p,
                     cudaStream_t stream) {
   constexpr int kThreads2 = Tc2Shape<FUSE>::kThreads;
@@ -638,7 +656,7 @@ cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Param
   cudaGetDevice(&device);
   if (device < 0 || device >= 64) return cudaErrorInvalidDevice;
   if (resident_pairs[device] == 0) {
-    cudaError_t e = cudaFuncSetAttribute(conv_tc2_kernel<BN, D, CPG, FUSE>,
+    cudaError_t e = cudaFuncSetAttribute(conv_tc2_kernel<BN, D, CPG, FUSE, GG>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2);
     if (e != cudaSuccess) return e;
     int sms = 148;
@@ -649,7 +667,7 @@ cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Param
     cfg.dynamicSmemBytes = kSmem2;
     cfg.stream = stream;
     int n = 0;
-    e = cudaOccupancyMaxActiveClusters(&n, conv_tc2_kernel<BN, D, CPG, FUSE>, &cfg);
+    e = cudaOccupancyMaxActiveClusters(&n, conv_tc2_kernel<BN, D, CPG, FUSE, GG>, &cfg);
     if (e != cudaSuccess) return e;
     if (n <= 0) return cudaErrorNotSupported;
     resident_pairs[device] = n < sms / 2 ? n : sms / 2;
@@ -657,7 +675,7 @@ cudaError_t launch2(const CUtensorMap& ta, const CUtensorMap& tb, const Tc2Param
   const int pairs = p.num_m_tiles / 2 * p.phases * p.n_tiles;
   int clusters = resident_pairs[device];
   if (clusters > pairs) clusters = pairs;
-  conv_tc2_kernel<BN, D, CPG, FUSE><<<2 * clusters, kThreads2, kSmem2, stream>>>(ta, tb, p);
+  conv_tc2_kernel<BN, D, CPG, FUSE, GG><<<2 * clusters, kThreads2, kSmem2, stream>>>(ta, tb, p);
   return cudaGetLastError();
 }
 
@@ -693,6 +711,9 @@ const char* conv_tc2_check(const ConvTcArgs& a) {
   if (a.gn_part && a.gn_cpg != 4 && a.gn_cpg != 8 && a.gn_cpg != 16) return "statistics";
   if (a.dtype != kBf16 && a.dtype != kF16) return "dtype";
   if (m_tiles * kM > 0x7fffffffLL) return "problem too large";
+  if (a.geglu && (a.ksize != 1 || a.upsample || a.in_coef || a.residual || a.gn_part ||
+                  a.row_scale || a.cout % 256 != 0))
+    return "pair kernel: GEGLU products are plain 1x1 with Cout a multiple of 256";
   if (a.in_coef) {
     if (a.upsample || a.ksize != 3 || a.stride != 1 || a.pad != 1 || tile_h != 1 ||
         !row_shift_enabled())
@@ -709,6 +730,16 @@ namespace {
 template <int BN, int FUSE>
 cudaError_t launch_cpg(int dtype, int cpg, const CUtensorMap& ta, const CUtensorMap& tb,
                        const Tc2Params& p, cudaStream_t stream) {
+  if (p.geglu) {
+    // Its own instantiation, so the other epilogues keep their registers.
+    if constexpr (BN == 256 && FUSE == 0) {
+      if (cpg != 0) return cudaErrorInvalidValue;
+      return dtype == kF16 ? launch2<BN, kF16, 0, 0, 1>(ta, tb, p, stream)
+                           : launch2<BN, kBf16, 0, 0, 1>(ta, tb, p, stream);
+    } else {
+      return cudaErrorInvalidValue;
+    }
+  }
   if (dtype == kF16) {
     switch (cpg) {
       case 4: return launch2<BN, kF16, 4, FUSE>(ta, tb, p, stream);
@@ -826,6 +857,7 @@ cudaError_t conv_tc2_launch_bn(const ConvTcArgs& a, cudaStream_t stream) {
   p.in_y0 = a.in_y0;
   p.in_y1 = a.in_y1 < 0 ? a.in_h : a.in_y1;
   p.in_w = a.in_w;
+  p.geglu = a.geglu;
   if (fuse) return launch_cpg<BN, 1>(a.dtype, cpg, ta, tb, p, stream);
   return launch_cpg<BN, 0>(a.dtype, cpg, ta, tb, p, stream);
 }

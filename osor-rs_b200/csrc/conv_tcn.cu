@@ -569,7 +569,7 @@ cudaError_t launch_cpg_n(int dtype, int cpg, const CUtensorMap& tx, const CUtens
 }  // namespace
 
 const char* conv_tcn_check(const ConvTcArgs& a) {
-  if (a.upsample || a.row_scale || a.softmax_stats || a.softmax_max)
+  if (a.upsample || a.row_scale || a.softmax_stats || a.softmax_max || a.geglu)
     return "pixel-N kernel: plain convolution only";
   if (!((a.ksize == 3 && a.pad == 1) || (a.ksize == 1 && a.pad == 0)) || a.stride != 1)
     return "pixel-N kernel: 3x3 pad 1 or 1x1, stride 1";

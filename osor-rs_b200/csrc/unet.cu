@@ -184,18 +184,24 @@ __global__ void __launch_bounds__(256)
 }
 
 // ------------------------------------------------------------ GEGLU
+// interleaved = 0: row r holds the values in columns [0, features) and the
+// gates in [features, 2 features). interleaved = 1: 256-column tiles of 128
+// values then their 128 gates (the GEGLU product's weight-row order).
 template <int D>
 __global__ void geglu_kernel(const uint4* __restrict__ x, uint4* __restrict__ y, long long rows,
-                             int features) {
+                             int features, int interleaved) {
   const int vf = features / 8;
   const long long total = rows * vf;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / vf;
     const int c = (int)(i % vf);
+    // 16 vectors of 8 channels per 128-channel block.
+    const int vc = interleaved ? (c >> 4) * 32 + (c & 15) : c;
+    const int vg = interleaved ? vc + 16 : vf + c;
     float a[8], g[8], o[8];
-    unpack8<D>(__ldg(x + r * 2 * vf + c), a);
-    unpack8<D>(__ldg(x + r * 2 * vf + vf + c), g);
+    unpack8<D>(__ldg(x + r * 2 * vf + vc), a);
+    unpack8<D>(__ldg(x + r * 2 * vf + vg), g);
 #pragma unroll
     for (int u = 0; u < 8; ++u)
       o[u] = a[u] * (0.5f * g[u] * (1.0f + erff(g[u] * 0.70710678118654752f)));
@@ -655,15 +661,15 @@ cudaError_t layer_norm_launch(int dtype, const void* x, void* y, const float* ga
 }
 
 cudaError_t geglu_launch(int dtype, const void* x, void* y, long long rows, int features,
-                         cudaStream_t s) {
-  if (features % 8 != 0) return cudaErrorInvalidValue;
+                         cudaStream_t s, int interleaved) {
+  if (features % 8 != 0 || (interleaved && features % 128 != 0)) return cudaErrorInvalidValue;
   const long long total = rows * (features / 8);
   const uint4* xv = static_cast<const uint4*>(x);
   uint4* yv = static_cast<uint4*>(y);
   if (dtype == kF16)
-    geglu_kernel<kF16><<<grid_for(total, 256), 256, 0, s>>>(xv, yv, rows, features);
+    geglu_kernel<kF16><<<grid_for(total, 256), 256, 0, s>>>(xv, yv, rows, features, interleaved);
   else
-    geglu_kernel<kBf16><<<grid_for(total, 256), 256, 0, s>>>(xv, yv, rows, features);
+    geglu_kernel<kBf16><<<grid_for(total, 256), 256, 0, s>>>(xv, yv, rows, features, interleaved);
   return cudaGetLastError();
 }
 

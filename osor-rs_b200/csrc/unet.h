@@ -26,8 +26,10 @@ cudaError_t layer_norm_launch(int dtype, const void* x, void* y, const float* ga
                               cudaStream_t s);
 
 // y[r][f] = x[r][f] * gelu_erf(x[r][features + f]); features multiple of 8.
+// interleaved = 1: x rows are 256-column tiles of 128 values then their 128
+// gates (the GEGLU product's order; features multiple of 128).
 cudaError_t geglu_launch(int dtype, const void* x, void* y, long long rows, int features,
-                         cudaStream_t s);
+                         cudaStream_t s, int interleaved = 0);
 
 // y[p] = a[p] (ca channels) followed by b[p] (cb channels); ca, cb multiples of 8.
 cudaError_t concat_channels_launch(const void* a, int ca, const void* b, int cb, void* y,

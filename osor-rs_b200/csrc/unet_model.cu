@@ -44,6 +44,9 @@ struct Product {
   int cin = 0, cout = 0, cpad = 0, k = 1;
   uint16_t* w = nullptr;  // [cpad][k*k*cin], rows >= cout zero
   float* bias = nullptr;  // [cpad] or null
+  // GEGLU input projection with its rows in run_geglu_product's interleaved
+  // order (value rows and their gate rows per 128 features).
+  bool geglu = false;
 };
 
 struct Norm {
@@ -416,6 +419,18 @@ class Run {
       {  // GEGLU feed-forward
         Act ln, hidden, gated, next;
         OSOR_TRY(layer_norm(xs, blk.ln3, &ln));
+        if (blk.ff1.geglu) {
+          const int f = blk.ff1.cout / 2;
+          OSOR_TRY(act(ln.b, ln.h, ln.w, f, &gated));
+          const size_t need = geglu_product_workspace(m_.dtype, ln.b, ln.h, ln.w, ln.c, f);
+          Buf ws;
+          if (need) OSOR_TRY(raw(need, &ws));
+          OSOR_TRY(run_geglu_product(m_.dtype, blk.ff1.w, blk.ff1.bias, ln.p(), ln.b, ln.h, ln.w,
+                                     ln.c, f, gated.p(), ws.get(), need, s_));
+          OSOR_TRY(conv(gated, blk.ff2, 1, &xs, nullptr, &next));
+          xs = std::move(next);
+          continue;
+        }
         if (blk.ff1.cpad == blk.ff1.cout)
           OSOR_TRY(raw_product(ln, blk.ff1, 1, nullptr, &hidden));
         else
@@ -630,7 +645,28 @@ Status load_transformer(Loader& ld, const std::string& p, int c, int depth, int 
     for (size_t i = 0; i < q2.size(); ++i) q2[i] = cq[i] * scale;
     OSOR_TRY(ld.product_from(q2.data(), nullptr, c, c, 1, true, &blk.q2));
     OSOR_TRY(ld.linear(q + ".attn2.to_out.0", c, c, true, &blk.out2));
-    OSOR_TRY(ld.linear(q + ".ff.net.0.proj", c, 8 * c, true, &blk.ff1));
+    {
+      // GEGLU input projection: with 4c a multiple of 128 its rows are
+      // interleaved (128 value rows, then their 128 gate rows) so that the
+      // product's epilogue applies the gate.
+      const float *fw, *fb;
+      OSOR_TRY(ld.get(q + ".ff.net.0.proj.weight", {8 * c, c}, &fw));
+      OSOR_TRY(ld.get(q + ".ff.net.0.proj.bias", {8 * c}, &fb));
+      const int f = 4 * c;
+      if (f % 128 == 0 && c % 8 == 0) {
+        std::vector<float> iw((size_t)8 * c * c), ib((size_t)8 * c);
+        for (int r = 0; r < 2 * f; ++r) {
+          const int t = r / 256, j = r % 256;
+          const int src = j < 128 ? t * 128 + j : f + t * 128 + (j - 128);
+          std::memcpy(iw.data() + (size_t)r * c, fw + (size_t)src * c, sizeof(float) * c);
+          ib[r] = fb[src];
+        }
+        OSOR_TRY(ld.product_from(iw.data(), ib.data(), 2 * f, c, 1, false, &blk.ff1));
+        blk.ff1.geglu = true;
+      } else {
+        OSOR_TRY(ld.linear(q + ".ff.net.0.proj", c, 8 * c, true, &blk.ff1));
+      }
+    }
     OSOR_TRY(ld.linear(q + ".ff.net.2", 4 * c, c, true, &blk.ff2));
     // The prompt's keys / values: [tokens][context] x W^T on the device.
     OSOR_TRY(ld.get(q + ".attn2.to_k.weight", {c, context}, &ck));

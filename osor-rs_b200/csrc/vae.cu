@@ -26,6 +26,7 @@
 #include "groupnorm.h"
 #include "ops.h"
 #include "profile.h"
+#include "unet.h"
 #include "vae.h"
 
 namespace osor {
@@ -878,6 +879,68 @@ Status run_conv(int dtype, const ConvLayer& L, const void* x, int in_mode, int b
   return cuda_status(
       direct_conv_launch(dtype, x, in_mode, L.w, L.bias, residual, out, out_mode, d, s),
       "direct convolution");
+}
+
+namespace {
+ConvTcArgs geglu_args(int dtype, const void* x, const uint16_t* weight, const float* bias,
+                      int batch, int h, int w, int cin, int features, void* y) {
+  ConvTcArgs a;
+  a.dtype = dtype;
+  a.x = x;
+  a.batch = batch;
+  a.in_h = h;
+  a.in_w = w;
+  a.cin = cin;
+  a.pixel_stride = cin;
+  a.ksize = 1;
+  a.stride = 1;
+  a.pad = 0;
+  a.out_h = h;
+  a.out_w = w;
+  a.cout = 2 * features;
+  a.w = weight;
+  a.ldw = cin;
+  a.w_rows = 2 * features;
+  a.bias = bias;
+  a.out = y;
+  a.ld_out = features;
+  a.geglu = 1;
+  return a;
+}
+}  // namespace
+
+size_t geglu_product_workspace(int dtype, int batch, int h, int w, int cin, int features) {
+  // Placeholder 256-byte-aligned operands: the shape alone decides the path.
+  void* const aligned = reinterpret_cast<void*>(256);
+  const ConvTcArgs a = geglu_args(dtype, aligned, static_cast<const uint16_t*>(aligned), nullptr,
+                                  batch, h, w, cin, features, aligned);
+  if (conv_tc_check(a) == nullptr) return 0;
+  return (size_t)batch * h * w * 2 * features * 2;
+}
+
+Status run_geglu_product(int dtype, const uint16_t* weight, const float* bias, const void* x,
+                         int batch, int h, int w, int cin, int features, void* y, void* workspace,
+                         size_t workspace_bytes, cudaStream_t s) {
+  const long long rows = (long long)batch * h * w;
+  const double flops = 4.0 * rows * cin * features;
+  const ConvTcArgs a = geglu_args(dtype, x, weight, bias, batch, h, w, cin, features, y);
+  if (conv_tc_check(a) == nullptr) {
+    OpScope scope("geglu_product", flops, 2.0 * rows * (cin + features), s, 1);
+    return cuda_status(conv_tc_launch(a, s), "GEGLU product");
+  }
+  if (!workspace || workspace_bytes < (size_t)rows * 2 * features * 2)
+    return Status::err(OSOR_ERR_INVALID_INPUT, "GEGLU product: workspace too small for this shape");
+  ConvLayer L;
+  L.cin = cin;
+  L.cout = 2 * features;
+  L.k = 1;
+  L.w = weight;
+  L.bias = bias;
+  Status st = run_conv(dtype, L, x, kLayoutNhwc16, batch, h, w, cin, workspace, kLayoutNhwc16,
+                       2 * features, nullptr, 2 * features, s);
+  if (!st.good()) return st;
+  OpScope scope("geglu", 0.0, 6.0 * rows * features, s, 1);
+  return cuda_status(geglu_launch(dtype, workspace, y, rows, features, s, 1), "GEGLU");
 }
 
 Vae::~Vae() {

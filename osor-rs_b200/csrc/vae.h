@@ -171,6 +171,16 @@ Status run_conv(int dtype, const ConvLayer& L, const void* x, int in_mode, int b
                 long long out_pixel_stride, const void* residual, long long ld_res,
                 cudaStream_t s, float* gn_part = nullptr, bool* gn_done = nullptr,
                 const InputNorm* norm = nullptr);
+// GEGLU feed-forward input: y[pixel][f] = value * gelu_erf(gate) of the 1x1
+// product x W^T + bias with 2 * features weight rows in the interleaved order
+// of ConvTcArgs::geglu (features a multiple of 128; x NHWC 16-bit [pixels][cin],
+// y [pixels][features]). On CTA pairs the gate is applied in the product's
+// epilogue and no workspace is used; other shapes store the product in
+// `workspace` (geglu_product_workspace bytes) and gate it in a second pass.
+size_t geglu_product_workspace(int dtype, int batch, int h, int w, int cin, int features);
+Status run_geglu_product(int dtype, const uint16_t* weight, const float* bias, const void* x,
+                         int batch, int h, int w, int cin, int features, void* y, void* workspace,
+                         size_t workspace_bytes, cudaStream_t s);
 bool conv_takes_input_norm(int dtype, const ConvLayer& L, const void* x, int batch, int in_h,
                            int in_w, long long in_pixel_stride, void* out,
                            long long out_pixel_stride, const void* residual, long long ld_res,

@@ -366,14 +366,30 @@ def _padded(cout: int, cin: int) -> int:
     return cout
 
 
+def _geglu_rows(features: int, device) -> torch.Tensor:
+    """Row order of a GEGLU input projection for osor_linear_geglu: per 128
+    features, the 128 value rows and then their 128 gate rows."""
+    r = torch.arange(2 * features, device=device)
+    t, j = r // 256, r % 256
+    return torch.where(j < 128, t * 128 + j, features + t * 128 + (j - 128))
+
+
 class _Product:
     """A convolution / linear layer packed once: 16-bit [Cpad][k*k*Cin] in
-    (ky, kx, ci) order (rows >= Cout zero) and f32 bias [Cpad]."""
-    __slots__ = ("weight", "bias", "cin", "cout", "cpad", "k")
+    (ky, kx, ci) order (rows >= Cout zero) and f32 bias [Cpad]. geglu: a
+    GEGLU input projection with its rows in _geglu_rows order."""
+    __slots__ = ("weight", "bias", "cin", "cout", "cpad", "k", "geglu")
 
     def __init__(self, weight: torch.Tensor, bias: Optional[torch.Tensor], device, dtype,
-                 pad: bool = True):
+                 pad: bool = True, geglu: bool = False):
         w = weight.to(device=device, dtype=torch.float32)
+        self.geglu = geglu
+        if geglu:
+            order = _geglu_rows(w.shape[0] // 2, w.device)
+            w = w[order]
+            if bias is not None:
+                bias = bias.to(device=device, dtype=torch.float32)[order]
+            pad = False
         if w.ndim == 2:
             w = w[:, :, None, None]
         self.cout, self.cin, self.k = w.shape[0], w.shape[1], w.shape[2]
@@ -440,8 +456,11 @@ class CudaUnetOps:
             elif stem.startswith(("time_embedding.", "add_embedding.")) or leaf == "time_emb_proj":
                 continue
             else:
+                # GEGLU input projections with 128-multiple widths run fused.
+                geglu = (stem.endswith(".ff.net.0.proj") and w[name].shape[0] % 256 == 0
+                         and w[name].shape[1] % 8 == 0)
                 self.products[stem] = _Product(w[name], w.get(stem + ".bias"), device, dtype,
-                                               pad=stem != "conv_in")
+                                               pad=stem != "conv_in", geglu=geglu)
         # Attention: fused self-attention q|k|v, scaled cross-attention q, prompt K / V.
         self.cross_kv: Dict[str, Tuple[torch.Tensor, torch.Tensor]] = {}
         ctx16 = ctx.to(dtype).reshape(1, 1, ctx.shape[1], arch.context).contiguous()
@@ -598,6 +617,16 @@ class CudaUnetOps:
 
     def feed_forward(self, x, prefix, residual):
         p = self.products[prefix + ".net.0.proj"]
+        if p.geglu:
+            b, h, w, c = x.shape
+            f = p.cout // 2
+            gated = torch.empty((b, h, w, f), device=x.device, dtype=self.dtype)
+            need = self.lib.osor_linear_geglu_workspace_size(b, h, w, c, f, self.dt)
+            ws = torch.empty(need, dtype=torch.uint8, device=x.device) if need else None
+            check(self.lib.osor_linear_geglu(_ptr(x), _ptr(gated), _ptr(p.weight), _ptr(p.bias),
+                                             b, h, w, c, f, self.dt, _ptr(ws), need,
+                                             self.stream))
+            return self.linear(gated, prefix + ".net.2", residual=residual)
         hidden, ld = self._raw(x, p)
         if ld != p.cout:
             hidden = self.conv(x, prefix + ".net.0.proj")

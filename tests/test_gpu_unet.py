@@ -112,6 +112,42 @@ def test_geglu_matches_exact_erf(cuda_device):
     assert abs(float(out[0, 0]) - 1.9544997215270996) < 1e-3
 
 
+# (batch, h, w, cin, features, fused): 2048 pixels (16 tiles) on CTA pairs
+# with the gate in the product's epilogue; 384 pixels (3 tiles, odd) through
+# the workspace (product, then the interleaved GEGLU pass).
+@pytest.mark.parametrize("shape", [(2, 16, 64, 256, 256, True), (1, 3, 128, 128, 128, False)])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_linear_geglu_matches_f64(shape, dt, cuda_device):
+    """osor_linear_geglu against the projection and exact-erf gate in f64 on
+    the same 16-bit operands (transformer.rs:18-24)."""
+    b, h, w, cin, f, fused = shape
+    rng = np.random.default_rng(11)
+    x = dev16(rng.standard_normal((b, h, w, cin)), dt)
+    wt = dev16(rng.standard_normal((2 * f, cin)) / np.sqrt(cin), dt)
+    bias = torch.from_numpy(rng.uniform(-0.2, 0.2, 2 * f).astype(np.float32)).cuda()
+    r = np.arange(2 * f)
+    order = np.where(r % 256 < 128, (r // 256) * 128 + r % 256, f + (r // 256) * 128 + r % 256 - 128)
+    order_t = torch.from_numpy(order).cuda()
+    wi = wt[order_t].contiguous()
+    bi = bias[order_t].contiguous()
+    need = _lib.lib().osor_linear_geglu_workspace_size(b, h, w, cin, f, dtype_code(dt))
+    assert (need == 0) == fused
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
+    y = torch.empty((b, h, w, f), device="cuda", dtype=dt)
+    check(_lib.lib().osor_linear_geglu(P(x), P(y), P(wi), P(bi), b, h, w, cin, f, dtype_code(dt),
+                                       P(ws), need, S()))
+    proj = host(x).reshape(-1, cin).astype(np.float64) @ host(wt).astype(np.float64).T
+    proj += host(bias)
+    want = proj[:, :f] * U.gelu_erf(proj[:, f:])
+    got = host(y).reshape(-1, f)
+    # The unfused path rounds the projection to 16 bits before the gate.
+    assert np.all(np.abs(got - want) <= 2e-2 * np.abs(want) + 2e-2), np.abs(got - want).max()
+    if not fused:
+        with pytest.raises(InvalidInput):
+            check(_lib.lib().osor_linear_geglu(P(x), P(y), P(wi), P(bi), b, h, w, cin, f,
+                                               dtype_code(dt), None, 0, S()))
+
+
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
 def test_concat_resize_and_channel_update_are_exact(dt, cuda_device):
     lb = _lib.lib()
