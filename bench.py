@@ -528,13 +528,17 @@ def run_e2e(args, dev, flush):
         ev.record(stream)
         marks.append((stage.name, ev))
 
-    flush.fill_(1)
-    start = torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    step(observe)
-    end = torch.cuda.Event(enable_timing=True)
-    end.record(stream)
-    end.synchronize()
+    # The first observed call also allocates the tensors only an observer gets
+    # (predicted original, blend); the second one is the one reported.
+    for _ in range(2):
+        marks.clear()
+        flush.fill_(1)
+        start = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        step(observe)
+        end = torch.cuda.Event(enable_timing=True)
+        end.record(stream)
+        end.synchronize()
     stages, prev = {}, start
     for name, ev in marks:
         stages[name] = round(prev.elapsed_time(ev), 3)

@@ -357,6 +357,17 @@ int osor_layer_norm(const void* x, void* y, const float* gamma, const float* bet
  * (src/native/transformer.rs:17-23). */
 int osor_geglu(const void* x, void* y, long long rows, int features, int dtype, void* stream);
 
+/* Column matrix of a thin-input k x k convolution (zero padding pad, stride
+ * 1): x NCHW f32 [B][cin][H][W] -> cols 16-bit [B][H][W][ncols] (ncols 64 or
+ * 128, k * k * cin <= ncols) with column (ky * k + kx) * cin + ci = x[b][ci]
+ * [y + ky - pad][x + kx - pad] (zero outside the image) and the columns past
+ * k * k * cin zero, so that the convolution is a 1x1 tensor-core product
+ * over ncols input channels (the UNet's conv_in: 9 channels, 81 taps).
+ * Replaces the column fill of conv2d_checked for thin inputs
+ * (src/native/columns.rs:42-75, 297-368). */
+int osor_thin_columns(const float* x, void* cols, int batch, int cin, int height, int width,
+                      int ksize, int pad, int ncols, int dtype, void* stream);
+
 /* FeedForward's input projection and GEGLU gate in one call: y[p][f] =
  * value * gelu_erf(gate) with (value, gate) = the 1x1 product x W^T + bias,
  * x NHWC [B][H][W][cin] 16-bit, y [B][H][W][features] 16-bit (features %

@@ -708,6 +708,25 @@ int osor_geglu(const void* x, void* y, long long rows, int features, int dtype, 
   return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "GEGLU");
 }
 
+int osor_thin_columns(const float* x, void* cols, int batch, int cin, int height, int width,
+                      int ksize, int pad, int ncols, int dtype, void* stream) {
+  if (!x || !cols) return fail(OSOR_ERR_INVALID_INPUT, "null argument");
+  if (batch <= 0 || cin <= 0 || height <= 0 || width <= 0 || ksize <= 0 || pad < 0)
+    return fail(OSOR_ERR_INVALID_INPUT, "invalid column-matrix shape");
+  if ((ncols != 64 && ncols != 128) || ksize * ksize * cin > ncols)
+    return fail(OSOR_ERR_INVALID_INPUT, "the taps x channels must fit 64 or 128 columns");
+  if (!is16(dtype)) return fail(OSOR_ERR_INVALID_INPUT, "column dtype must be BF16 or F16");
+  if (!aligned16(cols)) return fail(OSOR_ERR_INVALID_INPUT, "columns must be 16-byte aligned");
+  DeviceOf dev(x);
+  osor::OpScope scope("thin_columns", 0.0, 4.0 * batch * height * width * cin +
+                                               2.0 * ncols * batch * height * width,
+                      static_cast<cudaStream_t>(stream), 1);
+  const cudaError_t e =
+      osor::thin_columns_launch(internal_dtype(dtype), x, cols, batch, cin, height, width, ksize,
+                                pad, nullptr, nullptr, static_cast<cudaStream_t>(stream), ncols);
+  return e == cudaSuccess ? OSOR_OK : cuda_fail(e, "column matrix");
+}
+
 size_t osor_linear_geglu_workspace_size(int batch, int height, int width, int cin, int features,
                                         int dtype) {
   if (batch <= 0 || height <= 0 || width <= 0 || cin <= 0 || cin % 8 != 0 || features <= 0 ||

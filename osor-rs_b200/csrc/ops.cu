@@ -268,7 +268,7 @@ __global__ void nhwc16_to_nchw_f32_kernel(const uint16_t* __restrict__ xb, float
 
 // Column matrix of a thin-input convolution: for output pixel (b, oy, ox),
 // column j < k*k*cin holds input channel j % cin at tap j / cin = (ky, kx)
-// (zero outside the image), columns up to 64 are zero. With pre_w, every input
+// (zero outside the image), columns up to ncols (64 or 128) are zero. With pre_w, every input
 // pixel first goes through a 1x1 convolution pre_w [cin][cin] + pre_b (the
 // decoder's post_quant_conv), and padding stays zero as in the reference
 // (the second convolution pads the first one's output). One thread per pixel.
@@ -276,7 +276,7 @@ template <int D>
 __global__ void thin_columns_kernel(const float* __restrict__ x, uint4* __restrict__ cols,
                                     int batch, int cin, int h, int w, int k, int pad,
                                     const float* __restrict__ pre_w,
-                                    const float* __restrict__ pre_b) {
+                                    const float* __restrict__ pre_b, int ncols) {
   const long long pix = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long total = (long long)batch * h * w;
   if (pix >= total) return;
@@ -287,7 +287,7 @@ __global__ void thin_columns_kernel(const float* __restrict__ x, uint4* __restri
   const float* xb = x + b * cin * plane;
   const int used = k * k * cin;
 #pragma unroll 1
-  for (int j0 = 0; j0 < 64; j0 += 8) {
+  for (int j0 = 0; j0 < ncols; j0 += 8) {
     float v[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
@@ -308,7 +308,7 @@ __global__ void thin_columns_kernel(const float* __restrict__ x, uint4* __restri
       }
       v[u] = val;
     }
-    cols[pix * 8 + j0 / 8] = pack8<D>(v);
+    cols[pix * (ncols / 8) + j0 / 8] = pack8<D>(v);
   }
 }
 
@@ -396,15 +396,17 @@ cudaError_t nhwc16_to_nchw_f32_launch(int dtype, const void* x, float* y, int ba
 
 cudaError_t thin_columns_launch(int dtype, const float* x, void* cols, int batch, int cin, int h,
                                 int w, int k, int pad, const float* pre_w, const float* pre_b,
-                                cudaStream_t s) {
-  if (k * k * cin > 64) return cudaErrorInvalidValue;
+                                cudaStream_t s, int ncols) {
+  if ((ncols != 64 && ncols != 128) || k * k * cin > ncols) return cudaErrorInvalidValue;
   const long long total = (long long)batch * h * w;
   const unsigned grid = (unsigned)((total + 127) / 128);
   uint4* c = static_cast<uint4*>(cols);
   if (dtype == kF16)
-    thin_columns_kernel<kF16><<<grid, 128, 0, s>>>(x, c, batch, cin, h, w, k, pad, pre_w, pre_b);
+    thin_columns_kernel<kF16><<<grid, 128, 0, s>>>(x, c, batch, cin, h, w, k, pad, pre_w, pre_b,
+                                                   ncols);
   else
-    thin_columns_kernel<kBf16><<<grid, 128, 0, s>>>(x, c, batch, cin, h, w, k, pad, pre_w, pre_b);
+    thin_columns_kernel<kBf16><<<grid, 128, 0, s>>>(x, c, batch, cin, h, w, k, pad, pre_w, pre_b,
+                                                    ncols);
   return cudaGetLastError();
 }
 

@@ -44,11 +44,12 @@ cudaError_t nchw_f32_to_nhwc16_launch(int dtype, const float* x, void* y, int ba
                                       long long hw, cudaStream_t s);
 cudaError_t nhwc16_to_nchw_f32_launch(int dtype, const void* x, float* y, int batch, int c,
                                       long long hw, cudaStream_t s);
-// 64-column matrix [B*h*w][64] (16-bit) of a thin-input k x k convolution over
-// NCHW f32 x (k*k*cin <= 64), with an optional per-pixel 1x1 pre-convolution
-// pre_w [cin][cin] + pre_b applied to x first (nullable).
+// Column matrix [B*h*w][ncols] (16-bit, ncols 64 or 128) of a thin-input
+// k x k convolution over NCHW f32 x (k*k*cin <= ncols), with an optional
+// per-pixel 1x1 pre-convolution pre_w [cin][cin] + pre_b applied to x first
+// (nullable).
 cudaError_t thin_columns_launch(int dtype, const float* x, void* cols, int batch, int cin, int h,
                                 int w, int k, int pad, const float* pre_w, const float* pre_b,
-                                cudaStream_t s);
+                                cudaStream_t s, int ncols = 64);
 
 }  // namespace osor

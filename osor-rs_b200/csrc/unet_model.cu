@@ -97,6 +97,10 @@ struct Unet {
   int tokens = 0;
   int base = 0, time_dim = 0, feat_w = 0;
   Product conv_in, conv_out;
+  // conv_in as a 1x1 product over the 128-column matrix of its 81 taps x
+  // channels (thin_columns_launch's order; 384 rows at SDXL width, rows past
+  // 320 zero).
+  Product conv_in_cols;
   Norm norm_out;
   uint16_t* emb_w1 = nullptr;
   float* emb_b1 = nullptr;
@@ -494,7 +498,19 @@ class Run {
     // host.
     using ActP = std::shared_ptr<Act>;
     ActP xs = std::make_shared<Act>();
-    {
+    if (m.conv_in_cols.w) {
+      // conv_in on tensor cores: the column matrix of the nine-channel input,
+      // then a 1x1 product (narrowed from 384 to 320 channels).
+      Act cols;
+      OSOR_TRY(act(b, h, w, 128, &cols));
+      {
+        OpScope scope("thin_columns", 0.0, 4.0 * b * h * w * 9 + 256.0 * b * h * w, s_, 1);
+        OSOR_TRY(cuda_err(thin_columns_launch(m.dtype, input, cols.p(), b, 9, h, w, 3, 1, nullptr,
+                                              nullptr, s_, 128),
+                          "thin input columns"));
+      }
+      OSOR_TRY(conv(cols, m.conv_in_cols, 1, nullptr, nullptr, xs.get()));
+    } else {
       OSOR_TRY(act(b, h, w, m.conv_in.cout, xs.get()));
       ConvLayer L;
       L.cin = m.conv_in.cin;
@@ -742,6 +758,19 @@ Status unet_create(const osor_tensor* tensors, size_t count, const osor_unet_con
   OSOR_TRY(ld.pack(context, tokens, cfg->context, 1, tokens, &ctx16));
   OSOR_TRY(ld.upload(pooled, (size_t)cfg->pooled > 0 ? cfg->pooled : 1, &m->pooled));
   OSOR_TRY(ld.conv("conv_in", 9, base, 3, &m->conv_in, false));
+  {
+    // conv_in's 3 x 3 x 9 taps as columns (tap-major, then channel) of a 1x1
+    // product over 128 columns.
+    const float *w, *b;
+    OSOR_TRY(ld.get("conv_in.weight", {base, 9, 3, 3}, &w));
+    OSOR_TRY(ld.get("conv_in.bias", {base}, &b));
+    std::vector<float> cols((size_t)base * 128, 0.0f);
+    for (int co = 0; co < base; ++co)
+      for (int ci = 0; ci < 9; ++ci)
+        for (int t = 0; t < 9; ++t)
+          cols[(size_t)co * 128 + t * 9 + ci] = w[((size_t)co * 9 + ci) * 9 + t];
+    OSOR_TRY(ld.product_from(cols.data(), b, base, 128, 1, true, &m->conv_in_cols));
+  }
   {
     const float *w1t, *b1t, *w2t, *b2t, *w1a, *b1a, *w2a, *b2a;
     const int add_w = cfg->pooled + 6 * cfg->time_projection;

@@ -132,6 +132,7 @@ SIGNATURES = {
     "osor_rows_linear": (_i, [_vp, _i, _i, _vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "osor_layer_norm": (_i, [_vp, _vp, _vp, _vp, _ll, _i, _f, _i, _vp]),
     "osor_geglu": (_i, [_vp, _vp, _ll, _i, _i, _vp]),
+    "osor_thin_columns": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "osor_linear_geglu_workspace_size": (_sz, [_i, _i, _i, _i, _i, _i]),
     "osor_linear_geglu": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _sz, _vp]),
     "osor_concat_channels": (_i, [_vp, _i, _vp, _i, _vp, _ll, _i, _vp]),

@@ -461,6 +461,13 @@ class CudaUnetOps:
                          and w[name].shape[1] % 8 == 0)
                 self.products[stem] = _Product(w[name], w.get(stem + ".bias"), device, dtype,
                                                pad=stem != "conv_in", geglu=geglu)
+        # conv_in as a 1x1 product over the 128-column matrix of its 3 x 3 x 9
+        # taps (osor_thin_columns' order: tap-major, then channel).
+        cw = w["conv_in.weight"].to(device=device, dtype=torch.float32)
+        co, ci = cw.shape[0], cw.shape[1]
+        cols = torch.zeros((co, 128), device=device, dtype=torch.float32)
+        cols[:, :9 * ci] = cw.permute(0, 2, 3, 1).reshape(co, 9 * ci)
+        self.products["conv_in.cols"] = _Product(cols, w.get("conv_in.bias"), device, dtype)
         # Attention: fused self-attention q|k|v, scaled cross-attention q, prompt K / V.
         self.cross_kv: Dict[str, Tuple[torch.Tensor, torch.Tensor]] = {}
         ctx16 = ctx.to(dtype).reshape(1, 1, ctx.shape[1], arch.context).contiguous()
@@ -550,8 +557,14 @@ class CudaUnetOps:
     linear = conv
 
     def conv_in(self, sample: torch.Tensor) -> torch.Tensor:
-        p = self.products["conv_in"]
         b, c, h, w = sample.shape
+        if 9 * c <= 128:
+            # The column matrix, then a tensor-core 1x1 product (narrowed).
+            cols = torch.empty((b, h, w, 128), device=sample.device, dtype=self.dtype)
+            check(self.lib.osor_thin_columns(_ptr(sample), _ptr(cols), b, c, h, w, 3, 1, 128,
+                                             self.dt, self.stream))
+            return self.conv(cols, "conv_in.cols")
+        p = self.products["conv_in"]
         y = torch.empty((b, h, w, p.cout), device=sample.device, dtype=self.dtype)
         check(self.lib.osor_conv2d(_ptr(sample), _ptr(y), _ptr(p.weight), _ptr(p.bias), None, b,
                                    h, w, c, p.cout, 3, 1, 1, 1, _lib.LAYOUT_NCHW,

@@ -112,6 +112,27 @@ def test_geglu_matches_exact_erf(cuda_device):
     assert abs(float(out[0, 0]) - 1.9544997215270996) < 1e-3
 
 
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_thin_columns_match_im2col(dt, cuda_device):
+    """osor_thin_columns: the UNet conv_in's 3 x 3 x 9 column matrix over 128
+    columns, tap-major then channel, zero outside the image and past 81."""
+    rng = np.random.default_rng(12)
+    b, c, h, w = 2, 9, 5, 7
+    x = torch.from_numpy(rng.standard_normal((b, c, h, w)).astype(np.float32)).cuda()
+    cols = torch.full((b, h, w, 128), 7.0, device="cuda", dtype=dt)
+    check(_lib.lib().osor_thin_columns(P(x), P(cols), b, c, h, w, 3, 1, 128, dtype_code(dt), S()))
+    xp = np.pad(host(x.to(dt)), ((0, 0), (0, 0), (1, 1), (1, 1)))
+    want = np.zeros((b, h, w, 128), np.float32)
+    for ky in range(3):
+        for kx in range(3):
+            t = ky * 3 + kx
+            want[..., t * c:(t + 1) * c] = xp[:, :, ky:ky + h, kx:kx + w].transpose(0, 2, 3, 1)
+    np.testing.assert_array_equal(host(cols), want)
+    with pytest.raises(InvalidInput):
+        check(_lib.lib().osor_thin_columns(P(x), P(cols), b, c, h, w, 3, 1, 64, dtype_code(dt),
+                                           S()))
+
+
 # (batch, h, w, cin, features, fused): 2048 pixels (16 tiles) on CTA pairs
 # with the gate in the product's epilogue; 384 pixels (3 tiles, odd) through
 # the workspace (product, then the interleaved GEGLU pass).
