@@ -59,7 +59,10 @@ def _peaks():
 
 
 class ClockSampler:
-    """Samples nvidia-smi SM clocks and throttle reasons during the timed region."""
+    """Samples SM clocks and throttle reasons during the timed region: nvidia-smi
+    every 200 ms and, where the NVML bindings load, NVML every 20 ms (reads
+    only), so that a timed region of a few hundred milliseconds still gets a
+    median over many samples."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -69,8 +72,26 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.lines = []
+        self.nvml = []  # (sm MHz, max MHz, reasons bitmask)
+        self.stop = threading.Event()
+        self.thread = None
+
+    def _poll_nvml(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            while not self.stop.is_set():
+                self.nvml.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), mx,
+                                  pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                self.stop.wait(0.02)
+        except Exception:  # no NVML here: nvidia-smi's samples stand alone
+            return
 
     def __enter__(self):
+        self.thread = threading.Thread(target=self._poll_nvml, daemon=True)
+        self.thread.start()
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
@@ -86,6 +107,9 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self.stop.set()
+        if self.thread:
+            self.thread.join(timeout=5)
         if self.proc:
             self.proc.terminate()
             try:
@@ -94,6 +118,16 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        if len(self.nvml) >= 3:
+            bits = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40,
+                    "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
+            seen = set()
+            for _, _, r in self.nvml:
+                seen |= {name for name, bit in bits.items() if r & bit}
+            return {"sm_mhz": statistics.median(c for c, _, _ in self.nvml),
+                    "sm_max_mhz": float(self.nvml[0][1]), "reasons": sorted(seen),
+                    "samples": len(self.nvml), "source": "NVML every 20 ms",
+                    "nvidia_smi_samples": len(self.lines)}
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.lines:
