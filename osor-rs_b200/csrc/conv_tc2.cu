@@ -433,10 +433,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Tc2Shape<FUSE>::kThr
       tc_fence_after();
       const float scale = p.row_scale ? __ldg(p.row_scale + m) : 1.0f;
       // GEGLU (GG): with BN 256 and four slots this warp's chunks are `slot`
-      // (values) and `slot + 4` (their gates); the values wait here.
+      // (values) and `slot + 4` (their gates); the values wait here, rounded
+      // to the 16-bit type as a stored projection would be.
       static_assert(!GG || (BN == 256 && kChunks == 2 && CPG == 0 && FUSE == 0),
                     "GEGLU epilogue: BN 256, four slots, no statistics");
-      float gv[GG ? 32 : 1];
+      uint32_t gv[GG ? 16 : 1];
 #pragma unroll 1
       for (int ci = 0; ci < kChunks; ++ci) {
         const int chunk = slot + kSlots * ci;
@@ -486,12 +487,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Tc2Shape<FUSE>::kThr
         if constexpr (GG != 0) {
           if (ci == 0) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) gv[j] = v[j];
+            for (int j = 0; j < 16; ++j) gv[j] = Elem<D>::pack(v[2 * j], v[2 * j + 1]);
             continue;
           }
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            v[j] = gv[j] * (0.5f * v[j] * (1.0f + erff(v[j] * 0.70710678118654752f)));
+          for (int j = 0; j < 16; ++j) {
+            const float2 a = Elem<D>::unpack(gv[j]);
+            const float g0 = v[2 * j], g1 = v[2 * j + 1];
+            v[2 * j] = a.x * (0.5f * g0 * (1.0f + erff(g0 * 0.70710678118654752f)));
+            v[2 * j + 1] = a.y * (0.5f * g1 * (1.0f + erff(g1 * 0.70710678118654752f)));
+          }
           oc = (long long)n_tile * (BN / 2) + slot * 32;
         }
         uint4* o4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + orow * p.ld_out + oc);
