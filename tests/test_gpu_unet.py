@@ -1,9 +1,10 @@
 """SDXL UNet on the GPU against the oracle.
 
 Op level: the UNet kernels of libosor_b200 (time features, row linear,
-LayerNorm, GEGLU, multi-head attention, concatenation, nearest resize, channel
-update, wide-channel GroupNorm, the zero-padded 320-channel convolution)
-against numpy / float64 restatements on the same 16-bit inputs. Model level:
+LayerNorm, GEGLU, the fused GEGLU product, conv_in's column matrix,
+multi-head attention, concatenation, nearest resize, channel update,
+wide-channel GroupNorm, the zero-padded 320-channel convolution) against
+numpy / float64 restatements on the same 16-bit inputs. Model level:
 ``NativeUnet`` against ``oracle.unet.forward`` for the reference's tiny test
 model (deterministic weights) and for a one-layer model with SDXL's widths
 (320 / 640 / 1280 channels, 5 / 10 / 20 heads, 2560-channel skip
