@@ -148,6 +148,47 @@ def test_unet_handle_entry_points_validate_on_the_host():
     lb.osor_unet_destroy(None)
 
 
+def test_geglu_product_and_columns_validate_on_the_host():
+    """osor_linear_geglu's workspace query is shape arithmetic: zero where the
+    CTA-pair kernel takes the product (an even count of 128-pixel tiles, 2F a
+    multiple of 256, Cin % 64 == 0), the [pixels, 2F] 16-bit product
+    otherwise, zero for shapes it refuses; both entry points refuse bad
+    arguments before any device work."""
+    lb = _lib.lib()
+    bad = _lib.OSOR_ERR_INVALID_INPUT
+    bf16 = _lib.DTYPE_BF16
+    assert lb.osor_linear_geglu_workspace_size(4, 32, 32, 1280, 5120, bf16) == 0
+    assert lb.osor_linear_geglu_workspace_size(4, 64, 64, 640, 2560, bf16) == 0
+    assert lb.osor_linear_geglu_workspace_size(1, 3, 128, 128, 128, bf16) == 384 * 256 * 2
+    assert lb.osor_linear_geglu_workspace_size(1, 2, 128, 72, 128, bf16) == 256 * 256 * 2
+    assert lb.osor_linear_geglu_workspace_size(1, 2, 128, 128, 100, bf16) == 0
+    assert lb.osor_linear_geglu_workspace_size(1, 2, 128, 128, 128, _lib.DTYPE_F32) == 0
+    assert lb.osor_linear_geglu(None, None, None, None, 1, 2, 128, 128, 128, bf16, None, 0,
+                                None) == bad
+    x = np.zeros(64, np.float32)
+    assert lb.osor_linear_geglu(x.ctypes.data, x.ctypes.data, x.ctypes.data, None, 1, 2, 128,
+                                128, 100, bf16, None, 0, None) == bad
+    assert lb.osor_thin_columns(x.ctypes.data, x.ctypes.data, 1, 9, 4, 4, 3, 1, 64, bf16,
+                                None) == bad  # 81 taps x channels need 128 columns
+    assert lb.osor_thin_columns(x.ctypes.data, x.ctypes.data, 1, 9, 4, 4, 3, 1, 96, bf16,
+                                None) == bad
+    assert lb.osor_thin_columns(None, None, 1, 9, 4, 4, 3, 1, 128, bf16, None) == bad
+
+
+def test_unet_geglu_rows_follow_the_documented_order():
+    """The Python host's GEGLU row order: per 128 features, the 128 value rows
+    and then their gate rows (the order osor_linear_geglu documents)."""
+    import torch
+    from osor_b200.unet import _geglu_rows
+    f = 384
+    got = _geglu_rows(f, torch.device("cpu")).tolist()
+    want = []
+    for t in range(f // 128):
+        want += list(range(t * 128, t * 128 + 128))
+        want += list(range(f + t * 128, f + t * 128 + 128))
+    assert got == want
+
+
 def test_device_check_reports_unavailable_without_gpu():
     import torch
     if torch.cuda.is_available():
