@@ -442,6 +442,55 @@ def run_ops(args):
                           "frac_of_sustained_peak": round(tf / tflops_sus, 4),
                           "gpu_launches": launches, "peak_source": src,
                           "breakdown": breakdown}), flush=True)
+    elif args.op == "geglu":
+        # FeedForward's input projection and GEGLU gate at the SDXL UNet's two
+        # transformer levels for the 4 x 1024^2 job (bf16): the fused product
+        # (osor_linear_geglu, gate in the CTA-pair epilogue) against the
+        # product stored at 2F channels followed by the GEGLU pass.
+        import ctypes
+        lb = _lib.lib()
+        dt = torch.bfloat16
+        code = _lib.dtype_code(dt)
+        g = torch.Generator(device=dev).manual_seed(4)
+        stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+        def ptr(t):
+            return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+        for b, h, w, cin, f in [(4, 64, 64, 640, 2560), (4, 32, 32, 1280, 5120)]:
+            x = torch.randn((b, h, w, cin), generator=g, device=dev).to(dt)
+            wt = (torch.randn((2 * f, cin), generator=g, device=dev) / cin ** 0.5).to(dt)
+            bias = torch.randn((2 * f,), generator=g, device=dev) * 0.1
+            r = torch.arange(2 * f, device=dev)
+            order = torch.where(r % 256 < 128, (r // 256) * 128 + r % 256,
+                                f + (r // 256) * 128 + r % 256 - 128)
+            wi, bi = wt[order].contiguous(), bias[order].contiguous()
+            y = torch.empty((b, h, w, f), device=dev, dtype=dt)
+            hidden = torch.empty((b, h, w, 2 * f), device=dev, dtype=dt)
+            need = lb.osor_linear_geglu_workspace_size(b, h, w, cin, f, code)
+            ws = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+
+            def fused():
+                _lib.check(lb.osor_linear_geglu(ptr(x), ptr(y), ptr(wi), ptr(bi), b, h, w, cin, f,
+                                                code, ptr(ws), need, stream))
+
+            def unfused():
+                _lib.check(lb.osor_conv2d(ptr(x), ptr(hidden), ptr(wt), ptr(bias), None, b, h, w,
+                                          cin, 2 * f, 1, 1, 0, 0, _lib.LAYOUT_NHWC,
+                                          _lib.LAYOUT_NHWC, code, stream))
+                _lib.check(lb.osor_geglu(ptr(hidden), ptr(y), b * h * w, f, code, stream))
+
+            ms = _timed(fused, args.steps, args.warmup, flush)
+            ms_unfused = _timed(unfused, args.steps, args.warmup, flush)
+            flop = 2.0 * b * h * w * cin * 2 * f
+            print(json.dumps({"op": "geglu product (FeedForward net.0.proj + gate)",
+                              "shape": [b * h * w, cin, 2 * f], "dtype": "bf16",
+                              "path": "fused (CTA pairs, gate in the epilogue)" if need == 0
+                              else "workspace (product, then GEGLU pass)",
+                              "ms": round(ms, 4), "tflops": round(flop / (ms / 1e3) / 1e12, 1),
+                              "unfused_ms": round(ms_unfused, 4),
+                              "unfused_tflops": round(flop / (ms_unfused / 1e3) / 1e12, 1),
+                              "peak_source": src}), flush=True)
     elif args.op == "attn_heads":
         # The SDXL UNet's multi-head attention for the 4 x 1024^2 job (batch 4,
         # head width 64, f16 or bf16): self-attention on the fused q|k|v
@@ -776,7 +825,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op", default="decode",
                     choices=["decode", "conv3x3", "groupnorm", "encode", "noise", "unet", "e2e",
-                             "attn_heads"],
+                             "attn_heads", "geglu"],
                     help="decode: the headline line; others: standalone op lines; e2e: the "
                          "end-to-end inpainting call at B=4, 1024^2")
     ap.add_argument("--shape", default=None, help="comma-separated shape for --op conv3x3/groupnorm")
