@@ -40,6 +40,14 @@
 // `ready` barrier, which gates the MMAs instead. 448 threads: warps 2..9
 // epilogue (two per TMEM lane quadrant), warps 10..13 transform.
 //
+// GEGLU epilogue (GG = 1, its own instantiation: BN 256, no statistics or
+// FUSE): the 1x1 product of a GEGLU input projection whose weight rows come
+// as 128 value rows then their 128 gate rows per 256-row channel tile. An
+// epilogue warp's two chunks of a tile are then a value chunk and its gate
+// chunk; it stores value * gelu_erf(gate) at channel tile * 128 + chunk * 32
+// of a cout / 2 wide output (FeedForward::forward, src/native/transformer.rs:
+// 18-24).
+//
 // Reference counterpart: the same convolution as conv_tc.cu
 // (BandedConv2d::forward_checked, src/native/conv.rs:54-145).
 #include <atomic>
