@@ -416,7 +416,8 @@ def run_ops(args):
         launches = _lib.launch_count() - before
         eager_ms = _timed(lambda: unet(x, 400, ids), args.steps, args.warmup, flush)
         native_ms = _timed(lambda: native(x, 400, ids), args.steps, args.warmup, flush)
-        ms = _timed(lambda: replay(x, 400, ids), args.steps, args.warmup, flush)
+        with ClockSampler(0) as clocks:
+            ms = _timed(lambda: replay(x, 400, ids), args.steps, args.warmup, flush)
         flop = unet_flops(arch, 4, 128, 128)
         tf = flop / (ms / 1e3) / 1e12
         # Per-kind breakdown of one call from CUDA events around each op.
@@ -441,7 +442,7 @@ def run_ops(args):
                           "tflop_per_call": round(flop / 1e12, 2), "tflops": round(tf, 1),
                           "frac_of_sustained_peak": round(tf / tflops_sus, 4),
                           "gpu_launches": launches, "peak_source": src,
-                          "breakdown": breakdown}), flush=True)
+                          "clocks": clocks.summary(), "breakdown": breakdown}), flush=True)
     elif args.op == "geglu":
         # FeedForward's input projection and GEGLU gate at the SDXL UNet's two
         # transformer levels for the 4 x 1024^2 job (bf16): the fused product
