@@ -188,3 +188,26 @@ def test_native_runtime_handle_requires_a_cuda_device():
     with pytest.raises(_lib.InvalidInput):  # prompt width does not match the architecture
         UnetExecutor(random_unet_weights(arch), np.zeros((1, 2, 4), np.float32),
                      np.zeros((1, 8), np.float32), arch=arch)
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_fused_geglu_rounding_is_no_worse_than_the_stored_projection(dt):
+    """The fused GEGLU product rounds the value half to 16 bits (as a stored
+    projection would be) but gates with the f32 accumulator, where the unfused
+    path also rounds the gate before gelu_erf. A CPU emulation of both on the
+    same 16-bit operands: against the f64 result the fused rounding is never
+    worse than the stored projection's (transformer.rs:18-24)."""
+    rng = np.random.default_rng(21)
+    rows, cin, f = 512, 320, 256
+    q = lambda a: torch.from_numpy(np.asarray(a, np.float32)).to(dt).float().numpy()  # noqa: E731
+    x = q(rng.standard_normal((rows, cin)))
+    w = q(rng.standard_normal((2 * f, cin)) / np.sqrt(cin))
+    proj = x.astype(np.float64) @ w.astype(np.float64).T
+    value, gate = proj[:, :f], proj[:, f:]
+    exact = value * U.gelu_erf(gate).astype(np.float64)
+    acc = proj.astype(np.float32)  # the f32 accumulator
+    unfused = q(q(acc[:, :f]) * U.gelu_erf(q(acc[:, f:])))
+    fused = q(q(acc[:, :f]) * U.gelu_erf(acc[:, f:]))
+    err_unfused = np.abs(unfused - exact).max()
+    err_fused = np.abs(fused - exact).max()
+    assert err_fused <= err_unfused * 1.001 + 1e-7, (err_fused, err_unfused)
